@@ -1,0 +1,222 @@
+// Shared helpers for the sm_100a kernels: status plumbing, dtype traits,
+// block-wide scans and the inline-PTX wrappers (mbarrier, TMA, ldmatrix,
+// mma.sync, movmatrix) used by the attention pipeline.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <string>
+
+#include "sdl_b200.h"
+
+// ------------------------------------------------------------------ host side
+namespace sdl {
+
+void set_last_error(const std::string& msg);
+
+inline int fail(sdl_status code, const char* msg) {
+    set_last_error(msg);
+    return (int)code;
+}
+
+inline int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error(std::string(what) + ": " + cudaGetErrorString(e));
+        return (int)SDL_ERR_CUDA;
+    }
+    return (int)SDL_OK;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int dtype_bytes(int dt) { return dt == SDL_F32 ? 4 : 2; }
+
+}  // namespace sdl
+
+// ---------------------------------------------------------------- device side
+#define SDL_DEV __device__ __forceinline__
+
+SDL_DEV void sdl_raise(int32_t* err, int bits) {
+    if (err != nullptr) atomicOr(err, bits);
+}
+
+template <typename T> SDL_DEV float to_f32(T v);
+template <> SDL_DEV float to_f32<float>(float v) { return v; }
+template <> SDL_DEV float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> SDL_DEV float to_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T> SDL_DEV T from_f32(float v);
+template <> SDL_DEV float from_f32<float>(float v) { return v; }
+template <> SDL_DEV __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> SDL_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+SDL_DEV float load_as_f32(const void* base, int64_t idx, int dtype) {
+    if (dtype == SDL_F32) return reinterpret_cast<const float*>(base)[idx];
+    if (dtype == SDL_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+    return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+}
+
+SDL_DEV void store_from_f32(void* base, int64_t idx, int dtype, float v) {
+    if (dtype == SDL_F32) reinterpret_cast<float*>(base)[idx] = v;
+    else if (dtype == SDL_BF16) reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+}
+
+// Exclusive scan of one int per thread across the whole block (blockDim a
+// multiple of 32, <= 1024).  `warp_sums` needs 32 ints of shared memory.
+// Returns the exclusive prefix; *total receives the block sum.
+template <typename V>
+SDL_DEV V block_exclusive_scan(V v, V* warp_sums, V* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    V x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        V y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        V w = lane < nwarps ? warp_sums[lane] : V(0);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            V y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nwarps) warp_sums[lane] = w;  // inclusive warp prefix
+    }
+    __syncthreads();
+    V warp_off = warp > 0 ? warp_sums[warp - 1] : V(0);
+    *total = warp_sums[nwarps - 1];
+    V res = warp_off + x - v;
+    __syncthreads();  // warp_sums may be reused by the caller
+    return res;
+}
+
+template <typename V>
+SDL_DEV V block_sum(V v, V* warp_sums) {
+    V total;
+    (void)block_exclusive_scan<V>(v, warp_sums, &total);
+    return total;
+}
+
+SDL_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+SDL_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// -------------------------------------------------------------- inline PTX
+SDL_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+SDL_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+
+SDL_DEV void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+SDL_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+SDL_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+SDL_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false when the barrier did not complete within
+// `limit` polls (each try_wait already suspends for a system-defined time).
+SDL_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+
+// 4-D tiled TMA load global -> shared, completing on `bar`.
+SDL_DEV void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar,
+                         int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tmap)),
+           "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+
+SDL_DEV void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+SDL_DEV void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+SDL_DEV void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+SDL_DEV uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, fp32 accumulate.
+template <typename T> SDL_DEV void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1);
+
+template <> SDL_DEV void mma_16816<__nv_bfloat16>(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <> SDL_DEV void mma_16816<__half>(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Pack two fp32 values into one 32-bit register of the 16-bit type T
+// (lower half = first argument).
+template <typename T> SDL_DEV uint32_t pack2(float lo, float hi);
+template <> SDL_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> SDL_DEV uint32_t pack2<__half>(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T> SDL_DEV float round_trip(float v) { return to_f32<T>(from_f32<T>(v)); }

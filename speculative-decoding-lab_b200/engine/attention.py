@@ -1,0 +1,234 @@
+"""Paged attention entry points backed by the sm_100a kernels.
+
+Drop-in for the reference's ``engine/attention.py`` (engine/attention.py:32-215):
+the same function names, arguments, shapes and semantics.  Instead of
+gathering each sequence's pages into a dense tensor and calling SDPA per
+sequence, every call is one launch of ``sdl_paged_attention`` over the whole
+batch, reading K/V pages in place through the device block table:
+
+* decode  -- row ``b`` attends its first ``seq_token_lengths[b]`` positions,
+  unmasked (engine/attention.py:96-118);
+* extend  -- chunk row ``j`` of sequence ``b`` attends positions
+  ``0 .. start_positions[b] + j`` (engine/attention.py:170-215);
+* prefill -- causal attention within a dense chunk, padded rows zeroed
+  (engine/attention.py:121-167).
+
+Softmax scale is ``1/sqrt(head_dim)`` (SDPA's default) and GQA maps q head
+``h`` to kv head ``h // (Hq / Hkv)`` (engine/attention.py:32-38).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from .kv import PagedKVCache
+
+
+class AttnBatch:
+    """Device-side description of one attention call's rows.
+
+    ``rows`` are block-table rows (sequence ids), ``starts[b]`` the absolute
+    position of chunk row 0 of entry ``b``; ``max_limit`` is a host upper
+    bound of ``starts[b] + chunk`` used to size the launch grid.
+    """
+
+    __slots__ = ("rows", "starts", "max_limit", "valid_rows")
+
+    def __init__(self, rows: torch.Tensor, starts: torch.Tensor, max_limit: int,
+                 valid_rows: Optional[torch.Tensor] = None) -> None:
+        self.rows = rows
+        self.starts = starts
+        self.max_limit = int(max_limit)
+        self.valid_rows = valid_rows
+
+    @classmethod
+    def from_lists(cls, device: torch.device, seq_ids: Sequence[int], starts: Sequence[int], chunk: int) -> "AttnBatch":
+        seq_ids = [int(s) for s in seq_ids]
+        starts = [int(s) for s in starts]
+        n = len(seq_ids)
+        packed = _lib.i32(seq_ids + starts, device)
+        max_limit = (max(starts) + chunk) if n else chunk
+        return cls(packed[:n], packed[n:], max_limit)
+
+
+def _args_common(q: torch.Tensor, out: torch.Tensor, Hkv: int, err: Optional[torch.Tensor]) -> _lib.SdlAttnArgs:
+    a = _lib.SdlAttnArgs()
+    a.q = q.data_ptr()
+    a.q_sb, a.q_sj, a.q_sh = q.stride(0), q.stride(1), q.stride(2)
+    a.out = out.data_ptr()
+    a.o_sb, a.o_sj, a.o_sh = out.stride(0), out.stride(1), out.stride(2)
+    a.out_dtype = _lib.dtype_code(out.dtype)
+    a.dtype = _lib.dtype_code(q.dtype)
+    a.B, a.chunk, a.Hq, a.head_dim = q.shape[0], q.shape[1], q.shape[2], q.shape[3]
+    a.Hkv = Hkv
+    a.scale = 1.0 / math.sqrt(q.shape[3])
+    a.err = err.data_ptr() if err is not None else None
+    return a
+
+
+def _launch(a: _lib.SdlAttnArgs, device: torch.device, fn: str = "sdl_paged_attention") -> None:
+    lib = _lib.load()
+    need = lib.sdl_attention_workspace_bytes(a)
+    if need:
+        ws = _lib.Workspace.get(device, int(need))
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = ws.numel() * 4
+    _lib.check(getattr(lib, fn)(a, _lib.stream_handle(device)), fn)
+
+
+def paged_attention(
+    q: torch.Tensor,
+    kv: PagedKVCache,
+    layer: int,
+    batch: AttnBatch,
+    out: Optional[torch.Tensor] = None,
+    out_dtype: Optional[torch.dtype] = None,
+    force_generic: bool = False,
+    pages_per_split: int = 0,
+) -> torch.Tensor:
+    """One launch over ``q`` of shape ``(B, chunk, Hq, d)`` against the pages of ``kv``."""
+    _lib.require_cuda(q, "query")
+    if q.dim() != 4 or q.shape[3] != kv.head_dim:
+        raise ValueError("query must be (B, chunk, Hq, {}), got {}".format(kv.head_dim, tuple(q.shape)))
+    if q.dtype != kv.dtype:
+        q = q.to(kv.dtype)
+    if q.stride(3) != 1:
+        q = q.contiguous()
+    if out is None:
+        out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
+    a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
+    a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
+    mk, mv = kv.tensor_maps()
+    if mk is not None:
+        import ctypes
+        a.tmap_k, a.tmap_v = ctypes.addressof(mk), ctypes.addressof(mv)
+    a.block_table, a.width, a.capacity = kv._table.data_ptr(), kv.width, kv.capacity
+    a.num_layers, a.layer, a.block_size = kv.num_layers, int(layer), kv.block_size
+    a.rows = batch.rows.data_ptr()
+    a.starts = batch.starts.data_ptr()
+    a.valid_rows = batch.valid_rows.data_ptr() if batch.valid_rows is not None else None
+    a.max_limit = batch.max_limit
+    a.pages_per_split = int(pages_per_split)
+    a.force_generic = 1 if force_generic else 0
+    if batch.max_limit > kv.width * kv.block_size:
+        raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))
+    _launch(a, q.device)
+    return out
+
+
+def _expand_to_q_heads(kv: torch.Tensor, num_q_heads: int) -> torch.Tensor:
+    """Broadcast ``(.., kv_heads, d)`` to ``(.., num_q_heads, d)`` for GQA."""
+    kv_heads = kv.shape[-2]
+    ratio = num_q_heads // kv_heads
+    if ratio == 1:
+        return kv
+    return kv.repeat_interleave(ratio, dim=-2)
+
+
+def gather_ctx(kv: PagedKVCache, layer: int, seq_id: int, length: int) -> torch.Tensor:
+    """Return the stored K/V prefix of one sequence as ``(2, length, kv_heads, d)``.
+
+    Reads the device block table directly (no host round trip).
+    """
+    if length <= 0:
+        return torch.zeros((2, 0, kv.num_kv_heads, kv.head_dim), dtype=kv.dtype, device=kv.device)
+    n_blocks = -(-length // kv.block_size)
+    if n_blocks > kv.num_blocks_of(seq_id):
+        raise IndexError("list index out of range")
+    phys = kv._table[seq_id, :n_blocks].long()
+    key = kv._k[layer][phys].reshape(-1, kv.num_kv_heads, kv.head_dim)[:length]
+    value = kv._v[layer][phys].reshape(-1, kv.num_kv_heads, kv.head_dim)[:length]
+    return torch.stack((key, value), dim=0)
+
+
+def _dense_attention(q4: torch.Tensor, k: torch.Tensor, v: torch.Tensor, starts: List[int],
+                     valid_rows: Optional[List[int]]) -> torch.Tensor:
+    """Dense-K/V launch: q4 (B, chunk, Hq, d), k/v (B, kv_len, Hkv, d)."""
+    _lib.require_cuda(q4, "query")
+    B, chunk, Hq, d = q4.shape
+    k = k.to(q4.dtype).contiguous()
+    v = v.to(q4.dtype).contiguous()
+    if q4.stride(3) != 1:
+        q4 = q4.contiguous()
+    out = torch.zeros(q4.shape, dtype=q4.dtype, device=q4.device)
+    if B == 0:
+        return out
+    a = _args_common(q4, out, k.shape[2], None)
+    a.k_dense, a.v_dense, a.kv_len = k.data_ptr(), v.data_ptr(), k.shape[1]
+    packed = _lib.i32(list(starts) + (list(valid_rows) if valid_rows is not None else []), q4.device)
+    a.starts = packed.data_ptr()
+    a.valid_rows = packed.data_ptr() + 4 * B if valid_rows is not None else None
+    a.max_limit = max(int(s) for s in starts) + chunk
+    _launch(a, q4.device)
+    return out
+
+
+def full_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    num_q_heads: int,
+) -> torch.Tensor:
+    """Unmasked attention of ``query (Hq, d)`` over ``key/value (ctx, kv_heads, d)``."""
+    ctx = key.shape[0]
+    if ctx == 0:
+        return torch.zeros_like(query)
+    out = _dense_attention(query.reshape(1, 1, num_q_heads, -1), key.unsqueeze(0), value.unsqueeze(0),
+                           [ctx - 1], None)
+    return out[0, 0]
+
+
+def paged_attention_decode(
+    query_2d: torch.Tensor,
+    kv: PagedKVCache,
+    layer: int,
+    seq_ids: Sequence[int],
+    seq_token_lengths: Sequence[int],
+    num_q_heads: int,
+) -> torch.Tensor:
+    """Attend one new query token per row against its full stored prefix.
+
+    ``query_2d`` is ``(B, num_q_heads, d)``; returns ``(B, num_q_heads, d)``.
+    """
+    B = query_2d.shape[0]
+    lengths = [int(x) for x in seq_token_lengths]
+    batch = AttnBatch.from_lists(query_2d.device, seq_ids, [ln - 1 for ln in lengths], 1)
+    out = paged_attention(query_2d.reshape(B, 1, num_q_heads, -1), kv, layer, batch)
+    return out.reshape(B, num_q_heads, -1)
+
+
+def paged_attention_prefill_chunk(
+    query_3d: torch.Tensor,
+    key_3d: torch.Tensor,
+    value_3d: torch.Tensor,
+    num_q_heads: int,
+    chunk_query_lengths: Sequence[int],
+) -> torch.Tensor:
+    """Causal attention over a freshly prefilled prompt chunk (``query_start=0``).
+
+    Returns ``(B, chunk_len, num_q_heads, d)`` with padded rows exactly zero.
+    """
+    B = query_3d.shape[0]
+    lengths = [int(x) for x in chunk_query_lengths]
+    return _dense_attention(query_3d, key_3d, value_3d, [0] * B, lengths)
+
+
+def paged_attention_extend(
+    query_3d: torch.Tensor,
+    kv: PagedKVCache,
+    layer: int,
+    seq_ids: Sequence[int],
+    start_positions: Sequence[int],
+    num_q_heads: int,
+) -> torch.Tensor:
+    """Attend a chunk of fresh tokens against an existing prefix plus prior rows.
+
+    ``query_3d`` is ``(B, chunk, num_q_heads, d)``; returns the same shape.
+    """
+    chunk = query_3d.shape[1]
+    batch = AttnBatch.from_lists(query_3d.device, seq_ids, start_positions, chunk)
+    return paged_attention(query_3d, kv, layer, batch)

@@ -1,0 +1,353 @@
+"""Paged language-model interface and the deterministic toy implementation.
+
+Drop-in for the reference's ``engine/model.py`` (engine/model.py:41-398).  The
+"PagedLM" duck type the schedulers drive is unchanged:
+
+* ``prefill(prompt_2d, kv, seq_ids, seq_lengths) -> (B, V)`` first-token logits;
+* ``decode(input_ids, kv, seq_ids, ctx_lengths) -> (B, V)``;
+* ``decode_block(input_ids_2d, kv, seq_ids, start_positions) -> (B, chunk, V)``.
+
+The attention call sites are what change: each forward reserves the new
+positions once (``PagedKVCache.reserve``: one kernel, reference allocation
+order), and every layer does one batched K/V append and one paged-attention
+launch instead of per-token ``kv.write`` loops and per-sequence SDPA.  The
+write-then-attend order of engine/model.py:142-149 / 184-190 is kept: a token
+attends its own freshly written K/V.
+
+Module construction order (and so the torch RNG draws of the default
+``nn.Linear`` / ``nn.Embedding`` initialisers under ``torch.manual_seed``) is
+the reference's, so ``ToyPagedLM(ToyConfig(seed=s))`` has the reference's
+weights bit-for-bit.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Union
+
+import torch
+from torch import nn
+
+from .attention import AttnBatch, paged_attention
+from .kv import PagedKVCache
+from . import _lib
+from .utils import setup_logger
+
+logger = setup_logger(__name__)
+
+
+# --------------------------------------------------------------------- rotary
+def make_rotary_cache(head_dim: int, theta: float, max_len: int, device: torch.device) -> torch.Tensor:
+    """RoPE ``cos``/``sin`` table ``(max_len, 2, head_dim)`` (rotate_half convention)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device="cpu") / head_dim))
+    positions = torch.arange(max_len, dtype=torch.float32, device="cpu").unsqueeze(-1)
+    freqs = positions * inv_freq.unsqueeze(0)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    table = torch.stack((emb.cos(), emb.sin()), dim=1)
+    return table.to(device)
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    d = x.shape[-1]
+    return torch.cat((-x[..., d // 2:], x[..., : d // 2]), dim=-1)
+
+
+def apply_rotary(x: torch.Tensor, sin: torch.Tensor, cos: torch.Tensor) -> torch.Tensor:
+    return x * cos + rotate_half(x) * sin
+
+
+# --------------------------------------------------------------------- norms
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        input_dtype = x.dtype
+        xf = x.float()
+        rms = torch.sqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return ((xf / rms) * self.weight.float()).to(input_dtype)
+
+
+class SwiGLU(nn.Module):
+    def __init__(self, hidden: int, intermediate: int) -> None:
+        super().__init__()
+        self.gate = nn.Linear(hidden, intermediate, bias=False)
+        self.up = nn.Linear(hidden, intermediate, bias=False)
+        self.down = nn.Linear(intermediate, hidden, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down(torch.nn.functional.silu(self.gate(x)) * self.up(x))
+
+
+# ------------------------------------------------------------ forward plans
+class ForwardPlan:
+    """Slots and attention rows of one forward, shared by every layer.
+
+    ``slots`` has one int32 entry per (row, chunk position) in row-major order
+    (-1 for padded prefill positions); ``batch`` describes the attention rows.
+    """
+
+    __slots__ = ("slots", "batch", "positions", "chunk")
+
+    def __init__(self, slots: torch.Tensor, batch: AttnBatch, positions: torch.Tensor, chunk: int) -> None:
+        self.slots = slots
+        self.batch = batch
+        self.positions = positions
+        self.chunk = chunk
+
+
+def plan_decode(kv: PagedKVCache, seq_ids: Sequence[int], ctx_lengths: Sequence[int],
+                slots: Optional[torch.Tensor] = None) -> ForwardPlan:
+    """One new token per row at position ``ctx_lengths[b]``; it attends ``[0, ctx]``."""
+    ctx = [int(c) for c in ctx_lengths]
+    if slots is None:
+        slots = kv.reserve(seq_ids, ctx, [1] * len(ctx))
+    batch = AttnBatch.from_lists(kv.device, seq_ids, ctx, 1)
+    return ForwardPlan(slots, batch, batch.starts.long().unsqueeze(1), 1)
+
+
+def plan_block(kv: PagedKVCache, seq_ids: Sequence[int], start_positions: Sequence[int], chunk: int) -> ForwardPlan:
+    """``chunk`` consecutive tokens per row from ``start_positions[b]``."""
+    starts = [int(s) for s in start_positions]
+    slots = kv.reserve(seq_ids, starts, [chunk] * len(starts))
+    batch = AttnBatch.from_lists(kv.device, seq_ids, starts, chunk)
+    pos = batch.starts.long().unsqueeze(1) + torch.arange(chunk, device=kv.device).unsqueeze(0)
+    return ForwardPlan(slots, batch, pos, chunk)
+
+
+def plan_prefill(kv: PagedKVCache, seq_ids: Sequence[int], seq_lengths: Sequence[int], chunk: int) -> ForwardPlan:
+    """Ragged prompts (tail-padded to ``chunk``) written from position 0."""
+    lengths = [int(x) for x in seq_lengths]
+    B = len(lengths)
+    slots = kv.reserve(seq_ids, [0] * B, lengths)
+    if any(ln != chunk for ln in lengths):
+        grid = torch.full((B * chunk,), -1, dtype=torch.int32, device=kv.device)
+        lens_t = torch.tensor(lengths, device=kv.device)
+        mask = (torch.arange(chunk, device=kv.device).unsqueeze(0) < lens_t.unsqueeze(1)).reshape(-1)
+        grid[mask] = slots
+        slots = grid
+    packed = _lib.i32([int(s) for s in seq_ids] + [0] * B + lengths, kv.device)
+    batch = AttnBatch(packed[:B], packed[B:2 * B], chunk, packed[2 * B:])
+    pos = torch.arange(chunk, device=kv.device).unsqueeze(0).expand(B, chunk)
+    return ForwardPlan(slots, batch, pos, chunk)
+
+
+def paged_attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv: PagedKVCache, layer: int,
+                 plan: ForwardPlan) -> torch.Tensor:
+    """Append this layer's K/V at the plan's slots, then attend (write first)."""
+    B = q.shape[0]
+    kv.append(layer, plan.slots, k.reshape(-1, kv.num_kv_heads, kv.head_dim),
+              v.reshape(-1, kv.num_kv_heads, kv.head_dim))
+    q4 = q.reshape(B, plan.chunk, q.shape[-2], q.shape[-1])
+    return paged_attention(q4, kv, layer, plan.batch)
+
+
+# ------------------------------------------------------------- decoder layer
+class PagedDecoderLayer(nn.Module):
+    """Decoder block with paged self-attention + SwiGLU MLP (engine/model.py:96-194)."""
+
+    def __init__(self, hidden: int, num_q_heads: int, num_kv_heads: int, head_dim: int, intermediate: int) -> None:
+        super().__init__()
+        self.num_q_heads = num_q_heads
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.input_layernorm = RMSNorm(hidden)
+        self.q = nn.Linear(hidden, num_q_heads * head_dim, bias=False)
+        self.k = nn.Linear(hidden, num_kv_heads * head_dim, bias=False)
+        self.v = nn.Linear(hidden, num_kv_heads * head_dim, bias=False)
+        self.o = nn.Linear(num_q_heads * head_dim, hidden, bias=False)
+        self.post_attention_layernorm = RMSNorm(hidden)
+        self.mlp = SwiGLU(hidden, intermediate)
+
+    def _qkv(self, x: torch.Tensor, lead: tuple):
+        q = self.q(x).view(*lead, self.num_q_heads, self.head_dim)
+        k = self.k(x).view(*lead, self.num_kv_heads, self.head_dim)
+        v = self.v(x).view(*lead, self.num_kv_heads, self.head_dim)
+        return q, k, v
+
+    def forward_plan(self, hidden: torch.Tensor, kv: PagedKVCache, layer_index: int, plan: ForwardPlan,
+                     cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """``hidden`` is ``(B, H)`` (chunk 1) or ``(B, chunk, H)``; cos/sin broadcast over heads."""
+        lead = tuple(hidden.shape[:-1])
+        residual = hidden
+        x = self.input_layernorm(hidden)
+        q_raw, k_raw, v_raw = self._qkv(x, lead)
+        q = apply_rotary(q_raw, sin, cos)
+        k = apply_rotary(k_raw, sin, cos)
+        out = paged_attend(q, k, v_raw, kv, layer_index, plan)
+        hidden = residual + self.o(out.reshape(*lead, -1))
+        return hidden + self.mlp(self.post_attention_layernorm(hidden))
+
+    def decode_step(self, hidden, kv, layer_index, seq_ids, ctx_lengths, cos, sin):
+        plan = seq_ids if isinstance(seq_ids, ForwardPlan) else plan_decode(kv, seq_ids, ctx_lengths)
+        return self.forward_plan(hidden, kv, layer_index, plan, cos, sin)
+
+    def extend_block(self, hidden, kv, layer_index, seq_ids, start_positions, cos, sin):
+        if isinstance(seq_ids, ForwardPlan):
+            plan = seq_ids
+        else:
+            plan = plan_block(kv, seq_ids, start_positions, hidden.shape[1])
+        return self.forward_plan(hidden, kv, layer_index, plan, cos[:, :, None, :], sin[:, :, None, :])
+
+
+# ----------------------------------------------------------------- plain text
+class ToyTokenizer:
+    """Character-level tokenizer covering ``vocab_size`` symbols."""
+
+    def __init__(self, vocab_size: int = 16) -> None:
+        alphabet = "abcdefghijklmnopqrstuvwxyz"
+        self.vocab_size = vocab_size
+        self.itos = list(alphabet[:vocab_size])
+        self.stoi = {ch: idx for idx, ch in enumerate(self.itos)}
+        self.pad_token_id = 0
+        self.eos_token_id = None
+
+    def encode(self, text: Union[str, Sequence[int]]) -> List[int]:
+        if not isinstance(text, str):
+            return [int(t) for t in text]
+        return [self.stoi[ch] for ch in text if ch in self.stoi]
+
+    def decode(self, token_ids: Sequence[int], skip_special_tokens: bool = True) -> str:
+        return "".join(self.itos[int(i) % self.vocab_size] for i in token_ids)
+
+
+class IdTokenizer:
+    """Pass-through "tokenizer" for random-init models fed token-id prompts."""
+
+    def __init__(self, vocab_size: int, eos_token_id: Optional[int] = None) -> None:
+        self.vocab_size = vocab_size
+        self.eos_token_id = eos_token_id
+        self.pad_token_id = 0
+
+    def encode(self, text: Union[str, Sequence[int]]) -> List[int]:
+        if isinstance(text, str):
+            return [int(t) % self.vocab_size for t in text.split()]
+        return [int(t) for t in text]
+
+    def decode(self, token_ids: Sequence[int], skip_special_tokens: bool = True) -> str:
+        return " ".join(str(int(t)) for t in token_ids)
+
+
+# ----------------------------------------------------------------- toy model
+@dataclass
+class ToyConfig:
+    vocab_size: int = 16
+    hidden_size: int = 64
+    num_layers: int = 2
+    num_attention_heads: int = 4
+    num_key_value_heads: int = 2
+    head_dim: int = 16
+    intermediate_size: int = 128
+    max_position_embeddings: int = 256
+    theta: float = 10000.0
+    logit_scale: float = 6.0
+    seed: int = 0
+
+
+class PagedLMMixin:
+    """prefill / decode / decode_block over a stack of layers with ``forward_plan``."""
+
+    def _rope(self, positions: torch.Tensor):
+        cs = self._rope_table()[positions]
+        return cs[..., 0, :], cs[..., 1, :]
+
+    def _run_layers(self, hidden: torch.Tensor, kv: PagedKVCache, plan: ForwardPlan,
+                    cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        for index, layer in enumerate(self.layers):
+            hidden = layer.forward_plan(hidden, kv, index, plan, cos, sin)
+        return hidden
+
+    def prefill(self, prompt_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
+                seq_lengths: Sequence[int]) -> torch.Tensor:
+        """Prefill ragged prompts; return first-token logits ``(B, V)``."""
+        self.forward_calls += 1
+        B, chunk = prompt_2d.shape
+        plan = plan_prefill(kv, seq_ids, seq_lengths, chunk)
+        hidden = self.embed_tokens(prompt_2d.to(self.device))
+        cos, sin = self._rope(plan.positions)
+        hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+        last = torch.tensor([int(x) - 1 for x in seq_lengths], device=self.device)
+        h_last = hidden[torch.arange(B, device=self.device), last]
+        return self._logits(h_last)
+
+    def decode(self, input_ids: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
+               ctx_lengths: Sequence[int], slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One token per row at position ``ctx_lengths[b]``; returns ``(B, V)``.
+
+        ``slots`` (optional) are positions already reserved by a commit kernel.
+        """
+        self.forward_calls += 1
+        plan = plan_decode(kv, seq_ids, ctx_lengths, slots)
+        hidden = self.embed_tokens(input_ids.to(self.device).reshape(-1))
+        cos, sin = self._rope(plan.positions[:, 0])
+        hidden = self._run_layers(hidden, kv, plan, cos.unsqueeze(1), sin.unsqueeze(1))
+        return self._logits(hidden)
+
+    def decode_block(self, input_ids_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
+                     start_positions: Sequence[int]) -> torch.Tensor:
+        """``chunk`` consecutive tokens per row; returns ``(B, chunk, V)``."""
+        self.forward_calls += 1
+        B, chunk = input_ids_2d.shape
+        plan = plan_block(kv, seq_ids, start_positions, chunk)
+        hidden = self.embed_tokens(input_ids_2d.to(self.device))
+        cos, sin = self._rope(plan.positions)
+        hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+        return self._logits(hidden)
+
+
+class ToyPagedLM(PagedLMMixin, nn.Module):
+    """Deterministic, memory-lean transformer consuming ``PagedKVCache``."""
+
+    def __init__(self, cfg: ToyConfig, device: torch.device) -> None:
+        super().__init__()
+        torch.manual_seed(cfg.seed)
+        self.cfg = cfg
+        self.tokenizer = ToyTokenizer(cfg.vocab_size)
+        self.device = torch.device(device)
+        self.num_layers = cfg.num_layers
+        self.num_q_heads = cfg.num_attention_heads
+        self.num_kv_heads = cfg.num_key_value_heads
+        self.head_dim = cfg.head_dim
+        self._cos_sin = make_rotary_cache(cfg.head_dim, cfg.theta, cfg.max_position_embeddings, self.device)
+        self.embed_tokens = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.layers = nn.ModuleList(
+            [
+                PagedDecoderLayer(cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim,
+                                  cfg.intermediate_size)
+                for _ in range(cfg.num_layers)
+            ]
+        )
+        self.norm = RMSNorm(cfg.hidden_size)
+        self.lm_head = nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False)
+        if cfg.logit_scale != 1.0:
+            with torch.no_grad():
+                self.lm_head.weight.mul_(cfg.logit_scale)
+        self.config = cfg
+        self.forward_calls = 0
+        self.to(device=self.device)
+        self.requires_grad_(False)
+
+    def _rope_table(self) -> torch.Tensor:
+        return self._cos_sin
+
+    def _logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(self.norm(hidden))
+
+    @property
+    def vocab_size(self) -> int:
+        return self.cfg.vocab_size
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return next(self.parameters()).dtype
+
+    def encode(self, text) -> List[int]:
+        return self.tokenizer.encode(text)
+
+    def decode_text(self, token_ids: Sequence[int], skip_special_tokens: bool = True) -> str:
+        return self.tokenizer.decode(token_ids, skip_special_tokens)
+
+    def reset_counters(self) -> None:
+        self.forward_calls = 0

@@ -1,0 +1,320 @@
+"""Speculative decoding fused into the continuous-batching engine, on B200.
+
+Drop-in for the reference's ``engine/spec_scheduler.py``
+(engine/spec_scheduler.py:41-322).  Cache invariant per model, unchanged:
+``kv.seq_lengths[sid] == len(prompt) + len(generated) - 1``.
+
+One round (``_spec_step``) is, on the device:
+
+1. ``gamma`` batched draft decodes; each picks its proposals in-kernel
+   (argmax, or temperature softmax + one uniform per sequence);
+2. one batched target ``decode_block`` over ``[pending] + proposals``;
+3. the fused rejection sampler (``sdl_spec_sample``): fp64 ``min(1, p/q)``
+   tests against the stream's uniforms in the reference's draw order, the
+   residual ``(p - q)+`` or bonus draw, accept lengths;
+4. ``sdl_spec_commit``: budget clip, EOS cut, rewind of the target cache to
+   ``start + k`` and alignment of the draft cache (truncate, or reserve the
+   single catch-up position), clears of finished sequences -- walked in batch
+   order so both free lists see the reference's push/pop order.
+
+The host then reads one packed int32 tensor (tokens, counts, flags, error
+words) to update the Python ``Sequence`` records and runs the batched draft
+catch-up decode for sequences that accepted everything plus the bonus.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Dict, List, Optional, Sequence as Seq
+
+import torch
+
+from . import _lib
+from .config import EngineConfig, SamplingConfig, WorkloadRequest
+from .kv import PagedKVCache, _exhausted
+from .scheduler import PagedScheduler, SchedulerResult, Sequence
+from .utils import Stopwatch, setup_logger, sync_device
+from specdec.sampler import (
+    UniformStream,
+    apply_top_k,
+    apply_top_p,
+    argmax_rows,
+    probs_rows,
+    sample_rows,
+    spec_sample,
+)
+
+logger = setup_logger(__name__)
+
+
+def _draw_uniform(generator: torch.Generator) -> float:
+    """Deterministic uniform coin (engine/spec_scheduler.py:41-43)."""
+    return float(torch.rand(1, generator=generator).item())
+
+
+def batch_accept(
+    p_by_sid: Dict[int, torch.Tensor],
+    q_by_sid: Dict[int, Seq[torch.Tensor]],
+    proposals_by_sid: Dict[int, Seq[int]],
+    generator: Any,
+) -> Dict[int, List[int]]:
+    """Accept/reject each sequence's draft block; return the committed tokens.
+
+    Same contract as engine/spec_scheduler.py:46-88: sequences in dict order;
+    scan proposals with ``u < min(1, p/q)``; on the first rejection draw from
+    ``(p - q)+`` and stop; if all are accepted draw a bonus from ``p[gamma]``.
+    One fused launch (``sdl_spec_sample``) for the whole batch.
+
+    ``generator`` is a :class:`UniformStream` (uniforms consumed in the
+    reference's order) or a ``torch.Generator`` (then ``B * (gamma + 1)``
+    uniforms are pre-drawn from it, the most the round can use).
+    """
+    sids = list(p_by_sid.keys())
+    if not sids:
+        return {}
+    p = torch.stack([p_by_sid[s].float() for s in sids]).contiguous()
+    q = torch.stack([torch.stack([r.float() for r in q_by_sid[s]]) for s in sids]).contiguous()
+    gamma = q.shape[1]
+    props = torch.tensor([list(proposals_by_sid[s]) for s in sids], dtype=torch.int32, device=p.device)
+    if isinstance(generator, UniformStream):
+        stream = generator
+    else:
+        u = torch.rand(len(sids) * (gamma + 1), generator=generator)
+        stream = UniformStream(p.device, uniforms=u)
+    tokens, n_out = spec_sample(p, q, props, stream, greedy=False)
+    tok_h = tokens.tolist()
+    n_h = n_out.tolist()
+    return {sid: tok_h[b][: n_h[b]] for b, sid in enumerate(sids)}
+
+
+class SpeculativePagedScheduler(PagedScheduler):
+    """Continuous-batching scheduler with an integrated draft/verify round."""
+
+    def __init__(self, model: Any, kv: PagedKVCache, draft_model: Any, draft_kv: PagedKVCache,
+                 engine_cfg: EngineConfig, sampling: SamplingConfig, gamma: int,
+                 uniforms: Optional[torch.Tensor] = None) -> None:
+        super().__init__(model, kv, engine_cfg, sampling, uniforms=uniforms)
+        self.draft_model = draft_model
+        self.draft_kv = draft_kv
+        self.gamma = int(gamma)
+        if not 1 <= self.gamma <= 32:
+            raise ValueError("gamma must be within [1, 32]")
+        self._q_buf: Optional[torch.Tensor] = None
+
+    # ------------------------------------------------------------ admission
+    def _flush_arrivals(self, arrivals: List[WorkloadRequest], when: int, result: SchedulerResult,
+                        stream: Optional[UniformStream]) -> List[Sequence]:
+        admitted: List[Sequence] = []
+        for request in arrivals:
+            seq = Sequence(
+                sid=self._next_sid,
+                prompt_ids=self.model.encode(request.prompt),
+                max_new_tokens=request.max_new_tokens,
+                arrive_time=request.arrive_time,
+                admit_step=when,
+            )
+            self._next_sid += 1
+            self.kv.add_sequence(seq.sid)
+            self.draft_kv.add_sequence(seq.sid)
+            seq.ttft_ms = self._prefill_spec_one(seq, result, stream)
+            admitted.append(seq)
+        result.sequences.extend(admitted)
+        return admitted
+
+    def _prefill_spec_one(self, seq: Sequence, result: SchedulerResult,
+                          stream: Optional[UniformStream]) -> Optional[float]:
+        watch = Stopwatch()
+        with watch:
+            ids = torch.tensor([list(seq.prompt_ids)], dtype=torch.long, device=self.model.device)
+            logits = self.model.prefill(ids, self.kv, [seq.sid], [len(seq.prompt_ids)])
+            tok = self._next_tokens(logits, stream)
+            self.draft_model.prefill(ids, self.draft_kv, [seq.sid], [len(seq.prompt_ids)])
+            seq.generated.append(int(tok[0].item()))
+        seq.prefilled = True
+        return watch.elapsed_ms
+
+    # ------------------------------------------------------------ spec loop
+    def run_spec_continuous(self, requests: Seq[WorkloadRequest], seed: int, measure: bool = True) -> SchedulerResult:
+        result = SchedulerResult(mode="spec-continuous", sampling=self.sampling.describe())
+        stream = self._make_stream(seed)
+        device = self.model.device
+        arrivals = sorted(requests, key=lambda r: r.arrive_time)
+        step = 0
+        if measure:
+            sync_device(device)
+            torch.cuda.reset_peak_memory_stats(device)
+        stopwatch = Stopwatch()
+        with stopwatch:
+            due = [r for r in arrivals if r.arrive_time <= step]
+            pending = [r for r in arrivals if r.arrive_time > step]
+            self._flush_arrivals(due, step, result, stream)
+            running = [s for s in result.sequences if not s.finished]
+            while running or pending:
+                running = [s for s in result.sequences if not s.finished]
+                if running:
+                    self._spec_step(running, result, stream)
+                    result.total_forwards += 1
+                step += 1
+                due = [r for r in pending if r.arrive_time <= step]
+                pending = [r for r in pending if r.arrive_time > step]
+                if due:
+                    self._flush_arrivals(due, step, result, stream)
+                running = [s for s in result.sequences if not s.finished]
+                result.batch_hist.append(len(running))
+                result.block_util_hist.append(self.kv.block_utilization)
+                if self.kv.num_allocated_blocks > result.kv_peak_blocks:
+                    result.kv_peak_blocks = self.kv.num_allocated_blocks
+                if self.draft_kv.num_allocated_blocks > result.draft_kv_peak_blocks:
+                    result.draft_kv_peak_blocks = self.draft_kv.num_allocated_blocks
+            result.steps = step
+            if measure:
+                sync_device(device)
+        result.makespan_ms = stopwatch.elapsed_ms
+        result.generated_tokens = sum(len(s.generated) for s in result.sequences)
+        result.kv_peak_bytes = result.kv_peak_blocks * self._bytes_per_block()
+        if result.tokens_per_round:
+            result.mean_tokens_per_round = sum(result.tokens_per_round) / len(result.tokens_per_round)
+            result.mean_acceptance = sum(result.tokens_per_round) / (len(result.tokens_per_round) * (self.gamma + 1))
+        if measure:
+            result.peak_memory_mb = round(torch.cuda.max_memory_allocated(device) / (1024.0 ** 2), 2)
+        return result
+
+    # ------------------------------------------------------------ one round
+    def _probs_spec(self, logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """specdec logits_to_probs semantics (T floor 1e-12, optional top-k/top-p)."""
+        s = self.sampling
+        top_k = int(getattr(s, "top_k", 0) or 0)
+        top_p = float(getattr(s, "top_p", 1.0))
+        if (top_k <= 0 or top_k >= logits.shape[-1]) and (top_p >= 1.0 or top_p <= 0.0):
+            return probs_rows(logits, s.temperature, False, eps=1e-12, out=out)
+        scaled = logits.float() / max(s.temperature, 1e-12)
+        filtered = apply_top_p(apply_top_k(scaled, top_k), top_p)
+        return probs_rows(filtered, 1.0, False, out=out)
+
+    def _spec_step(self, running: Seq[Sequence], result: SchedulerResult, stream: Optional[UniformStream]) -> None:
+        model, draft = self.model, self.draft_model
+        device = model.device
+        gamma = self.gamma
+        chunk = gamma + 1
+        greedy = self.sampling.is_greedy
+        sids = [s.sid for s in running]
+        B = len(running)
+        starts = [self.kv.seq_len(sid) for sid in sids]
+        d0 = [self.draft_kv.seq_len(sid) for sid in sids]
+
+        # ---- 1. draft proposes gamma tokens per sequence
+        proposals = torch.empty((B, gamma), dtype=torch.int32, device=device)
+        q_probs = None
+        if not greedy:
+            stream.reserve(gamma * B)
+        cur = torch.tensor([s.generated[-1] for s in running], dtype=torch.long, device=device)
+        for t in range(gamma):
+            q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0])
+            result.draft_forward_calls += 1
+            if greedy:
+                prop_t = argmax_rows(q_logits)
+            else:
+                V = q_logits.shape[-1]
+                if self._q_buf is None or self._q_buf.shape[0] < B or self._q_buf.shape[2] != V:
+                    rows_cap = max(B, self._q_buf.shape[0] if self._q_buf is not None else 0)
+                    self._q_buf = torch.empty((rows_cap, gamma, V), dtype=torch.float32, device=device)
+                q_probs = self._q_buf[:B]
+                self._probs_spec(q_logits, out=q_probs[:, t, :])
+                prop_t = sample_rows(q_probs[:, t, :], stream, offset=t * B, err=self.draft_kv.err_word)
+            proposals[:, t] = prop_t
+            cur = prop_t.long()
+
+        # ---- 2. target verifies [pending] + proposals in one forward
+        rows = torch.cat((torch.tensor([[s.generated[-1]] for s in running], dtype=torch.long, device=device),
+                          proposals.long()), dim=1)
+        p_logits = model.decode_block(rows, self.kv, sids, starts)  # (B, chunk, V)
+
+        # ---- 3. fused rejection sampling
+        if greedy:
+            p_arg = argmax_rows(p_logits.reshape(B * chunk, -1)).reshape(B, chunk)
+            tokens, n_out = spec_sample(None, None, proposals, None, greedy=True, p_arg=p_arg)
+        else:
+            p_probs = self._probs_spec(p_logits).reshape(B, chunk, -1)
+            tokens, n_out = spec_sample(p_probs, q_probs, proposals, stream, greedy=False, u_skip=gamma * B,
+                                        err=self.kv.err_word)
+
+        # ---- 4. device commit: clip, EOS cut, rewind, draft alignment, clears
+        remaining = [s.max_new_tokens - len(s.generated) for s in running]
+        packed = _lib.i32(sids + remaining + starts, device)
+        outs = torch.empty((3, B), dtype=torch.int32, device=device)
+        eos = -1 if self._eos is None else int(self._eos)
+        _lib.check(
+            _lib.load().sdl_spec_commit(
+                ctypes.byref(self.kv.meta), ctypes.byref(self.draft_kv.meta), B, packed.data_ptr(),
+                n_out.data_ptr(), tokens.data_ptr(), chunk, packed.data_ptr() + 4 * B, eos,
+                packed.data_ptr() + 8 * B, outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(),
+                _lib.stream_handle(device),
+            ),
+            "sdl_spec_commit",
+        )
+        host = torch.cat((tokens.reshape(-1), outs.reshape(-1), self.kv.err_word, self.draft_kv.err_word)).tolist()
+        tok_h = host[: B * chunk]
+        k_h = host[B * chunk: B * chunk + B]
+        f_h = host[B * chunk + B: B * chunk + 2 * B]
+        c_h = host[B * chunk + 2 * B: B * chunk + 3 * B]
+        err_t, err_d = host[-2], host[-1]
+        if err_t or err_d:
+            self.kv.err_word.zero_()
+            self.draft_kv.err_word.zero_()
+            if (err_t | err_d) & _lib.DEVERR_EXHAUSTED:
+                raise _exhausted(self.kv.capacity if err_t & _lib.DEVERR_EXHAUSTED else self.draft_kv.capacity)
+            raise RuntimeError("device error during spec round: target 0x{:x} draft 0x{:x}".format(err_t, err_d))
+
+        # ---- 5. host bookkeeping (mirrors engine/spec_scheduler.py:270-322)
+        catch_sids: List[int] = []
+        catch_pos: List[int] = []
+        catch_tok: List[int] = []
+        catch_slot: List[int] = []
+        for b, s in enumerate(running):
+            sid = s.sid
+            k = k_h[b]
+            fin = bool(f_h[b] & 1)
+            result.tokens_per_round.append(k)
+            if f_h[b] & 2:
+                s.eos_hit = True
+            if k == 0:
+                s.finished = True
+                s.finish_step = result.steps
+            else:
+                s.generated.extend(tok_h[b * chunk: b * chunk + k])
+                if fin:
+                    s.finished = True
+                    s.finish_step = result.steps
+                keep = len(s.prompt_ids) + len(s.generated) - 1
+                self.kv._shadow_release(sid, keep, _lib.REL_TRUNCATE)
+                d_len = self.draft_kv.seq_len(sid)
+                if d_len > keep:
+                    self.draft_kv._shadow_release(sid, keep, _lib.REL_TRUNCATE)
+                elif d_len < keep:
+                    self._shadow_extend_one(self.draft_kv, sid, d_len)
+                    if c_h[b] >= 0:
+                        catch_sids.append(sid)
+                        catch_pos.append(d_len)
+                        catch_tok.append(s.generated[d_len - len(s.prompt_ids)])
+                        catch_slot.append(c_h[b])
+            if s.finished:
+                self.kv._shadow_release(sid, 0, _lib.REL_CLEAR)
+                self.draft_kv._shadow_release(sid, 0, _lib.REL_CLEAR)
+        self.kv._mirror = None
+        self.draft_kv._mirror = None
+
+        # ---- 6. draft catch-up for fully accepted rounds (engine/spec_scheduler.py:308-319)
+        if catch_sids:
+            ids = torch.tensor(catch_tok, dtype=torch.long, device=device)
+            slots = _lib.i32(catch_slot, device)
+            draft.decode(ids, self.draft_kv, catch_sids, catch_pos, slots=slots)
+            result.draft_forward_calls += len(catch_sids)
+
+    @staticmethod
+    def _shadow_extend_one(kv: PagedKVCache, sid: int, pos: int) -> None:
+        need_b = pos // kv.block_size + 1
+        if need_b > kv._h_nb[sid]:
+            kv.allocator._h_free -= need_b - kv._h_nb[sid]
+            kv._h_nb[sid] = need_b
+        if kv._h_len[sid] <= pos:
+            kv._h_len[sid] = pos + 1
