@@ -21,20 +21,28 @@ def expand_to_q_heads(x: np.ndarray, num_q_heads: int) -> np.ndarray:
 def attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, limits: Sequence[int]) -> np.ndarray:
     """Rows of ``q`` (rows, Hq, d) attend ``k/v`` (L, Hkv, d); row r sees [0, limits[r]).
 
-    Scale 1/sqrt(d) like SDPA's default (engine/attention.py:92,212).
+    Scale 1/sqrt(d) like SDPA's default (engine/attention.py:92,212); q head h
+    reads kv head h // (Hq/Hkv) (engine/attention.py:32-38).  fp64 matmuls per
+    kv head (BLAS releases the GIL, so callers may thread over sequences).
     """
     rows, Hq, d = q.shape
-    ke = expand_to_q_heads(k.astype(np.float64), Hq)  # (L, Hq, d)
-    ve = expand_to_q_heads(v.astype(np.float64), Hq)
+    L, Hkv = k.shape[0], k.shape[1]
+    ratio = Hq // Hkv
     scale = 1.0 / np.sqrt(d)
-    s = np.einsum("rhd,lhd->rhl", q.astype(np.float64), ke) * scale
-    L = k.shape[0]
     mask = np.arange(L)[None, :] < np.asarray(limits)[:, None]  # (rows, L)
-    s = np.where(mask[:, None, :], s, -np.inf)
-    s = s - s.max(axis=-1, keepdims=True)
-    p = np.exp(s)
-    p /= p.sum(axis=-1, keepdims=True)
-    return np.einsum("rhl,lhd->rhd", p, ve)
+    out = np.empty((rows, Hq, d), dtype=np.float64)
+    q64 = q.astype(np.float64)
+    for g in range(Hkv):
+        kg = k[:, g, :].astype(np.float64)
+        vg = v[:, g, :].astype(np.float64)
+        qg = q64[:, g * ratio:(g + 1) * ratio, :].reshape(rows * ratio, d)
+        s = (qg @ kg.T) * scale                                   # (rows*ratio, L)
+        s = np.where(np.repeat(mask, ratio, axis=0), s, -np.inf)
+        s -= s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=-1, keepdims=True)
+        out[:, g * ratio:(g + 1) * ratio, :] = (p @ vg).reshape(rows, ratio, d)
+    return out
 
 
 def paged_attention_decode(q2d: np.ndarray, kv: PagedKVCache, layer: int, seq_ids, lengths) -> np.ndarray:

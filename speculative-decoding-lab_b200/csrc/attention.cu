@@ -35,7 +35,7 @@ constexpr int kPage = 16;          // tokens per TMA page (= block_size on the T
 constexpr int kStages = 4;         // TMA ring depth
 constexpr int kMaxConsumerWarps = 8;
 constexpr int kBoxBytes = kPage * 128;  // one [16 tokens][64 cols] 16-bit box
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint32_t kWaitLimit = 1u << 20;
 
 struct TcParams {
     const void* q;

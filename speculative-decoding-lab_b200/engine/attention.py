@@ -19,6 +19,7 @@ Softmax scale is ``1/sqrt(head_dim)`` (SDPA's default) and GQA maps q head
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import List, Optional, Sequence
 
@@ -80,6 +81,30 @@ def _launch(a: _lib.SdlAttnArgs, device: torch.device, fn: str = "sdl_paged_atte
     _lib.check(getattr(lib, fn)(a, _lib.stream_handle(device)), fn)
 
 
+def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0) -> _lib.SdlAttnArgs:
+    a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
+    a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
+    mk, mv = kv.tensor_maps()
+    if mk is not None:
+        a.tmap_k, a.tmap_v = ctypes.addressof(mk), ctypes.addressof(mv)
+    a.block_table, a.width, a.capacity = kv._table.data_ptr(), kv.width, kv.capacity
+    a.num_layers, a.layer, a.block_size = kv.num_layers, int(layer), kv.block_size
+    a.rows = batch.rows.data_ptr()
+    a.starts = batch.starts.data_ptr()
+    a.valid_rows = batch.valid_rows.data_ptr() if batch.valid_rows is not None else None
+    a.max_limit = batch.max_limit
+    a.pages_per_split = int(pages_per_split)
+    a.force_generic = 1 if force_generic else 0
+    return a
+
+
+def attention_splits(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch) -> bool:
+    """Whether a call with this shape runs split-K (and so a combine launch)."""
+    q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
+    a = _paged_args(q4, kv, 0, batch, q4)
+    return bool(_lib.load().sdl_attention_workspace_bytes(a))
+
+
 def paged_attention(
     q: torch.Tensor,
     kv: PagedKVCache,
@@ -100,20 +125,7 @@ def paged_attention(
         q = q.contiguous()
     if out is None:
         out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
-    a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
-    a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
-    mk, mv = kv.tensor_maps()
-    if mk is not None:
-        import ctypes
-        a.tmap_k, a.tmap_v = ctypes.addressof(mk), ctypes.addressof(mv)
-    a.block_table, a.width, a.capacity = kv._table.data_ptr(), kv.width, kv.capacity
-    a.num_layers, a.layer, a.block_size = kv.num_layers, int(layer), kv.block_size
-    a.rows = batch.rows.data_ptr()
-    a.starts = batch.starts.data_ptr()
-    a.valid_rows = batch.valid_rows.data_ptr() if batch.valid_rows is not None else None
-    a.max_limit = batch.max_limit
-    a.pages_per_split = int(pages_per_split)
-    a.force_generic = 1 if force_generic else 0
+    a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split)
     if batch.max_limit > kv.width * kv.block_size:
         raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))
     _launch(a, q.device)

@@ -1,0 +1,228 @@
+"""Paged attention kernels vs the reference fixtures and the fp64 oracle.
+
+Tolerances (north star: 1e-5 relative in fp32, 2e-3 in bf16):
+* fp32 pools (CUDA-core kernel): ``allclose(rtol=1e-5, atol=1e-5)``.
+* bf16 pools (tensor-core kernel):
+  - fp32 output: relative error <= 2e-3 of max|out| per row block
+    (the arithmetic keeps ~16 mantissa bits, so this holds with margin);
+  - bf16 output: within one bf16 rounding of the exact value,
+    ``|out - exact| <= 2^-8 |exact| + 2e-3 * max|exact|``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_npz
+from engine.attention import (
+    AttnBatch,
+    full_attention,
+    gather_ctx,
+    paged_attention,
+    paged_attention_decode,
+    paged_attention_extend,
+    paged_attention_prefill_chunk,
+)
+from engine.kv import PagedKVCache
+from oracle import attention as oatt
+from oracle import kv as okv
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _build(lens_total, Hkv, d, bs, dtype, seed, extra_blocks=3, shuffle=True, layers=1):
+    """Device cache + oracle cache holding identical random K/V."""
+    rng = np.random.default_rng(seed)
+    cap = sum(-(-T // bs) for T in lens_total) + extra_blocks
+    kv = PagedKVCache(layers, Hkv, d, cap, bs, DEV, dtype)
+    ref = okv.PagedKVCache(layers, Hkv, d, cap, bs)
+    B = len(lens_total)
+    for sid in range(B):
+        kv.add_sequence(sid)
+        ref.add_sequence(sid)
+    if shuffle:  # interleave the sequences' allocations so tables are scattered
+        order = []
+        pos = [0] * B
+        while any(p < T for p, T in zip(pos, lens_total)):
+            for sid in rng.permutation(B):
+                if pos[sid] < lens_total[sid]:
+                    n = int(min(lens_total[sid] - pos[sid], rng.integers(1, 3 * bs)))
+                    order.append((int(sid), pos[sid], n))
+                    pos[sid] += n
+    else:
+        order = [(sid, 0, T) for sid, T in enumerate(lens_total) if T > 0]
+    for sid, st, n in order:
+        slots = kv.reserve([sid], [st], [n])
+        want = ref.reserve([sid], [st], [n])
+        assert slots.tolist() == want
+        for layer in range(layers):
+            k = torch.from_numpy(rng.standard_normal((n, Hkv, d)).astype(np.float32)).to(DEV, dtype)
+            v = torch.from_numpy(rng.standard_normal((n, Hkv, d)).astype(np.float32)).to(DEV, dtype)
+            kv.append(layer, slots, k, v)
+            ref.append(layer, want, k.float().cpu().numpy(), v.float().cpu().numpy())
+    return kv, ref
+
+
+def _check_bf16(out_bf16, out_f32, exact):
+    ex = exact.astype(np.float64)
+    scale = np.abs(ex).max() + 1e-30
+    err32 = np.abs(out_f32.astype(np.float64) - ex).max() / scale
+    assert err32 <= 2e-3, err32
+    diff = np.abs(out_bf16.astype(np.float64) - ex)
+    assert np.all(diff <= 2.0 ** -8 * np.abs(ex) + 2e-3 * scale), diff.max()
+
+
+# --------------------------------------------------------------- fixtures
+def _golden_case(tag):
+    a = load_npz("attention.npz")
+    Hq, Hkv, d, bs, chunk, cap = (int(x) for x in a[tag + "_meta"])
+    starts = a[tag + "_starts"].tolist()
+    dtype = torch.bfloat16 if "bf16" in tag else torch.float32
+    kv = PagedKVCache(1, Hkv, d, cap, bs, DEV, dtype)
+    for sid, st in enumerate(starts):
+        kv.add_sequence(sid)
+        kv.reserve([sid], [0], [st + chunk])  # same order as the reference's writes
+    tables = [[int(x) for x in row if x >= 0] for row in a[tag + "_tables"]]
+    assert kv.block_tables == tables
+    kv._k.copy_(torch.from_numpy(a[tag + "_k"]).to(DEV, dtype))
+    kv._v.copy_(torch.from_numpy(a[tag + "_v"]).to(DEV, dtype))
+    q = torch.from_numpy(a[tag + "_q"]).to(DEV, dtype)
+    return kv, q, starts, chunk, Hq, a[tag + "_out"]
+
+
+@pytest.mark.parametrize("tag", ["dec_f32_small", "dec_f32_d64", "ext_f32_d64"])
+def test_fp32_attention_matches_reference_fixture(tag):
+    kv, q, starts, chunk, Hq, ref = _golden_case(tag)
+    if chunk == 1:
+        out = paged_attention_decode(q[:, 0], kv, 0, list(range(len(starts))), [s + 1 for s in starts], Hq)[:, None]
+    else:
+        out = paged_attention_extend(q, kv, 0, list(range(len(starts))), starts, Hq)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("tag", ["dec_bf16_d128", "ext_bf16_d128", "dec_bf16_d64_r7"])
+def test_bf16_attention_matches_reference_fixture(tag):
+    kv, q, starts, chunk, Hq, ref = _golden_case(tag)
+    batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
+    out = paged_attention(q, kv, 0, batch)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32)
+    # exact value from the fp64 oracle on the same bf16 inputs
+    a = load_npz("attention.npz")
+    okvc = okv.PagedKVCache(1, kv.num_kv_heads, kv.head_dim, kv.capacity, kv.block_size)
+    okvc.k[:] = a[tag + "_k"]
+    okvc.v[:] = a[tag + "_v"]
+    for sid, st in enumerate(starts):
+        okvc.add_sequence(sid)
+        okvc.block_tables[sid] = kv.block_tables[sid]
+    exact = oatt.paged_attention_extend(a[tag + "_q"], okvc, 0, range(len(starts)), starts)
+    _check_bf16(out.float().cpu().numpy(), out32.cpu().numpy(), exact)
+    # and the reference's own bf16 result agrees to bf16 resolution
+    assert np.abs(out.float().cpu().numpy() - ref).max() <= 2.0 ** -7 * np.abs(ref).max() + 1e-6
+
+
+# ---------------------------------------------------------- random vs oracle
+CASES = [
+    # Hq, Hkv, d, chunk, lens (start positions), bs, dtype
+    (12, 2, 128, 1, [1, 15, 16, 17, 300, 1029, 4095], 16, torch.bfloat16),     # C2 decode shape, split-K
+    (12, 2, 128, 6, [0, 5, 250, 2047], 16, torch.bfloat16),                     # C3 verify (gamma=5)
+    (16, 2, 128, 7, [100, 3000, 8191], 16, torch.bfloat16),                     # C5 verify (gamma=6, ratio 8)
+    (14, 2, 64, 1, [2, 64, 777, 2100], 16, torch.bfloat16),                     # 0.5B draft (ratio 7, d 64)
+    (14, 2, 64, 5, [0, 31, 1000], 16, torch.float16),                           # fp16, extend
+    (4, 2, 64, 1, [0, 40, 333], 16, torch.bfloat16),                            # C1 shape (ratio 2)
+    (8, 8, 128, 3, [10, 700], 16, torch.bfloat16),                              # MHA, Hkv 8
+]
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+@pytest.mark.parametrize("generic", [False, True])
+def test_paged_attention_matches_oracle(case, generic):
+    Hq, Hkv, d, chunk, starts, bs, dtype = CASES[case]
+    kv, ref = _build([s + chunk for s in starts], Hkv, d, bs, dtype, seed=100 + case)
+    rng = np.random.default_rng(case)
+    q = torch.from_numpy(rng.standard_normal((len(starts), chunk, Hq, d)).astype(np.float32)).to(DEV, dtype)
+    batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
+    out = paged_attention(q, kv, 0, batch, force_generic=generic)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, force_generic=generic)
+    exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(len(starts)), starts)
+    _check_bf16(out.float().cpu().numpy(), out32.cpu().numpy(), exact)
+    kv.check_errors()
+
+
+@pytest.mark.parametrize("pps", [1, 3, 64])
+def test_split_plans_agree(pps):
+    """Any pages-per-split choice gives the same result (split-K combine)."""
+    kv, ref = _build([2500, 17, 900], 2, 128, 16, torch.bfloat16, seed=5)
+    q = torch.randn(3, 1, 12, 128, device=DEV, dtype=torch.bfloat16)
+    batch = AttnBatch.from_lists(DEV, [0, 1, 2], [2499, 16, 899], 1)
+    out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps)
+    exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), [2499, 16, 899])
+    assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
+
+
+def test_fp32_pools_use_exact_cuda_core_path():
+    kv, ref = _build([9, 100, 1], 2, 16, 4, torch.float32, seed=9)
+    q = torch.randn(3, 4, 4, 16, device=DEV)
+    starts = [5, 96, 0]
+    batch = AttnBatch.from_lists(DEV, [0, 1, 2], starts, 1)
+    out = paged_attention(q[:, :1], kv, 0, batch)
+    exact = oatt.paged_attention_extend(q[:, :1].cpu().numpy(), ref, 0, range(3), starts)
+    np.testing.assert_allclose(out.cpu().numpy(), exact, rtol=1e-5, atol=1e-5)
+
+
+def test_multi_layer_pool_reads_the_right_layer():
+    kv, ref = _build([300, 45], 2, 128, 16, torch.bfloat16, seed=21, layers=3)
+    q = torch.randn(2, 1, 12, 128, device=DEV, dtype=torch.bfloat16)
+    for layer in range(3):
+        out = paged_attention(q, kv, layer, AttnBatch.from_lists(DEV, [0, 1], [299, 44], 1), out_dtype=torch.float32)
+        exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, layer, range(2), [299, 44])
+        assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
+
+
+# ------------------------------------------------------ reference entry points
+def test_decode_api_and_full_attention_match_oracle():
+    kv, ref = _build([9, 10, 1, 7], 2, 8, 4, torch.float32, seed=3)
+    q = torch.randn(4, 4, 8, device=DEV)
+    lens = [9, 10, 1, 7]
+    out = paged_attention_decode(q, kv, 0, [0, 1, 2, 3], lens, 4)
+    exact = oatt.paged_attention_decode(q.cpu().numpy(), ref, 0, range(4), lens)
+    np.testing.assert_allclose(out.cpu().numpy(), exact, rtol=1e-5, atol=1e-5)
+    for sid in range(4):
+        kvp = gather_ctx(kv, 0, sid, lens[sid])
+        fo = full_attention(q[sid], kvp[0], kvp[1], 4)
+        np.testing.assert_allclose(fo.cpu().numpy(), exact[sid], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.float32, 8), (torch.bfloat16, 128), (torch.bfloat16, 64)])
+def test_prefill_chunk_matches_oracle_and_zeroes_padding(dtype, d):
+    Hq, Hkv = (4, 2) if d == 8 else (12, 2)
+    lens = [4, 6, 1] if d == 8 else [40, 77, 13]
+    chunk = max(lens)
+    q = torch.randn(3, chunk, Hq, d, device=DEV).to(dtype)
+    k = torch.randn(3, chunk, Hkv, d, device=DEV).to(dtype)
+    v = torch.randn(3, chunk, Hkv, d, device=DEV).to(dtype)
+    out = paged_attention_prefill_chunk(q, k, v, Hq, lens)
+    exact = oatt.paged_attention_prefill_chunk(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                               v.float().cpu().numpy(), lens)
+    o = out.float().cpu().numpy()
+    for b, ln in enumerate(lens):
+        assert np.all(o[b, ln:] == 0.0)
+    if dtype == torch.float32:
+        np.testing.assert_allclose(o, exact, rtol=1e-5, atol=1e-5)
+    else:
+        assert np.all(np.abs(o - exact) <= 2.0 ** -8 * np.abs(exact) + 2e-3 * np.abs(exact).max())
+
+
+def test_extend_matches_per_position_full_attention():
+    """tests/test_paged_attention_extend.py restated: row j == full attention over start+j+1."""
+    kv, ref = _build([12], 2, 16, 4, torch.float32, seed=12)
+    q = torch.randn(1, 5, 4, 16, device=DEV)
+    out = paged_attention_extend(q, kv, 0, [0], [7], 4)
+    for j in range(5):
+        kvp = gather_ctx(kv, 0, 0, 7 + j + 1)
+        fo = full_attention(q[0, j], kvp[0], kvp[1], 4)
+        torch.testing.assert_close(out[0, j], fo, rtol=1e-5, atol=1e-5)
