@@ -226,10 +226,10 @@ def run_gpu(args, rank: int, world: int, device):
     kv.release(sids, ctx, rel_flags)
     torch.cuda.synchronize(device)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
+    with torch.cuda.graph(graph):  # captured on torch's side stream, replayed on `stream`
         step_layers()
     attn_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(attn_graph, stream=stream):
+    with torch.cuda.graph(attn_graph):
         step_layers(with_append=False)
     torch.cuda.synchronize(device)
 

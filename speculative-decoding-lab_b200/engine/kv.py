@@ -271,16 +271,17 @@ class PagedKVCache:
             if c <= 0:
                 continue
             nb_need = _cdiv(st + c, bs)
-            if nb_need > self.width:
-                raise RuntimeError(
-                    "sequence {} needs {} blocks > max_blocks_per_seq={}".format(sid, nb_need, self.width)
-                )
             new = nb_need - self._h_nb[sid]
             if new > 0:
                 need_total += new
             plan.append((sid, nb_need, st + c))
         if need_total > self.allocator._h_free:
             raise _exhausted(self.capacity)
+        for sid, nb_need, _ in plan:
+            if nb_need > self.width:
+                raise RuntimeError(
+                    "sequence {} needs {} blocks > max_blocks_per_seq={}".format(sid, nb_need, self.width)
+                )
         for sid, nb_need, end in plan:
             if nb_need > self._h_nb[sid]:
                 self._h_nb[sid] = nb_need

@@ -292,6 +292,9 @@ class SpeculativePagedScheduler(PagedScheduler):
                     self.draft_kv._shadow_release(sid, keep, _lib.REL_TRUNCATE)
                 elif d_len < keep:
                     self._shadow_extend_one(self.draft_kv, sid, d_len)
+                    # the reference decodes (and counts) the catch-up token even
+                    # when the sequence finishes this round; its K/V is discarded
+                    result.draft_forward_calls += keep - d_len
                     if c_h[b] >= 0:
                         catch_sids.append(sid)
                         catch_pos.append(d_len)
@@ -308,7 +311,6 @@ class SpeculativePagedScheduler(PagedScheduler):
             ids = torch.tensor(catch_tok, dtype=torch.long, device=device)
             slots = _lib.i32(catch_slot, device)
             draft.decode(ids, self.draft_kv, catch_sids, catch_pos, slots=slots)
-            result.draft_forward_calls += len(catch_sids)
 
     @staticmethod
     def _shadow_extend_one(kv: PagedKVCache, sid: int, pos: int) -> None:
