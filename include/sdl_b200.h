@@ -198,6 +198,19 @@ size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
 /* Paged / dense attention for decode, verify (extend) and prefill rows. */
 int sdl_paged_attention(const sdl_attn_args* args, void* stream);
 
+/* Allocation-free variant of sdl_paged_attention (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they call
+ * in: a runtime whose pool allocator owns all HBM, or an FFI host that only
+ * owns its input/output buffers.  args->workspace is ignored; split-K
+ * partials go to a static 8 MiB device array (sdl_noalloc_scratch_bytes())
+ * that every GPU loading the library keeps until exit.  Calls whose plan
+ * needs more scratch return SDL_ERR_WORKSPACE without launching.  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls that overlap on the GPU (other streams, other threads) race. */
+int sdl_paged_attention_noalloc(const sdl_attn_args* args, void* stream);
+size_t sdl_noalloc_scratch_bytes(void);
+
 /* Named aliases a reference-side binding would call:
  *   sdl_paged_decode  -> paged_attention_decode  (engine/attention.py:96)
  *   sdl_paged_verify  -> paged_attention_extend  (engine/attention.py:170)

@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -698,6 +699,68 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     else if (a->dtype == SDL_BF16) attn_generic_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(gp);
     else attn_generic_kernel<__half><<<grid, 128, 0, st>>>(gp);
     return sdl::check_launch("attn_generic_kernel");
+}
+
+// ------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory at call time: a serving runtime
+// that hands all HBM to its own pool allocator at start-up (cudaMalloc then
+// fails or fragments that pool), or a foreign-language host (FFI) that only
+// owns the input and output buffers it passes in.  For them,
+// sdl_paged_attention_noalloc keeps the split-K partials in this file-scope
+// array instead of a caller workspace.  Every GPU that loads the library
+// holds the array (kNoAllocScratchBytes) until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[128] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// symbol is only a stand-in, so the address is looked up once per device
+// (with that device current) and cached.
+int noalloc_scratch(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    if (dev < 0 || dev >= 128) return sdl::fail(SDL_ERR_INVALID, "sdl_paged_attention_noalloc: device ordinal >= 128");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            return sdl::fail(SDL_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) failed");
+        g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    }
+    *out = g_noalloc_ptr[dev];
+    return SDL_OK;
+}
+}  // namespace
+
+extern "C" size_t sdl_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int sdl_paged_attention_noalloc(const sdl_attn_args* args, void* stream) {
+    int rc = validate(args);
+    if (rc != SDL_OK) return rc;
+    sdl_attn_args a = *args;
+    a.workspace = nullptr;
+    a.workspace_bytes = 0;
+    const size_t need = sdl_attention_workspace_bytes(&a);
+    if (need > kNoAllocScratchBytes) {
+        char msg[256];
+        snprintf(msg, sizeof(msg),
+                 "sdl_paged_attention_noalloc: this call needs %zu bytes of split-K scratch, more than the "
+                 "%zu-byte static scratch; pass a workspace to sdl_paged_attention instead",
+                 need, kNoAllocScratchBytes);
+        return sdl::fail(SDL_ERR_WORKSPACE, msg);
+    }
+    if (need > 0) {
+        float* scratch = nullptr;
+        if ((rc = noalloc_scratch(&scratch)) != SDL_OK) return rc;
+        a.workspace = scratch;
+        a.workspace_bytes = kNoAllocScratchBytes;
+    }
+    return sdl_paged_attention(&a, stream);
 }
 
 extern "C" int sdl_paged_decode(const sdl_attn_args* args, void* stream) {

@@ -52,6 +52,8 @@ EXPORTED_SYMBOLS = (
     "sdl_make_kv_tensor_map",
     "sdl_attention_workspace_bytes",
     "sdl_paged_attention",
+    "sdl_paged_attention_noalloc",
+    "sdl_noalloc_scratch_bytes",
     "sdl_paged_decode",
     "sdl_paged_verify",
     "sdl_prefill_chunk",
@@ -127,6 +129,8 @@ _SIGS = {
     "sdl_make_kv_tensor_map": (c_int, [c_void, c_void, c_int, c_i64, c_int, c_int]),
     "sdl_attention_workspace_bytes": (c_size, [_P(SdlAttnArgs)]),
     "sdl_paged_attention": (c_int, [_P(SdlAttnArgs), c_void]),
+    "sdl_paged_attention_noalloc": (c_int, [_P(SdlAttnArgs), c_void]),
+    "sdl_noalloc_scratch_bytes": (c_size, []),
     "sdl_paged_decode": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_paged_verify": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_prefill_chunk": (c_int, [_P(SdlAttnArgs), c_void]),

@@ -1,0 +1,80 @@
+"""The allocation-free attention entry point, called through the C ABI.
+
+``sdl_paged_attention_noalloc`` serves callers that cannot allocate device
+memory at call time (a runtime whose pool allocator owns all HBM, or an FFI
+host that only owns the buffers it passes in): its split-K partials live in a
+static device array instead of a caller workspace.  It must give the same
+output as ``sdl_paged_attention`` with a workspace, on consecutive calls that
+reuse the shared array, and refuse shapes whose scratch exceeds the array.
+
+This file sorts last so that a stop-at-first-failure run has already run
+every other test; it is also self-contained for a fresh process.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from engine import _lib
+from engine.attention import AttnBatch, _paged_args, paged_attention
+from engine.kv import PagedKVCache
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _case(seed: int, lens, chunk: int):
+    """A paged bf16 cache with Qwen2.5-1.5B attention shapes and random K/V."""
+    Hq, Hkv, d, bs = 12, 2, 128, 16
+    rng = np.random.default_rng(seed)
+    cap = sum(-(-(n + chunk) // bs) for n in lens) + 2
+    kv = PagedKVCache(1, Hkv, d, cap, bs, DEV, torch.bfloat16)
+    for sid, n in enumerate(lens):
+        kv.add_sequence(sid)
+        slots = kv.reserve([sid], [0], [n + chunk])
+        k = torch.from_numpy(rng.standard_normal((n + chunk, Hkv, d)).astype(np.float32)).to(DEV, torch.bfloat16)
+        v = torch.from_numpy(rng.standard_normal((n + chunk, Hkv, d)).astype(np.float32)).to(DEV, torch.bfloat16)
+        kv.append(0, slots, k, v)
+    q = torch.from_numpy(rng.standard_normal((len(lens), chunk, Hq, d)).astype(np.float32)).to(DEV, torch.bfloat16)
+    return kv, q, AttnBatch.from_lists(DEV, list(range(len(lens))), lens, chunk)
+
+
+def _noalloc(q, kv, batch):
+    out = torch.zeros(q.shape, dtype=q.dtype, device=DEV)
+    args = _paged_args(q, kv, 0, batch, out)
+    lib = _lib.load()
+    assert lib.sdl_attention_workspace_bytes(args) > 0, "case must exercise the split-K scratch"
+    rc = lib.sdl_paged_attention_noalloc(ctypes.byref(args), _lib.stream_handle(DEV))
+    _lib.check(rc, "sdl_paged_attention_noalloc")
+    return out
+
+
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
+    for seed, lens, chunk in ((1, [3000, 17, 1200, 640], 1), (2, [2047, 900, 5], 6)):
+        kv, q, batch = _case(seed, lens, chunk)
+        want = paged_attention(q, kv, 0, batch)           # caller-provided workspace
+        got = _noalloc(q, kv, batch)                      # static scratch, reused across calls
+        torch.cuda.synchronize()
+        # same plan and arithmetic: equal within the attention tolerance (in fact bit-equal)
+        torch.testing.assert_close(got.float(), want.float(), rtol=2e-3, atol=2e-3)
+        assert torch.equal(got, want)
+        kv.check_errors()
+
+
+def test_noalloc_refuses_scratch_beyond_its_array():
+    lib = _lib.load()
+    kv = PagedKVCache(1, 2, 128, 8, 16, DEV, torch.bfloat16, max_blocks_per_seq=2100)
+    q = torch.zeros((64, 7, 16, 128), device=DEV, dtype=torch.bfloat16)
+    rows = torch.arange(64, dtype=torch.int32, device=DEV)
+    starts = torch.zeros(64, dtype=torch.int32, device=DEV)
+    batch = AttnBatch(rows, starts, 32768)
+    args = _paged_args(q, kv, 0, batch, q)
+    assert lib.sdl_attention_workspace_bytes(args) > lib.sdl_noalloc_scratch_bytes()
+    rc = lib.sdl_paged_attention_noalloc(ctypes.byref(args), _lib.stream_handle(DEV))
+    assert rc == 4  # SDL_ERR_WORKSPACE, refused on the host before any launch
+    assert "static scratch" in _lib.last_error()
+    assert int(kv.err_word.item()) == 0
