@@ -181,7 +181,7 @@ def run_gpu(args, rank: int, world: int, device):
     import torch
 
     from engine import _lib
-    from engine.attention import AttnBatch, attention_splits, paged_attention
+    from engine.attention import AttnBatch, attention_launches, paged_attention
     from engine.kv import PagedKVCache
     from engine.workloads import c2_layout
 
@@ -316,7 +316,7 @@ def run_gpu(args, rank: int, world: int, device):
         raise RuntimeError("e2e outputs differ from the graph path")
 
     attn_bytes = sum((x + 1) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * Hq * d * 2 + sum(-(-(x + 1) // bs) * 4 for x in ctx)
-    per_layer = 2 + (1 if attention_splits(q[0], kv, batch) else 0)  # append, attention, split combine
+    per_layer = 1 + attention_launches(q[0], kv, batch)  # append + attention (+ split merge)
     launches_per_step = 2 + L * per_layer  # + reserve + release
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms], device=device)

@@ -188,6 +188,7 @@ typedef struct sdl_attn_args {
     size_t workspace_bytes;
     int32_t pages_per_split;  /* 0 = choose automatically                  */
     int32_t force_generic;    /* 1 = CUDA-core path even when TC applies   */
+    int32_t kv_heads_per_cta; /* 0 = automatic; caps kv heads per CTA      */
     int32_t* err;
 } sdl_attn_args;
 

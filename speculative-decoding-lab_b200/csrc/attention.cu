@@ -74,6 +74,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
+    // Launched as a programmatic dependent: everything below may read what
+    // the preceding kernel (K/V append, block-table reserve) wrote.
+    pdl_wait();
+
     const int b = blockIdx.z;
     const int split = blockIdx.x;
     const int coltile = blockIdx.y % p.ncoltiles;
@@ -162,6 +166,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             for (int i = max(0, issued - kStages); i < issued; ++i)
                 (void)mbar_wait_bounded(&full[i % kStages], (i / kStages) & 1, kWaitLimit);
         }
+        pdl_launch_dependents();
         return;
     }
 
@@ -292,6 +297,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         if (lane == 0) mbar_arrive(&empty[st]);
     }
     __syncthreads();
+    pdl_launch_dependents();  // the split merge may be scheduled during the epilogue
     if (aborted || *s_abort) return;
 
     // Epilogue: finished rows write the output, split rows write partials.
@@ -336,11 +342,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
 }
 
-// Merge split-K partials (m in log2 units, unnormalised O, l).
-__global__ void attn_combine_kernel(TcParams p, int hd) {
-    const int h = blockIdx.x % p.Hq;
-    const int j = (blockIdx.x / p.Hq) % p.chunk;
-    const int b = blockIdx.x / (p.Hq * p.chunk);
+// Merge split-K partials (m in log2 units, unnormalised O, l).  One warp per
+// (sequence, chunk row, q head): lanes reduce the split maxima and
+// denominators in parallel, then each lane owns 4 consecutive head dims and
+// keeps 8 splits' loads in flight at once (the merge is latency bound).
+__global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
+    pdl_wait();  // partials come from the attention launch just before
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 4 + warp;
+    if (r >= p.B * p.chunk * p.Hq) return;
+    const int h = r % p.Hq;
+    const int j = (r / p.Hq) % p.chunk;
+    const int b = r / (p.Hq * p.chunk);
     const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
     if (j >= nvalid) return;
     const int L = p.starts[b] + j + 1;
@@ -351,21 +364,50 @@ __global__ void attn_combine_kernel(TcParams p, int hd) {
     const int64_t idx0 = (((int64_t)b * p.nsplit) * p.chunk + j) * p.Hq + h;
     const int64_t sstride = (int64_t)p.chunk * p.Hq;
     float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, p.ml_part[(idx0 + s * sstride) * 2]);
+    for (int s = lane; s < ns; s += 32) M = fmaxf(M, p.ml_part[(idx0 + s * sstride) * 2]);
+    M = warp_max(M);
     float den = 0.f;
-    for (int s = 0; s < ns; ++s) {
+    for (int s = lane; s < ns; s += 32) {
         const float* ml = p.ml_part + (idx0 + s * sstride) * 2;
         den += exp2f(ml[0] - M) * ml[1];
     }
+    den = warp_sum(den);
     const float inv = 1.f / den;
     const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float num = 0.f;
-        for (int s = 0; s < ns; ++s) {
-            const int64_t idx = idx0 + s * sstride;
-            num += exp2f(p.ml_part[idx * 2] - M) * p.o_part[idx * hd + d];
+    for (int d0 = lane * 4; d0 < hd; d0 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int s = 0;
+        for (; s + 8 <= ns; s += 8) {
+            float w[8];
+            float4 o[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int64_t idx = idx0 + (s + t) * sstride;
+                w[t] = p.ml_part[idx * 2];
+                o[t] = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const float wt = exp2f(w[t] - M);
+                acc.x += wt * o[t].x;
+                acc.y += wt * o[t].y;
+                acc.z += wt * o[t].z;
+                acc.w += wt * o[t].w;
+            }
         }
-        store_from_f32(p.out, ob + d, p.out_dtype, num * inv);
+        for (; s < ns; ++s) {
+            const int64_t idx = idx0 + s * sstride;
+            const float wt = exp2f(p.ml_part[idx * 2] - M);
+            const float4 o = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
+            acc.x += wt * o.x;
+            acc.y += wt * o.y;
+            acc.z += wt * o.z;
+            acc.w += wt * o.w;
+        }
+        store_from_f32(p.out, ob + d0, p.out_dtype, acc.x * inv);
+        store_from_f32(p.out, ob + d0 + 1, p.out_dtype, acc.y * inv);
+        store_from_f32(p.out, ob + d0 + 2, p.out_dtype, acc.z * inv);
+        store_from_f32(p.out, ob + d0 + 3, p.out_dtype, acc.w * inv);
     }
 }
 
@@ -549,6 +591,7 @@ Plan make_plan(const sdl_attn_args* a) {
         if (a->Hkv % gc) continue;
         if (gc * pl.wpg > kMaxConsumerWarps) continue;
         if ((size_t)kStages * gc * head_stage > 160 * 1024) continue;
+        if (a->kv_heads_per_cta > 0 && gc > a->kv_heads_per_cta) continue;
         pl.g_cta = gc;
         break;
     }
@@ -581,7 +624,8 @@ int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams&
     }
     dim3 grid(pl.nsplit, pl.ncoltiles * pl.kvgroups, tp.B);
     dim3 block((pl.g_cta * pl.wpg + 1) * 32);
-    kern<<<grid, block, pl.smem, st>>>(mk, mv, tp);
+    cudaError_t e = sdl::launch_pdl(kern, grid, block, pl.smem, st, mk, mv, tp);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("attn_tc_kernel");
 }
 
@@ -678,7 +722,10 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         else rc = launch_tc_dtype<__half>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
         if (rc != SDL_OK) return rc;
         if (pl.nsplit > 1) {
-            attn_combine_kernel<<<a->B * a->chunk * a->Hq, 128, 0, st>>>(tp, a->head_dim);
+            const int rows = a->B * a->chunk * a->Hq;
+            cudaError_t e = sdl::launch_pdl(attn_combine_kernel, dim3((rows + 3) / 4), dim3(128), 0, st, tp,
+                                            (int)a->head_dim);
+            if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
             rc = sdl::check_launch("attn_combine_kernel");
         }
         return rc;

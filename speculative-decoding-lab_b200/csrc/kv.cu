@@ -199,6 +199,7 @@ __global__ void kv_append_kernel(char* __restrict__ kpool, char* __restrict__ vp
                                  int64_t pool_slots, int32_t row_bytes, int32_t ntok,
                                  const int32_t* __restrict__ slots, const char* __restrict__ ksrc,
                                  const char* __restrict__ vsrc, int64_t src_stride, int32_t* err) {
+    pdl_launch_dependents();  // the attention launch may start its prologue now
     const int32_t chunks = row_bytes / (int32_t)sizeof(W);
     const int64_t total = (int64_t)ntok * chunks * 2;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;

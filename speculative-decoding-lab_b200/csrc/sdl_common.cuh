@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "sdl_b200.h"
 
@@ -33,6 +34,25 @@ inline int check_launch(const char* what) {
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline int dtype_bytes(int dt) { return dt == SDL_F32 ? 4 : 2; }
+
+// Launch with the programmatic-stream-serialization attribute so the kernel
+// may start while its predecessor drains (it must call pdl_wait() before
+// touching the predecessor's results).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace sdl
 
@@ -117,6 +137,13 @@ SDL_DEV float warp_sum(float v) {
 }
 
 // -------------------------------------------------------------- inline PTX
+// Programmatic dependent launch: wait until the preceding kernel in the
+// stream has completed and its writes are visible (no-op when the kernel was
+// launched without the programmatic-serialization attribute), and allow the
+// next kernel to be scheduled early.
+SDL_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SDL_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 SDL_DEV uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

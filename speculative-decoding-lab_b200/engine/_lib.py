@@ -108,6 +108,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("workspace_bytes", c_size),
         ("pages_per_split", c_int),
         ("force_generic", c_int),
+        ("kv_heads_per_cta", c_int),
         ("err", c_void),
     ]
 

@@ -81,7 +81,8 @@ def _launch(a: _lib.SdlAttnArgs, device: torch.device, fn: str = "sdl_paged_atte
     _lib.check(getattr(lib, fn)(a, _lib.stream_handle(device)), fn)
 
 
-def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0) -> _lib.SdlAttnArgs:
+def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0,
+                kv_heads_per_cta=0) -> _lib.SdlAttnArgs:
     a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
     a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
     mk, mv = kv.tensor_maps()
@@ -95,14 +96,16 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
     a.max_limit = batch.max_limit
     a.pages_per_split = int(pages_per_split)
     a.force_generic = 1 if force_generic else 0
+    a.kv_heads_per_cta = int(kv_heads_per_cta)
     return a
 
 
-def attention_splits(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch) -> bool:
-    """Whether a call with this shape runs split-K (and so a combine launch)."""
+def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch) -> int:
+    """Kernel launches one call makes: the attention launch, plus the split-K
+    merge when the plan splits a row's pages across CTAs."""
     q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
     a = _paged_args(q4, kv, 0, batch, q4)
-    return bool(_lib.load().sdl_attention_workspace_bytes(a))
+    return 2 if _lib.load().sdl_attention_workspace_bytes(a) else 1
 
 
 def paged_attention(
@@ -114,8 +117,14 @@ def paged_attention(
     out_dtype: Optional[torch.dtype] = None,
     force_generic: bool = False,
     pages_per_split: int = 0,
+    kv_heads_per_cta: int = 0,
 ) -> torch.Tensor:
-    """One launch over ``q`` of shape ``(B, chunk, Hq, d)`` against the pages of ``kv``."""
+    """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
+
+    ``pages_per_split`` / ``kv_heads_per_cta`` override the launch plan
+    (pages per split-K CTA, kv heads sharing one CTA); every plan gives the
+    same result within rounding of the split merge.
+    """
     _lib.require_cuda(q, "query")
     if q.dim() != 4 or q.shape[3] != kv.head_dim:
         raise ValueError("query must be (B, chunk, Hq, {}), got {}".format(kv.head_dim, tuple(q.shape)))
@@ -125,7 +134,7 @@ def paged_attention(
         q = q.contiguous()
     if out is None:
         out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
-    a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split)
+    a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta)
     if batch.max_limit > kv.width * kv.block_size:
         raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))
     _launch(a, q.device)

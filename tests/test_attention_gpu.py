@@ -153,15 +153,32 @@ def test_paged_attention_matches_oracle(case, generic):
     kv.check_errors()
 
 
-@pytest.mark.parametrize("pps", [1, 3, 64])
-def test_split_plans_agree(pps):
-    """Any pages-per-split choice gives the same result (split-K combine)."""
-    kv, ref = _build([2500, 17, 900], 2, 128, 16, torch.bfloat16, seed=5)
+@pytest.mark.parametrize("pps", [1, 3, 0, 64])
+@pytest.mark.parametrize("heads_per_cta", [0, 1])
+def test_split_plans_agree(pps, heads_per_cta):
+    """Every launch plan (pages per split-K CTA from 1, i.e. 150+ splits per
+    row, to one split; one or two kv heads per CTA) gives the oracle's result
+    for decode and verify rows."""
+    kv, ref = _build([2500 + 6, 17 + 6, 900 + 6], 2, 128, 16, torch.bfloat16, seed=5)
+    for chunk, starts in ((1, [2505, 22, 905]), (6, [2500, 17, 900])):
+        q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
+        batch = AttnBatch.from_lists(DEV, [0, 1, 2], starts, chunk)
+        out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps,
+                              kv_heads_per_cta=heads_per_cta)
+        exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), starts)
+        assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
+    kv.check_errors()
+
+
+def test_split_merge_is_deterministic():
+    """The split-K merge has a fixed reduction order: repeated calls give
+    identical bits."""
+    kv, _ = _build([3000, 1500, 40], 2, 128, 16, torch.bfloat16, seed=6)
     q = torch.randn(3, 1, 12, 128, device=DEV, dtype=torch.bfloat16)
-    batch = AttnBatch.from_lists(DEV, [0, 1, 2], [2499, 16, 899], 1)
-    out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps)
-    exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), [2499, 16, 899])
-    assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
+    batch = AttnBatch.from_lists(DEV, [0, 1, 2], [2999, 1499, 39], 1)
+    first = paged_attention(q, kv, 0, batch, pages_per_split=4)
+    for _ in range(5):
+        assert torch.equal(paged_attention(q, kv, 0, batch, pages_per_split=4), first)
 
 
 def test_fp32_pools_use_exact_cuda_core_path():
