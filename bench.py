@@ -19,7 +19,17 @@ Arms:
   --impl reference   the reference's CPU algorithm (the numpy oracle port, all
                      host threads) on a bounded sample of the same workload.
 
-Multi-GPU (torchrun): every rank runs its own batch of 64 sequences (weak
+``--workload c3`` instead times the verify step of
+a speculative round at gamma = 5: 32 sequences per GPU with contexts
+U[256, 2048] reserve gamma+1 positions, every one of the 28 layers appends
+their K/V and runs the (gamma+1)-row extend attention (Qwen2.5-1.5B
+attention shapes, bf16), then target and draft logits ~ N(0, 2) (fp32,
+vocab 151936, fixed draft proposals drawn from the draft distribution) go
+through temperature-1 softmax and the fused rejection sampler with fp32
+uniforms from a seeded stream, and the commit kernel rewinds every block
+table to its accept length.  tokens/s = committed tokens / time.
+
+Multi-GPU (torchrun): every rank runs its own batch of sequences (weak
 scaling, no data-path collective); a barrier brackets the timed region and the
 slowest rank's time is used.
 """
@@ -46,6 +56,8 @@ for _p in (PKG, ROOT):
 
 METRIC = "spec-decode tokens/s (paged KV, 1/2/4/8 GPU); paged-attn HBM GB/s vs 8 TB/s"
 C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=64, ctx_lo=512, ctx_hi=4096)
+C3 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=32, ctx_lo=256, ctx_hi=2048,
+          gamma=5, vocab=151936, temperature=1.0, logit_std=2.0)
 
 
 def _peaks():
@@ -173,6 +185,104 @@ class CpuC2:
             "sample": "{} (sequence, layer) units of C2 (layer 0 of the 64 sequences: KV write + paged decode "
                       "attention, numpy fp64) in {:.2f} s on {} threads, scaled to 28 layers x 64 sequences "
                       "per step".format(done, dt, self.threads),
+        }
+
+
+class CpuC3:
+    """The reference algorithm (numpy oracle port) on a bounded sample of C3.
+
+    A unit is one sequence's verify step: for every layer write the gamma+1
+    new K/V rows into the paged pool and run the masked extend attention
+    (engine/attention.py:170-215 after engine/kv.py:125-147); then softmax the
+    sequence's 2*gamma+1 logit rows, run batch_accept
+    (engine/spec_scheduler.py:46-88) and truncate the table to the accept
+    length (engine/kv.py:150-162).  Units run on ``layers_sampled`` layers
+    and are scaled to 28; tokens/s = committed tokens / scaled seconds.
+    """
+
+    def __init__(self, seed: int = 0, threads: int = 0, layers_sampled: int = 2, batch: int = 32) -> None:
+        from engine.workloads import c2_layout
+        from oracle import kv as okv
+        from oracle import sampler as osm
+
+        c = C3
+        self.gamma = c["gamma"]
+        self.chunk = c["gamma"] + 1
+        self.layers = layers_sampled
+        self.B = batch
+        bs = c["block_size"]
+        self.ctx, _, _ = c2_layout(seed, batch, c["ctx_lo"], c["ctx_hi"], bs)
+        cap = sum(-(-(x + self.chunk) // bs) for x in self.ctx) + batch
+        rng = np.random.default_rng(seed)
+        self.kv = okv.PagedKVCache(layers_sampled, c["kv_heads"], c["head_dim"], cap, bs)
+        self.kv.k[:] = rng.standard_normal(self.kv.k.shape, dtype=np.float32)
+        self.kv.v[:] = rng.standard_normal(self.kv.v.shape, dtype=np.float32)
+        for sid, n in enumerate(self.ctx):
+            self.kv.add_sequence(sid)
+            self.kv.reserve([sid], [0], [n])
+        self.lock = threading.Lock()  # the pool's free list is shared by the worker threads
+        H, d, V = c["q_heads"], c["head_dim"], c["vocab"]
+        self.q = rng.standard_normal((batch, self.chunk, H, d)).astype(np.float32)
+        self.knew = rng.standard_normal((batch, self.chunk, c["kv_heads"], d)).astype(np.float32)
+        self.p_logits = (rng.standard_normal((batch, self.chunk, V)) * c["logit_std"]).astype(np.float32)
+        self.q_logits = (rng.standard_normal((batch, self.gamma, V)) * c["logit_std"]).astype(np.float32)
+        self.uniforms = rng.random(1 << 16, dtype=np.float32)
+        self.props = []
+        for b in range(batch):
+            qp = osm.logits_to_probs(self.q_logits[b], c["temperature"])
+            self.props.append([osm.sample_index(qp[t], self.uniforms[b * self.gamma + t]) for t in range(self.gamma)])
+        self.threads = threads or (os.cpu_count() or 1)
+
+    def _unit(self, b: int) -> int:
+        from oracle import attention as oatt
+        from oracle import sampler as osm
+
+        c = C3
+        start = self.ctx[b]
+        t0 = time.perf_counter()
+        with self.lock:
+            slots = self.kv.reserve([b], [start], [self.chunk])
+        for layer in range(self.layers):
+            self.kv.append(layer, slots, self.knew[b], self.knew[b])
+            oatt.paged_attention_extend(self.q[b][None], self.kv, layer, [b], [start])
+        t1 = time.perf_counter()
+        p = osm.logits_to_probs(self.p_logits[b], c["temperature"])
+        q = osm.logits_to_probs(self.q_logits[b], c["temperature"])
+        stream = osm.UniformStream(self.uniforms[(b * 97) % 4096:])
+        acc = osm.batch_accept([p], [list(q)], [self.props[b]], stream)[0]
+        with self.lock:
+            self.kv.truncate(b, start + len(acc))
+        return len(acc), t1 - t0, time.perf_counter() - t1
+
+    def measure(self, seconds: float):
+        from concurrent.futures import ThreadPoolExecutor
+
+        c = C3
+        toks = units = 0
+        t_attn = t_samp = 0.0
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=self.threads) as ex:
+            while True:
+                res = list(ex.map(self._unit, range(self.B)))
+                toks += sum(r[0] for r in res)
+                t_attn += sum(r[1] for r in res)
+                t_samp += sum(r[2] for r in res)
+                units += len(res)
+                if time.perf_counter() - t0 >= seconds:
+                    break
+        dt = time.perf_counter() - t0
+        # scale the per-layer share of the wall time from the sampled layers to all 28
+        f = t_attn / max(t_attn + t_samp, 1e-12)
+        scaled = dt * (f * c["layers"] / self.layers + (1.0 - f))
+        return {
+            "value": round(toks / scaled, 4),
+            "unit": "tokens/s",
+            "cores": self.threads,
+            "kind": "port",
+            "sample": "{} verify units of C3 ({} of 28 layers: K/V write + masked extend attention, then softmax "
+                      "of 11 vocab rows, batch_accept and truncate; numpy) in {:.2f} s on {} threads, {} committed "
+                      "tokens; the per-layer share ({:.0%}) of the time scaled by 28/{}".format(
+                          units, self.layers, dt, self.threads, toks, f, self.layers),
         }
 
 
@@ -327,20 +437,241 @@ def run_gpu(args, rank: int, world: int, device):
                 d2h=d2h, launches=launches_per_step * args.steps, ctx_mean=float(np.mean(ctx)))
 
 
+def run_gpu_c3(args, rank: int, world: int, device):
+    """The C3 verify step (see the module docstring) on one GPU."""
+    import ctypes
+
+    import torch
+
+    from engine import _lib
+    from engine.attention import AttnBatch, attention_launches, paged_attention
+    from engine.kv import PagedKVCache
+    from engine.workloads import c2_layout
+    from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample
+
+    c = dict(C3)
+    L, B, gam = args.layers, args.batch, c["gamma"]
+    chunk = gam + 1
+    Hq, Hkv, d, bs, V, T = c["q_heads"], c["kv_heads"], c["head_dim"], c["block_size"], c["vocab"], c["temperature"]
+    seed = args.seed + rank
+    ctx, _, _ = c2_layout(seed, B, c["ctx_lo"], c["ctx_hi"], bs)
+    cap = sum(-(-(x + chunk) // bs) for x in ctx) + B
+    kv = PagedKVCache(L, Hkv, d, cap, bs, device, torch.bfloat16,
+                      max_blocks_per_seq=-(-(c["ctx_hi"] + chunk + 1) // bs), max_seqs=B)
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    kv.allocator._free_stack.copy_(torch.randperm(cap, generator=g).to(torch.int32))  # random-permutation pool
+    sids = list(range(B))
+    for sid in sids:
+        kv.add_sequence(sid)
+    kv.reserve(sids, [0] * B, ctx)
+    gd = torch.Generator(device=device)
+    gd.manual_seed(seed)
+    kv._k.normal_(generator=gd)
+    kv._v.normal_(generator=gd)
+    q = torch.randn((L, B, chunk, Hq, d), generator=gd, device=device).to(torch.bfloat16)
+    knew = torch.randn((L, B * chunk, Hkv, d), generator=gd, device=device).to(torch.bfloat16)
+    vnew = torch.randn((L, B * chunk, Hkv, d), generator=gd, device=device).to(torch.bfloat16)
+    out = torch.empty((L, B, chunk, Hq, d), device=device, dtype=torch.bfloat16)
+    p_logits = torch.randn((B, chunk, V), generator=gd, device=device) * c["logit_std"]
+    q_logits = torch.randn((B, gam, V), generator=gd, device=device) * c["logit_std"]
+    p_probs = torch.empty((B, chunk, V), device=device, dtype=torch.float32)
+    q_probs = torch.empty((B, gam, V), device=device, dtype=torch.float32)
+    # the draft's proposals: its own draws from q, fixed for every step
+    probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
+    proposals = sample_rows(q_probs.view(B * gam, V), UniformStream(device, seed=seed + 7)).view(B, gam)
+    ustream = UniformStream(device, seed=seed + 11)
+    batch = AttnBatch.from_lists(device, sids, ctx, chunk)  # row j sits at ctx + j
+    slots_static = torch.empty(B * chunk, dtype=torch.int32, device=device)
+    tokens = torch.empty((B, chunk), dtype=torch.int32, device=device)
+    n_out = torch.empty(B, dtype=torch.int32, device=device)
+    scratch = torch.empty(2 * B, dtype=torch.int32, device=device)
+    packed = _lib.i32(sids + [1 << 30] * B + ctx, device)  # rows, remaining budget, round starts
+    outs = torch.empty((3, B), dtype=torch.int32, device=device)
+    lib = _lib.load()
+    meta = ctypes.byref(kv.meta)
+
+    def verify_layers(with_append=True):
+        for layer in range(L):
+            if with_append:
+                kv.append(layer, slots_static, knew[layer], vnew[layer])
+            paged_attention(q[layer], kv, layer, batch, out=out[layer])
+
+    def sample_commit():
+        probs_rows(p_logits, T, False, out=p_probs.view(B * chunk, V))
+        probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
+        spec_sample(p_probs, q_probs, proposals, ustream, greedy=False, err=kv.err_word, out=(tokens, n_out, scratch))
+        _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), n_out.data_ptr(), tokens.data_ptr(), chunk,
+                                       packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
+                                       outs[1].data_ptr(), outs[2].data_ptr(), _lib.stream_handle(device)),
+                   "sdl_spec_commit")
+
+    # warm every path once outside capture
+    slots_static.copy_(kv.reserve(sids, ctx, [chunk] * B))
+    verify_layers()
+    sample_commit()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        verify_layers()
+    attn_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(attn_graph):
+        verify_layers(with_append=False)
+    torch.cuda.synchronize(device)
+
+    k_hist = torch.zeros((args.steps, B), dtype=torch.int32, device=device)
+
+    def device_step(i=None):
+        # the commit left every table at ctx + k; reserving from ctx backs the round's gamma+1 positions again
+        slots_static.copy_(kv.reserve(sids, ctx, [chunk] * B))
+        graph.replay()
+        sample_commit()
+        if i is not None:
+            k_hist[i].copy_(outs[0])
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize(device)
+    kv.resync()
+    kv.check_errors()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(torch.cuda.current_stream(device))
+    for i in range(args.steps):
+        device_step(i)
+    e1.record(torch.cuda.current_stream(device))
+    torch.cuda.synchronize(device)
+    step_ms = e0.elapsed_time(e1) / args.steps
+    committed = int(k_hist.sum().item())
+    kv.resync()
+
+    # roofline: the verify attention op alone, replayed over the 28 layers
+    reps = max(3, args.steps // 4)
+    slots_static.copy_(kv.reserve(sids, ctx, [chunk] * B))
+    stream = torch.cuda.current_stream(device)
+    for _ in range(2):
+        attn_graph.replay()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(reps):
+        attn_graph.replay()
+    a1.record(stream)
+    torch.cuda.synchronize(device)
+    attn_ms = a0.elapsed_time(a1) / (reps * L)
+    # the sampler alone (softmax of both logit blocks + fused accept/resample)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(reps):
+        probs_rows(p_logits, T, False, out=p_probs.view(B * chunk, V))
+        probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
+        spec_sample(p_probs, q_probs, proposals, ustream, greedy=False, err=kv.err_word,
+                    out=(tokens, n_out, scratch))
+    s1.record(stream)
+    torch.cuda.synchronize(device)
+    samp_ms = s0.elapsed_time(s1) / reps
+    clk = clocks.stop() if clocks else None
+    kv.release(sids, ctx, [_lib.REL_TRUNCATE] * B)
+    kv.check_errors()
+
+    # e2e through the public API: pinned host Q/K/V and logits in, tokens and accept lengths out
+    q_h = q.cpu().pin_memory()
+    k_h = knew.cpu().pin_memory()
+    v_h = vnew.cpu().pin_memory()
+    pl_h = p_logits.cpu().pin_memory()
+    ql_h = q_logits.cpu().pin_memory()
+    pr_h = proposals.cpu().pin_memory()
+    tok_h = torch.empty((args.steps, B, chunk), dtype=torch.int32).pin_memory()
+    k_out_h = torch.empty((args.steps, B), dtype=torch.int32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, pl_h, ql_h, pr_h))
+    d2h = B * chunk * 4 + B * 4
+
+    def e2e_step(i):
+        qd = q_h.to(device, non_blocking=True)
+        kd = k_h.to(device, non_blocking=True)
+        vd = v_h.to(device, non_blocking=True)
+        pld = pl_h.to(device, non_blocking=True)
+        qld = ql_h.to(device, non_blocking=True)
+        prd = pr_h.to(device, non_blocking=True)
+        slots = kv.reserve(sids, ctx, [chunk] * B)
+        b2 = AttnBatch.from_lists(device, sids, ctx, chunk)
+        od = torch.empty_like(out)
+        for layer in range(L):
+            kv.append(layer, slots, kd[layer], vd[layer])
+            paged_attention(qd[layer], kv, layer, b2, out=od[layer])
+        pp = probs_rows(pld, T, False).view(B, chunk, V)
+        qp = probs_rows(qld, T, False).view(B, gam, V)
+        toks, no = spec_sample(pp, qp, prd, ustream, greedy=False, err=kv.err_word)
+        _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), no.data_ptr(), toks.data_ptr(), chunk,
+                                       packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
+                                       outs[1].data_ptr(), outs[2].data_ptr(), _lib.stream_handle(device)),
+                   "sdl_spec_commit")
+        tok_h[i].copy_(toks, non_blocking=True)
+        k_out_h[i].copy_(outs[0], non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 50))
+    for i in range(max(1, args.warmup)):
+        e2e_step(0)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    torch.cuda.synchronize(device)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / e2e_steps
+    e2e_committed = int(k_out_h[:e2e_steps].sum())
+    kv.resync()
+    kv.release(sids, ctx, [_lib.REL_TRUNCATE] * B)
+    kv.check_errors()
+
+    attn_bytes = (sum((x + chunk) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * chunk * Hq * d * 2
+                  + sum(-(-(x + chunk) // bs) * 4 for x in ctx))
+    samp_bytes = B * (2 * gam + 1) * V * 4  # the fp32 logit rows of p and q, each read once
+    per_layer = 1 + attention_launches(q[0], kv, batch)
+    launches_per_step = 1 + L * per_layer + 2 + 2 + 1  # reserve, layers, 2 softmax, accept + resample, commit
+    if world > 1:
+        t = torch.tensor([step_ms, e2e_ms, attn_ms, samp_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, e2e_ms, attn_ms, samp_ms = t.tolist()
+        cnt = torch.tensor([committed, e2e_committed], device=device, dtype=torch.float64)
+        dist.all_reduce(cnt)
+        committed, e2e_committed = [int(x) for x in cnt.tolist()]
+    del graph, attn_graph
+    return dict(step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, samp_ms=samp_ms,
+                samp_bytes=samp_bytes, clocks=clk, h2d=h2d, d2h=d2h, launches=launches_per_step * args.steps,
+                committed=committed, e2e_committed=e2e_committed, e2e_steps=e2e_steps,
+                tokens_per_round=committed / float(args.steps * B * world))
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--layers", type=int, default=C2["layers"], help="fewer layers only for profiling captures")
-    ap.add_argument("--batch", type=int, default=C2["batch"])
+    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
+                    help="c2: decode attention + KV append (default); c3: verify step at gamma=5")
+    ap.add_argument("--layers", type=int, default=28, help="fewer layers only for profiling captures")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (C2: 64, C3: 32)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
+    if args.batch is None:
+        args.batch = C3["batch"] if args.workload == "c3" else C2["batch"]
+    if args.workload == "c3":
+        return main_c3(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -425,6 +756,107 @@ def main(argv=None) -> int:
         "e2e": {"value": round(args.batch * world / (res["e2e_ms"] * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
                 "path": "public per-layer API (PagedKVCache.reserve/append/release + paged_attention), pinned host I/O"},
+        "gpu_launches": res["launches"],
+        "clocks": res["clocks"],
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main_c3(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    c = C3
+    cfg = {"workload": "C3: verify step at gamma=5 (extend attention + fused rejection sampling + rewind)",
+           "layers": args.layers, "q_heads": c["q_heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
+           "block_size": c["block_size"], "gamma": c["gamma"], "vocab": c["vocab"], "temperature": c["temperature"],
+           "batch_per_gpu": args.batch, "global_batch": args.batch * world,
+           "ctx": "U[{},{}] seeded per rank".format(c["ctx_lo"], c["ctx_hi"]),
+           "logits": "N(0, 2) fp32, target gamma+1 rows and draft gamma rows per sequence",
+           "block_tables": "random permutation of a pool holding every context",
+           "l2": "no flush needed: a step streams ~1.06 GB of K/V over 28 disjoint layers and 214 MB of logits",
+           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world)}
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        threads = os.cpu_count() or 1
+        per = min(args.cpu_seconds, 150.0 / max(1, args.steps + args.warmup))
+        base = CpuC3(seed=args.seed, threads=threads, batch=args.batch)
+        vals = []
+        for i in range(args.warmup + args.steps):
+            r = base.measure(per)
+            if i >= args.warmup:
+                vals.append(r["value"])
+        value = float(np.mean(vals))
+        line = {"metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": cfg, "impl": "reference",
+                "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the B200 path has no CPU fallback)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    res = run_gpu_c3(args, rank, world, device)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuC3(seed=args.seed, batch=args.batch).measure(args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    hbm, peak_kind = _peaks()
+    achieved = res["attn_bytes"] / (res["attn_ms"] * 1e-3) / 1e9
+    samp_gbs = res["samp_bytes"] / (res["samp_ms"] * 1e-3) / 1e9
+    value = res["committed"] / (args.steps * res["step_ms"] * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["step_ms"], 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V, N(0,2) logits, U[256,2048] contexts, random-permutation tables)",
+        "config": cfg,
+        "tokens_per_round": round(res["tokens_per_round"], 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "attn_tc_kernel (+ attn_combine_kernel when split): (gamma+1)-row verify attention",
+                     "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
+                     "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
+        "sampler": {"achieved": round(samp_gbs, 1), "unit": "GB/s", "frac": round(samp_gbs / hbm, 4),
+                    "algorithmic_bytes": res["samp_bytes"], "ms": round(res["samp_ms"], 5),
+                    "kernels": "probs_kernel x2 + spec_accept_kernel + spec_resample_kernel"},
+        "e2e": {"value": round(res["e2e_committed"] / (res["e2e_steps"] * res["e2e_ms"] * 1e-3), 2),
+                "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
+                "path": "public API (PagedKVCache.reserve/append, paged_attention, probs_rows, spec_sample, "
+                        "sdl_spec_commit), pinned host Q/K/V, logits and proposals in, tokens and accept lengths out"},
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],
     }

@@ -257,6 +257,16 @@ class PagedKVCache:
     def num_blocks_of(self, seq_id: int) -> int:
         return self._h_nb[seq_id]
 
+    def resync(self) -> None:
+        """Reload the host shadows (block counts, lengths, free count) from the
+        device (synchronises).  For callers that ran device-side commits
+        without mirroring them on the host."""
+        n = len(self._h_len)
+        self._h_nb = self._nb[:n].tolist()
+        self._h_len = self._len[:n].tolist()
+        self.allocator.resync()
+        self._mirror = None
+
     # ------------------------------------------------------------ allocation
     def _plan_reserve(self, seq_ids: Sequence[int], starts: Sequence[int], counts: Sequence[int]) -> None:
         """Check capacity on the host and apply the reserve to the shadows."""
