@@ -56,6 +56,9 @@ for _p in (PKG, ROOT):
 
 METRIC = "spec-decode tokens/s (paged KV, 1/2/4/8 GPU); paged-attn HBM GB/s vs 8 TB/s"
 C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=64, ctx_lo=512, ctx_hi=4096)
+# DRAM bytes (read + write) of one C2 attention launch of attn_tc_kernel, from the
+# ncu --set full capture summarised under profiles/ (refreshed when re-profiled).
+C2_ATTN_TRAFFIC = 154_140_672 + 4_491_008
 C3 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=32, ctx_lo=256, ctx_hi=2048,
           gamma=5, vocab=151936, temperature=1.0, logit_std=2.0)
 
@@ -447,7 +450,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
     from engine.attention import AttnBatch, attention_launches, paged_attention
     from engine.kv import PagedKVCache
     from engine.workloads import c2_layout
-    from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample
+    from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample_logits
 
     c = dict(C3)
     L, B, gam = args.layers, args.batch, c["gamma"]
@@ -475,17 +478,15 @@ def run_gpu_c3(args, rank: int, world: int, device):
     out = torch.empty((L, B, chunk, Hq, d), device=device, dtype=torch.bfloat16)
     p_logits = torch.randn((B, chunk, V), generator=gd, device=device) * c["logit_std"]
     q_logits = torch.randn((B, gam, V), generator=gd, device=device) * c["logit_std"]
-    p_probs = torch.empty((B, chunk, V), device=device, dtype=torch.float32)
-    q_probs = torch.empty((B, gam, V), device=device, dtype=torch.float32)
     # the draft's proposals: its own draws from q, fixed for every step
-    probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
-    proposals = sample_rows(q_probs.view(B * gam, V), UniformStream(device, seed=seed + 7)).view(B, gam)
+    q_probs = probs_rows(q_logits, T, False)
+    proposals = sample_rows(q_probs, UniformStream(device, seed=seed + 7)).view(B, gam)
+    del q_probs
     ustream = UniformStream(device, seed=seed + 11)
     batch = AttnBatch.from_lists(device, sids, ctx, chunk)  # row j sits at ctx + j
     slots_static = torch.empty(B * chunk, dtype=torch.int32, device=device)
     tokens = torch.empty((B, chunk), dtype=torch.int32, device=device)
     n_out = torch.empty(B, dtype=torch.int32, device=device)
-    scratch = torch.empty(2 * B, dtype=torch.int32, device=device)
     packed = _lib.i32(sids + [1 << 30] * B + ctx, device)  # rows, remaining budget, round starts
     outs = torch.empty((3, B), dtype=torch.int32, device=device)
     lib = _lib.load()
@@ -498,9 +499,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
             paged_attention(q[layer], kv, layer, batch, out=out[layer])
 
     def sample_commit():
-        probs_rows(p_logits, T, False, out=p_probs.view(B * chunk, V))
-        probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
-        spec_sample(p_probs, q_probs, proposals, ustream, greedy=False, err=kv.err_word, out=(tokens, n_out, scratch))
+        spec_sample_logits(p_logits, q_logits, T, proposals, ustream, err=kv.err_word, out=(tokens, n_out))
         _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), n_out.data_ptr(), tokens.data_ptr(), chunk,
                                        packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
                                        outs[1].data_ptr(), outs[2].data_ptr(), _lib.stream_handle(device)),
@@ -567,14 +566,11 @@ def run_gpu_c3(args, rank: int, world: int, device):
     a1.record(stream)
     torch.cuda.synchronize(device)
     attn_ms = a0.elapsed_time(a1) / (reps * L)
-    # the sampler alone (softmax of both logit blocks + fused accept/resample)
+    # the fused sampler alone (statistics, accept walk, draw sums, draw)
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record(stream)
     for _ in range(reps):
-        probs_rows(p_logits, T, False, out=p_probs.view(B * chunk, V))
-        probs_rows(q_logits, T, False, out=q_probs.view(B * gam, V))
-        spec_sample(p_probs, q_probs, proposals, ustream, greedy=False, err=kv.err_word,
-                    out=(tokens, n_out, scratch))
+        spec_sample_logits(p_logits, q_logits, T, proposals, ustream, err=kv.err_word, out=(tokens, n_out))
     s1.record(stream)
     torch.cuda.synchronize(device)
     samp_ms = s0.elapsed_time(s1) / reps
@@ -607,9 +603,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
         for layer in range(L):
             kv.append(layer, slots, kd[layer], vd[layer])
             paged_attention(qd[layer], kv, layer, b2, out=od[layer])
-        pp = probs_rows(pld, T, False).view(B, chunk, V)
-        qp = probs_rows(qld, T, False).view(B, gam, V)
-        toks, no = spec_sample(pp, qp, prd, ustream, greedy=False, err=kv.err_word)
+        toks, no = spec_sample_logits(pld, qld, T, prd, ustream, err=kv.err_word)
         _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), no.data_ptr(), toks.data_ptr(), chunk,
                                        packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
                                        outs[1].data_ptr(), outs[2].data_ptr(), _lib.stream_handle(device)),
@@ -636,8 +630,9 @@ def run_gpu_c3(args, rank: int, world: int, device):
     attn_bytes = (sum((x + chunk) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * chunk * Hq * d * 2
                   + sum(-(-(x + chunk) // bs) * 4 for x in ctx))
     samp_bytes = B * (2 * gam + 1) * V * 4  # the fp32 logit rows of p and q, each read once
+    launches_sampler = 4  # statistics, accept walk, draw sums, draw
     per_layer = 1 + attention_launches(q[0], kv, batch)
-    launches_per_step = 1 + L * per_layer + 2 + 2 + 1  # reserve, layers, 2 softmax, accept + resample, commit
+    launches_per_step = 1 + L * per_layer + launches_sampler + 1  # reserve, layers, sampler, commit
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms, samp_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -749,7 +744,9 @@ def main(argv=None) -> int:
         "data": "synthetic (seeded N(0,1) Q/K/V, U[512,4096] contexts, random-permutation block tables)",
         "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "frac": round(achieved / hbm, 4), "traffic": C2_ATTN_TRAFFIC if args.layers == 28 else None,
+                     "traffic_source": "ncu --set full capture of attn_tc_kernel on this workload (dram read + "
+                                       "write per launch, main kernel only; summary under profiles/)",
                      "kernel": "attn_tc_kernel + attn_combine_kernel (one paged decode attention op per layer)",
                      "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
@@ -852,10 +849,11 @@ def main_c3(args) -> int:
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
         "sampler": {"achieved": round(samp_gbs, 1), "unit": "GB/s", "frac": round(samp_gbs / hbm, 4),
                     "algorithmic_bytes": res["samp_bytes"], "ms": round(res["samp_ms"], 5),
-                    "kernels": "probs_kernel x2 + spec_accept_kernel + spec_resample_kernel"},
+                    "kernels": "stats_kernel + accept_logits_kernel + wsum_kernel + finish_kernel "
+                               "(sdl_spec_sample_logits)"},
         "e2e": {"value": round(res["e2e_committed"] / (res["e2e_steps"] * res["e2e_ms"] * 1e-3), 2),
                 "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
-                "path": "public API (PagedKVCache.reserve/append, paged_attention, probs_rows, spec_sample, "
+                "path": "public API (PagedKVCache.reserve/append, paged_attention, spec_sample_logits, "
                         "sdl_spec_commit), pinned host Q/K/V, logits and proposals in, tokens and accept lengths out"},
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],

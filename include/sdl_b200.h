@@ -277,6 +277,42 @@ int sdl_spec_sample(const float* p, int64_t p_sb, int64_t p_sj,
 /* Bytes of int32 scratch sdl_spec_sample needs (2*B entries). */
 size_t sdl_spec_sample_scratch_bytes(int32_t B);
 
+/* ------------------------------------------------------ logits-in sampling
+ * The temperature softmax p = softmax(logits / max(T, eps)) is defined with
+ * a fixed reduction order (chunks of 4096 elements, see
+ * csrc/sampler_logits.cu), so every entry point below derives bit-identical
+ * p_i from the same logits; sdl_logits_to_probs (temperature mode) writes
+ * exactly those values.  Draws use the integer rule of sdl_sample_rows.
+ * Workspaces must be 256-byte aligned and at least
+ * sdl_sampler_workspace_bytes(rows, vocab) bytes, rows = logit rows read. */
+size_t sdl_sampler_workspace_bytes(int32_t rows, int32_t vocab);
+
+/* sample_token (specdec/sampler.py:59-69) applied to logits_to_probs
+ * (specdec/sampler.py:19-36) of every row, without writing p: equal to
+ * sdl_logits_to_probs followed by sdl_sample_rows.  Row r uses uniform
+ * *u_base + u_offset + r. */
+int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t row_stride,
+                           int32_t rows, int32_t vocab, float temperature,
+                           float eps, const float* uniforms,
+                           int64_t num_uniforms, const int64_t* u_base,
+                           int64_t u_offset, int32_t* out, void* workspace,
+                           size_t workspace_bytes, int32_t* err, void* stream);
+
+/* batch_accept (engine/spec_scheduler.py:46-88) from target logits
+ * [B][gamma+1][V] and draft logits [B][gamma][V] (same dtype) in four
+ * launches (row statistics, accept walk, per-chunk draw sums, draw) without
+ * materialising probability rows: equal to sdl_logits_to_probs on both
+ * blocks followed by sdl_spec_sample (sampling mode), including the uniform
+ * consumption and *u_base update. */
+int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj,
+                           const void* q_logits, int64_t q_sb, int64_t q_sj,
+                           int32_t dtype, float temperature, float eps,
+                           const int32_t* proposals, int32_t B, int32_t gamma,
+                           int32_t vocab, const float* uniforms,
+                           int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
+                           int32_t* tokens, int32_t* n_out, void* workspace,
+                           size_t workspace_bytes, int32_t* err, void* stream);
+
 /* Copy the device error word to *out (stream-ordered D2H; *out is valid
  * after the stream synchronises) and optionally clear it. */
 int sdl_get_error(int32_t* err_word, int32_t* out_host, int32_t clear,

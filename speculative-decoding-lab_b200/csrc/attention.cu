@@ -581,7 +581,10 @@ Plan make_plan(const sdl_attn_args* a) {
     const int ratio = a->Hq / a->Hkv;
     const int ncol = a->chunk * ratio;
     const int ntiles = (ncol + 7) / 8;
-    pl.ntg = ntiles >= 2 ? 2 : 1;
+    // Eight query columns per consumer warp while the tiles fit the warp
+    // budget: the 16-column variant needs ~165 registers, which caps a CTA
+    // of it at one per SM; the 8-column variant runs three per SM.
+    pl.ntg = ntiles > kMaxConsumerWarps ? 2 : 1;
     pl.wpg = std::min((ntiles + pl.ntg - 1) / pl.ntg, kMaxConsumerWarps);
     pl.ncoltiles = (ntiles + pl.wpg * pl.ntg - 1) / (pl.wpg * pl.ntg);
     const int DO = a->head_dim / 64;
@@ -619,6 +622,11 @@ int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams&
     static size_t configured = 0;
     if (pl.smem > configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+        // all of the unified L1/shared array as shared memory: the ring buffers,
+        // not L1, decide how many CTAs an SM holds
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
         configured = pl.smem;
     }

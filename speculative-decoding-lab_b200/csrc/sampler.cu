@@ -300,6 +300,10 @@ __global__ void __launch_bounds__(1024) spec_resample_kernel(const float* __rest
 
 }  // namespace
 
+// Canonical temperature softmax (csrc/sampler_logits.cu).
+int sdl_probs_canon(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab, float temp,
+                    float* probs, int64_t probs_stride, cudaStream_t st);
+
 extern "C" int sdl_logits_to_probs(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab,
                                    float temperature, float eps, int32_t greedy, float* probs, int64_t probs_stride,
                                    void* stream) {
@@ -308,6 +312,7 @@ extern "C" int sdl_logits_to_probs(const void* logits, int32_t dtype, int64_t ro
     if (rows == 0) return SDL_OK;
     const float t = temperature > eps ? temperature : eps;
     cudaStream_t st = sdl::as_stream(stream);
+    if (!greedy) return sdl_probs_canon(logits, dtype, row_stride, rows, vocab, t, probs, probs_stride, st);
     if (dtype == SDL_F32)
         probs_kernel<float><<<rows, 1024, 0, st>>>((const float*)logits, row_stride, vocab, t, greedy, probs, probs_stride);
     else if (dtype == SDL_BF16)

@@ -1,0 +1,622 @@
+// Logits-in sampling: canonical chunked softmax statistics, draws straight
+// from logits, and the fused rejection sampler of a speculative round that
+// never materialises a probability row.
+//
+// Canonical softmax.  p = softmax(logits / T) in fp32 (specdec/sampler.py:
+// 19-36) needs a row maximum m and a row sum s.  The maximum is exact; the
+// sum's rounding depends on the summation order, so this file fixes it:
+//   * the row is cut into chunks of kChunk = 4096 elements;
+//   * in a chunk, thread t of a 256-thread group owns elements
+//     lo + 4t + j + 1024k (k = 0..3 outer, j = 0..3 inner) and adds
+//     expf(x/T - m_c) over them in that order (m_c = the chunk maximum);
+//     lanes combine by an xor butterfly (16, 8, 4, 2, 1) and lane 0's value
+//     is kept; warps 0..7 are added in order;
+//   * chunks merge in order: m = max m_c, s = fma(s_c, expf(m_c - m), s).
+// Every kernel here (one CTA per row or one CTA per chunk) evaluates exactly
+// these operations with explicit round-to-nearest intrinsics, so p_i =
+// expf(x_i/T - m) / s is the same bit pattern whichever kernel computes it:
+// sdl_logits_to_probs, sdl_sample_logits_rows and sdl_spec_sample_logits
+// agree bit for bit, and the draws below equal sdl_sample_rows /
+// sdl_spec_sample applied to sdl_logits_to_probs' output.
+//
+// Draws use the integer inverse-CDF rule of sampler.cu (W_i = floor(w_i *
+// 2^62), exact u64 sums), so splitting a row across CTAs cannot change them.
+#include "sdl_common.cuh"
+
+namespace {
+
+constexpr int kChunk = 4096;   // elements per statistics chunk
+constexpr int kGroup = 256;    // threads that reduce one chunk
+constexpr int kPerThread = kChunk / kGroup;
+constexpr int kMaxChunks = 1024;  // vocab <= 4M
+
+constexpr double kTwo62 = 4611686018427387904.0;
+constexpr double kTwo64 = 18446744073709551616.0;
+
+SDL_DEV uint64_t wfix(float w) {
+    if (!(w > 0.f)) return 0ull;
+    double x = (double)w * kTwo62;
+    if (x >= kTwo64) return 0xffffffffffffffffull;
+    return __double2ull_rz(x);
+}
+
+SDL_DEV uint64_t ufix(float u) {
+    if (!(u > 0.f)) return 0ull;
+    double x = (double)u * kTwo64;
+    if (x >= kTwo64) return 0xffffffffffffffffull;
+    return __double2ull_rz(x);
+}
+
+SDL_DEV uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+SDL_DEV uint64_t warp_incl_scan_u64(uint64_t v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+    }
+    return v;
+}
+
+SDL_DEV void group_sync(int id) { asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(kGroup) : "memory"); }
+
+// Logical rows of a [B, J, V] logits tensor with strides (sb, sj).
+template <typename T>
+struct Rows {
+    const T* p;
+    int64_t sb, sj;
+    int J, n;
+    SDL_DEV const T* row(int r) const { return p + (int64_t)(r / J) * sb + (int64_t)(r % J) * sj; }
+};
+
+SDL_DEV float scaled(float x, float temp) { return __fdiv_rn(x, temp); }
+
+// p_i from the scaled logit and the merged row statistics.
+SDL_DEV float prob_of(float xs, float m, float s) { return __fdiv_rn(expf(__fsub_rn(xs, m)), s); }
+
+// Statistics (m_c, s_c) of elements [lo, hi) of row x, reduced by one
+// 256-thread group (g = thread index in the group, bar_id its named barrier,
+// red = 8 floats of group-private shared memory).  Valid in every thread.
+template <typename T>
+SDL_DEV float2 chunk_stats(const T* __restrict__ x, int lo, int hi, float temp, int g, int bar_id, float* red) {
+    float v[kPerThread];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = lo + 4 * g + j + 1024 * k;
+            const float xv = i < hi ? scaled(to_f32<T>(x[i]), temp) : -INFINITY;
+            v[k * 4 + j] = xv;
+            mt = fmaxf(mt, xv);
+        }
+    const int lane = g & 31, w = g >> 5;
+    mt = warp_max(mt);
+    if (lane == 0) red[w] = mt;
+    group_sync(bar_id);
+    float mc = red[0];
+#pragma unroll
+    for (int i = 1; i < kGroup / 32; ++i) mc = fmaxf(mc, red[i]);
+    group_sync(bar_id);
+    float st = 0.f;
+    if (mc != -INFINITY) {
+#pragma unroll
+        for (int e = 0; e < kPerThread; ++e)
+            if (v[e] != -INFINITY) st = __fadd_rn(st, expf(__fsub_rn(v[e], mc)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) st = __fadd_rn(st, __shfl_xor_sync(0xffffffffu, st, o));
+    if (lane == 0) red[w] = st;
+    group_sync(bar_id);
+    float sc = red[0];
+#pragma unroll
+    for (int i = 1; i < kGroup / 32; ++i) sc = __fadd_rn(sc, red[i]);
+    group_sync(bar_id);
+    return make_float2(mc, sc);
+}
+
+// Sequential merge of a row's chunk statistics (one thread).
+SDL_DEV float2 merge_stats(const float2* st, int nchunks) {
+    float m = -INFINITY;
+    for (int c = 0; c < nchunks; ++c) m = fmaxf(m, st[c].x);
+    float s = 0.f;
+    if (m != -INFINITY)
+        for (int c = 0; c < nchunks; ++c)
+            if (st[c].x != -INFINITY) s = __fmaf_rn(st[c].y, expf(__fsub_rn(st[c].x, m)), s);
+    return make_float2(m, s);
+}
+
+// ------------------------------------------------------------ probabilities
+// One CTA (4 groups of 256) per row: chunk statistics, merge, then p_i.
+template <typename T>
+__global__ void __launch_bounds__(1024) probs_canon_kernel(const T* __restrict__ logits, int64_t row_stride, int V,
+                                                           float temp, float* __restrict__ out, int64_t out_stride) {
+    __shared__ float red[4][8];
+    __shared__ float2 s_st[kMaxChunks];
+    __shared__ float2 s_row;
+    const T* x = logits + blockIdx.x * row_stride;
+    float* o = out + blockIdx.x * out_stride;
+    const int grp = threadIdx.x / kGroup, g = threadIdx.x % kGroup;
+    const int nchunks = (V + kChunk - 1) / kChunk;
+    for (int c = grp; c < nchunks; c += 4) {
+        const float2 st = chunk_stats<T>(x, c * kChunk, min(V, (c + 1) * kChunk), temp, g, 1 + grp, red[grp]);
+        if (g == 0) s_st[c] = st;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_row = merge_stats(s_st, nchunks);
+    __syncthreads();
+    const float m = s_row.x, s = s_row.y;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) o[i] = prob_of(scaled(to_f32<T>(x[i]), temp), m, s);
+}
+
+// Chunk statistics of every (row, chunk); rows [0, A.n) come from A and
+// [A.n, A.n + Bq.n) from Bq.  Grid (nchunks, A.n + Bq.n), 256 threads.
+template <typename T>
+__global__ void __launch_bounds__(kGroup) stats_kernel(Rows<T> A, Rows<T> Bq, int V, float temp, float2* stats) {
+    __shared__ float red[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int r = blockIdx.y, c = blockIdx.x;
+    const T* x = r < A.n ? A.row(r) : Bq.row(r - A.n);
+    const float2 st = chunk_stats<T>(x, c * kChunk, min(V, (c + 1) * kChunk), temp, threadIdx.x, 1, red);
+    if (threadIdx.x == 0) stats[(int64_t)r * gridDim.x + c] = st;
+}
+
+// Merge row r's statistics with the whole CTA: lanes evaluate the rescale
+// factors in parallel, thread 0 accumulates them in chunk order.
+SDL_DEV float2 cta_merge(const float2* st, int nchunks, float* s_fac, float2* s_out) {
+    float m = -INFINITY;
+    for (int c = 0; c < nchunks; ++c) m = fmaxf(m, st[c].x);  // every thread, exact
+    for (int c = threadIdx.x; c < nchunks; c += blockDim.x)
+        s_fac[c] = st[c].x != -INFINITY ? expf(__fsub_rn(st[c].x, m)) : 0.f;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        if (m != -INFINITY)
+            for (int c = 0; c < nchunks; ++c)
+                if (st[c].x != -INFINITY) s = __fmaf_rn(st[c].y, s_fac[c], s);
+        *s_out = make_float2(m, s);
+    }
+    __syncthreads();
+    const float2 r = *s_out;
+    __syncthreads();
+    return r;
+}
+
+// ----------------------------------------------------------------- draws
+// What one draw row samples from.
+//   kind 0: p of logits row pr (plain draw)
+//   kind 1: residual clamp(p - q, 0) of rows pr / qr, with p as fallback
+struct DrawRow {
+    int kind;
+    int pr, qr;  // statistics row indices
+};
+
+// Per-chunk exact integer weight sums.  Grid (nchunks, n_draw), 256 threads.
+// wsum[d][c] = sum of W over chunk c of draw d's distribution; for residual
+// rows wsum_p[d][c] holds the fallback distribution p's sums.
+template <typename T>
+__global__ void __launch_bounds__(kGroup) wsum_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
+                                                      const float2* __restrict__ stats, int nchunks, int mode, int gamma,
+                                                      const int* __restrict__ n_acc, uint64_t* wsum, uint64_t* wsum_p) {
+    __shared__ float s_fac[kMaxChunks];
+    __shared__ float2 s_tmp;
+    __shared__ uint64_t red[8], red_p[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int d = blockIdx.y, c = blockIdx.x;
+    // mode 0: draw d samples p of row d (A).  mode 1: spec round of sequence d.
+    int pr, qr = -1;
+    if (mode == 0) {
+        pr = d;
+    } else {
+        const int r = n_acc[d];
+        pr = d * (gamma + 1) + r;                         // target row r of sequence d
+        if (r < gamma) qr = A.n + d * gamma + r;          // draft row r (stats rows after A's)
+    }
+    const float2 sp = cta_merge(stats + (int64_t)pr * nchunks, nchunks, s_fac, &s_tmp);
+    float2 sq = make_float2(0.f, 1.f);
+    if (qr >= 0) sq = cta_merge(stats + (int64_t)qr * nchunks, nchunks, s_fac, &s_tmp);
+    const T* xp = A.row(pr);
+    const T* xq = qr >= 0 ? Bq.row(qr - A.n) : nullptr;
+    const int lo = c * kChunk, hi = min(V, lo + kChunk);
+    uint64_t w = 0, wp = 0;
+    for (int i = lo + threadIdx.x; i < hi; i += kGroup) {
+        const float p = prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y);
+        if (xq) {
+            const float q = prob_of(scaled(to_f32<T>(xq[i]), temp), sq.x, sq.y);
+            w += wfix(fmaxf(__fsub_rn(p, q), 0.f));
+            wp += wfix(p);
+        } else {
+            w += wfix(p);
+        }
+    }
+    w = warp_sum_u64(w);
+    wp = warp_sum_u64(wp);
+    if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = w; red_p[threadIdx.x >> 5] = wp; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t a = 0, b = 0;
+        for (int i = 0; i < kGroup / 32; ++i) { a += red[i]; b += red_p[i]; }
+        wsum[(int64_t)d * nchunks + c] = a;
+        if (xq) wsum_p[(int64_t)d * nchunks + c] = b;
+    }
+}
+
+// First index i in [lo, hi) whose prefix (from lo) of W exceeds `target`.
+// Whole CTA (1024 threads); warps own contiguous ranges.
+template <typename WF>
+SDL_DEV int block_find(WF wf, int lo, int hi, uint64_t target, uint64_t* s_w, int* s_tok) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int seg = (hi - lo + nw - 1) / nw;
+    seg = (seg + 31) & ~31;
+    const int a = lo + warp * seg, b = min(hi, a + seg);
+    uint64_t s = 0;
+    for (int i = a + lane; i < b; i += 32) s += wfix(wf(i));
+    s = warp_sum_u64(s);
+    if (lane == 0) s_w[warp] = s;
+    if (threadIdx.x == 0) *s_tok = -1;
+    __syncthreads();
+    uint64_t excl = 0;
+    for (int w = 0; w < warp; ++w) excl += s_w[w];
+    if (excl <= target && target < excl + s_w[warp]) {
+        uint64_t run = excl;
+        for (int base = a; base < b; base += 32) {
+            const int i = base + lane;
+            const uint64_t val = i < b ? wfix(wf(i)) : 0ull;
+            const uint64_t pre = warp_incl_scan_u64(val, lane);
+            const unsigned hit = __ballot_sync(0xffffffffu, run + pre > target);
+            if (hit) {
+                if (lane == 0) *s_tok = base + __ffs(hit) - 1;
+                break;
+            }
+            run += __shfl_sync(0xffffffffu, pre, 31);
+        }
+    }
+    __syncthreads();
+    const int t = *s_tok;
+    __syncthreads();
+    return t;
+}
+
+// Finish every draw: total of the chunk sums, the residual fallback test,
+// the target, the chunk holding it, then the index inside that chunk.
+// Grid n_draw, 1024 threads.
+template <typename T>
+__global__ void __launch_bounds__(1024) finish_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
+                                                      const float2* __restrict__ stats, int nchunks, int mode,
+                                                      int gamma, const int* __restrict__ n_acc,
+                                                      const int* __restrict__ u_bits, const float* __restrict__ uniforms,
+                                                      int64_t nu, const int64_t* u_base, int64_t u_off,
+                                                      const uint64_t* __restrict__ wsum,
+                                                      const uint64_t* __restrict__ wsum_p,
+                                                      const int* __restrict__ prop, int* out, int* n_out, int* err) {
+    __shared__ float s_fac[kMaxChunks];
+    __shared__ float2 s_tmp;
+    __shared__ uint64_t s_w[32];
+    __shared__ int s_tok, s_chunk, s_usep;
+    __shared__ uint64_t s_target;
+    pdl_wait();
+    const int d = blockIdx.x;
+    int pr, qr = -1, r = 0;
+    float u;
+    if (mode == 0) {
+        pr = d;
+        const int64_t ui = (u_base ? *u_base : 0) + u_off + d;
+        if (ui < 0 || ui >= nu) {
+            if (threadIdx.x == 0) { sdl_raise(err, SDL_DEVERR_UNIFORMS); out[d] = 0; }
+            return;
+        }
+        u = uniforms[ui];
+    } else {
+        r = n_acc[d];
+        pr = d * (gamma + 1) + r;
+        if (r < gamma) qr = A.n + d * gamma + r;
+        u = __int_as_float(u_bits[d]);
+    }
+    const uint64_t* ws = wsum + (int64_t)d * nchunks;
+    const uint64_t* wsp = wsum_p + (int64_t)d * nchunks;
+    if (threadIdx.x == 0) {
+        uint64_t S = 0;
+        for (int c = 0; c < nchunks; ++c) S += ws[c];
+        int usep = 0;
+        if (qr >= 0 && (double)S / kTwo62 <= 1e-12) {  // residual mass <= 1e-12: draw from p
+            usep = 1;
+            S = 0;
+            for (int c = 0; c < nchunks; ++c) S += wsp[c];
+        }
+        int chunk = -1;
+        uint64_t target = 0;
+        if (S != 0) {
+            target = __umul64hi(ufix(u), S);
+            uint64_t run = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                const uint64_t wc = usep ? wsp[c] : ws[c];
+                if (run + wc > target) { chunk = c; target -= run; break; }
+                run += wc;
+            }
+        }
+        s_chunk = chunk;
+        s_target = target;
+        s_usep = usep;
+    }
+    __syncthreads();
+    const int chunk = s_chunk;
+    int tok = -1;
+    if (chunk >= 0) {
+        const float2 sp = cta_merge(stats + (int64_t)pr * nchunks, nchunks, s_fac, &s_tmp);
+        const T* xp = A.row(pr);
+        const int lo = chunk * kChunk, hi = min(V, lo + kChunk);
+        if (qr >= 0 && !s_usep) {
+            const float2 sq = cta_merge(stats + (int64_t)qr * nchunks, nchunks, s_fac, &s_tmp);
+            const T* xq = Bq.row(qr - A.n);
+            tok = block_find(
+                [&](int i) {
+                    const float p = prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y);
+                    const float q = prob_of(scaled(to_f32<T>(xq[i]), temp), sq.x, sq.y);
+                    return fmaxf(__fsub_rn(p, q), 0.f);
+                },
+                lo, hi, s_target, s_w, &s_tok);
+        } else {
+            tok = block_find([&](int i) { return prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y); }, lo, hi,
+                             s_target, s_w, &s_tok);
+        }
+    }
+    if (threadIdx.x == 0) {
+        if (tok < 0) { sdl_raise(err, SDL_DEVERR_BAD_SAMPLE); tok = 0; }
+        if (mode == 0) {
+            out[d] = tok;
+        } else {
+            for (int j = 0; j < r; ++j) out[d * (gamma + 1) + j] = prop[d * gamma + j];
+            out[d * (gamma + 1) + r] = tok;
+            n_out[d] = r + 1;
+        }
+    }
+}
+
+// Accept walk of a speculative round from logits (one CTA): acceptance
+// probabilities min(1, p/q) in fp64 from the canonical p_x, q_x
+// (specdec/sampler.py:86-92), then the reference's uniform consumption
+// (engine/spec_scheduler.py:67-87): per sequence one uniform per accept
+// test, plus one for the residual or bonus draw.
+template <typename T>
+__global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
+                                                             const float2* __restrict__ stats, int nchunks,
+                                                             const int* __restrict__ prop, int B, int gamma,
+                                                             const float* __restrict__ uniforms, int64_t nu,
+                                                             int64_t* u_base, int64_t u_skip, int* n_acc,
+                                                             int* u_bits, int* err) {
+    extern __shared__ double s_dyn[];
+    double* a = s_dyn;                                                // [B*gamma]
+    float* uc = reinterpret_cast<float*>(s_dyn + (size_t)B * gamma);  // [B*(gamma+1)]
+    pdl_wait();
+    const int64_t base = (u_base ? *u_base : 0) + u_skip;
+    for (int idx = threadIdx.x; idx < B * gamma; idx += blockDim.x) {
+        const int b = idx / gamma, j = idx % gamma;
+        const int x = prop[idx];
+        if (x < 0 || x >= V) {  // a proposal outside the vocabulary is rejected
+            sdl_raise(err, SDL_DEVERR_BAD_INDEX);
+            a[idx] = 0.0;
+            continue;
+        }
+        const int pr = b * (gamma + 1) + j, qr = A.n + idx;
+        const float2 sp = merge_stats(stats + (int64_t)pr * nchunks, nchunks);
+        const float2 sq = merge_stats(stats + (int64_t)qr * nchunks, nchunks);
+        const double pv = prob_of(scaled(to_f32<T>(A.row(pr)[x]), temp), sp.x, sp.y);
+        const double qv = prob_of(scaled(to_f32<T>(Bq.row(idx)[x]), temp), sq.x, sq.y);
+        double acc;
+        if (qv <= 1e-12) acc = pv > 1e-12 ? 1.0 : 0.0;
+        else acc = fmin(1.0, pv / qv);
+        a[idx] = acc;
+    }
+    for (int i = threadIdx.x; i < B * (gamma + 1); i += blockDim.x) {
+        const int64_t ui = base + i;
+        uc[i] = (ui >= 0 && ui < nu) ? uniforms[ui] : __int_as_float(0x7fc00000);
+    }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    int off = 0;
+    bool bad_u = false;
+    for (int b = 0; b < B; ++b) {
+        bool reject = false;
+        if (lane < gamma) {
+            const float u = uc[off + lane];
+            if (u != u) bad_u = true;
+            reject = !((double)u < a[b * gamma + lane]);
+        }
+        const unsigned rj = __ballot_sync(0xffffffffu, reject);
+        const int r = rj ? __ffs(rj) - 1 : gamma;
+        const int consumed = r < gamma ? r + 2 : gamma + 1;
+        if (lane == 0) {
+            n_acc[b] = r;
+            const float uf = uc[off + consumed - 1];
+            if (uf != uf) bad_u = true;
+            u_bits[b] = __float_as_int(uf);
+        }
+        off += consumed;
+    }
+    bad_u = __any_sync(0xffffffffu, bad_u);
+    if (lane == 0) {
+        if (bad_u) sdl_raise(err, SDL_DEVERR_UNIFORMS);
+        if (u_base) *u_base = base + off;
+    }
+}
+
+// ------------------------------------------------------------ host side
+struct Ws {
+    float2* stats;
+    uint64_t* wsum;
+    uint64_t* wsum_p;
+    int* n_acc;
+    int* u_bits;
+    size_t bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Ws carve(void* base, int stat_rows, int draws, int nchunks) {
+    Ws w;
+    char* p = static_cast<char*>(base);
+    size_t o = 0;
+    w.stats = reinterpret_cast<float2*>(p + o);
+    o = align256(o + (size_t)stat_rows * nchunks * sizeof(float2));
+    w.wsum = reinterpret_cast<uint64_t*>(p + o);
+    o = align256(o + (size_t)draws * nchunks * sizeof(uint64_t));
+    w.wsum_p = reinterpret_cast<uint64_t*>(p + o);
+    o = align256(o + (size_t)draws * nchunks * sizeof(uint64_t));
+    w.n_acc = reinterpret_cast<int*>(p + o);
+    o = align256(o + (size_t)draws * sizeof(int));
+    w.u_bits = reinterpret_cast<int*>(p + o);
+    o = align256(o + (size_t)draws * sizeof(int));
+    w.bytes = o;
+    return w;
+}
+
+template <typename T>
+int sample_logits_t(const T* logits, int64_t row_stride, int rows, int V, float temp, const float* uniforms, int64_t nu,
+                    const int64_t* u_base, int64_t u_off, int* out, void* ws_base, int* err, cudaStream_t st) {
+    const int nchunks = (V + kChunk - 1) / kChunk;
+    Ws w = carve(ws_base, rows, rows, nchunks);
+    Rows<T> A{logits, row_stride, 0, 1, rows};
+    Rows<T> none{logits, 0, 0, 1, 0};
+    cudaError_t e = sdl::launch_pdl(stats_kernel<T>, dim3(nchunks, rows), dim3(kGroup), 0, st, A, none, V, temp,
+                                    w.stats);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(wsum_kernel<T>, dim3(nchunks, rows), dim3(kGroup), 0, st, A, none, V, temp,
+                            (const float2*)w.stats, nchunks, 0, 0, (const int*)nullptr, w.wsum, w.wsum_p);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(finish_kernel<T>, dim3(rows), dim3(1024), 0, st, A, none, V, temp, (const float2*)w.stats,
+                            nchunks, 0, 0, (const int*)nullptr, (const int*)nullptr, uniforms, nu, u_base, u_off,
+                            (const uint64_t*)w.wsum, (const uint64_t*)w.wsum_p, (const int*)nullptr, out,
+                            (int*)nullptr, err);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("sample_logits");
+}
+
+template <typename T>
+int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t q_sb, int64_t q_sj, float temp,
+                  const int* prop, int B, int gamma, int V, const float* uniforms, int64_t nu, int64_t* u_base,
+                  int64_t u_skip, int* tokens, int* n_out, void* ws_base, int* err, cudaStream_t st) {
+    const int nchunks = (V + kChunk - 1) / kChunk;
+    const int prow = B * (gamma + 1), qrow = B * gamma;
+    Ws w = carve(ws_base, prow + qrow, B, nchunks);
+    Rows<T> A{pl, p_sb, p_sj, gamma + 1, prow};
+    Rows<T> Q{ql, q_sb, q_sj, gamma, qrow};
+    const size_t smem = (size_t)B * gamma * sizeof(double) + (size_t)B * (gamma + 1) * sizeof(float);
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(accept_logits_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+        configured = smem;
+    }
+    cudaError_t e = sdl::launch_pdl(stats_kernel<T>, dim3(nchunks, prow + qrow), dim3(kGroup), 0, st, A, Q, V, temp,
+                                    w.stats);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(accept_logits_kernel<T>, dim3(1), dim3(1024), smem, st, A, Q, V, temp, (const float2*)w.stats,
+                            nchunks, prop, B, gamma, uniforms, nu, u_base, u_skip, w.n_acc, w.u_bits, err);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(wsum_kernel<T>, dim3(nchunks, B), dim3(kGroup), 0, st, A, Q, V, temp,
+                            (const float2*)w.stats, nchunks, 1, gamma, (const int*)w.n_acc, w.wsum, w.wsum_p);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(finish_kernel<T>, dim3(B), dim3(1024), 0, st, A, Q, V, temp, (const float2*)w.stats,
+                            nchunks, 1, gamma, (const int*)w.n_acc, (const int*)w.u_bits, uniforms, nu,
+                            (const int64_t*)nullptr, (int64_t)0, (const uint64_t*)w.wsum, (const uint64_t*)w.wsum_p,
+                            prop, tokens, n_out, err);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("spec_sample_logits");
+}
+
+}  // namespace
+
+// Canonical p = softmax(logits / T) rows (one CTA per row); used by
+// sdl_logits_to_probs for temperature sampling.
+int sdl_probs_canon(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab, float temp,
+                    float* probs, int64_t probs_stride, cudaStream_t st) {
+    if ((vocab + kChunk - 1) / kChunk > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "vocab above 4M");
+    if (dtype == SDL_F32)
+        probs_canon_kernel<float><<<rows, 1024, 0, st>>>((const float*)logits, row_stride, vocab, temp, probs,
+                                                         probs_stride);
+    else if (dtype == SDL_BF16)
+        probs_canon_kernel<__nv_bfloat16><<<rows, 1024, 0, st>>>((const __nv_bfloat16*)logits, row_stride, vocab, temp,
+                                                                 probs, probs_stride);
+    else if (dtype == SDL_F16)
+        probs_canon_kernel<__half><<<rows, 1024, 0, st>>>((const __half*)logits, row_stride, vocab, temp, probs,
+                                                          probs_stride);
+    else
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_logits_to_probs: dtype");
+    return sdl::check_launch("probs_canon_kernel");
+}
+
+extern "C" size_t sdl_sampler_workspace_bytes(int32_t rows, int32_t vocab) {
+    if (rows < 0 || vocab < 1) return 0;
+    const int nchunks = (vocab + kChunk - 1) / kChunk;
+    // statistics for `rows` logit rows and draw sums for as many draws
+    return carve(nullptr, rows, rows, nchunks).bytes;
+}
+
+extern "C" int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows,
+                                      int32_t vocab, float temperature, float eps, const float* uniforms,
+                                      int64_t num_uniforms, const int64_t* u_base, int64_t u_offset, int32_t* out,
+                                      void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+    if (!logits || !uniforms || !out || rows < 0 || vocab < 1 || row_stride < vocab)
+        return sdl::fail(SDL_ERR_INVALID, "sdl_sample_logits_rows: bad args");
+    if (rows == 0) return SDL_OK;
+    const int nchunks = (vocab + kChunk - 1) / kChunk;
+    if (nchunks > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: vocab above 4M");
+    if (!workspace || workspace_bytes < carve(nullptr, rows, rows, nchunks).bytes ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return sdl::fail(SDL_ERR_WORKSPACE, "sdl_sample_logits_rows: workspace missing, small or not 256-B aligned");
+    const float t = temperature > eps ? temperature : eps;
+    cudaStream_t st = sdl::as_stream(stream);
+    if (dtype == SDL_F32)
+        return sample_logits_t<float>((const float*)logits, row_stride, rows, vocab, t, uniforms, num_uniforms, u_base,
+                                      u_offset, out, workspace, err, st);
+    if (dtype == SDL_BF16)
+        return sample_logits_t<__nv_bfloat16>((const __nv_bfloat16*)logits, row_stride, rows, vocab, t, uniforms,
+                                              num_uniforms, u_base, u_offset, out, workspace, err, st);
+    if (dtype == SDL_F16)
+        return sample_logits_t<__half>((const __half*)logits, row_stride, rows, vocab, t, uniforms, num_uniforms,
+                                       u_base, u_offset, out, workspace, err, st);
+    return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: dtype");
+}
+
+extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj, const void* q_logits,
+                                      int64_t q_sb, int64_t q_sj, int32_t dtype, float temperature, float eps,
+                                      const int32_t* proposals, int32_t B, int32_t gamma, int32_t vocab,
+                                      const float* uniforms, int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
+                                      int32_t* tokens, int32_t* n_out, void* workspace, size_t workspace_bytes,
+                                      int32_t* err, void* stream) {
+    if (!p_logits || !q_logits || !proposals || !uniforms || !tokens || !n_out || B < 0 || gamma < 1 || gamma > 32 ||
+        vocab < 1)
+        return sdl::fail(SDL_ERR_INVALID, "sdl_spec_sample_logits: bad args (gamma must be 1..32)");
+    if (B == 0) return SDL_OK;
+    const int nchunks = (vocab + kChunk - 1) / kChunk;
+    if (nchunks > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: vocab above 4M");
+    const int stat_rows = B * (2 * gamma + 1);
+    if (!workspace || workspace_bytes < carve(nullptr, stat_rows, B, nchunks).bytes ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return sdl::fail(SDL_ERR_WORKSPACE, "sdl_spec_sample_logits: workspace missing, small or not 256-B aligned");
+    const size_t smem = (size_t)B * gamma * sizeof(double) + (size_t)B * (gamma + 1) * sizeof(float);
+    if (smem > 200 * 1024) return sdl::fail(SDL_ERR_INVALID, "sdl_spec_sample_logits: batch too large for one CTA");
+    const float t = temperature > eps ? temperature : eps;
+    cudaStream_t st = sdl::as_stream(stream);
+    if (dtype == SDL_F32)
+        return spec_logits_t<float>((const float*)p_logits, p_sb, p_sj, (const float*)q_logits, q_sb, q_sj, t,
+                                    proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens, n_out,
+                                    workspace, err, st);
+    if (dtype == SDL_BF16)
+        return spec_logits_t<__nv_bfloat16>((const __nv_bfloat16*)p_logits, p_sb, p_sj,
+                                            (const __nv_bfloat16*)q_logits, q_sb, q_sj, t, proposals, B, gamma, vocab,
+                                            uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace, err, st);
+    if (dtype == SDL_F16)
+        return spec_logits_t<__half>((const __half*)p_logits, p_sb, p_sj, (const __half*)q_logits, q_sb, q_sj, t,
+                                     proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens,
+                                     n_out, workspace, err, st);
+    return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: dtype");
+}

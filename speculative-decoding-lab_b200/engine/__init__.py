@@ -8,20 +8,53 @@ attention, fused rejection sampling, device-side round commit).
 
 from __future__ import annotations
 
-from .attention import (
-    full_attention,
-    gather_ctx,
-    paged_attention,
-    paged_attention_decode,
-    paged_attention_extend,
-    paged_attention_prefill_chunk,
-)
-from .config import EngineConfig, SamplingConfig, WorkloadConfig, WorkloadRequest, build_workload
-from .kv import BlockAllocator, BlockExhaustedError, PagedKVCache
-from .model import RMSNorm, ToyConfig, ToyPagedLM, ToyTokenizer, apply_rotary, make_rotary_cache, rotate_half
-from .qwen import QwenPagedModel, build_paged_model, build_random_model, shape_config
-from .scheduler import PagedScheduler, SchedulerResult, Sequence, build_kv
-from .spec_scheduler import SpeculativePagedScheduler, batch_accept
+import importlib
+
+# Public names resolve lazily (PEP 562), so ``from engine import _lib`` -- which
+# specdec.sampler does -- never re-enters modules that import specdec.sampler.
+_EXPORTS = {
+    "full_attention": ".attention",
+    "gather_ctx": ".attention",
+    "paged_attention": ".attention",
+    "paged_attention_decode": ".attention",
+    "paged_attention_extend": ".attention",
+    "paged_attention_prefill_chunk": ".attention",
+    "EngineConfig": ".config",
+    "SamplingConfig": ".config",
+    "WorkloadConfig": ".config",
+    "WorkloadRequest": ".config",
+    "build_workload": ".config",
+    "BlockAllocator": ".kv",
+    "BlockExhaustedError": ".kv",
+    "PagedKVCache": ".kv",
+    "RMSNorm": ".model",
+    "ToyConfig": ".model",
+    "ToyPagedLM": ".model",
+    "ToyTokenizer": ".model",
+    "apply_rotary": ".model",
+    "make_rotary_cache": ".model",
+    "rotate_half": ".model",
+    "QwenPagedModel": ".qwen",
+    "build_paged_model": ".qwen",
+    "build_random_model": ".qwen",
+    "shape_config": ".qwen",
+    "PagedScheduler": ".scheduler",
+    "SchedulerResult": ".scheduler",
+    "Sequence": ".scheduler",
+    "build_kv": ".scheduler",
+    "SpeculativePagedScheduler": ".spec_scheduler",
+    "batch_accept": ".spec_scheduler",
+}
+
+
+def __getattr__(name):
+    mod = _EXPORTS.get(name)
+    if mod is None:
+        raise AttributeError("module 'engine' has no attribute {!r}".format(name))
+    value = getattr(importlib.import_module(mod, __name__), name)
+    globals()[name] = value
+    return value
+
 
 __version__ = "0.1.0-b200"
 

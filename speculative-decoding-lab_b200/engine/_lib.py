@@ -63,6 +63,9 @@ EXPORTED_SYMBOLS = (
     "sdl_counter_add",
     "sdl_spec_sample",
     "sdl_spec_sample_scratch_bytes",
+    "sdl_sampler_workspace_bytes",
+    "sdl_sample_logits_rows",
+    "sdl_spec_sample_logits",
     "sdl_get_error",
 )
 
@@ -145,6 +148,12 @@ _SIGS = {
                                 c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void, c_void, c_void,
                                 c_void]),
     "sdl_spec_sample_scratch_bytes": (c_size, [c_int]),
+    "sdl_sampler_workspace_bytes": (c_size, [c_int, c_int]),
+    "sdl_sample_logits_rows": (c_int, [c_void, c_int, c_i64, c_int, c_int, c_float, c_float, c_void, c_i64, c_void,
+                                       c_i64, c_void, c_void, c_size, c_void, c_void]),
+    "sdl_spec_sample_logits": (c_int, [c_void, c_i64, c_i64, c_void, c_i64, c_i64, c_int, c_float, c_float, c_void,
+                                       c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void, c_void,
+                                       c_size, c_void, c_void]),
     "sdl_get_error": (c_int, [c_void, c_void, c_int, c_void]),
 }
 
@@ -212,16 +221,24 @@ def i32(values, device: torch.device) -> torch.Tensor:
 
 
 class Workspace:
-    """Per-device growable fp32 scratch used for split-K attention partials."""
+    """Per-device growable fp32 scratch (split-K attention partials under the
+    default tag, sampler statistics under ``"sampler"``).
+
+    A buffer that is outgrown is kept alive rather than freed: CUDA graphs
+    captured earlier still hold its address.
+    """
 
     _bufs = {}
+    _retired = []
 
     @classmethod
-    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    def get(cls, device: torch.device, nbytes: int, tag: str = "attention") -> torch.Tensor:
+        key = (device.type, device.index if device.index is not None else torch.cuda.current_device(), tag)
         buf = cls._bufs.get(key)
         need = max(4, (nbytes + 3) // 4)
         if buf is None or buf.numel() < need:
+            if buf is not None:
+                cls._retired.append(buf)
             buf = torch.empty(int(need * 1.25) + 1024, dtype=torch.float32, device=device)
             cls._bufs[key] = buf
         return buf

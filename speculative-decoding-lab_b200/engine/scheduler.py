@@ -28,7 +28,7 @@ from . import _lib
 from .config import EngineConfig, SamplingConfig, WorkloadRequest
 from .kv import PagedKVCache
 from .utils import Stopwatch, mean_std, setup_logger, sync_device
-from specdec.sampler import UniformStream, argmax_rows, probs_rows, sample_rows, sample_token
+from specdec.sampler import UniformStream, argmax_rows, probs_rows, sample_logits_rows, sample_rows, sample_token
 
 logger = setup_logger(__name__)
 
@@ -152,10 +152,10 @@ class PagedScheduler:
         """Device int32 next token per row (PagedScheduler._probs/_sample semantics)."""
         if self.sampling.is_greedy:
             return argmax_rows(logits)
-        probs = probs_rows(logits, self.sampling.temperature, False, eps=1e-9)
-        rows = probs.shape[0]
+        x = logits.reshape(-1, logits.shape[-1])
+        rows = x.shape[0]
         stream.reserve(rows)
-        toks = sample_rows(probs, stream, err=self.kv.err_word)
+        toks = sample_logits_rows(x, self.sampling.temperature, stream, err=self.kv.err_word, eps=1e-9)
         stream.advance(rows)
         return toks
 

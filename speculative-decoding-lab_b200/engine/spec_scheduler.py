@@ -9,9 +9,11 @@ One round (``_spec_step``) is, on the device:
 1. ``gamma`` batched draft decodes; each picks its proposals in-kernel
    (argmax, or temperature softmax + one uniform per sequence);
 2. one batched target ``decode_block`` over ``[pending] + proposals``;
-3. the fused rejection sampler (``sdl_spec_sample``): fp64 ``min(1, p/q)``
-   tests against the stream's uniforms in the reference's draw order, the
-   residual ``(p - q)+`` or bonus draw, accept lengths;
+3. the fused rejection sampler (``sdl_spec_sample_logits``, straight from
+   the target and draft logits): fp64 ``min(1, p/q)`` tests against the
+   stream's uniforms in the reference's draw order, the residual ``(p - q)+``
+   or bonus draw, accept lengths (with top-k / top-p filtering the
+   probability rows are materialised and ``sdl_spec_sample`` runs instead);
 4. ``sdl_spec_commit``: budget clip, EOS cut, rewind of the target cache to
    ``start + k`` and alignment of the draft cache (truncate, or reserve the
    single catch-up position), clears of finished sequences -- walked in batch
@@ -40,8 +42,10 @@ from specdec.sampler import (
     apply_top_p,
     argmax_rows,
     probs_rows,
+    sample_logits_rows,
     sample_rows,
     spec_sample,
+    spec_sample_logits,
 )
 
 logger = setup_logger(__name__)
@@ -180,12 +184,19 @@ class SpeculativePagedScheduler(PagedScheduler):
         return result
 
     # ------------------------------------------------------------ one round
+    def _plain_temperature(self, vocab: int) -> bool:
+        """True when sampling is softmax(logits / T) with no top-k / top-p."""
+        s = self.sampling
+        top_k = int(getattr(s, "top_k", 0) or 0)
+        top_p = float(getattr(s, "top_p", 1.0))
+        return (top_k <= 0 or top_k >= vocab) and (top_p >= 1.0 or top_p <= 0.0)
+
     def _probs_spec(self, logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """specdec logits_to_probs semantics (T floor 1e-12, optional top-k/top-p)."""
         s = self.sampling
         top_k = int(getattr(s, "top_k", 0) or 0)
         top_p = float(getattr(s, "top_p", 1.0))
-        if (top_k <= 0 or top_k >= logits.shape[-1]) and (top_p >= 1.0 or top_p <= 0.0):
+        if self._plain_temperature(logits.shape[-1]):
             return probs_rows(logits, s.temperature, False, eps=1e-12, out=out)
         scaled = logits.float() / max(s.temperature, 1e-12)
         filtered = apply_top_p(apply_top_k(scaled, top_k), top_p)
@@ -208,6 +219,7 @@ class SpeculativePagedScheduler(PagedScheduler):
         if not greedy:
             stream.reserve(gamma * B)
         cur = torch.tensor([s.generated[-1] for s in running], dtype=torch.long, device=device)
+        fused = False
         for t in range(gamma):
             q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0])
             result.draft_forward_calls += 1
@@ -215,12 +227,22 @@ class SpeculativePagedScheduler(PagedScheduler):
                 prop_t = argmax_rows(q_logits)
             else:
                 V = q_logits.shape[-1]
-                if self._q_buf is None or self._q_buf.shape[0] < B or self._q_buf.shape[2] != V:
+                fused = self._plain_temperature(V)
+                # plain temperature keeps the draft logits (the fused sampler reads
+                # them); filtering keeps the filtered probability rows instead
+                dt = q_logits.dtype if fused else torch.float32
+                if (self._q_buf is None or self._q_buf.shape[0] < B or self._q_buf.shape[2] != V
+                        or self._q_buf.dtype != dt):
                     rows_cap = max(B, self._q_buf.shape[0] if self._q_buf is not None else 0)
-                    self._q_buf = torch.empty((rows_cap, gamma, V), dtype=torch.float32, device=device)
+                    self._q_buf = torch.empty((rows_cap, gamma, V), dtype=dt, device=device)
                 q_probs = self._q_buf[:B]
-                self._probs_spec(q_logits, out=q_probs[:, t, :])
-                prop_t = sample_rows(q_probs[:, t, :], stream, offset=t * B, err=self.draft_kv.err_word)
+                if fused:
+                    q_probs[:, t, :].copy_(q_logits.reshape(B, V))
+                    prop_t = sample_logits_rows(q_probs[:, t, :], self.sampling.temperature, stream, offset=t * B,
+                                                err=self.draft_kv.err_word, eps=1e-12)
+                else:
+                    self._probs_spec(q_logits, out=q_probs[:, t, :])
+                    prop_t = sample_rows(q_probs[:, t, :], stream, offset=t * B, err=self.draft_kv.err_word)
             proposals[:, t] = prop_t
             cur = prop_t.long()
 
@@ -233,6 +255,13 @@ class SpeculativePagedScheduler(PagedScheduler):
         if greedy:
             p_arg = argmax_rows(p_logits.reshape(B * chunk, -1)).reshape(B, chunk)
             tokens, n_out = spec_sample(None, None, proposals, None, greedy=True, p_arg=p_arg)
+        elif fused:
+            pl = p_logits.reshape(B, chunk, -1)
+            ql = q_probs
+            if pl.dtype != ql.dtype:  # upcasts are exact, so the probabilities do not change
+                pl, ql = pl.float(), ql.float()
+            tokens, n_out = spec_sample_logits(pl, ql, self.sampling.temperature, proposals, stream,
+                                               u_skip=gamma * B, err=self.kv.err_word, eps=1e-12)
         else:
             p_probs = self._probs_spec(p_logits).reshape(B, chunk, -1)
             tokens, n_out = spec_sample(p_probs, q_probs, proposals, stream, greedy=False, u_skip=gamma * B,

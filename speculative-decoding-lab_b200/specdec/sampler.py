@@ -219,6 +219,89 @@ def spec_sample(
     return tokens, n_out
 
 
+def _sampler_ws(device: torch.device, rows: int, vocab: int) -> torch.Tensor:
+    need = int(_lib.load().sdl_sampler_workspace_bytes(int(rows), int(vocab)))
+    return _lib.Workspace.get(device, need, tag="sampler")
+
+
+def sample_logits_rows(logits: torch.Tensor, temperature: float, stream: UniformStream, offset: int = 0,
+                       out: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None,
+                       eps: float = _EPS) -> torch.Tensor:
+    """One draw per row of ``softmax(logits / T)`` without writing the
+    probabilities; bit-equal to ``sample_rows(probs_rows(logits, T))``.
+
+    Row ``r`` reads uniform ``counter + offset + r``; the counter is not
+    advanced.
+    """
+    _lib.require_cuda(logits, "logits")
+    x = _rows2d(logits)
+    rows, V = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    ws = _sampler_ws(x.device, rows, V)
+    _lib.check(
+        _lib.load().sdl_sample_logits_rows(
+            x.data_ptr(), _lib.dtype_code(x.dtype), x.stride(0), rows, V, float(temperature), float(eps),
+            stream.buffer.data_ptr(), stream.buffer.numel(), stream.counter.data_ptr(), int(offset), out.data_ptr(),
+            ws.data_ptr(), ws.numel() * 4, err.data_ptr() if err is not None else None,
+            _lib.stream_handle(x.device),
+        ),
+        "sdl_sample_logits_rows",
+    )
+    return out
+
+
+def spec_sample_logits(
+    p_logits: torch.Tensor,
+    q_logits: torch.Tensor,
+    temperature: float,
+    proposals: torch.Tensor,
+    stream: UniformStream,
+    u_skip: int = 0,
+    err: Optional[torch.Tensor] = None,
+    out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+    eps: float = _EPS,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Fused rejection sampling straight from logits (sdl_spec_sample_logits).
+
+    ``p_logits`` (B, gamma+1, V) target logits, ``q_logits`` (B, gamma, V)
+    draft logits of the same dtype, ``proposals`` (B, gamma).  Returns
+    ``tokens`` (B, gamma+1) and ``n_out`` (B,), bit-equal to
+    ``spec_sample(probs_rows(p), probs_rows(q), ...)``.
+    """
+    _lib.require_cuda(p_logits, "p_logits")
+    device = p_logits.device
+    B, gamma = proposals.shape
+    if p_logits.dtype != q_logits.dtype:
+        raise TypeError("p_logits and q_logits must share a dtype")
+    pl, ql = p_logits, q_logits
+    if pl.stride(-1) != 1:
+        pl = pl.contiguous()
+    if ql.stride(-1) != 1:
+        ql = ql.contiguous()
+    V = pl.shape[-1]
+    prop = proposals if (proposals.dtype == torch.int32 and proposals.is_contiguous()) else \
+        proposals.to(torch.int32).contiguous()
+    if out is None:
+        tokens = torch.empty((B, gamma + 1), dtype=torch.int32, device=device)
+        n_out = torch.empty(B, dtype=torch.int32, device=device)
+    else:
+        tokens, n_out = out
+    ws = _sampler_ws(device, B * (2 * gamma + 1), V)
+    stream.reserve(u_skip + B * (gamma + 1))
+    _lib.check(
+        _lib.load().sdl_spec_sample_logits(
+            pl.data_ptr(), pl.stride(0), pl.stride(1), ql.data_ptr(), ql.stride(0), ql.stride(1),
+            _lib.dtype_code(pl.dtype), float(temperature), float(eps), prop.data_ptr(), B, gamma, V,
+            stream.buffer.data_ptr(), stream.buffer.numel(), stream.counter.data_ptr(), int(u_skip),
+            tokens.data_ptr(), n_out.data_ptr(), ws.data_ptr(), ws.numel() * 4,
+            err.data_ptr() if err is not None else None, _lib.stream_handle(device),
+        ),
+        "sdl_spec_sample_logits",
+    )
+    return tokens, n_out
+
+
 # ------------------------------------------------------- reference-shaped API
 def logits_to_probs(logits: torch.Tensor, sampling: SamplingConfig) -> torch.Tensor:
     """Convert raw logits of shape (..., vocab) into a probability distribution."""

@@ -135,6 +135,8 @@ CASES = [
     (14, 2, 64, 5, [0, 31, 1000], 16, torch.float16),                           # fp16, extend
     (4, 2, 64, 1, [0, 40, 333], 16, torch.bfloat16),                            # C1 shape (ratio 2)
     (8, 8, 128, 3, [10, 700], 16, torch.bfloat16),                              # MHA, Hkv 8
+    (16, 2, 128, 8, [33, 1500], 16, torch.bfloat16),                            # 64 columns: 8 warps x 8
+    (12, 2, 128, 11, [7, 640, 2000], 16, torch.bfloat16),                       # 66 columns: 16-column tiles
 ]
 
 
