@@ -279,7 +279,7 @@ size_t sdl_spec_sample_scratch_bytes(int32_t B);
 
 /* ------------------------------------------------------ logits-in sampling
  * The temperature softmax p = softmax(logits / max(T, eps)) is defined with
- * a fixed reduction order (chunks of 4096 elements, see
+ * a fixed reduction order (chunks of 8192 elements, see
  * csrc/sampler_logits.cu), so every entry point below derives bit-identical
  * p_i from the same logits; sdl_logits_to_probs (temperature mode) writes
  * exactly those values.  Draws use the integer rule of sdl_sample_rows.

@@ -19,12 +19,10 @@ namespace {
 constexpr double kTwo62 = 4611686018427387904.0;
 constexpr double kTwo64 = 18446744073709551616.0;
 
-SDL_DEV uint64_t wfix(float w) {
-    if (!(w > 0.f)) return 0ull;
-    double x = (double)w * kTwo62;
-    if (x >= kTwo64) return 0xffffffffffffffffull;
-    return __double2ull_rz(x);
-}
+// floor(w * 2^62): the fp32 product with a power of two is exact (no
+// rounding below 2^66), and the truncating conversion to u64 saturates
+// (w >= 4 gives 2^64 - 1) and maps NaN and w <= 0 to 0.
+SDL_DEV uint64_t wfix(float w) { return __float2ull_rz(__fmul_rn(w, 4611686018427387904.0f)); }
 
 SDL_DEV uint64_t ufix(float u) {
     if (!(u > 0.f)) return 0ull;

@@ -5,19 +5,23 @@
 // Canonical softmax.  p = softmax(logits / T) in fp32 (specdec/sampler.py:
 // 19-36) needs a row maximum m and a row sum s.  The maximum is exact; the
 // sum's rounding depends on the summation order, so this file fixes it:
-//   * the row is cut into chunks of kChunk = 4096 elements;
+//   * x/T is the correctly rounded quotient (skipped when T == 1: x/1 == x);
+//   * the row is cut into chunks of kChunk = 8192 elements;
 //   * in a chunk, thread t of a 256-thread group owns elements
-//     lo + 4t + j + 1024k (k = 0..3 outer, j = 0..3 inner) and adds
-//     expf(x/T - m_c) over them in that order (m_c = the chunk maximum);
-//     lanes combine by an xor butterfly (16, 8, 4, 2, 1) and lane 0's value
-//     is kept; warps 0..7 are added in order;
-//   * chunks merge in order: m = max m_c, s = fma(s_c, expf(m_c - m), s).
+//     lo + 4t + j + 1024k (k = 0..7 outer, j = 0..3 inner) and adds
+//     expf(x/T - m_c) over them in that order (m_c = the chunk maximum;
+//     masked -inf logits add expf(-inf) = +0); lanes combine by an xor
+//     butterfly (16, 8, 4, 2, 1) and lane 0's value is kept; warps 0..7 are
+//     added in order;
+//   * chunks merge in order: m = max m_c, s = fma(s_c, expf(m_c - m), s);
+//   * p_i = expf(x_i/T - m) * r with r = 1/s correctly rounded (one product
+//     per element instead of a divide; within one ulp of the quotient).
 // Every kernel here (one CTA per row or one CTA per chunk) evaluates exactly
-// these operations with explicit round-to-nearest intrinsics, so p_i =
-// expf(x_i/T - m) / s is the same bit pattern whichever kernel computes it:
-// sdl_logits_to_probs, sdl_sample_logits_rows and sdl_spec_sample_logits
-// agree bit for bit, and the draws below equal sdl_sample_rows /
-// sdl_spec_sample applied to sdl_logits_to_probs' output.
+// these operations with explicit round-to-nearest intrinsics, so p_i is the
+// same bit pattern whichever kernel computes it: sdl_logits_to_probs,
+// sdl_sample_logits_rows and sdl_spec_sample_logits agree bit for bit, and
+// the draws below equal sdl_sample_rows / sdl_spec_sample applied to
+// sdl_logits_to_probs' output.
 //
 // Draws use the integer inverse-CDF rule of sampler.cu (W_i = floor(w_i *
 // 2^62), exact u64 sums), so splitting a row across CTAs cannot change them.
@@ -25,20 +29,23 @@
 
 namespace {
 
-constexpr int kChunk = 4096;   // elements per statistics chunk
+constexpr int kChunk = 8192;   // elements per statistics chunk
 constexpr int kGroup = 256;    // threads that reduce one chunk
 constexpr int kPerThread = kChunk / kGroup;
-constexpr int kMaxChunks = 1024;  // vocab <= 4M
+constexpr int kMaxChunks = 1024;  // vocab <= 8M
+// Draws sum integer weights, which is exact in any order, so they use their
+// own finer slices: 2048 elements, 8 per thread of a 256-thread CTA.
+constexpr int kDrawChunk = 2048;
+constexpr int kDrawPerThread = kDrawChunk / kGroup;
+constexpr int kMaxDrawChunks = 1024;  // vocab <= 2M for draws
 
 constexpr double kTwo62 = 4611686018427387904.0;
 constexpr double kTwo64 = 18446744073709551616.0;
 
-SDL_DEV uint64_t wfix(float w) {
-    if (!(w > 0.f)) return 0ull;
-    double x = (double)w * kTwo62;
-    if (x >= kTwo64) return 0xffffffffffffffffull;
-    return __double2ull_rz(x);
-}
+// floor(w * 2^62): the fp32 product with a power of two is exact (no
+// rounding below 2^66), and the truncating conversion to u64 saturates
+// (w >= 4 gives 2^64 - 1) and maps NaN and w <= 0 to 0.
+SDL_DEV uint64_t wfix(float w) { return __float2ull_rz(__fmul_rn(w, 4611686018427387904.0f)); }
 
 SDL_DEV uint64_t ufix(float u) {
     if (!(u > 0.f)) return 0ull;
@@ -73,10 +80,49 @@ struct Rows {
     SDL_DEV const T* row(int r) const { return p + (int64_t)(r / J) * sb + (int64_t)(r % J) * sj; }
 };
 
-SDL_DEV float scaled(float x, float temp) { return __fdiv_rn(x, temp); }
+// x / T, correctly rounded; x / 1 == x exactly, so T == 1 skips the divide.
+SDL_DEV float scaled(float x, float temp) { return temp == 1.f ? x : __fdiv_rn(x, temp); }
 
-// p_i from the scaled logit and the merged row statistics.
-SDL_DEV float prob_of(float xs, float m, float s) { return __fdiv_rn(expf(__fsub_rn(xs, m)), s); }
+// Four consecutive logits [i, i+4) as fp32 (-inf past hi); one vector load
+// when the row is aligned for it.
+template <typename T>
+SDL_DEV void load4(const T* __restrict__ x, int i, int hi, bool vec, float* o);
+template <>
+SDL_DEV void load4<float>(const float* __restrict__ x, int i, int hi, bool vec, float* o) {
+    if (vec && i + 3 < hi) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x + i));
+        o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = i + j < hi ? x[i + j] : -INFINITY;
+}
+template <typename H>
+SDL_DEV void load4_16(const H* __restrict__ x, int i, int hi, bool vec, float* o) {
+    if (vec && i + 3 < hi) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(x + i));
+        const H* h = reinterpret_cast<const H*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = to_f32<H>(h[j]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = i + j < hi ? to_f32<H>(x[i + j]) : -INFINITY;
+}
+template <>
+SDL_DEV void load4<__nv_bfloat16>(const __nv_bfloat16* __restrict__ x, int i, int hi, bool vec, float* o) {
+    load4_16<__nv_bfloat16>(x, i, hi, vec, o);
+}
+template <>
+SDL_DEV void load4<__half>(const __half* __restrict__ x, int i, int hi, bool vec, float* o) {
+    load4_16<__half>(x, i, hi, vec, o);
+}
+
+template <typename T>
+SDL_DEV bool row_vec_ok(const T* x) { return reinterpret_cast<uintptr_t>(x) % (4 * sizeof(T)) == 0; }
+
+// p_i from the scaled logit and the row statistics (m, r = 1/s).
+SDL_DEV float prob_of(float xs, float m, float r) { return __fmul_rn(expf(__fsub_rn(xs, m)), r); }
 
 // Statistics (m_c, s_c) of elements [lo, hi) of row x, reduced by one
 // 256-thread group (g = thread index in the group, bar_id its named barrier,
@@ -85,15 +131,15 @@ template <typename T>
 SDL_DEV float2 chunk_stats(const T* __restrict__ x, int lo, int hi, float temp, int g, int bar_id, float* red) {
     float v[kPerThread];
     float mt = -INFINITY;
+    const bool vec = row_vec_ok<T>(x);
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
+    for (int k = 0; k < kPerThread / 4; ++k) load4<T>(x, lo + 4 * g + 1024 * k, hi, vec, v + 4 * k);
+    if (temp != 1.f) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = lo + 4 * g + j + 1024 * k;
-            const float xv = i < hi ? scaled(to_f32<T>(x[i]), temp) : -INFINITY;
-            v[k * 4 + j] = xv;
-            mt = fmaxf(mt, xv);
-        }
+        for (int e = 0; e < kPerThread; ++e) v[e] = __fdiv_rn(v[e], temp);
+    }
+#pragma unroll
+    for (int e = 0; e < kPerThread; ++e) mt = fmaxf(mt, v[e]);
     const int lane = g & 31, w = g >> 5;
     mt = warp_max(mt);
     if (lane == 0) red[w] = mt;
@@ -105,8 +151,7 @@ SDL_DEV float2 chunk_stats(const T* __restrict__ x, int lo, int hi, float temp, 
     float st = 0.f;
     if (mc != -INFINITY) {
 #pragma unroll
-        for (int e = 0; e < kPerThread; ++e)
-            if (v[e] != -INFINITY) st = __fadd_rn(st, expf(__fsub_rn(v[e], mc)));
+        for (int e = 0; e < kPerThread; ++e) st = __fadd_rn(st, expf(__fsub_rn(v[e], mc)));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) st = __fadd_rn(st, __shfl_xor_sync(0xffffffffu, st, o));
@@ -147,10 +192,13 @@ __global__ void __launch_bounds__(1024) probs_canon_kernel(const T* __restrict__
         if (g == 0) s_st[c] = st;
     }
     __syncthreads();
-    if (threadIdx.x == 0) s_row = merge_stats(s_st, nchunks);
+    if (threadIdx.x == 0) {
+        const float2 ms = merge_stats(s_st, nchunks);
+        s_row = make_float2(ms.x, __frcp_rn(ms.y));
+    }
     __syncthreads();
-    const float m = s_row.x, s = s_row.y;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) o[i] = prob_of(scaled(to_f32<T>(x[i]), temp), m, s);
+    const float m = s_row.x, r = s_row.y;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) o[i] = prob_of(scaled(to_f32<T>(x[i]), temp), m, r);
 }
 
 // Chunk statistics of every (row, chunk); rows [0, A.n) come from A and
@@ -166,25 +214,56 @@ __global__ void __launch_bounds__(kGroup) stats_kernel(Rows<T> A, Rows<T> Bq, in
     if (threadIdx.x == 0) stats[(int64_t)r * gridDim.x + c] = st;
 }
 
-// Merge row r's statistics with the whole CTA: lanes evaluate the rescale
-// factors in parallel, thread 0 accumulates them in chunk order.
-SDL_DEV float2 cta_merge(const float2* st, int nchunks, float* s_fac, float2* s_out) {
+// Row statistics (m, 1/s) from the chunk statistics of every row: the chunk
+// entries are loaded in parallel, the maximum is reduced in any order (it is
+// exact), the rescale factors are evaluated in parallel and thread 0 adds
+// them in chunk order -- the operations of merge_stats.  Grid rows, 128
+// threads.
+__global__ void __launch_bounds__(128) merge_kernel(const float2* __restrict__ stats, int nchunks,
+                                                    float2* __restrict__ rowstat) {
+    __shared__ float2 s_st[kMaxChunks];
+    __shared__ float s_fac[kMaxChunks];
+    __shared__ float s_red[4];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int r = blockIdx.x;
+    const float2* st = stats + (int64_t)r * nchunks;
     float m = -INFINITY;
-    for (int c = 0; c < nchunks; ++c) m = fmaxf(m, st[c].x);  // every thread, exact
+    for (int c = threadIdx.x; c < nchunks; c += blockDim.x) {
+        const float2 v = st[c];
+        s_st[c] = v;
+        m = fmaxf(m, v.x);
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
     for (int c = threadIdx.x; c < nchunks; c += blockDim.x)
-        s_fac[c] = st[c].x != -INFINITY ? expf(__fsub_rn(st[c].x, m)) : 0.f;
+        s_fac[c] = s_st[c].x != -INFINITY ? expf(__fsub_rn(s_st[c].x, m)) : 0.f;
     __syncthreads();
     if (threadIdx.x == 0) {
         float s = 0.f;
         if (m != -INFINITY)
             for (int c = 0; c < nchunks; ++c)
-                if (st[c].x != -INFINITY) s = __fmaf_rn(st[c].y, s_fac[c], s);
-        *s_out = make_float2(m, s);
+                if (s_st[c].x != -INFINITY) s = __fmaf_rn(s_st[c].y, s_fac[c], s);
+        rowstat[r] = make_float2(m, __frcp_rn(s));
+    }
+}
+
+// Inclusive block scan of one u64 per thread (blockDim a multiple of 32).
+SDL_DEV uint64_t block_incl_scan_u64(uint64_t v, uint64_t* s_w /*[32]*/, uint64_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint64_t x = warp_incl_scan_u64(v, lane);
+    if (lane == 31) s_w[warp] = x;
+    __syncthreads();
+    uint64_t off = 0, tot = 0;
+    for (int w = 0; w < nw; ++w) {
+        if (w < warp) off += s_w[w];
+        tot += s_w[w];
     }
     __syncthreads();
-    const float2 r = *s_out;
-    __syncthreads();
-    return r;
+    *total = tot;
+    return off + x;
 }
 
 // ----------------------------------------------------------------- draws
@@ -196,16 +275,14 @@ struct DrawRow {
     int pr, qr;  // statistics row indices
 };
 
-// Per-chunk exact integer weight sums.  Grid (nchunks, n_draw), 256 threads.
-// wsum[d][c] = sum of W over chunk c of draw d's distribution; for residual
-// rows wsum_p[d][c] holds the fallback distribution p's sums.
+// Per-slice exact integer weight sums of each draw's distribution (p, or the
+// residual clamp(p - q, 0) for a rejected proposal).  Grid (nchunks = draw
+// slices, n_draw), 256 threads: wsum[d][c] = sum of W over slice c.
 template <typename T>
 __global__ void __launch_bounds__(kGroup) wsum_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
-                                                      const float2* __restrict__ stats, int nchunks, int mode, int gamma,
-                                                      const int* __restrict__ n_acc, uint64_t* wsum, uint64_t* wsum_p) {
-    __shared__ float s_fac[kMaxChunks];
-    __shared__ float2 s_tmp;
-    __shared__ uint64_t red[8], red_p[8];
+                                                      const float2* __restrict__ rowstat, int nchunks, int mode,
+                                                      int gamma, const int* __restrict__ n_acc, uint64_t* wsum) {
+    __shared__ uint64_t red[8];
     pdl_wait();
     pdl_launch_dependents();
     const int d = blockIdx.y, c = blockIdx.x;
@@ -218,32 +295,41 @@ __global__ void __launch_bounds__(kGroup) wsum_kernel(Rows<T> A, Rows<T> Bq, int
         pr = d * (gamma + 1) + r;                         // target row r of sequence d
         if (r < gamma) qr = A.n + d * gamma + r;          // draft row r (stats rows after A's)
     }
-    const float2 sp = cta_merge(stats + (int64_t)pr * nchunks, nchunks, s_fac, &s_tmp);
-    float2 sq = make_float2(0.f, 1.f);
-    if (qr >= 0) sq = cta_merge(stats + (int64_t)qr * nchunks, nchunks, s_fac, &s_tmp);
+    const float2 sp = rowstat[pr];
+    const float2 sq = qr >= 0 ? rowstat[qr] : make_float2(0.f, 1.f);
     const T* xp = A.row(pr);
     const T* xq = qr >= 0 ? Bq.row(qr - A.n) : nullptr;
-    const int lo = c * kChunk, hi = min(V, lo + kChunk);
-    uint64_t w = 0, wp = 0;
-    for (int i = lo + threadIdx.x; i < hi; i += kGroup) {
-        const float p = prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y);
-        if (xq) {
-            const float q = prob_of(scaled(to_f32<T>(xq[i]), temp), sq.x, sq.y);
+    const int lo = c * kDrawChunk, hi = min(V, lo + kDrawChunk);
+    // every load of the thread's slice in flight before any arithmetic
+    float vp[kDrawPerThread], vq[kDrawPerThread];
+    const bool vecp = row_vec_ok<T>(xp);
+#pragma unroll
+    for (int k = 0; k < kDrawPerThread / 4; ++k) load4<T>(xp, lo + 4 * threadIdx.x + 1024 * k, hi, vecp, vp + 4 * k);
+    if (xq) {
+        const bool vecq = row_vec_ok<T>(xq);
+#pragma unroll
+        for (int k = 0; k < kDrawPerThread / 4; ++k)
+            load4<T>(xq, lo + 4 * threadIdx.x + 1024 * k, hi, vecq, vq + 4 * k);
+    }
+    uint64_t w = 0;
+    if (xq) {
+#pragma unroll
+        for (int e = 0; e < kDrawPerThread; ++e) {
+            const float p = prob_of(scaled(vp[e], temp), sp.x, sp.y);
+            const float q = prob_of(scaled(vq[e], temp), sq.x, sq.y);
             w += wfix(fmaxf(__fsub_rn(p, q), 0.f));
-            wp += wfix(p);
-        } else {
-            w += wfix(p);
         }
+    } else {
+#pragma unroll
+        for (int e = 0; e < kDrawPerThread; ++e) w += wfix(prob_of(scaled(vp[e], temp), sp.x, sp.y));
     }
     w = warp_sum_u64(w);
-    wp = warp_sum_u64(wp);
-    if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = w; red_p[threadIdx.x >> 5] = wp; }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = w;
     __syncthreads();
     if (threadIdx.x == 0) {
-        uint64_t a = 0, b = 0;
-        for (int i = 0; i < kGroup / 32; ++i) { a += red[i]; b += red_p[i]; }
+        uint64_t a = 0;
+        for (int i = 0; i < kGroup / 32; ++i) a += red[i];
         wsum[(int64_t)d * nchunks + c] = a;
-        if (xq) wsum_p[(int64_t)d * nchunks + c] = b;
     }
 }
 
@@ -288,17 +374,14 @@ SDL_DEV int block_find(WF wf, int lo, int hi, uint64_t target, uint64_t* s_w, in
 // Grid n_draw, 1024 threads.
 template <typename T>
 __global__ void __launch_bounds__(1024) finish_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
-                                                      const float2* __restrict__ stats, int nchunks, int mode,
+                                                      const float2* __restrict__ rowstat, int nchunks, int mode,
                                                       int gamma, const int* __restrict__ n_acc,
                                                       const int* __restrict__ u_bits, const float* __restrict__ uniforms,
                                                       int64_t nu, const int64_t* u_base, int64_t u_off,
-                                                      const uint64_t* __restrict__ wsum,
-                                                      const uint64_t* __restrict__ wsum_p,
+                                                      const uint64_t* __restrict__ wsum, uint64_t* wsum_p,
                                                       const int* __restrict__ prop, int* out, int* n_out, int* err) {
-    __shared__ float s_fac[kMaxChunks];
-    __shared__ float2 s_tmp;
     __shared__ uint64_t s_w[32];
-    __shared__ int s_tok, s_chunk, s_usep;
+    __shared__ int s_tok, s_chunk;
     __shared__ uint64_t s_target;
     pdl_wait();
     const int d = blockIdx.x;
@@ -319,40 +402,47 @@ __global__ void __launch_bounds__(1024) finish_kernel(Rows<T> A, Rows<T> Bq, int
         u = __int_as_float(u_bits[d]);
     }
     const uint64_t* ws = wsum + (int64_t)d * nchunks;
-    const uint64_t* wsp = wsum_p + (int64_t)d * nchunks;
-    if (threadIdx.x == 0) {
-        uint64_t S = 0;
-        for (int c = 0; c < nchunks; ++c) S += ws[c];
-        int usep = 0;
-        if (qr >= 0 && (double)S / kTwo62 <= 1e-12) {  // residual mass <= 1e-12: draw from p
-            usep = 1;
-            S = 0;
-            for (int c = 0; c < nchunks; ++c) S += wsp[c];
+    // slice sums (one slice per thread; nchunks <= blockDim) and their total
+    const int c = threadIdx.x;
+    uint64_t wc = c < nchunks ? ws[c] : 0ull;
+    uint64_t S;
+    uint64_t incl = block_incl_scan_u64(wc, s_w, &S);
+    bool usep = false;
+    if (qr >= 0 && (double)S / kTwo62 <= 1e-12) {
+        // residual mass <= 1e-12 (rare): draw from p; its slice sums are made
+        // here, one warp per slice
+        usep = true;
+        const float2 sp = rowstat[pr];
+        const T* xp = A.row(pr);
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        for (int sl = warp; sl < nchunks; sl += blockDim.x >> 5) {
+            const int lo = sl * kDrawChunk, hi = min(V, lo + kDrawChunk);
+            uint64_t a = 0;
+            for (int i = lo + lane; i < hi; i += 32) a += wfix(prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y));
+            a = warp_sum_u64(a);
+            if (lane == 0) wsum_p[(int64_t)d * nchunks + sl] = a;
         }
-        int chunk = -1;
-        uint64_t target = 0;
-        if (S != 0) {
-            target = __umul64hi(ufix(u), S);
-            uint64_t run = 0;
-            for (int c = 0; c < nchunks; ++c) {
-                const uint64_t wc = usep ? wsp[c] : ws[c];
-                if (run + wc > target) { chunk = c; target -= run; break; }
-                run += wc;
-            }
-        }
-        s_chunk = chunk;
-        s_target = target;
-        s_usep = usep;
+        __threadfence_block();
+        __syncthreads();
+        wc = c < nchunks ? wsum_p[(int64_t)d * nchunks + c] : 0ull;
+        incl = block_incl_scan_u64(wc, s_w, &S);
+    }
+    if (threadIdx.x == 0) s_chunk = -1;
+    __syncthreads();
+    const uint64_t target = S != 0 ? __umul64hi(ufix(u), S) : 0ull;
+    if (S != 0 && wc != 0 && incl - wc <= target && target < incl) {  // the chunk holding the target
+        s_chunk = c;
+        s_target = target - (incl - wc);
     }
     __syncthreads();
     const int chunk = s_chunk;
     int tok = -1;
     if (chunk >= 0) {
-        const float2 sp = cta_merge(stats + (int64_t)pr * nchunks, nchunks, s_fac, &s_tmp);
+        const float2 sp = rowstat[pr];
         const T* xp = A.row(pr);
-        const int lo = chunk * kChunk, hi = min(V, lo + kChunk);
-        if (qr >= 0 && !s_usep) {
-            const float2 sq = cta_merge(stats + (int64_t)qr * nchunks, nchunks, s_fac, &s_tmp);
+        const int lo = chunk * kDrawChunk, hi = min(V, lo + kDrawChunk);
+        if (qr >= 0 && !usep) {
+            const float2 sq = rowstat[qr];
             const T* xq = Bq.row(qr - A.n);
             tok = block_find(
                 [&](int i) {
@@ -385,7 +475,7 @@ __global__ void __launch_bounds__(1024) finish_kernel(Rows<T> A, Rows<T> Bq, int
 // test, plus one for the residual or bonus draw.
 template <typename T>
 __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> Bq, int V, float temp,
-                                                             const float2* __restrict__ stats, int nchunks,
+                                                             const float2* __restrict__ rowstat,
                                                              const int* __restrict__ prop, int B, int gamma,
                                                              const float* __restrict__ uniforms, int64_t nu,
                                                              int64_t* u_base, int64_t u_skip, int* n_acc,
@@ -404,8 +494,8 @@ __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> 
             continue;
         }
         const int pr = b * (gamma + 1) + j, qr = A.n + idx;
-        const float2 sp = merge_stats(stats + (int64_t)pr * nchunks, nchunks);
-        const float2 sq = merge_stats(stats + (int64_t)qr * nchunks, nchunks);
+        const float2 sp = rowstat[pr];
+        const float2 sq = rowstat[qr];
         const double pv = prob_of(scaled(to_f32<T>(A.row(pr)[x]), temp), sp.x, sp.y);
         const double qv = prob_of(scaled(to_f32<T>(Bq.row(idx)[x]), temp), sq.x, sq.y);
         double acc;
@@ -450,6 +540,7 @@ __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> 
 // ------------------------------------------------------------ host side
 struct Ws {
     float2* stats;
+    float2* rowstat;
     uint64_t* wsum;
     uint64_t* wsum_p;
     int* n_acc;
@@ -459,16 +550,18 @@ struct Ws {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-Ws carve(void* base, int stat_rows, int draws, int nchunks) {
+Ws carve(void* base, int stat_rows, int draws, int nchunks, int ndc) {
     Ws w;
     char* p = static_cast<char*>(base);
     size_t o = 0;
     w.stats = reinterpret_cast<float2*>(p + o);
     o = align256(o + (size_t)stat_rows * nchunks * sizeof(float2));
+    w.rowstat = reinterpret_cast<float2*>(p + o);
+    o = align256(o + (size_t)stat_rows * sizeof(float2));
     w.wsum = reinterpret_cast<uint64_t*>(p + o);
-    o = align256(o + (size_t)draws * nchunks * sizeof(uint64_t));
+    o = align256(o + (size_t)draws * ndc * sizeof(uint64_t));
     w.wsum_p = reinterpret_cast<uint64_t*>(p + o);
-    o = align256(o + (size_t)draws * nchunks * sizeof(uint64_t));
+    o = align256(o + (size_t)draws * ndc * sizeof(uint64_t));
     w.n_acc = reinterpret_cast<int*>(p + o);
     o = align256(o + (size_t)draws * sizeof(int));
     w.u_bits = reinterpret_cast<int*>(p + o);
@@ -481,18 +574,21 @@ template <typename T>
 int sample_logits_t(const T* logits, int64_t row_stride, int rows, int V, float temp, const float* uniforms, int64_t nu,
                     const int64_t* u_base, int64_t u_off, int* out, void* ws_base, int* err, cudaStream_t st) {
     const int nchunks = (V + kChunk - 1) / kChunk;
-    Ws w = carve(ws_base, rows, rows, nchunks);
+    const int ndc = (V + kDrawChunk - 1) / kDrawChunk;
+    Ws w = carve(ws_base, rows, rows, nchunks, ndc);
     Rows<T> A{logits, row_stride, 0, 1, rows};
     Rows<T> none{logits, 0, 0, 1, 0};
     cudaError_t e = sdl::launch_pdl(stats_kernel<T>, dim3(nchunks, rows), dim3(kGroup), 0, st, A, none, V, temp,
                                     w.stats);
     if (e == cudaSuccess)
-        e = sdl::launch_pdl(wsum_kernel<T>, dim3(nchunks, rows), dim3(kGroup), 0, st, A, none, V, temp,
-                            (const float2*)w.stats, nchunks, 0, 0, (const int*)nullptr, w.wsum, w.wsum_p);
+        e = sdl::launch_pdl(merge_kernel, dim3(rows), dim3(128), 0, st, (const float2*)w.stats, nchunks, w.rowstat);
     if (e == cudaSuccess)
-        e = sdl::launch_pdl(finish_kernel<T>, dim3(rows), dim3(1024), 0, st, A, none, V, temp, (const float2*)w.stats,
-                            nchunks, 0, 0, (const int*)nullptr, (const int*)nullptr, uniforms, nu, u_base, u_off,
-                            (const uint64_t*)w.wsum, (const uint64_t*)w.wsum_p, (const int*)nullptr, out,
+        e = sdl::launch_pdl(wsum_kernel<T>, dim3(ndc, rows), dim3(kGroup), 0, st, A, none, V, temp,
+                            (const float2*)w.rowstat, ndc, 0, 0, (const int*)nullptr, w.wsum);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(finish_kernel<T>, dim3(rows), dim3(1024), 0, st, A, none, V, temp, (const float2*)w.rowstat,
+                            ndc, 0, 0, (const int*)nullptr, (const int*)nullptr, uniforms, nu, u_base, u_off,
+                            (const uint64_t*)w.wsum, w.wsum_p, (const int*)nullptr, out,
                             (int*)nullptr, err);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("sample_logits");
@@ -503,8 +599,9 @@ int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t 
                   const int* prop, int B, int gamma, int V, const float* uniforms, int64_t nu, int64_t* u_base,
                   int64_t u_skip, int* tokens, int* n_out, void* ws_base, int* err, cudaStream_t st) {
     const int nchunks = (V + kChunk - 1) / kChunk;
+    const int ndc = (V + kDrawChunk - 1) / kDrawChunk;
     const int prow = B * (gamma + 1), qrow = B * gamma;
-    Ws w = carve(ws_base, prow + qrow, B, nchunks);
+    Ws w = carve(ws_base, prow + qrow, B, nchunks, ndc);
     Rows<T> A{pl, p_sb, p_sj, gamma + 1, prow};
     Rows<T> Q{ql, q_sb, q_sj, gamma, qrow};
     const size_t smem = (size_t)B * gamma * sizeof(double) + (size_t)B * (gamma + 1) * sizeof(float);
@@ -518,15 +615,19 @@ int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t 
     cudaError_t e = sdl::launch_pdl(stats_kernel<T>, dim3(nchunks, prow + qrow), dim3(kGroup), 0, st, A, Q, V, temp,
                                     w.stats);
     if (e == cudaSuccess)
-        e = sdl::launch_pdl(accept_logits_kernel<T>, dim3(1), dim3(1024), smem, st, A, Q, V, temp, (const float2*)w.stats,
-                            nchunks, prop, B, gamma, uniforms, nu, u_base, u_skip, w.n_acc, w.u_bits, err);
+        e = sdl::launch_pdl(merge_kernel, dim3(prow + qrow), dim3(128), 0, st, (const float2*)w.stats, nchunks,
+                            w.rowstat);
     if (e == cudaSuccess)
-        e = sdl::launch_pdl(wsum_kernel<T>, dim3(nchunks, B), dim3(kGroup), 0, st, A, Q, V, temp,
-                            (const float2*)w.stats, nchunks, 1, gamma, (const int*)w.n_acc, w.wsum, w.wsum_p);
+        e = sdl::launch_pdl(accept_logits_kernel<T>, dim3(1), dim3(1024), smem, st, A, Q, V, temp,
+                            (const float2*)w.rowstat, prop, B, gamma, uniforms, nu, u_base, u_skip, w.n_acc, w.u_bits,
+                            err);
     if (e == cudaSuccess)
-        e = sdl::launch_pdl(finish_kernel<T>, dim3(B), dim3(1024), 0, st, A, Q, V, temp, (const float2*)w.stats,
-                            nchunks, 1, gamma, (const int*)w.n_acc, (const int*)w.u_bits, uniforms, nu,
-                            (const int64_t*)nullptr, (int64_t)0, (const uint64_t*)w.wsum, (const uint64_t*)w.wsum_p,
+        e = sdl::launch_pdl(wsum_kernel<T>, dim3(ndc, B), dim3(kGroup), 0, st, A, Q, V, temp,
+                            (const float2*)w.rowstat, ndc, 1, gamma, (const int*)w.n_acc, w.wsum);
+    if (e == cudaSuccess)
+        e = sdl::launch_pdl(finish_kernel<T>, dim3(B), dim3(1024), 0, st, A, Q, V, temp, (const float2*)w.rowstat,
+                            ndc, 1, gamma, (const int*)w.n_acc, (const int*)w.u_bits, uniforms, nu,
+                            (const int64_t*)nullptr, (int64_t)0, (const uint64_t*)w.wsum, w.wsum_p,
                             prop, tokens, n_out, err);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("spec_sample_logits");
@@ -538,7 +639,7 @@ int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t 
 // sdl_logits_to_probs for temperature sampling.
 int sdl_probs_canon(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab, float temp,
                     float* probs, int64_t probs_stride, cudaStream_t st) {
-    if ((vocab + kChunk - 1) / kChunk > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "vocab above 4M");
+    if ((vocab + kChunk - 1) / kChunk > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "vocab above 8M");
     if (dtype == SDL_F32)
         probs_canon_kernel<float><<<rows, 1024, 0, st>>>((const float*)logits, row_stride, vocab, temp, probs,
                                                          probs_stride);
@@ -556,8 +657,9 @@ int sdl_probs_canon(const void* logits, int32_t dtype, int64_t row_stride, int32
 extern "C" size_t sdl_sampler_workspace_bytes(int32_t rows, int32_t vocab) {
     if (rows < 0 || vocab < 1) return 0;
     const int nchunks = (vocab + kChunk - 1) / kChunk;
+    const int ndc = (vocab + kDrawChunk - 1) / kDrawChunk;
     // statistics for `rows` logit rows and draw sums for as many draws
-    return carve(nullptr, rows, rows, nchunks).bytes;
+    return carve(nullptr, rows, rows, nchunks, ndc).bytes;
 }
 
 extern "C" int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows,
@@ -568,8 +670,10 @@ extern "C" int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t
         return sdl::fail(SDL_ERR_INVALID, "sdl_sample_logits_rows: bad args");
     if (rows == 0) return SDL_OK;
     const int nchunks = (vocab + kChunk - 1) / kChunk;
-    if (nchunks > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: vocab above 4M");
-    if (!workspace || workspace_bytes < carve(nullptr, rows, rows, nchunks).bytes ||
+    const int ndc = (vocab + kDrawChunk - 1) / kDrawChunk;
+    if (ndc > kMaxDrawChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: vocab above 2M");
+    if (rows > 65535) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: more than 65535 rows");
+    if (!workspace || workspace_bytes < carve(nullptr, rows, rows, nchunks, ndc).bytes ||
         reinterpret_cast<uintptr_t>(workspace) % 256)
         return sdl::fail(SDL_ERR_WORKSPACE, "sdl_sample_logits_rows: workspace missing, small or not 256-B aligned");
     const float t = temperature > eps ? temperature : eps;
@@ -597,9 +701,11 @@ extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_
         return sdl::fail(SDL_ERR_INVALID, "sdl_spec_sample_logits: bad args (gamma must be 1..32)");
     if (B == 0) return SDL_OK;
     const int nchunks = (vocab + kChunk - 1) / kChunk;
-    if (nchunks > kMaxChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: vocab above 4M");
+    const int ndc = (vocab + kDrawChunk - 1) / kDrawChunk;
+    if (ndc > kMaxDrawChunks) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: vocab above 2M");
     const int stat_rows = B * (2 * gamma + 1);
-    if (!workspace || workspace_bytes < carve(nullptr, stat_rows, B, nchunks).bytes ||
+    if (stat_rows > 65535) return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: too many rows");
+    if (!workspace || workspace_bytes < carve(nullptr, stat_rows, B, nchunks, ndc).bytes ||
         reinterpret_cast<uintptr_t>(workspace) % 256)
         return sdl::fail(SDL_ERR_WORKSPACE, "sdl_spec_sample_logits: workspace missing, small or not 256-B aligned");
     const size_t smem = (size_t)B * gamma * sizeof(double) + (size_t)B * (gamma + 1) * sizeof(float);

@@ -138,3 +138,31 @@ def test_oracle_batch_accept_stochastic_matches_reference():
         props = [case["proposals"][str(b)] for b in range(B)]
         acc = osamp.batch_accept(p, q, props, osamp.UniformStream(case["u"]))
         assert acc == [case["accepted"][str(b)] for b in range(B)]
+
+
+def test_fp32_weight_rule_equals_double_rule():
+    """The kernels compute W = floor(w * 2^62) as the fp32 product with 2^62
+    (exact: a power-of-two scaling) truncated to u64 with saturation
+    (csrc/sampler*.cu wfix).  The premise -- the fp32 product equals the
+    exact product wherever it is below 2^64 -- and the resulting integers
+    must match the oracle's double-precision floor on edge and random values."""
+    vals = [0.0, -1.0, float("nan"), float("inf"), 1e-45, 2.0 ** -62, 2.0 ** -62 * 1.5, 2.0 ** -63, 2.0 ** -40,
+            0.5, 1.0, 1.9999999, 2.0, 3.9999998, 4.0, 7.5]
+    rng = np.random.default_rng(0)
+    vals += list(rng.random(2000).astype(np.float32)) + list((rng.random(500) * 1e-12).astype(np.float32))
+    w = np.array(vals, dtype=np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        prod32 = w * np.float32(2.0 ** 62)                       # what the kernel multiplies
+        exact = w.astype(np.float64) * 2.0 ** 62
+    finite = np.isfinite(exact) & (exact < 2.0 ** 64)
+    assert np.array_equal(prod32[finite].astype(np.float64), exact[finite])
+
+    def trunc_sat(x: float) -> int:                              # cvt.rzi.u64.f32 semantics
+        if x != x or x <= 0.0:
+            return 0
+        if x >= 2.0 ** 64:
+            return (1 << 64) - 1
+        return int(x)
+
+    want = [int(v) for v in osamp.wfix(w)]
+    assert [trunc_sat(float(x)) for x in prod32] == want
