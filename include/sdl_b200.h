@@ -189,6 +189,9 @@ typedef struct sdl_attn_args {
     int32_t pages_per_split;  /* 0 = choose automatically                  */
     int32_t force_generic;    /* 1 = CUDA-core path even when TC applies   */
     int32_t kv_heads_per_cta; /* 0 = automatic; caps kv heads per CTA      */
+    int32_t use_umma;         /* 1 = the tcgen05 kernel where it applies
+                                 (up to 64 query rows per kv head);
+                                 0 / -1 = the mma.sync kernel              */
     int32_t* err;
 } sdl_attn_args;
 

@@ -29,6 +29,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 namespace {
 
@@ -411,6 +412,410 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     }
 }
 
+// ------------------------------------------------------ tcgen05 verify path
+// attn_umma_kernel: the (gamma+1)-row verify -- any block of up to 64 query
+// rows per kv head -- on the 5th-generation tensor cores.  One CTA = one
+// sequence x one kv head x one split of its pages; 6 warps:
+//   warp 4     producer: TMA of 64-token K/V tiles (4 pages, 2 KB boxes)
+//              into a ring laid out as the canonical 128-byte swizzled
+//              K-major (K) / MN-major (V) operand layouts;
+//   warp 5     owns TMEM (256 columns); one thread issues tcgen05.mma (M = 64):
+//              S[64 x 64] = Q[64 x d] K^T into a double-buffered TMEM tile,
+//              then O[64 x d] += P_hi V + P_lo V into a TMEM accumulator;
+//   warps 0-3  softmax: query row m = 16*w + (lane % 16) (row m = j * ratio
+//              + head offset; rows >= chunk*ratio are zero padding) lives in
+//              TMEM lane 32*w + m % 16; lanes l and l + 16 hold the two
+//              32-column halves of the row's S tile (16x32bx2 loads) and
+//              share its max and sum by one shuffle.  Online softmax in the
+//              log2 domain with a lazy rescale (O and l are rescaled in TMEM
+//              only when the row max grows by more than 2^8); P is written as
+//              a bf16/f16 hi+lo pair into swizzled shared memory; the
+//              epilogue writes finished rows, or fp32 split partials in the
+//              layout attn_combine_kernel reads.
+// Every mbarrier wait is bounded; on expiry the CTA records
+// SDL_DEVERR_TIMEOUT, stops issuing, lets issued copies and MMAs land, and
+// releases TMEM before exiting.
+constexpr int kUTok = 64;             // tokens per tile
+constexpr int kUPages = kUTok / kPage;
+constexpr int kURows = 64;            // MMA M: padded query rows of one kv head
+constexpr int kUThreads = 192;
+constexpr int kUProducer = 4, kUMma = 5;
+constexpr uint32_t kUTmemCols = 256;  // S double buffer (2 x 64 columns) + O (64 or 128)
+
+template <int HD>
+struct USmem {
+    static constexpr int DO = HD / 64;
+    static constexpr int kNst = HD == 128 ? 5 : 6;  // K/V ring depth
+    static constexpr int kQ = DO * kURows * 128;   // Q, per 64-column half 8 KB
+    static constexpr int kHalf = kUTok * 128;      // one 64-column half of a K or V tile
+    static constexpr int kStage = 2 * DO * kHalf;  // K halves then V halves
+    static constexpr int kP = kURows * 128;        // one 64 x 64 16-bit P matrix
+    static constexpr int kOffKV = kQ;
+    static constexpr int kOffP = kQ + kNst * kStage;
+    static constexpr int kBytes = kOffP + 4 * kP;  // P hi / lo, double buffered
+};
+
+// p as a hi + lo pair of 16-bit values (hi = round(p), lo = round(p - hi)),
+// two columns at a time.
+template <typename T> SDL_DEV void split_pair(float p0, float p1, uint32_t& hi, uint32_t& lo);
+template <> SDL_DEV void split_pair<__nv_bfloat16>(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+template <> SDL_DEV void split_pair<__half>(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(p0, p1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD, typename T>
+__global__ void __launch_bounds__(kUThreads, 1)
+attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const TcParams p) {
+    using L = USmem<HD>;
+    constexpr int kUNst = L::kNst;
+    constexpr int DO = L::DO;
+    constexpr int SK = HD / 16;  // k-steps of the S product
+    constexpr int OH = HD / 2;   // O columns per softmax thread
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    constexpr uint32_t kIdescS = umma_idesc_f16(kURows, kUTok, kBf16, false);
+    constexpr uint32_t kIdescO = umma_idesc_f16(kURows, HD, kBf16, true);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t kv_full[kUNst], kv_empty[kUNst], s_full[2], s_free[2], p_full[2], p_free[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort_flag;
+    volatile int* s_abort = &s_abort_flag;
+
+    pdl_wait();
+    const int b = blockIdx.z, g = blockIdx.y, split = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int start = p.starts[b];
+    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
+    const int lmax = start + nvalid;
+    if (nvalid <= 0 || lmax <= 0) return;
+    const int npages = (lmax + kPage - 1) / kPage;
+    const int pbeg = split * p.pps, pend = min(npages, pbeg + p.pps);
+    if (pbeg >= pend) return;
+    const int ntiles = (pend - pbeg + kUPages - 1) / kUPages;
+    const int row = p.dense ? 0 : p.rows[b];
+    const int R = p.chunk * p.ratio;
+    // Live query rows are [0, min(R, nvalid * ratio)); softmax warps whose
+    // 16 rows are all padding sit the loop out.
+    const int live_rows = min(R, nvalid * p.ratio);
+    const int nsoft = (live_rows + 15) / 16;
+
+    uint8_t* sQ = smem;
+    uint8_t* sKV = smem + L::kOffKV;
+    uint8_t* sP = smem + L::kOffP;
+    const uint32_t aQ = smem_u32(sQ), aKV = smem_u32(sKV), aP = smem_u32(sP);
+
+    if (threadIdx.x == 0) {
+        *s_abort = 0;
+        for (int i = 0; i < kUNst; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], nsoft);
+            mbar_init(&p_full[i], nsoft);
+            mbar_init(&p_free[i], 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == kUMma) {
+        tmem_alloc(&s_tmem, kUTmemCols);
+        tmem_relinquish();
+    }
+    if (warp < 4) {
+        // Rows 16*warp .. +15 of Q: lane l copies half (l / 16) of row
+        // 16*warp + l % 16 into the swizzled K-major tile (zero for padding
+        // rows); the P rows of rows that are not live stay zero.
+        const int m = 16 * warp + (lane & 15), hq = lane >> 4;
+        const int j = m / p.ratio;
+        const bool live = m < R && j < nvalid;
+        const T* qrow = nullptr;
+        if (live)
+            qrow = reinterpret_cast<const T*>(p.q) + b * p.q_sb + j * p.q_sj + (g * p.ratio + m % p.ratio) * p.q_sh;
+#pragma unroll
+        for (int c = hq * (HD / 16); c < (hq + 1) * (HD / 16); ++c) {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (live) v = make_uint4(ld_u32(qrow + 8 * c), ld_u32(qrow + 8 * c + 2), ld_u32(qrow + 8 * c + 4),
+                                     ld_u32(qrow + 8 * c + 6));
+            *reinterpret_cast<uint4*>(sQ + (c >> 3) * (kURows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4)) = v;
+        }
+        if (!live) {
+#pragma unroll
+            for (int mm = 0; mm < 4; ++mm)
+#pragma unroll
+                for (int c = 4 * hq; c < 4 * hq + 4; ++c)
+                    *reinterpret_cast<uint4*>(sP + mm * L::kP + m * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == kUProducer) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
+        int issued = 0;
+        bool stop = false;
+        // Page-table lookups run 32 tiles ahead: lane l resolves the first
+        // token of every page of tile i0 + l before any of them is issued.
+        for (int i0 = 0; i0 < ntiles && !stop; i0 += 32) {
+            int tok[kUPages];
+#pragma unroll
+            for (int u = 0; u < kUPages; ++u) {
+                tok[u] = 0;
+                const int ti = i0 + lane;
+                if (ti < ntiles) {
+                    int pg = pbeg + ti * kUPages + u;
+                    if (pg >= pend) pg = pbeg + ti * kUPages;  // pad a short tile with a real page; masked later
+                    if (p.dense) {
+                        tok[u] = b * p.kv_len + pg * kPage;
+                    } else {
+                        int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+                        if (phys < 0 || phys >= p.capacity) { sdl_raise(p.err, SDL_DEVERR_BAD_INDEX); phys = 0; }
+                        tok[u] = (p.layer * p.capacity + phys) * kPage;
+                    }
+                }
+            }
+            const int cnt = min(32, ntiles - i0);
+            for (int k = 0; k < cnt; ++k) {
+                const int i = i0 + k;
+                const int st = i % kUNst;
+                int t0[kUPages];
+#pragma unroll
+                for (int u = 0; u < kUPages; ++u) t0[u] = __shfl_sync(0xffffffffu, tok[u], k);
+                int ok = 1;
+                if (i >= kUNst && lane == 0)
+                    ok = mbar_wait_bounded(&kv_empty[st], ((i / kUNst) - 1) & 1, kWaitLimit) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok || *s_abort) {
+                    if (lane == 0 && !ok) { sdl_raise(p.err, SDL_DEVERR_TIMEOUT); *s_abort = 1; }
+                    stop = true;
+                    break;
+                }
+                // lane 0 posts the byte count, then one lane per 2 KB box issues it
+                if (lane == 0) mbar_arrive_expect_tx(&kv_full[st], L::kStage);
+                __syncwarp();
+                if (lane < 2 * kUPages * DO) {
+                    const int u = lane % kUPages, dd = (lane / kUPages) % DO, isv = lane / (kUPages * DO);
+                    const int tu = u == 0 ? t0[0] : u == 1 ? t0[1] : u == 2 ? t0[2] : t0[3];
+                    uint8_t* dst = sKV + st * L::kStage + (isv * DO + dd) * L::kHalf + u * kBoxBytes;
+                    tma_load_4d(dst, isv ? &tmv : &tmk, &kv_full[st], 0, dd, g, tu);
+                }
+                __syncwarp();
+                issued = i + 1;
+            }
+        }
+        // Never leave the CTA with bulk copies still landing in shared memory.
+        if (lane == 0 && *s_abort) {
+            for (int i = max(0, issued - kUNst); i < issued; ++i)
+                (void)mbar_wait_bounded(&kv_full[i % kUNst], (i / kUNst) & 1, kWaitLimit);
+        }
+        pdl_launch_dependents();
+    } else if (warp == kUMma) {
+        // ------------------------------------------------------------ MMA
+        if (lane == 0) {
+            // Descriptors of the operand bases; an MMA adds its byte offset >> 4
+            // to the start-address field (shared addresses stay below 2^18).
+            const uint64_t dQ = umma_desc_sw128(aQ, 16, 1024);
+            const uint64_t dK = umma_desc_sw128(aKV, 16, 1024);
+            const uint64_t dP = umma_desc_sw128(aP, 16, 1024);
+            const uint64_t dV = umma_desc_sw128(aKV + DO * L::kHalf, L::kHalf, 1024);
+            int s_issued = 0, pv_issued = 0;
+            bool ok = true;
+            auto issue_s = [&](int t) -> bool {
+                const int st = t % kUNst, sb = t & 1;
+                if (!mbar_wait_bounded(&kv_full[st], (t / kUNst) & 1, kWaitLimit)) return false;
+                if (t >= 2 && !mbar_wait_bounded(&s_free[sb], ((t - 2) >> 1) & 1, kWaitLimit)) return false;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < SK; ++k) {
+                    const uint32_t qo = (k >> 2) * (kURows * 128) + (k & 3) * 32;
+                    const uint32_t ko = st * L::kStage + (k >> 2) * L::kHalf + (k & 3) * 32;
+                    umma_f16(tmem + sb * kUTok, dQ + (qo >> 4), dK + (ko >> 4), kIdescS, k > 0 ? 1u : 0u);
+                }
+                umma_commit(&s_full[sb]);
+                s_issued = t + 1;
+                return true;
+            };
+            ok = issue_s(0);
+            for (int i = 0; ok && i < ntiles; ++i) {
+                if (*s_abort) { ok = false; break; }
+                if (i + 1 < ntiles && !issue_s(i + 1)) { ok = false; break; }
+                const int pb = i & 1, st = i % kUNst;
+                if (!mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kWaitLimit)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int k = 0; k < kUTok / 16; ++k) {
+                        const uint32_t po = (2 * pb + h) * L::kP + k * 32;
+                        const uint32_t vo = st * L::kStage + k * 2048;
+                        umma_f16(tmem + 2 * kUTok, dP + (po >> 4), dV + (vo >> 4), kIdescO,
+                                 (i > 0 || h > 0 || k > 0) ? 1u : 0u);
+                    }
+                umma_commit(&p_free[pb]);
+                umma_commit(&kv_empty[st]);
+                pv_issued = i + 1;
+            }
+            if (!ok) {
+                sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
+                *s_abort = 1;
+            }
+            // every issued MMA completes before TMEM is released
+            if (s_issued > 0) (void)mbar_wait_bounded(&s_full[(s_issued - 1) & 1], ((s_issued - 1) >> 1) & 1, kWaitLimit);
+            if (pv_issued > 0)
+                (void)mbar_wait_bounded(&p_free[(pv_issued - 1) & 1], ((pv_issued - 1) >> 1) & 1, kWaitLimit);
+        }
+        __syncwarp();
+        pdl_launch_dependents();
+    } else if (warp < nsoft) {
+        // ------------------------------------------------------- softmax
+        const int hc = lane >> 4;                  // column half of S (and of O)
+        const int m = 16 * warp + (lane & 15);     // query row
+        const int j = m / p.ratio;
+        const bool live = m < R && j < nvalid;
+        const int lim = live ? start + j + 1 : 0;  // the row attends positions < lim
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        const int lim_eff = min(lim, pend * kPage);
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int i = 0; i < ntiles; ++i) {
+            const int sb = i & 1, pb = i & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], (i >> 1) & 1, kWaitLimit));
+            if (!ok || *s_abort) break;
+            tc_fence_after();
+            float sv[32];
+            __syncwarp();
+            tmem_ld16x2<32>(tmem + lane_base + sb * kUTok, reinterpret_cast<uint32_t*>(sv));
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[sb]);
+
+            // raw scores; positions at or past the row's limit are masked
+            const int c0 = (pbeg + i * kUPages) * kPage + 32 * hc;
+            if (c0 + 32 > lim_eff) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) sv[c] = c0 + c < lim_eff ? sv[c] : -INFINITY;
+            }
+            float tmax = sv[0];
+#pragma unroll
+            for (int c = 1; c < 32; ++c) tmax = fmaxf(tmax, sv[c]);
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+            const float m_new = fmaxf(m_run, tmax * p.scale_log2);
+            const bool need = m_new > m_run + 8.f;
+            if (i > 0 && __any_sync(0xffffffffu, need)) {
+                // O is rescaled in place once PV(i-1) has landed
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait_bounded(&p_free[(i - 1) & 1], ((i - 1) >> 1) & 1, kWaitLimit));
+                if (!ok) break;
+                tc_fence_after();
+                const float alpha = need ? exp2f(m_run - m_new) : 1.f;
+#pragma unroll
+                for (int o0 = 0; o0 < OH; o0 += 32) {
+                    uint32_t o[32];
+                    __syncwarp();
+                    tmem_ld16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
+                }
+                tmem_wait_st();
+                l_run *= alpha;
+            }
+            if (need) m_run = m_new;
+            const float muse = m_run == -INFINITY ? 0.f : m_run;
+            if (i >= 2) {
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[pb], ((i - 2) >> 1) & 1, kWaitLimit));
+                if (!ok) break;
+            }
+            if (live) {
+                float lsum = 0.f;
+                uint8_t* ph = sP + (2 * pb) * L::kP + m * 128;
+                uint8_t* pl = sP + (2 * pb + 1) * L::kP + m * 128;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float p0 = ex2_approx(fmaf(sv[8 * k + 2 * e], p.scale_log2, -muse));
+                        const float p1 = ex2_approx(fmaf(sv[8 * k + 2 * e + 1], p.scale_log2, -muse));
+                        lsum += p0 + p1;
+                        split_pair<T>(p0, p1, hw[e], lw[e]);
+                    }
+                    const int sw = ((4 * hc + k) ^ (m & 7)) << 4;
+                    *reinterpret_cast<uint4*>(ph + sw) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(pl + sw) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+                l_run += lsum;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[pb]);
+        }
+        pdl_launch_dependents();
+        const float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
+        if (ok && !*s_abort) {
+            const int last = ntiles - 1;
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[last & 1], (last >> 1) & 1, kWaitLimit));
+            tc_fence_after();
+            if (ok) {
+                const int L_row = start + j + 1;
+                const int ns_row = ((L_row + kPage - 1) / kPage + p.pps - 1) / p.pps;
+                const bool write = live && split < ns_row;
+                const int h = g * p.ratio + m % p.ratio;
+                const int64_t idx = (((int64_t)b * p.nsplit + split) * p.chunk + j) * p.Hq + h;
+                const float inv = 1.f / l_tot;
+#pragma unroll
+                for (int o0 = 0; o0 < OH; o0 += 32) {
+                    uint32_t o[32];
+                    __syncwarp();  // TMEM loads are warp-collective: converge first
+                    tmem_ld16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
+                    tmem_wait_ld();
+                    const int d0 = hc * OH + o0;
+                    if (write && ns_row == 1) {
+                        const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + d0;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) store_from_f32(p.out, ob + e, p.out_dtype, __uint_as_float(o[e]) * inv);
+                    } else if (write) {
+                        float4* dst = reinterpret_cast<float4*>(p.o_part + idx * HD + d0);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                                 __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+                    }
+                }
+                if (write && ns_row > 1 && hc == 0) {
+                    p.ml_part[idx * 2] = m_run;
+                    p.ml_part[idx * 2 + 1] = l_tot;
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
+            *s_abort = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kUMma) tmem_dealloc(tmem, kUTmemCols);
+}
+
 // ------------------------------------------------------------ generic path
 struct GenParams {
     const void* q;
@@ -546,6 +951,7 @@ struct Plan {
     int ntg = 1, wpg = 1, ncoltiles = 1, g_cta = 1, kvgroups = 1;
     int pps = 1, nsplit = 1;
     int stage_bytes = 0;
+    bool umma = false;  // tcgen05 verify kernel
     size_t smem = 0;
     size_t ws_bytes = 0;
 };
@@ -574,7 +980,39 @@ bool tc_applicable(const sdl_attn_args* a) {
     return true;
 }
 
+// The tcgen05 kernel takes row blocks of up to 64 query rows per kv head.
+// It runs when asked for (use_umma = 1); the automatic plan keeps the
+// mma.sync kernel, which is faster on the C2/C3 shapes as measured so far.
+bool umma_applicable(const sdl_attn_args* a) {
+    if (a->use_umma <= 0 || !tc_applicable(a)) return false;
+    const int rows = a->chunk * (a->Hq / a->Hkv);
+    return rows <= kURows;
+}
+
+Plan make_umma_plan(const sdl_attn_args* a) {
+    Plan pl;
+    pl.tc = true;
+    pl.umma = true;
+    pl.smem = (a->head_dim == 128 ? USmem<128>::kBytes : USmem<64>::kBytes) + 1024;
+    const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
+    const long base_ctas = (long)a->B * a->Hkv;  // one CTA per SM: aim for about two waves
+    const long target = (long)sm_count() * 2;
+    const int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
+    auto round_tile = [](int x) { return (x + kUPages - 1) / kUPages * kUPages; };
+    int pps = a->pages_per_split > 0 ? round_tile(a->pages_per_split)
+                                     : std::max(2 * kUPages, round_tile((max_pages + nsplit_target - 1) / nsplit_target));
+    for (;;) {
+        pl.pps = pps;
+        pl.nsplit = (max_pages + pps - 1) / pps;
+        pl.ws_bytes = pl.nsplit > 1 ? (size_t)a->B * pl.nsplit * a->chunk * a->Hq * (a->head_dim + 2) * sizeof(float) : 0;
+        if (a->pages_per_split > 0 || pl.ws_bytes <= a->workspace_bytes || pl.nsplit == 1 || !a->workspace) break;
+        pps *= 2;
+    }
+    return pl;
+}
+
 Plan make_plan(const sdl_attn_args* a) {
+    if (umma_applicable(a)) return make_umma_plan(a);
     Plan pl;
     pl.tc = tc_applicable(a);
     if (!pl.tc) return pl;
@@ -635,6 +1073,28 @@ int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams&
     cudaError_t e = sdl::launch_pdl(kern, grid, block, pl.smem, st, mk, mv, tp);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("attn_tc_kernel");
+}
+
+template <int HD, typename T>
+int launch_umma_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl, cudaStream_t st) {
+    auto kern = attn_umma_kernel<HD, T>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+        if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+        configured = true;
+    }
+    dim3 grid(pl.nsplit, tp.Hkv, tp.B);
+    cudaError_t e = sdl::launch_pdl(kern, grid, dim3(kUThreads), pl.smem, st, mk, mv, tp);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("attn_umma_kernel");
+}
+
+template <typename T>
+int launch_umma_dtype(int hd, const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl,
+                      cudaStream_t st) {
+    if (hd == 64) return launch_umma_inst<64, T>(mk, mv, tp, pl, st);
+    return launch_umma_inst<128, T>(mk, mv, tp, pl, st);
 }
 
 template <typename T>
@@ -726,8 +1186,14 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.o_part = a->workspace;
         tp.ml_part = a->workspace ? a->workspace + (size_t)a->B * pl.nsplit * a->chunk * a->Hq * a->head_dim : nullptr;
         tp.err = a->err;
-        if (a->dtype == SDL_BF16) rc = launch_tc_dtype<__nv_bfloat16>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
-        else rc = launch_tc_dtype<__half>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
+        if (pl.umma) {
+            if (a->dtype == SDL_BF16) rc = launch_umma_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
+            else rc = launch_umma_dtype<__half>(a->head_dim, mk, mv, tp, pl, st);
+        } else if (a->dtype == SDL_BF16) {
+            rc = launch_tc_dtype<__nv_bfloat16>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
+        } else {
+            rc = launch_tc_dtype<__half>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
+        }
         if (rc != SDL_OK) return rc;
         if (pl.nsplit > 1) {
             const int rows = a->B * a->chunk * a->Hq;

@@ -112,6 +112,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("pages_per_split", c_int),
         ("force_generic", c_int),
         ("kv_heads_per_cta", c_int),
+        ("use_umma", c_int),
         ("err", c_void),
     ]
 

@@ -141,32 +141,34 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", range(len(CASES)))
-@pytest.mark.parametrize("generic", [False, True])
-def test_paged_attention_matches_oracle(case, generic):
+@pytest.mark.parametrize("generic,umma", [(False, 0), (False, 1), (False, -1), (True, 0)])
+def test_paged_attention_matches_oracle(case, generic, umma):
+    """Every kernel (tcgen05, mma.sync, CUDA-core) against the oracle."""
     Hq, Hkv, d, chunk, starts, bs, dtype = CASES[case]
     kv, ref = _build([s + chunk for s in starts], Hkv, d, bs, dtype, seed=100 + case)
     rng = np.random.default_rng(case)
     q = torch.from_numpy(rng.standard_normal((len(starts), chunk, Hq, d)).astype(np.float32)).to(DEV, dtype)
     batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
-    out = paged_attention(q, kv, 0, batch, force_generic=generic)
-    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, force_generic=generic)
+    out = paged_attention(q, kv, 0, batch, force_generic=generic, use_umma=umma)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, force_generic=generic, use_umma=umma)
     exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(len(starts)), starts)
     _check_bf16(out.float().cpu().numpy(), out32.cpu().numpy(), exact)
     kv.check_errors()
 
 
 @pytest.mark.parametrize("pps", [1, 3, 0, 64])
-@pytest.mark.parametrize("heads_per_cta", [0, 1])
-def test_split_plans_agree(pps, heads_per_cta):
+@pytest.mark.parametrize("heads_per_cta,umma", [(0, -1), (1, -1), (0, 1)])
+def test_split_plans_agree(pps, heads_per_cta, umma):
     """Every launch plan (pages per split-K CTA from 1, i.e. 150+ splits per
-    row, to one split; one or two kv heads per CTA) gives the oracle's result
-    for decode and verify rows."""
+    row, to one split; one or two kv heads per CTA of the mma.sync kernel;
+    the tcgen05 kernel, whose 64-token tiles then end inside a split) gives
+    the oracle's result for decode and verify rows."""
     kv, ref = _build([2500 + 6, 17 + 6, 900 + 6], 2, 128, 16, torch.bfloat16, seed=5)
     for chunk, starts in ((1, [2505, 22, 905]), (6, [2500, 17, 900])):
         q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
         batch = AttnBatch.from_lists(DEV, [0, 1, 2], starts, chunk)
         out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps,
-                              kv_heads_per_cta=heads_per_cta)
+                              kv_heads_per_cta=heads_per_cta, use_umma=umma)
         exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), starts)
         assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
     kv.check_errors()
