@@ -58,6 +58,7 @@ struct TcParams {
     float scale_log2;
     float* o_part;
     float* ml_part;
+    int4* sk_table;  // persistent tcgen05 kernel: per (sequence, kv head) {first tile, tiles, slot, slots}
     int32_t* err;
 };
 
@@ -413,15 +414,21 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
 }
 
 // ------------------------------------------------------ tcgen05 verify path
-// attn_umma_kernel: the (gamma+1)-row verify -- any block of up to 64 query
-// rows per kv head -- on the 5th-generation tensor cores.  One CTA = one
-// sequence x one kv head x one split of its pages; 6 warps:
-//   warp 4     producer: TMA of 64-token K/V tiles (4 pages, 2 KB boxes)
-//              into a ring laid out as the canonical 128-byte swizzled
-//              K-major (K) / MN-major (V) operand layouts;
-//   warp 5     owns TMEM (256 columns); one thread issues tcgen05.mma (M = 64):
+// attn_sk_kernel: paged attention for blocks of up to 64 query rows per kv
+// head (decode and the (gamma+1)-row verify) on the 5th-generation tensor
+// cores, as a persistent stream-K kernel: the (sequence, kv head) pairs are
+// laid end to end as 64-token tiles and every CTA (one per SM) takes an
+// equal share of that tile sequence, so the grid is one balanced wave.  A
+// CTA walks its share as segments (the part of one pair's tiles it owns)
+// without draining its pipeline between them.  6 warps:
+//   warp 4     producer: TMA of 64-token K/V tiles (4 pages, 2 KB boxes, one
+//              lane per box) into a ring laid out as the canonical 128-byte
+//              swizzled K-major (K) / MN-major (V) operand layouts; page-table
+//              lookups run 32 tiles ahead;
+//   warp 5     owns TMEM (512 columns); one thread issues tcgen05.mma (M = 64):
 //              S[64 x 64] = Q[64 x d] K^T into a double-buffered TMEM tile,
-//              then O[64 x d] += P_hi V + P_lo V into a TMEM accumulator;
+//              then O[64 x d] += P_hi V + P_lo V into a TMEM accumulator that
+//              alternates between two buffers from one segment to the next;
 //   warps 0-3  softmax: query row m = 16*w + (lane % 16) (row m = j * ratio
 //              + head offset; rows >= chunk*ratio are zero padding) lives in
 //              TMEM lane 32*w + m % 16; lanes l and l + 16 hold the two
@@ -429,9 +436,12 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
 //              share its max and sum by one shuffle.  Online softmax in the
 //              log2 domain with a lazy rescale (O and l are rescaled in TMEM
 //              only when the row max grows by more than 2^8); P is written as
-//              a bf16/f16 hi+lo pair into swizzled shared memory; the
-//              epilogue writes finished rows, or fp32 split partials in the
-//              layout attn_combine_kernel reads.
+//              a bf16/f16 hi+lo pair into swizzled shared memory.  They also
+//              stage the next segment's Q (double buffered, cp.async issued at
+//              a segment's start and published after its first tile) and run
+//              each segment's epilogue: the final rows when the CTA owns the
+//              whole pair, else fp32 partials (m in log2 units, unnormalised
+//              O, l) that attn_sk_combine_kernel merges.
 // Every mbarrier wait is bounded; on expiry the CTA records
 // SDL_DEVERR_TIMEOUT, stops issuing, lets issued copies and MMAs land, and
 // releases TMEM before exiting.
@@ -440,18 +450,21 @@ constexpr int kUPages = kUTok / kPage;
 constexpr int kURows = 64;            // MMA M: padded query rows of one kv head
 constexpr int kUThreads = 192;
 constexpr int kUProducer = 4, kUMma = 5;
-constexpr uint32_t kUTmemCols = 256;  // S double buffer (2 x 64 columns) + O (64 or 128)
+constexpr uint32_t kUTmemCols = 512;  // S double buffer (2 x 64 columns) + O double buffer (2 x 128)
+constexpr int kUOCol = 2 * kUTok;     // TMEM column of O buffer 0; buffer 1 is 128 columns on
+constexpr int kSkMaxPairs = 512;      // (sequence, kv head) pairs one launch may hold
+constexpr int kSkMaxSeqs = 512;       // sequences one launch may hold
 
 template <int HD>
 struct USmem {
     static constexpr int DO = HD / 64;
-    static constexpr int kNst = HD == 128 ? 5 : 6;  // K/V ring depth
-    static constexpr int kQ = DO * kURows * 128;   // Q, per 64-column half 8 KB
+    static constexpr int kNst = 4;                 // K/V ring depth
+    static constexpr int kQ = DO * kURows * 128;   // one Q buffer (8 KB per 64-column half)
     static constexpr int kHalf = kUTok * 128;      // one 64-column half of a K or V tile
     static constexpr int kStage = 2 * DO * kHalf;  // K halves then V halves
     static constexpr int kP = kURows * 128;        // one 64 x 64 16-bit P matrix
-    static constexpr int kOffKV = kQ;
-    static constexpr int kOffP = kQ + kNst * kStage;
+    static constexpr int kOffKV = 2 * kQ;
+    static constexpr int kOffP = kOffKV + kNst * kStage;
     static constexpr int kBytes = kOffP + 4 * kP;  // P hi / lo, double buffered
 };
 
@@ -473,9 +486,23 @@ template <> SDL_DEV void split_pair<__half>(float p0, float p1, uint32_t& hi, ui
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
+// The pair holding global tile `pos`: the last pair whose first tile is <= pos
+// (empty pairs share their successor's first tile and are skipped this way).
+SDL_DEV int sk_pair_of(const int* first, int npairs, int pos) {
+    int lo = 0, hi = npairs;  // invariant: first[lo] <= pos < first[hi] (first[npairs] = total)
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (first[mid] <= pos) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// Rows of sequence b: position limit for query row j and whether it is valid.
+SDL_DEV int sk_nvalid(const TcParams& p, int b) { return p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk; }
+
 template <int HD, typename T>
 __global__ void __launch_bounds__(kUThreads, 1)
-attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const TcParams p) {
+attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const TcParams p) {
     using L = USmem<HD>;
     constexpr int kUNst = L::kNst;
     constexpr int DO = L::DO;
@@ -487,27 +514,66 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t kv_full[kUNst], kv_empty[kUNst], s_full[2], s_free[2], p_full[2], p_free[2];
+    __shared__ uint64_t q_full[2], q_free[2], o_free[2];
+    __shared__ int s_first[kSkMaxPairs + 1];  // first global tile of each pair (prefix of tiles)
+    __shared__ int s_start[kSkMaxSeqs], s_row[kSkMaxSeqs], s_nval[kSkMaxSeqs];  // per sequence
+    __shared__ int s_slot[kSkMaxPairs];       // first partial slot of each pair
+    __shared__ int s_red[32];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
     pdl_wait();
-    const int b = blockIdx.z, g = blockIdx.y, split = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int start = p.starts[b];
-    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
-    const int lmax = start + nvalid;
-    if (nvalid <= 0 || lmax <= 0) return;
-    const int npages = (lmax + kPage - 1) / kPage;
-    const int pbeg = split * p.pps, pend = min(npages, pbeg + p.pps);
-    if (pbeg >= pend) return;
-    const int ntiles = (pend - pbeg + kUPages - 1) / kUPages;
-    const int row = p.dense ? 0 : p.rows[b];
+    const int npairs = p.B * p.Hkv;
+    const int G = gridDim.x, c = blockIdx.x;
+
+    // --- per-sequence data, tile prefix over the pairs, tiles per CTA, slots
+    for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+        s_start[b] = p.starts[b];
+        s_nval[b] = sk_nvalid(p, b);
+        s_row[b] = p.dense ? 0 : p.rows[b];
+    }
+    __syncthreads();
+    int total = 0;
+    for (int base = 0; base < npairs; base += blockDim.x) {
+        const int idx = base + threadIdx.x;
+        int n = 0;
+        if (idx < npairs) {
+            const int b = idx / p.Hkv;
+            const int lmax = s_start[b] + s_nval[b];
+            n = lmax > 0 ? ((lmax + kPage - 1) / kPage + kUPages - 1) / kUPages : 0;
+        }
+        int tot;
+        const int ex = block_exclusive_scan<int>(n, s_red, &tot);
+        if (idx < npairs) s_first[idx] = total + ex;
+        total += tot;
+    }
+    if (threadIdx.x == 0) s_first[npairs] = total;
+    __syncthreads();
+    const int tpc = (total + G - 1) / G;  // tiles per CTA
+    int nslots = 0;
+    for (int base = 0; base < npairs; base += blockDim.x) {
+        const int idx = base + threadIdx.x;
+        int cnt = 0;
+        if (idx < npairs) {
+            const int f = s_first[idx], n = s_first[idx + 1] - f;
+            cnt = n > 0 ? (f + n - 1) / tpc - f / tpc + 1 : 0;
+        }
+        int tot;
+        const int ex = block_exclusive_scan<int>(cnt, s_red, &tot);
+        if (idx < npairs) {
+            s_slot[idx] = nslots + ex;
+            if (c == 0) p.sk_table[idx] = make_int4(s_first[idx], s_first[idx + 1] - s_first[idx], nslots + ex, cnt);
+        }
+        nslots += tot;
+    }
+    __syncthreads();
+    const int lo = c * tpc, hi = min(total, lo + tpc);
+    if (lo >= hi) return;
+    const int ntl = hi - lo;  // tiles of this CTA
     const int R = p.chunk * p.ratio;
-    // Live query rows are [0, min(R, nvalid * ratio)); softmax warps whose
-    // 16 rows are all padding sit the loop out.
-    const int live_rows = min(R, nvalid * p.ratio);
-    const int nsoft = (live_rows + 15) / 16;
+    const int nsoft = (R + 15) / 16;
 
     uint8_t* sQ = smem;
     uint8_t* sKV = smem + L::kOffKV;
@@ -525,6 +591,9 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             mbar_init(&s_free[i], nsoft);
             mbar_init(&p_full[i], nsoft);
             mbar_init(&p_free[i], 1);
+            mbar_init(&q_full[i], nsoft);
+            mbar_init(&q_free[i], 1);
+            mbar_init(&o_free[i], nsoft);
         }
         fence_mbar_init();
     }
@@ -533,28 +602,20 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         tmem_relinquish();
     }
     if (warp < 4) {
-        // Rows 16*warp .. +15 of Q: lane l copies half (l / 16) of row
-        // 16*warp + l % 16 into the swizzled K-major tile (zero for padding
-        // rows); the P rows of rows that are not live stay zero.
+        // rows >= chunk*ratio stay zero in both Q buffers and all P matrices
         const int m = 16 * warp + (lane & 15), hq = lane >> 4;
-        const int j = m / p.ratio;
-        const bool live = m < R && j < nvalid;
-        const T* qrow = nullptr;
-        if (live)
-            qrow = reinterpret_cast<const T*>(p.q) + b * p.q_sb + j * p.q_sj + (g * p.ratio + m % p.ratio) * p.q_sh;
+        if (m >= R) {
 #pragma unroll
-        for (int c = hq * (HD / 16); c < (hq + 1) * (HD / 16); ++c) {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (live) v = make_uint4(ld_u32(qrow + 8 * c), ld_u32(qrow + 8 * c + 2), ld_u32(qrow + 8 * c + 4),
-                                     ld_u32(qrow + 8 * c + 6));
-            *reinterpret_cast<uint4*>(sQ + (c >> 3) * (kURows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4)) = v;
-        }
-        if (!live) {
+            for (int qb = 0; qb < 2; ++qb)
+#pragma unroll
+                for (int cc = hq * (HD / 16); cc < (hq + 1) * (HD / 16); ++cc)
+                    *reinterpret_cast<uint4*>(sQ + qb * L::kQ + (cc >> 3) * (kURows * 128) + m * 128 + (cc & 7) * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
             for (int mm = 0; mm < 4; ++mm)
 #pragma unroll
-                for (int c = 4 * hq; c < 4 * hq + 4; ++c)
-                    *reinterpret_cast<uint4*>(sP + mm * L::kP + m * 128 + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+                for (int cc = 4 * hq; cc < 4 * hq + 4; ++cc)
+                    *reinterpret_cast<uint4*>(sP + mm * L::kP + m * 128 + (cc << 4)) = make_uint4(0u, 0u, 0u, 0u);
         }
         fence_proxy_async_smem();
     }
@@ -568,17 +629,23 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
         int issued = 0;
         bool stop = false;
-        // Page-table lookups run 32 tiles ahead: lane l resolves the first
-        // token of every page of tile i0 + l before any of them is issued.
-        for (int i0 = 0; i0 < ntiles && !stop; i0 += 32) {
-            int tok[kUPages];
+        for (int i0 = 0; i0 < ntl && !stop; i0 += 32) {
+            // lane l resolves tile i0 + l: its kv head and the first token of each page
+            int tok[kUPages], head = 0;
 #pragma unroll
-            for (int u = 0; u < kUPages; ++u) {
-                tok[u] = 0;
-                const int ti = i0 + lane;
-                if (ti < ntiles) {
-                    int pg = pbeg + ti * kUPages + u;
-                    if (pg >= pend) pg = pbeg + ti * kUPages;  // pad a short tile with a real page; masked later
+            for (int u = 0; u < kUPages; ++u) tok[u] = 0;
+            if (i0 + lane < ntl) {
+                const int pos = lo + i0 + lane;
+                const int idx = sk_pair_of(s_first, npairs, pos);
+                const int b = idx / p.Hkv, tile = pos - s_first[idx];
+                head = idx % p.Hkv;
+                const int lmax = s_start[b] + s_nval[b];
+                const int npg = (lmax + kPage - 1) / kPage;
+                const int row = s_row[b];
+#pragma unroll
+                for (int u = 0; u < kUPages; ++u) {
+                    int pg = tile * kUPages + u;
+                    if (pg >= npg) pg = tile * kUPages;  // pad a short tile with a real page; masked later
                     if (p.dense) {
                         tok[u] = b * p.kv_len + pg * kPage;
                     } else {
@@ -588,13 +655,14 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                     }
                 }
             }
-            const int cnt = min(32, ntiles - i0);
+            const int cnt = min(32, ntl - i0);
             for (int k = 0; k < cnt; ++k) {
                 const int i = i0 + k;
                 const int st = i % kUNst;
                 int t0[kUPages];
 #pragma unroll
                 for (int u = 0; u < kUPages; ++u) t0[u] = __shfl_sync(0xffffffffu, tok[u], k);
+                const int gh = __shfl_sync(0xffffffffu, head, k);
                 int ok = 1;
                 if (i >= kUNst && lane == 0)
                     ok = mbar_wait_bounded(&kv_empty[st], ((i / kUNst) - 1) & 1, kWaitLimit) ? 1 : 0;
@@ -611,7 +679,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                     const int u = lane % kUPages, dd = (lane / kUPages) % DO, isv = lane / (kUPages * DO);
                     const int tu = u == 0 ? t0[0] : u == 1 ? t0[1] : u == 2 ? t0[2] : t0[3];
                     uint8_t* dst = sKV + st * L::kStage + (isv * DO + dd) * L::kHalf + u * kBoxBytes;
-                    tma_load_4d(dst, isv ? &tmv : &tmk, &kv_full[st], 0, dd, g, tu);
+                    tma_load_4d(dst, isv ? &tmv : &tmk, &kv_full[st], 0, dd, gh, tu);
                 }
                 __syncwarp();
                 issued = i + 1;
@@ -634,27 +702,45 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             const uint64_t dV = umma_desc_sw128(aKV + DO * L::kHalf, L::kHalf, 1024);
             int s_issued = 0, pv_issued = 0;
             bool ok = true;
+            // S cursor: pair and segment ordinal of the next S to issue
+            int s_idx = sk_pair_of(s_first, npairs, lo), s_seg = 0;
             auto issue_s = [&](int t) -> bool {
-                const int st = t % kUNst, sb = t & 1;
+                const int pos = lo + t;
+                if (pos >= s_first[s_idx + 1]) { s_idx = sk_pair_of(s_first, npairs, pos); ++s_seg; }
+                const int seg_last = min(hi, s_first[s_idx + 1]) - 1;  // last global tile of this segment
+                const int qb = s_seg & 1, st = t % kUNst, sb = t & 1;
+                if (pos == max(lo, s_first[s_idx]) &&
+                    !mbar_wait_bounded(&q_full[qb], (s_seg >> 1) & 1, kWaitLimit)) return false;
                 if (!mbar_wait_bounded(&kv_full[st], (t / kUNst) & 1, kWaitLimit)) return false;
                 if (t >= 2 && !mbar_wait_bounded(&s_free[sb], ((t - 2) >> 1) & 1, kWaitLimit)) return false;
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < SK; ++k) {
-                    const uint32_t qo = (k >> 2) * (kURows * 128) + (k & 3) * 32;
+                    const uint32_t qo = qb * L::kQ + (k >> 2) * (kURows * 128) + (k & 3) * 32;
                     const uint32_t ko = st * L::kStage + (k >> 2) * L::kHalf + (k & 3) * 32;
                     umma_f16(tmem + sb * kUTok, dQ + (qo >> 4), dK + (ko >> 4), kIdescS, k > 0 ? 1u : 0u);
                 }
                 umma_commit(&s_full[sb]);
+                if (pos == seg_last) umma_commit(&q_free[qb]);  // the segment's Q buffer may be refilled
                 s_issued = t + 1;
                 return true;
             };
+            int v_idx = s_idx, v_seg = 0;  // PV cursor
             ok = issue_s(0);
-            for (int i = 0; ok && i < ntiles; ++i) {
+            for (int i = 0; ok && i < ntl; ++i) {
                 if (*s_abort) { ok = false; break; }
-                if (i + 1 < ntiles && !issue_s(i + 1)) { ok = false; break; }
+                if (i + 1 < ntl && !issue_s(i + 1)) { ok = false; break; }
+                const int pos = lo + i;
+                if (pos >= s_first[v_idx + 1]) { v_idx = sk_pair_of(s_first, npairs, pos); ++v_seg; }
+                const bool first = pos == max(lo, s_first[v_idx]);
                 const int pb = i & 1, st = i % kUNst;
                 if (!mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kWaitLimit)) { ok = false; break; }
+                // O buffer v_seg & 1 was last read by the epilogue of segment v_seg - 2
+                const int ob = v_seg & 1;
+                if (first && v_seg >= 2 && !mbar_wait_bounded(&o_free[ob], ((v_seg - 2) >> 1) & 1, kWaitLimit)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
@@ -662,8 +748,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                     for (int k = 0; k < kUTok / 16; ++k) {
                         const uint32_t po = (2 * pb + h) * L::kP + k * 32;
                         const uint32_t vo = st * L::kStage + k * 2048;
-                        umma_f16(tmem + 2 * kUTok, dP + (po >> 4), dV + (vo >> 4), kIdescO,
-                                 (i > 0 || h > 0 || k > 0) ? 1u : 0u);
+                        umma_f16(tmem + kUOCol + ob * 128, dP + (po >> 4), dV + (vo >> 4), kIdescO,
+                                 (!first || h > 0 || k > 0) ? 1u : 0u);
                     }
                 umma_commit(&p_free[pb]);
                 umma_commit(&kv_empty[st]);
@@ -682,129 +768,183 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         pdl_launch_dependents();
     } else if (warp < nsoft) {
         // ------------------------------------------------------- softmax
-        const int hc = lane >> 4;                  // column half of S (and of O)
-        const int m = 16 * warp + (lane & 15);     // query row
-        const int j = m / p.ratio;
-        const bool live = m < R && j < nvalid;
-        const int lim = live ? start + j + 1 : 0;  // the row attends positions < lim
+        const int hc = lane >> 4;               // column half of S (and of O)
+        const int m = 16 * warp + (lane & 15);  // query row
+        const int jr = m / p.ratio, hl = m % p.ratio;
         const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        const int lim_eff = min(lim, pend * kPage);
-        float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
-        for (int i = 0; i < ntiles; ++i) {
-            const int sb = i & 1, pb = i & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], (i >> 1) & 1, kWaitLimit));
-            if (!ok || *s_abort) break;
-            tc_fence_after();
-            float sv[32];
-            __syncwarp();
-            tmem_ld16x2<32>(tmem + lane_base + sb * kUTok, reinterpret_cast<uint32_t*>(sv));
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[sb]);
 
-            // raw scores; positions at or past the row's limit are masked
-            const int c0 = (pbeg + i * kUPages) * kPage + 32 * hc;
-            if (c0 + 32 > lim_eff) {
+        // Q rows of a segment's pair into Q buffer qb (rows >= R stay zero):
+        // 16-byte async copies now, published to the MMA thread later.
+        auto issue_q = [&](int idx, int qb) {
+            const int b = idx / p.Hkv, head = idx % p.Hkv;
+            if (m < R) {
+                const bool live = jr < s_nval[b];
+                const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.q_sb + jr * p.q_sj +
+                                (head * p.ratio + hl) * p.q_sh;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) sv[c] = c0 + c < lim_eff ? sv[c] : -INFINITY;
-            }
-            float tmax = sv[0];
-#pragma unroll
-            for (int c = 1; c < 32; ++c) tmax = fmaxf(tmax, sv[c]);
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-            const float m_new = fmaxf(m_run, tmax * p.scale_log2);
-            const bool need = m_new > m_run + 8.f;
-            if (i > 0 && __any_sync(0xffffffffu, need)) {
-                // O is rescaled in place once PV(i-1) has landed
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait_bounded(&p_free[(i - 1) & 1], ((i - 1) >> 1) & 1, kWaitLimit));
-                if (!ok) break;
-                tc_fence_after();
-                const float alpha = need ? exp2f(m_run - m_new) : 1.f;
-#pragma unroll
-                for (int o0 = 0; o0 < OH; o0 += 32) {
-                    uint32_t o[32];
-                    __syncwarp();
-                    tmem_ld16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tmem_st16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
+                for (int cc = hc * (HD / 16); cc < (hc + 1) * (HD / 16); ++cc) {
+                    uint8_t* dst = sQ + qb * L::kQ + (cc >> 3) * (kURows * 128) + m * 128 + (((cc & 7) ^ (m & 7)) << 4);
+                    if (live) cp_async16(dst, qrow + 8 * cc);
+                    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
                 }
-                tmem_wait_st();
-                l_run *= alpha;
             }
-            if (need) m_run = m_new;
-            const float muse = m_run == -INFINITY ? 0.f : m_run;
-            if (i >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[pb], ((i - 2) >> 1) & 1, kWaitLimit));
-                if (!ok) break;
-            }
-            if (live) {
-                float lsum = 0.f;
-                uint8_t* ph = sP + (2 * pb) * L::kP + m * 128;
-                uint8_t* pl = sP + (2 * pb + 1) * L::kP + m * 128;
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float p0 = ex2_approx(fmaf(sv[8 * k + 2 * e], p.scale_log2, -muse));
-                        const float p1 = ex2_approx(fmaf(sv[8 * k + 2 * e + 1], p.scale_log2, -muse));
-                        lsum += p0 + p1;
-                        split_pair<T>(p0, p1, hw[e], lw[e]);
-                    }
-                    const int sw = ((4 * hc + k) ^ (m & 7)) << 4;
-                    *reinterpret_cast<uint4*>(ph + sw) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    *reinterpret_cast<uint4*>(pl + sw) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-                }
-                l_run += lsum;
-            }
+        };
+        auto publish_q = [&](int qb) {
+            cp_async_wait_all();
             fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_full[qb]);
+        };
+
+        int idx = sk_pair_of(s_first, npairs, lo), seg = 0;
+        issue_q(idx, 0);
+        publish_q(0);
+        int i = 0;
+        while (i < ntl && ok) {
+            // ---- one segment: tiles [seg_lo, seg_hi) of pair idx (global positions)
+            const int seg_lo = max(lo, s_first[idx]), seg_hi = min(hi, s_first[idx + 1]);
+            const int b = idx / p.Hkv, head = idx % p.Hkv;
+            const int start = s_start[b], nvalid = s_nval[b];
+            const int ob = seg & 1;  // O buffer of this segment
+            const bool live = m < R && jr < nvalid;
+            const int npg = (start + nvalid + kPage - 1) / kPage;
+            const int lim = live ? start + jr + 1 : 0;  // the row attends positions < lim
+            const int lim_eff = min(lim, npg * kPage);
+            const int tile0 = seg_lo - s_first[idx];    // first tile of the segment within the pair
+            // the next segment's Q goes into the other buffer once its last user is done
+            const bool stage_next = seg_hi < hi;
+            const int nqb = (seg + 1) & 1;
+            if (stage_next) {
+                if (seg + 1 >= 2)
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&q_free[nqb], ((seg - 1) >> 1) & 1, kWaitLimit));
+                if (!ok) break;
+                issue_q(sk_pair_of(s_first, npairs, seg_hi), nqb);
+            }
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int pos = seg_lo; pos < seg_hi; ++pos, ++i) {
+                const int sb = i & 1, pb = i & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], (i >> 1) & 1, kWaitLimit));
+                if (!ok || *s_abort) { ok = false; break; }
+                tc_fence_after();
+                float sv[32];
+                __syncwarp();
+                tmem_ld16x2<32>(tmem + lane_base + sb * kUTok, reinterpret_cast<uint32_t*>(sv));
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[sb]);
+
+                // raw scores; positions at or past the row's limit are masked
+                const int c0 = (tile0 + pos - seg_lo) * kUTok + 32 * hc;
+                if (c0 + 32 > lim_eff) {
+#pragma unroll
+                    for (int cc = 0; cc < 32; ++cc) sv[cc] = c0 + cc < lim_eff ? sv[cc] : -INFINITY;
+                }
+                float tmax = sv[0];
+#pragma unroll
+                for (int cc = 1; cc < 32; ++cc) tmax = fmaxf(tmax, sv[cc]);
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+                const float m_new = fmaxf(m_run, tmax * p.scale_log2);
+                const bool need = m_new > m_run + 8.f;
+                if (pos > seg_lo && __any_sync(0xffffffffu, need)) {
+                    // O is rescaled in place once PV(i-1) has landed
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait_bounded(&p_free[(i - 1) & 1], ((i - 1) >> 1) & 1, kWaitLimit));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const float alpha = need ? exp2f(m_run - m_new) : 1.f;
+#pragma unroll
+                    for (int o0 = 0; o0 < OH; o0 += 32) {
+                        uint32_t o[32];
+                        __syncwarp();
+                        tmem_ld16x2<OH>(tmem + lane_base + kUOCol + ob * 128 + o0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st16x2<OH>(tmem + lane_base + kUOCol + ob * 128 + o0, o);
+                    }
+                    tmem_wait_st();
+                    l_run *= alpha;
+                }
+                if (need) m_run = m_new;
+                const float muse = m_run == -INFINITY ? 0.f : m_run;
+                if (i >= 2) {
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[pb], ((i - 2) >> 1) & 1, kWaitLimit));
+                    if (!ok) break;
+                }
+                if (m < R) {
+                    float lsum = 0.f;
+                    uint8_t* ph = sP + (2 * pb) * L::kP + m * 128;
+                    uint8_t* pl = sP + (2 * pb + 1) * L::kP + m * 128;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t hw[4], lw[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float p0 = ex2_approx(fmaf(sv[8 * k + 2 * e], p.scale_log2, -muse));
+                            const float p1 = ex2_approx(fmaf(sv[8 * k + 2 * e + 1], p.scale_log2, -muse));
+                            lsum += p0 + p1;
+                            split_pair<T>(p0, p1, hw[e], lw[e]);
+                        }
+                        const int sw = ((4 * hc + k) ^ (m & 7)) << 4;
+                        *reinterpret_cast<uint4*>(ph + sw) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                        *reinterpret_cast<uint4*>(pl + sw) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    }
+                    l_run += lsum;
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[pb]);
+                if (stage_next && pos == seg_lo) publish_q(nqb);  // after the segment's first tile
+            }
+            if (!ok) break;
+            // ---- segment epilogue
+            const float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
+            const int last = i - 1;
+            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[last & 1], (last >> 1) & 1, kWaitLimit));
+            if (!ok) break;
+            tc_fence_after();
+            const int f = s_first[idx], n = s_first[idx + 1] - f;
+            const bool whole = (f / tpc == c) && ((f + n - 1) / tpc == c);  // this CTA owns the pair
+            const int slot = s_slot[idx] + (c - f / tpc);
+            const int h = head * p.ratio + hl;
+            const int64_t part = (int64_t)slot * R + m;
+            const float inv = 1.f / l_tot;
+#pragma unroll
+            for (int o0 = 0; o0 < OH; o0 += 32) {
+                uint32_t o[32];
+                __syncwarp();  // TMEM loads are warp-collective: converge first
+                tmem_ld16x2<OH>(tmem + lane_base + kUOCol + ob * 128 + o0, o);
+                tmem_wait_ld();
+                const int d0 = hc * OH + o0;
+                if (live && whole) {
+                    const int64_t ob = b * p.o_sb + jr * p.o_sj + h * p.o_sh + d0;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) store_from_f32(p.out, ob + e, p.out_dtype, __uint_as_float(o[e]) * inv);
+                } else if (m < R && !whole) {
+                    float4* dst = reinterpret_cast<float4*>(p.o_part + part * HD + d0);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                             __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+                }
+            }
+            if (m < R && !whole && hc == 0) {
+                p.ml_part[part * 2] = m_run;
+                p.ml_part[part * 2 + 1] = l_tot;
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[pb]);
+            if (lane == 0) mbar_arrive(&o_free[ob]);
+            // next segment
+            if (seg_hi < hi) {
+                idx = sk_pair_of(s_first, npairs, seg_hi);
+                ++seg;
+            }
         }
         pdl_launch_dependents();
-        const float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
-        if (ok && !*s_abort) {
-            const int last = ntiles - 1;
-            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&p_free[last & 1], (last >> 1) & 1, kWaitLimit));
-            tc_fence_after();
-            if (ok) {
-                const int L_row = start + j + 1;
-                const int ns_row = ((L_row + kPage - 1) / kPage + p.pps - 1) / p.pps;
-                const bool write = live && split < ns_row;
-                const int h = g * p.ratio + m % p.ratio;
-                const int64_t idx = (((int64_t)b * p.nsplit + split) * p.chunk + j) * p.Hq + h;
-                const float inv = 1.f / l_tot;
-#pragma unroll
-                for (int o0 = 0; o0 < OH; o0 += 32) {
-                    uint32_t o[32];
-                    __syncwarp();  // TMEM loads are warp-collective: converge first
-                    tmem_ld16x2<OH>(tmem + lane_base + 2 * kUTok + o0, o);
-                    tmem_wait_ld();
-                    const int d0 = hc * OH + o0;
-                    if (write && ns_row == 1) {
-                        const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + d0;
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) store_from_f32(p.out, ob + e, p.out_dtype, __uint_as_float(o[e]) * inv);
-                    } else if (write) {
-                        float4* dst = reinterpret_cast<float4*>(p.o_part + idx * HD + d0);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
-                                                 __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
-                    }
-                }
-                if (write && ns_row > 1 && hc == 0) {
-                    p.ml_part[idx * 2] = m_run;
-                    p.ml_part[idx * 2 + 1] = l_tot;
-                }
-            }
-        }
         if (!ok && lane == 0) {
             sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
             *s_abort = 1;
@@ -814,6 +954,53 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     if (warp == kUMma) tmem_dealloc(tmem, kUTmemCols);
+}
+
+// Merge the partials of pairs split across CTAs: one warp per (pair, query
+// row), lanes reduce the slot maxima and sums, then own 4 head dims each.
+__global__ void __launch_bounds__(128) attn_sk_combine_kernel(TcParams p, int hd) {
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = p.chunk * p.ratio;
+    const int wr = blockIdx.x * 4 + warp;
+    if (wr >= p.B * p.Hkv * R) return;
+    const int idx = wr / R, m = wr % R;
+    const int4 t = p.sk_table[idx];
+    const int cnt = t.w;
+    if (cnt <= 1) return;
+    const int b = idx / p.Hkv, head = idx % p.Hkv;
+    const int j = m / p.ratio, h = head * p.ratio + m % p.ratio;
+    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
+    if (j >= nvalid) return;
+    const int64_t base = (int64_t)t.z * R + m;  // partial of slot t.z, row m
+    float M = -INFINITY;
+    for (int s = lane; s < cnt; s += 32) M = fmaxf(M, p.ml_part[(base + (int64_t)s * R) * 2]);
+    M = warp_max(M);
+    float den = 0.f;
+    for (int s = lane; s < cnt; s += 32) {
+        const float* ml = p.ml_part + (base + (int64_t)s * R) * 2;
+        den += ml[0] == -INFINITY ? 0.f : exp2f(ml[0] - M) * ml[1];
+    }
+    den = warp_sum(den);
+    const float inv = 1.f / den;
+    const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh;
+    for (int d0 = lane * 4; d0 < hd; d0 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < cnt; ++s) {
+            const int64_t row = base + (int64_t)s * R;
+            const float mv = p.ml_part[row * 2];
+            const float wt = mv == -INFINITY ? 0.f : exp2f(mv - M);
+            const float4 o = *reinterpret_cast<const float4*>(p.o_part + row * hd + d0);
+            acc.x += wt * o.x;
+            acc.y += wt * o.y;
+            acc.z += wt * o.z;
+            acc.w += wt * o.w;
+        }
+        store_from_f32(p.out, ob + d0, p.out_dtype, acc.x * inv);
+        store_from_f32(p.out, ob + d0 + 1, p.out_dtype, acc.y * inv);
+        store_from_f32(p.out, ob + d0 + 2, p.out_dtype, acc.z * inv);
+        store_from_f32(p.out, ob + d0 + 3, p.out_dtype, acc.w * inv);
+    }
 }
 
 // ------------------------------------------------------------ generic path
@@ -980,14 +1167,20 @@ bool tc_applicable(const sdl_attn_args* a) {
     return true;
 }
 
-// The tcgen05 kernel takes row blocks of up to 64 query rows per kv head.
-// It runs when asked for (use_umma = 1); the automatic plan keeps the
-// mma.sync kernel, which is faster on the C2/C3 shapes as measured so far.
+// The persistent tcgen05 kernel takes row blocks of up to 64 query rows per
+// kv head and up to 512 (sequence, kv head) pairs.  It runs when asked for
+// (use_umma = 1); the automatic plan keeps the mma.sync kernel.
 bool umma_applicable(const sdl_attn_args* a) {
     if (a->use_umma <= 0 || !tc_applicable(a)) return false;
+    // Q rows are staged with 16-byte async copies
+    if (((a->q_sb | a->q_sj | a->q_sh) & 7) || reinterpret_cast<uintptr_t>(a->q) % 16) return false;
     const int rows = a->chunk * (a->Hq / a->Hkv);
-    return rows <= kURows;
+    return rows <= kURows && (long)a->B * a->Hkv <= kSkMaxPairs;
 }
+
+// Workspace of the persistent kernel: the per-pair table, then fp32 partials
+// for at most (grid + pairs) slots of chunk*ratio rows.
+size_t sk_header_bytes(int npairs) { return ((size_t)npairs * sizeof(int4) + 255) & ~size_t(255); }
 
 Plan make_umma_plan(const sdl_attn_args* a) {
     Plan pl;
@@ -995,19 +1188,12 @@ Plan make_umma_plan(const sdl_attn_args* a) {
     pl.umma = true;
     pl.smem = (a->head_dim == 128 ? USmem<128>::kBytes : USmem<64>::kBytes) + 1024;
     const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
-    const long base_ctas = (long)a->B * a->Hkv;  // one CTA per SM: aim for about two waves
-    const long target = (long)sm_count() * 2;
-    const int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
-    auto round_tile = [](int x) { return (x + kUPages - 1) / kUPages * kUPages; };
-    int pps = a->pages_per_split > 0 ? round_tile(a->pages_per_split)
-                                     : std::max(2 * kUPages, round_tile((max_pages + nsplit_target - 1) / nsplit_target));
-    for (;;) {
-        pl.pps = pps;
-        pl.nsplit = (max_pages + pps - 1) / pps;
-        pl.ws_bytes = pl.nsplit > 1 ? (size_t)a->B * pl.nsplit * a->chunk * a->Hq * (a->head_dim + 2) * sizeof(float) : 0;
-        if (a->pages_per_split > 0 || pl.ws_bytes <= a->workspace_bytes || pl.nsplit == 1 || !a->workspace) break;
-        pps *= 2;
-    }
+    const long tiles_upper = (long)a->B * a->Hkv * ((max_pages + kUPages - 1) / kUPages);
+    pl.nsplit = (int)std::max(1L, std::min<long>(sm_count(), tiles_upper));  // persistent grid
+    pl.pps = kUPages;
+    const int npairs = a->B * a->Hkv;
+    const int rows = a->chunk * (a->Hq / a->Hkv);
+    pl.ws_bytes = sk_header_bytes(npairs) + (size_t)(pl.nsplit + npairs) * rows * (a->head_dim + 2) * sizeof(float);
     return pl;
 }
 
@@ -1077,17 +1263,21 @@ int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams&
 
 template <int HD, typename T>
 int launch_umma_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl, cudaStream_t st) {
-    auto kern = attn_umma_kernel<HD, T>;
+    auto kern = attn_sk_kernel<HD, T>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
         if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
         configured = true;
     }
-    dim3 grid(pl.nsplit, tp.Hkv, tp.B);
-    cudaError_t e = sdl::launch_pdl(kern, grid, dim3(kUThreads), pl.smem, st, mk, mv, tp);
+    cudaError_t e = sdl::launch_pdl(kern, dim3(pl.nsplit), dim3(kUThreads), pl.smem, st, mk, mv, tp);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
-    return sdl::check_launch("attn_umma_kernel");
+    int rc = sdl::check_launch("attn_sk_kernel");
+    if (rc != SDL_OK) return rc;
+    const int rows = tp.B * tp.Hkv * tp.chunk * tp.ratio;
+    e = sdl::launch_pdl(attn_sk_combine_kernel, dim3((rows + 3) / 4), dim3(128), 0, st, tp, HD);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("attn_sk_combine_kernel");
 }
 
 template <typename T>
@@ -1155,7 +1345,7 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     const int ratio = a->Hq / a->Hkv;
     Plan pl = make_plan(a);
     if (pl.tc) {
-        if (pl.nsplit > 1 && (!a->workspace || a->workspace_bytes < pl.ws_bytes))
+        if (pl.ws_bytes > 0 && (!a->workspace || a->workspace_bytes < pl.ws_bytes))
             return sdl::fail(SDL_ERR_WORKSPACE, "sdl_paged_attention: workspace too small");
         CUtensorMap mk, mv;
         if (a->k_pool) {
@@ -1185,6 +1375,14 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.scale_log2 = a->scale * 1.4426950408889634f;
         tp.o_part = a->workspace;
         tp.ml_part = a->workspace ? a->workspace + (size_t)a->B * pl.nsplit * a->chunk * a->Hq * a->head_dim : nullptr;
+        tp.sk_table = nullptr;
+        if (pl.umma) {
+            const int npairs = a->B * a->Hkv;
+            const size_t slots = (size_t)(pl.nsplit + npairs) * a->chunk * ratio;
+            tp.sk_table = reinterpret_cast<int4*>(a->workspace);
+            tp.o_part = a->workspace + sk_header_bytes(npairs) / sizeof(float);
+            tp.ml_part = tp.o_part + slots * a->head_dim;
+        }
         tp.err = a->err;
         if (pl.umma) {
             if (a->dtype == SDL_BF16) rc = launch_umma_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
@@ -1195,7 +1393,7 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
             rc = launch_tc_dtype<__half>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
         }
         if (rc != SDL_OK) return rc;
-        if (pl.nsplit > 1) {
+        if (pl.nsplit > 1 && !pl.umma) {
             const int rows = a->B * a->chunk * a->Hq;
             cudaError_t e = sdl::launch_pdl(attn_combine_kernel, dim3((rows + 3) / 4), dim3(128), 0, st, tp,
                                             (int)a->head_dim);
