@@ -299,6 +299,8 @@ def run_gpu(args, rank: int, world: int, device):
     from engine.workloads import c2_layout
 
     c = dict(C2)
+    umma = 1 if args.attn_kernel == "tcgen05" else 0
+    fused = args.append == "fused"
     L = args.layers
     B = args.batch
     Hq, Hkv, d, bs = c["q_heads"], c["kv_heads"], c["head_dim"], c["block_size"]
@@ -329,9 +331,13 @@ def run_gpu(args, rank: int, world: int, device):
 
     def step_layers(with_append=True):
         for layer in range(L):
+            if with_append and fused:  # store the new K/V row inside the attention launch
+                paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma, k_new=knew[layer],
+                                v_new=vnew[layer])
+                continue
             if with_append:
                 kv.append(layer, slots_static, knew[layer], vnew[layer])
-            paged_attention(q[layer], kv, layer, batch, out=out[layer])
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma)
 
     # warm up every code path once outside capture (attributes, workspace)
     slots_static.copy_(kv.reserve(sids, ctx, [1] * B))
@@ -342,8 +348,8 @@ def run_gpu(args, rank: int, world: int, device):
     with torch.cuda.graph(graph):  # captured on torch's side stream, replayed on `stream`
         step_layers()
     attn_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(attn_graph):
-        step_layers(with_append=False)
+    with torch.cuda.graph(attn_graph):  # the attention op as the step launches it
+        step_layers(with_append=fused)
     torch.cuda.synchronize(device)
 
     def device_step():
@@ -405,8 +411,12 @@ def run_gpu(args, rank: int, world: int, device):
         b2 = AttnBatch.from_lists(device, sids, ctx, 1)
         od = torch.empty_like(out)
         for layer in range(L):
-            kv.append(layer, slots, kd[layer], vd[layer])
-            paged_attention(qd[layer], kv, layer, b2, out=od[layer])
+            if fused:
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma, k_new=kd[layer],
+                                v_new=vd[layer])
+            else:
+                kv.append(layer, slots, kd[layer], vd[layer])
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma)
         o_h.copy_(od, non_blocking=True)
         kv.release(sids, ctx, rel_flags)
 
@@ -429,7 +439,11 @@ def run_gpu(args, rank: int, world: int, device):
         raise RuntimeError("e2e outputs differ from the graph path")
 
     attn_bytes = sum((x + 1) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * Hq * d * 2 + sum(-(-(x + 1) // bs) * 4 for x in ctx)
-    per_layer = 1 + attention_launches(q[0], kv, batch)  # append + attention (+ split merge)
+    if fused:  # the op also reads the new K/V rows and writes them into their pages
+        attn_bytes += 2 * (B * 2 * Hkv * d * 2)
+        per_layer = attention_launches(q[0], kv, batch, use_umma=umma, k_new=knew[0], v_new=vnew[0])
+    else:
+        per_layer = 1 + attention_launches(q[0], kv, batch, use_umma=umma)  # append + attention (+ merge)
     launches_per_step = 2 + L * per_layer  # + reserve + release
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms], device=device)
@@ -453,6 +467,8 @@ def run_gpu_c3(args, rank: int, world: int, device):
     from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample_logits
 
     c = dict(C3)
+    umma = 1 if args.attn_kernel == "tcgen05" else 0
+    fused = args.append == "fused"
     L, B, gam = args.layers, args.batch, c["gamma"]
     chunk = gam + 1
     Hq, Hkv, d, bs, V, T = c["q_heads"], c["kv_heads"], c["head_dim"], c["block_size"], c["vocab"], c["temperature"]
@@ -494,9 +510,13 @@ def run_gpu_c3(args, rank: int, world: int, device):
 
     def verify_layers(with_append=True):
         for layer in range(L):
+            if with_append and fused:  # store the round's K/V rows inside the attention launch
+                paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma, k_new=knew[layer],
+                                v_new=vnew[layer])
+                continue
             if with_append:
                 kv.append(layer, slots_static, knew[layer], vnew[layer])
-            paged_attention(q[layer], kv, layer, batch, out=out[layer])
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma)
 
     def sample_commit():
         spec_sample_logits(p_logits, q_logits, T, proposals, ustream, err=kv.err_word, out=(tokens, n_out))
@@ -514,8 +534,8 @@ def run_gpu_c3(args, rank: int, world: int, device):
     with torch.cuda.graph(graph):
         verify_layers()
     attn_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(attn_graph):
-        verify_layers(with_append=False)
+    with torch.cuda.graph(attn_graph):  # the attention op as the step launches it
+        verify_layers(with_append=fused)
     torch.cuda.synchronize(device)
 
     k_hist = torch.zeros((args.steps, B), dtype=torch.int32, device=device)
@@ -601,8 +621,12 @@ def run_gpu_c3(args, rank: int, world: int, device):
         b2 = AttnBatch.from_lists(device, sids, ctx, chunk)
         od = torch.empty_like(out)
         for layer in range(L):
-            kv.append(layer, slots, kd[layer], vd[layer])
-            paged_attention(qd[layer], kv, layer, b2, out=od[layer])
+            if fused:
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma, k_new=kd[layer],
+                                v_new=vd[layer])
+            else:
+                kv.append(layer, slots, kd[layer], vd[layer])
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma)
         toks, no = spec_sample_logits(pld, qld, T, prd, ustream, err=kv.err_word)
         _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), no.data_ptr(), toks.data_ptr(), chunk,
                                        packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
@@ -631,7 +655,11 @@ def run_gpu_c3(args, rank: int, world: int, device):
                   + sum(-(-(x + chunk) // bs) * 4 for x in ctx))
     samp_bytes = B * (2 * gam + 1) * V * 4  # the fp32 logit rows of p and q, each read once
     launches_sampler = 4  # statistics, accept walk, draw sums, draw
-    per_layer = 1 + attention_launches(q[0], kv, batch)
+    if fused:  # the op also reads the new K/V rows and writes them into their pages
+        attn_bytes += 2 * (B * chunk * 2 * Hkv * d * 2)
+        per_layer = attention_launches(q[0], kv, batch, use_umma=umma, k_new=knew[0], v_new=vnew[0])
+    else:
+        per_layer = 1 + attention_launches(q[0], kv, batch, use_umma=umma)
     launches_per_step = 1 + L * per_layer + launches_sampler + 1  # reserve, layers, sampler, commit
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms, samp_ms], device=device)
@@ -653,6 +681,11 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--attn-kernel", choices=["mma", "tcgen05"], default="mma",
+                    help="paged attention on the mma.sync kernel (default) or the persistent tcgen05 kernel")
+    ap.add_argument("--append", choices=["fused", "separate"], default="fused",
+                    help="store each layer's new K/V rows inside the attention launch (default) or with a "
+                         "separate append launch before it")
     ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
                     help="c2: decode attention + KV append (default); c3: verify step at gamma=5")
     ap.add_argument("--layers", type=int, default=28, help="fewer layers only for profiling captures")
@@ -677,7 +710,8 @@ def main(argv=None) -> int:
            "ctx": "U[{},{}] seeded per rank".format(C2["ctx_lo"], C2["ctx_hi"]),
            "block_tables": "random permutation of a pool holding every context",
            "l2": "no flush needed: each attention launch reads ~151 MB of K/V (> 126 MB L2), layers disjoint",
-           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world)}
+           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
+           "attention_kernel": args.attn_kernel, "kv_append": args.append}
 
     if args.impl == "reference":
         if rank != 0:
@@ -744,15 +778,20 @@ def main(argv=None) -> int:
         "data": "synthetic (seeded N(0,1) Q/K/V, U[512,4096] contexts, random-permutation block tables)",
         "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": C2_ATTN_TRAFFIC if args.layers == 28 else None,
+                     "frac": round(achieved / hbm, 4),
+                     "traffic": C2_ATTN_TRAFFIC if args.layers == 28 and args.attn_kernel == "mma" else None,
                      "traffic_source": "ncu --set full capture of attn_tc_kernel on this workload (dram read + "
                                        "write per launch, main kernel only; summary under profiles/)",
-                     "kernel": "attn_tc_kernel + attn_combine_kernel (one paged decode attention op per layer)",
+                     "kernel": ("attn_tc_kernel + attn_combine_kernel" if args.attn_kernel == "mma" else
+                                "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
+                               " (one paged decode attention op per layer{})".format(
+                                   ", new K/V row stored inside it" if args.append == "fused" else ""),
                      "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
         "e2e": {"value": round(args.batch * world / (res["e2e_ms"] * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
-                "path": "public per-layer API (PagedKVCache.reserve/append/release + paged_attention), pinned host I/O"},
+                "path": "public per-layer API (PagedKVCache.reserve/release + paged_attention{}), pinned host I/O".format(
+                    " with k_new/v_new" if args.append == "fused" else " after PagedKVCache.append")},
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],
     }
@@ -775,7 +814,8 @@ def main_c3(args) -> int:
            "logits": "N(0, 2) fp32, target gamma+1 rows and draft gamma rows per sequence",
            "block_tables": "random permutation of a pool holding every context",
            "l2": "no flush needed: a step streams ~1.06 GB of K/V over 28 disjoint layers and 214 MB of logits",
-           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world)}
+           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
+           "attention_kernel": args.attn_kernel, "kv_append": args.append}
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -844,7 +884,10 @@ def main_c3(args) -> int:
         "tokens_per_round": round(res["tokens_per_round"], 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
-                     "kernel": "attn_tc_kernel (+ attn_combine_kernel when split): (gamma+1)-row verify attention",
+                     "kernel": ("attn_tc_kernel (+ attn_combine_kernel when split)" if args.attn_kernel == "mma" else
+                                "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
+                               ": (gamma+1)-row verify attention{}".format(
+                                   ", new K/V rows stored inside it" if args.append == "fused" else ""),
                      "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
         "sampler": {"achieved": round(samp_gbs, 1), "unit": "GB/s", "frac": round(samp_gbs / hbm, 4),
@@ -853,8 +896,9 @@ def main_c3(args) -> int:
                                "(sdl_spec_sample_logits)"},
         "e2e": {"value": round(res["e2e_committed"] / (res["e2e_steps"] * res["e2e_ms"] * 1e-3), 2),
                 "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
-                "path": "public API (PagedKVCache.reserve/append, paged_attention, spec_sample_logits, "
-                        "sdl_spec_commit), pinned host Q/K/V, logits and proposals in, tokens and accept lengths out"},
+                "path": "public API (PagedKVCache.reserve, paged_attention {}, spec_sample_logits, "
+                        "sdl_spec_commit), pinned host Q/K/V, logits and proposals in, tokens and accept lengths "
+                        "out".format("with k_new/v_new" if args.append == "fused" else "after PagedKVCache.append")},
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],
     }

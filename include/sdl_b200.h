@@ -192,12 +192,29 @@ typedef struct sdl_attn_args {
     int32_t use_umma;         /* 1 = the tcgen05 kernel where it applies
                                  (up to 64 query rows per kv head);
                                  0 / -1 = the mma.sync kernel              */
+    /* Fused K/V append (paged pools only): when k_new != NULL the rows
+     * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
+     * elements, the pool's dtype) are stored at positions starts[b] + j
+     * (j below the valid rows) before attending -- the write-then-attend of
+     * engine/model.py:143-149 in one call.  The positions' blocks must be
+     * reserved already.  The mma.sync kernel writes them itself; other paths
+     * launch a small append kernel first. */
+    const void* k_new;
+    const void* v_new;
+    int64_t new_row_stride;
     int32_t* err;
 } sdl_attn_args;
 
 /* Bytes of workspace sdl_paged_attention needs for `args` (0 when one
  * split per row suffices). */
 size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
+
+/* Kernel launches sdl_paged_attention makes for `args` with a workspace of
+ * sdl_attention_workspace_bytes(args): the attention kernel, the split-K
+ * merge when the plan splits, and the positional append when k_new is set on
+ * a path that does not write inside the attention kernel.  -1 when `args`
+ * is invalid.  No counterpart in the reference. */
+int sdl_attention_launches(const sdl_attn_args* args);
 
 /* Paged / dense attention for decode, verify (extend) and prefill rows. */
 int sdl_paged_attention(const sdl_attn_args* args, void* stream);

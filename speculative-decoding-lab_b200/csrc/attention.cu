@@ -59,6 +59,13 @@ struct TcParams {
     float* o_part;
     float* ml_part;
     int4* sk_table;  // persistent tcgen05 kernel: per (sequence, kv head) {first tile, tiles, slot, slots}
+    // fused K/V append (mma.sync kernel): new rows [B*chunk][Hkv][d] written at
+    // positions starts[b] + j before they are attended; NULL = no append
+    char* k_pool;
+    char* v_pool;
+    const char* k_new;
+    const char* v_new;
+    int64_t new_stride;  // bytes between consecutive new rows
     int32_t* err;
 };
 
@@ -116,6 +123,35 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     if (warp == ncons) {
         // ------------------------------------------------------- producer
         if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
+        if (p.k_new != nullptr) {
+            // Fused append: every new row whose page lies in this CTA's range is
+            // written for this CTA's kv heads (CTAs sharing a page write the same
+            // bytes), then made visible to this CTA's own TMA reads.
+            constexpr int kChunks = HD * (int)sizeof(T) / 16;  // 16-byte pieces of one head row
+            const int row_bytes = p.Hkv * HD * (int)sizeof(T);
+            for (int j = 0; j < nvalid; ++j) {
+                const int pos = start + j, pg = pos / kPage;
+                if (pg < pbeg || pg >= pend) continue;
+                const int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+                if (phys < 0 || phys >= p.capacity) {
+                    if (lane == 0) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+                    continue;
+                }
+                const int64_t dst_row = ((int64_t)(p.layer * p.capacity + phys) * kPage + pos % kPage) * row_bytes;
+                const int64_t src_row = ((int64_t)b * p.chunk + j) * p.new_stride;
+                for (int gi = 0; gi < p.g_cta; ++gi) {
+                    const int hoff = (kvgrp * p.g_cta + gi) * HD * (int)sizeof(T);
+                    if (lane < 2 * kChunks) {
+                        const bool isv = lane >= kChunks;
+                        const int cb = (lane % kChunks) * 16;
+                        const uint4 v = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) + src_row + hoff + cb);
+                        *reinterpret_cast<uint4*>((isv ? p.v_pool : p.k_pool) + dst_row + hoff + cb) = v;
+                    }
+                }
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __syncwarp();
+        }
         int issued = 0;
         bool stop = false;
         for (int i0 = 0; i0 < np && !stop; i0 += 32) {
@@ -1003,6 +1039,33 @@ __global__ void __launch_bounds__(128) attn_sk_combine_kernel(TcParams p, int hd
     }
 }
 
+// ------------------------------------------------------ positional append
+// New K/V rows [B*chunk][Hkv*d] stored at positions starts[b] + j (j below the
+// valid rows) of each sequence's pages: the append half of a fused call on
+// the paths that do not write inside the attention kernel.  One warp per row.
+__global__ void __launch_bounds__(128) kv_append_pos_kernel(TcParams p, int row_bytes, int bs) {
+    const int r = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= p.B * p.chunk) return;
+    const int b = r / p.chunk, j = r % p.chunk;
+    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
+    if (j >= nvalid) return;
+    const int pos = p.starts[b] + j;
+    if (pos < 0) return;
+    const int pg = pos / bs;
+    const int row = p.rows[b];
+    const int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+    if (phys < 0 || phys >= p.capacity) {
+        if (lane == 0) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+        return;
+    }
+    const int64_t dst = ((int64_t)(p.layer * p.capacity + phys) * bs + pos % bs) * row_bytes;
+    const int64_t src = (int64_t)r * p.new_stride;
+    for (int o = lane * 4; o < row_bytes; o += 128) {
+        *reinterpret_cast<uint32_t*>(p.k_pool + dst + o) = *reinterpret_cast<const uint32_t*>(p.k_new + src + o);
+        *reinterpret_cast<uint32_t*>(p.v_pool + dst + o) = *reinterpret_cast<const uint32_t*>(p.v_new + src + o);
+    }
+}
+
 // ------------------------------------------------------------ generic path
 struct GenParams {
     const void* q;
@@ -1312,7 +1375,41 @@ int validate(const sdl_attn_args* a) {
         if (!a->k_dense || !a->v_dense || a->kv_len < 1)
             return sdl::fail(SDL_ERR_INVALID, "sdl_paged_attention: bad dense K/V arguments");
     }
+    if (a->k_new) {
+        const int es = sdl::dtype_bytes(a->dtype);
+        const int64_t sb = a->new_row_stride * es;
+        if (!a->k_pool || !a->v_new || a->new_row_stride < (int64_t)a->Hkv * a->head_dim || sb % 4 ||
+            reinterpret_cast<uintptr_t>(a->k_new) % 4 || reinterpret_cast<uintptr_t>(a->v_new) % 4 ||
+            reinterpret_cast<uintptr_t>(a->k_pool) % 4 || reinterpret_cast<uintptr_t>(a->v_pool) % 4 ||
+            ((int64_t)a->Hkv * a->head_dim * es) % 4)
+            return sdl::fail(SDL_ERR_INVALID, "sdl_paged_attention: bad fused-append arguments (k_new/v_new need a "
+                                              "paged pool, rows of at least Hkv*head_dim and 4-byte alignment)");
+    }
     return SDL_OK;
+}
+
+// Whether the mma.sync kernel writes the new K/V rows itself (16-byte pieces).
+bool append_fusable(const sdl_attn_args* a) {
+    const int64_t sb = a->new_row_stride * sdl::dtype_bytes(a->dtype);
+    auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    return a->k_new && al16(a->k_new) && al16(a->v_new) && al16(a->k_pool) && al16(a->v_pool) && sb % 16 == 0;
+}
+
+// Separate positional append (paths that do not write inside the kernel).
+int launch_append_pos(const sdl_attn_args* a, cudaStream_t st) {
+    TcParams tp = {};
+    tp.B = a->B; tp.chunk = a->chunk; tp.valid_rows = a->valid_rows; tp.starts = a->starts; tp.rows = a->rows;
+    tp.table = a->block_table; tp.width = a->width; tp.capacity = a->capacity; tp.layer = a->layer;
+    tp.k_pool = static_cast<char*>(const_cast<void*>(a->k_pool));
+    tp.v_pool = static_cast<char*>(const_cast<void*>(a->v_pool));
+    tp.k_new = static_cast<const char*>(a->k_new);
+    tp.v_new = static_cast<const char*>(a->v_new);
+    const int es = sdl::dtype_bytes(a->dtype);
+    tp.new_stride = a->new_row_stride * es;
+    tp.err = a->err;
+    const int rows = a->B * a->chunk;
+    kv_append_pos_kernel<<<(rows + 3) / 4, 128, 0, st>>>(tp, a->Hkv * a->head_dim * es, a->block_size);
+    return sdl::check_launch("kv_append_pos_kernel");
 }
 
 }  // namespace
@@ -1337,6 +1434,19 @@ extern "C" size_t sdl_attention_workspace_bytes(const sdl_attn_args* args) {
     return make_plan(&tmp).ws_bytes;
 }
 
+extern "C" int sdl_attention_launches(const sdl_attn_args* args) {
+    if (validate(args) != SDL_OK) return -1;
+    if (args->B == 0) return 0;
+    sdl_attn_args tmp = *args;
+    tmp.workspace = nullptr;
+    tmp.workspace_bytes = 0;
+    const Plan pl = make_plan(&tmp);
+    const bool fused_append = tmp.k_new && pl.tc && !pl.umma && append_fusable(&tmp);
+    int n = (tmp.k_new && !fused_append) ? 1 : 0;
+    if (!pl.tc) return n + 1;
+    return n + 1 + ((pl.umma || pl.nsplit > 1) ? 1 : 0);
+}
+
 extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     int rc = validate(a);
     if (rc != SDL_OK) return rc;
@@ -1344,6 +1454,8 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     cudaStream_t st = sdl::as_stream(stream);
     const int ratio = a->Hq / a->Hkv;
     Plan pl = make_plan(a);
+    const bool fused_append = a->k_new && pl.tc && !pl.umma && append_fusable(a);
+    if (a->k_new && !fused_append && (rc = launch_append_pos(a, st)) != SDL_OK) return rc;
     if (pl.tc) {
         if (pl.ws_bytes > 0 && (!a->workspace || a->workspace_bytes < pl.ws_bytes))
             return sdl::fail(SDL_ERR_WORKSPACE, "sdl_paged_attention: workspace too small");
@@ -1376,6 +1488,16 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.o_part = a->workspace;
         tp.ml_part = a->workspace ? a->workspace + (size_t)a->B * pl.nsplit * a->chunk * a->Hq * a->head_dim : nullptr;
         tp.sk_table = nullptr;
+        tp.k_pool = tp.v_pool = nullptr;
+        tp.k_new = tp.v_new = nullptr;
+        tp.new_stride = 0;
+        if (fused_append) {
+            tp.k_pool = static_cast<char*>(const_cast<void*>(a->k_pool));
+            tp.v_pool = static_cast<char*>(const_cast<void*>(a->v_pool));
+            tp.k_new = static_cast<const char*>(a->k_new);
+            tp.v_new = static_cast<const char*>(a->v_new);
+            tp.new_stride = a->new_row_stride * sdl::dtype_bytes(a->dtype);
+        }
         if (pl.umma) {
             const int npairs = a->B * a->Hkv;
             const size_t slots = (size_t)(pl.nsplit + npairs) * a->chunk * ratio;

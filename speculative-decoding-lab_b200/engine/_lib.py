@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "sdl_spec_commit",
     "sdl_make_kv_tensor_map",
     "sdl_attention_workspace_bytes",
+    "sdl_attention_launches",
     "sdl_paged_attention",
     "sdl_paged_attention_noalloc",
     "sdl_noalloc_scratch_bytes",
@@ -113,6 +114,9 @@ class SdlAttnArgs(ctypes.Structure):
         ("force_generic", c_int),
         ("kv_heads_per_cta", c_int),
         ("use_umma", c_int),
+        ("k_new", c_void),
+        ("v_new", c_void),
+        ("new_row_stride", c_i64),
         ("err", c_void),
     ]
 
@@ -133,6 +137,7 @@ _SIGS = {
                                 c_int, c_void, c_void, c_void, c_void, c_void]),
     "sdl_make_kv_tensor_map": (c_int, [c_void, c_void, c_int, c_i64, c_int, c_int]),
     "sdl_attention_workspace_bytes": (c_size, [_P(SdlAttnArgs)]),
+    "sdl_attention_launches": (c_int, [_P(SdlAttnArgs)]),
     "sdl_paged_attention": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_paged_attention_noalloc": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_noalloc_scratch_bytes": (c_size, []),

@@ -101,12 +101,39 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
     return a
 
 
-def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch) -> int:
-    """Kernel launches one call makes: the attention launch, plus the split-K
-    merge when the plan splits a row's pages across CTAs."""
+def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
+                       k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None) -> int:
+    """Kernel launches one ``paged_attention`` call with these arguments
+    makes: the attention launch, the split-K merge when the plan splits a
+    row's pages across CTAs, and a positional append when ``k_new`` is given
+    to a plan that does not write inside the attention kernel."""
     q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
-    a = _paged_args(q4, kv, 0, batch, q4)
-    return 2 if _lib.load().sdl_attention_workspace_bytes(a) else 1
+    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma)
+    keep = _set_new_rows(a, q4, kv, k_new, v_new)  # noqa: F841 (keeps copies alive)
+    n = _lib.load().sdl_attention_launches(a)
+    if n < 0:
+        raise RuntimeError("sdl_attention_launches: " + _lib.last_error())
+    return n
+
+
+def _set_new_rows(a: _lib.SdlAttnArgs, q4: torch.Tensor, kv: PagedKVCache, k_new: Optional[torch.Tensor],
+                  v_new: Optional[torch.Tensor]):
+    """Point ``a`` at the K/V rows to store before attending (fused append)."""
+    if k_new is None:
+        return None
+    rows = q4.shape[0] * q4.shape[1]
+    kn = k_new.reshape(rows, -1)
+    vn = v_new.reshape(rows, -1)
+    if kn.dtype != kv.dtype or vn.dtype != kv.dtype or kn.shape[1] != kv.num_kv_heads * kv.head_dim \
+            or vn.shape != kn.shape:
+        raise ValueError("k_new/v_new must be ({}, {}) rows of {}".format(rows, kv.num_kv_heads * kv.head_dim,
+                                                                       kv.dtype))
+    _lib.require_cuda(kn, "k_new")
+    _lib.require_cuda(vn, "v_new")
+    if kn.stride(1) != 1 or vn.stride(1) != 1 or kn.stride(0) != vn.stride(0):
+        kn, vn = kn.contiguous(), vn.contiguous()
+    a.k_new, a.v_new, a.new_row_stride = kn.data_ptr(), vn.data_ptr(), kn.stride(0)
+    return kn, vn
 
 
 def paged_attention(
@@ -120,8 +147,15 @@ def paged_attention(
     pages_per_split: int = 0,
     kv_heads_per_cta: int = 0,
     use_umma: int = 0,
+    k_new: Optional[torch.Tensor] = None,
+    v_new: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
+
+    With ``k_new`` / ``v_new`` (B*chunk rows of Hkv*d, the pool's dtype) the
+    call first stores them at positions ``starts[b] + j`` of layer ``layer``
+    (the positions must already be reserved) -- the write-then-attend of a
+    decoder layer in one launch on the tensor-core path.
 
     ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` override the
     launch plan (pages per split-K CTA, kv heads sharing one CTA of the
@@ -138,6 +172,7 @@ def paged_attention(
     if out is None:
         out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma)
+    keep = _set_new_rows(a, q, kv, k_new, v_new)  # noqa: F841 (keeps copies alive through the launch)
     if batch.max_limit > kv.width * kv.block_size:
         raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))
     _launch(a, q.device)

@@ -136,12 +136,12 @@ def plan_prefill(kv: PagedKVCache, seq_ids: Sequence[int], seq_lengths: Sequence
 
 def paged_attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv: PagedKVCache, layer: int,
                  plan: ForwardPlan) -> torch.Tensor:
-    """Append this layer's K/V at the plan's slots, then attend (write first)."""
+    """Store this layer's K/V at the plan's positions, then attend (write
+    first) -- one fused call; the positions were reserved by the plan."""
     B = q.shape[0]
-    kv.append(layer, plan.slots, k.reshape(-1, kv.num_kv_heads, kv.head_dim),
-              v.reshape(-1, kv.num_kv_heads, kv.head_dim))
     q4 = q.reshape(B, plan.chunk, q.shape[-2], q.shape[-1])
-    return paged_attention(q4, kv, layer, plan.batch)
+    return paged_attention(q4, kv, layer, plan.batch, k_new=k.reshape(B * plan.chunk, -1),
+                           v_new=v.reshape(B * plan.chunk, -1))
 
 
 # ------------------------------------------------------------- decoder layer

@@ -247,3 +247,83 @@ def test_extend_matches_per_position_full_attention():
         kvp = gather_ctx(kv, 0, 0, 7 + j + 1)
         fo = full_attention(q[0, j], kvp[0], kvp[1], 4)
         torch.testing.assert_close(out[0, j], fo, rtol=1e-5, atol=1e-5)
+
+
+# ------------------------------------------------------------ fused append
+FUSED_CASES = [
+    # Hq, Hkv, d, chunk, starts, valid rows, dtype, launch overrides
+    (12, 2, 128, 1, [15, 16, 17, 1029, 4095], None, torch.bfloat16, {}),             # decode, page edges
+    (12, 2, 128, 6, [0, 5, 250, 2047], None, torch.bfloat16, {}),                    # verify (gamma 5)
+    (12, 2, 128, 6, [10, 300, 2047], None, torch.bfloat16, {"pages_per_split": 1}),  # new rows span 2 splits
+    (12, 2, 128, 22, [3, 700], None, torch.bfloat16, {}),                            # 132 columns: 3 col tiles
+    (14, 2, 64, 5, [0, 31, 1000], None, torch.float16, {"kv_heads_per_cta": 1}),     # fp16, d 64
+    (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {}),                      # ragged valid rows
+    (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"use_umma": 1}),                # tcgen05: separate append
+    (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"force_generic": True}),        # CUDA-core: separate append
+    (4, 2, 16, 3, [0, 9, 33], None, torch.float32, {}),                              # fp32 pool: separate append
+]
+
+
+def _fused_pair(case, layers=2, layer=1, misalign=False):
+    Hq, Hkv, d, chunk, starts, valid, dtype, kw = FUSED_CASES[case]
+    B = len(starts)
+    valid = valid or [chunk] * B
+    bs = 4 if dtype == torch.float32 else 16
+    pair = [_build(starts, Hkv, d, bs, dtype, seed=300 + case, extra_blocks=4 + chunk, layers=layers)[0]
+            for _ in range(2)]
+    slots = [kvc.reserve(list(range(B)), starts, valid) for kvc in pair]
+    assert torch.equal(slots[0], slots[1])
+    g = torch.Generator().manual_seed(case)
+    q = torch.randn(B, chunk, Hq, d, generator=g).to(DEV, dtype)
+    width = Hkv * d + (2 if misalign else 0)
+    k_new = torch.randn(B * chunk, width, generator=g).to(DEV, dtype)[:, (2 if misalign else 0):]
+    v_new = torch.randn(B * chunk, width, generator=g).to(DEV, dtype)[:, (2 if misalign else 0):]
+    packed = _lib_i32(list(range(B)) + starts + valid)
+    batch = AttnBatch(packed[:B], packed[B:2 * B], max(s + chunk for s in starts), packed[2 * B:])
+    keep = torch.cat([torch.arange(b * chunk, b * chunk + valid[b]) for b in range(B)]).to(DEV)
+    pair[0].append(layer, slots[0], k_new[keep].reshape(-1, Hkv, d), v_new[keep].reshape(-1, Hkv, d))
+    sep = paged_attention(q, pair[0], layer, batch, **kw)
+    fused = paged_attention(q, pair[1], layer, batch, k_new=k_new, v_new=v_new, **kw)
+    torch.cuda.synchronize()
+    return pair, sep, fused, valid
+
+
+def _lib_i32(values):
+    from engine import _lib
+    return _lib.i32(values, DEV)
+
+
+@pytest.mark.parametrize("case", range(len(FUSED_CASES)))
+def test_fused_append_equals_append_then_attend(case):
+    """``paged_attention(..., k_new, v_new)`` stores the new rows exactly where
+    ``kv.append`` does (every layer's pool bit-identical afterwards) and
+    returns the same bits as append-then-attend, on the path that writes
+    inside the attention kernel and on those that launch a separate append."""
+    pair, sep, fused, valid = _fused_pair(case)
+    assert torch.equal(pair[0]._k, pair[1]._k)
+    assert torch.equal(pair[0]._v, pair[1]._v)
+    assert torch.equal(sep, fused)
+    for kvc in pair:
+        kvc.check_errors()
+
+
+def test_fused_append_unaligned_rows_fall_back_to_separate_append():
+    """k_new rows that are 4- but not 16-byte aligned take the separate
+    positional append and still match."""
+    pair, sep, fused, _ = _fused_pair(1, misalign=True)
+    assert torch.equal(pair[0]._k, pair[1]._k)
+    assert torch.equal(pair[0]._v, pair[1]._v)
+    assert torch.equal(sep, fused)
+
+
+def test_fused_append_rejects_bad_rows():
+    kv, _ = _build([40], 2, 128, 16, torch.bfloat16, seed=1)
+    kv.reserve([0], [40], [1])
+    q = torch.randn(1, 1, 12, 128, device=DEV, dtype=torch.bfloat16)
+    batch = AttnBatch.from_lists(DEV, [0], [40], 1)
+    with pytest.raises(ValueError):
+        paged_attention(q, kv, 0, batch, k_new=torch.zeros(1, 255, device=DEV, dtype=torch.bfloat16),
+                        v_new=torch.zeros(1, 255, device=DEV, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        paged_attention(q, kv, 0, batch, k_new=torch.zeros(1, 256, device=DEV),
+                        v_new=torch.zeros(1, 256, device=DEV))
