@@ -38,6 +38,7 @@ constexpr int kStages = 4;         // TMA ring depth
 constexpr int kMaxConsumerWarps = 8;
 constexpr int kBoxBytes = kPage * 128;  // one [16 tokens][64 cols] 16-bit box
 constexpr uint32_t kWaitLimit = 1u << 20;
+constexpr float kLazyLog2 = 8.f;   // running-max slack of the mma.sync kernel's softmax (log2 units)
 
 struct TcParams {
     const void* q;
@@ -242,6 +243,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             m_run[nt][e] = -INFINITY;
             l_run[nt][e] = 0.f;
         }
+    int lim_min = lmax;  // smallest key limit among this warp's valid columns
+#pragma unroll
+    for (int nt = 0; nt < NTG; ++nt) lim_min = min(lim_min, min(lim[nt][0], lim[nt][1]));
+    lim_min = __reduce_min_sync(0xffffffffu, lim_min);
     float acc[KSTEPS][NTG][4];
 #pragma unroll
     for (int mt = 0; mt < KSTEPS; ++mt)
@@ -281,33 +286,57 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             for (int nt = 0; nt < NTG; ++nt) mma_16816<T>(s[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
         }
 
-        // Online softmax per query column (log2 domain).
+        // Online softmax per query column (log2 domain) with a lazy running
+        // max: m_run only moves -- and O, l are rescaled -- when a page's max
+        // exceeds it by more than 2^kLazyLog2, so p <= 2^kLazyLog2 and most
+        // pages skip the rescale.  Pages wholly below every column's key
+        // limit skip the causal mask.
         const int pos_lo = (pbeg + i) * kPage + grp, pos_hi = pos_lo + 8;
+        const bool whole = (pbeg + i + 1) * kPage <= lim_min;
+        float mx[NTG][2];
+        bool need = false;
+#pragma unroll
+        for (int nt = 0; nt < NTG; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                if (!whole) {
+                    if (pos_lo >= lim[nt][e]) s[nt][e] = -INFINITY;
+                    if (pos_hi >= lim[nt][e]) s[nt][2 + e] = -INFINITY;
+                }
+                float m = fmaxf(s[nt][e], s[nt][2 + e]);
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+                mx[nt][e] = m * p.scale_log2;
+                need |= mx[nt][e] > m_run[nt][e] + kLazyLog2;
+            }
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int nt = 0; nt < NTG; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    if (!(mx[nt][e] > m_run[nt][e] + kLazyLog2)) continue;
+                    const float alpha = ex2_approx(m_run[nt][e] - mx[nt][e]);  // 0 on the first page
+                    m_run[nt][e] = mx[nt][e];
+                    l_run[nt][e] *= alpha;
+#pragma unroll
+                    for (int mt = 0; mt < KSTEPS; ++mt) {
+                        acc[mt][nt][e] *= alpha;
+                        acc[mt][nt][2 + e] *= alpha;
+                    }
+                }
+        }
         uint32_t pb[NTG][2], pl[NTG][2];
 #pragma unroll
         for (int nt = 0; nt < NTG; ++nt) {
             float pv[4];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const float x0 = pos_lo < lim[nt][e] ? s[nt][e] * p.scale_log2 : -INFINITY;
-                const float x1 = pos_hi < lim[nt][e] ? s[nt][2 + e] * p.scale_log2 : -INFINITY;
-                float mx = fmaxf(x0, x1);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mnew = fmaxf(m_run[nt][e], mx);
-                const float muse = mnew == -INFINITY ? 0.f : mnew;
-                const float alpha = exp2f(m_run[nt][e] - muse);
-                const float p0 = exp2f(x0 - muse), p1 = exp2f(x1 - muse);
-                l_run[nt][e] = l_run[nt][e] * alpha + p0 + p1;
-                m_run[nt][e] = mnew;
-#pragma unroll
-                for (int mt = 0; mt < KSTEPS; ++mt) {
-                    acc[mt][nt][e] *= alpha;
-                    acc[mt][nt][2 + e] *= alpha;
-                }
-                pv[e] = p0;
-                pv[2 + e] = p1;
+                // a column that has seen only masked keys keeps m_run = -inf; its p is 0
+                const float muse = m_run[nt][e] == -INFINITY ? 0.f : m_run[nt][e];
+                pv[e] = ex2_approx(fmaf(s[nt][e], p.scale_log2, -muse));
+                pv[2 + e] = ex2_approx(fmaf(s[nt][2 + e], p.scale_log2, -muse));
+                l_run[nt][e] += pv[e] + pv[2 + e];
             }
             const float h0 = round_trip<T>(pv[0]), h1 = round_trip<T>(pv[1]);
             const float h2 = round_trip<T>(pv[2]), h3 = round_trip<T>(pv[3]);
