@@ -192,6 +192,14 @@ typedef struct sdl_attn_args {
     int32_t use_umma;         /* 1 = the tcgen05 kernel where it applies
                                  (up to 64 query rows per kv head);
                                  0 / -1 = the mma.sync kernel              */
+    int32_t cluster_merge;    /* mma.sync kernel with split rows: 0 = fp32
+                                 partials in the workspace and a separate
+                                 merge launch (default); 1 = the splits of
+                                 a row run as one thread-block cluster and
+                                 merge their partials in distributed shared
+                                 memory, no workspace, when the split count
+                                 allows (<= 16).  Slower on ragged batches:
+                                 a cluster holds its idle splits' slots    */
     /* Fused K/V append (paged pools only): when k_new != NULL the rows
      * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
      * elements, the pool's dtype) are stored at positions starts[b] + j
@@ -206,7 +214,7 @@ typedef struct sdl_attn_args {
 } sdl_attn_args;
 
 /* Bytes of workspace sdl_paged_attention needs for `args` (0 when one
- * split per row suffices). */
+ * split per row suffices or the splits merge on chip). */
 size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
 
 /* Kernel launches sdl_paged_attention makes for `args` with a workspace of

@@ -30,6 +30,8 @@
 #include <cstring>
 #include <mutex>
 #include <type_traits>
+#include <utility>
+#include <vector>
 
 namespace {
 
@@ -38,6 +40,7 @@ constexpr int kStages = 4;         // TMA ring depth
 constexpr int kMaxConsumerWarps = 8;
 constexpr int kBoxBytes = kPage * 128;  // one [16 tokens][64 cols] 16-bit box
 constexpr uint32_t kWaitLimit = 1u << 20;
+constexpr int kMaxClusterSplits = 16;  // splits of one row merged on chip (non-portable cluster size)
 constexpr float kLazyLog2 = 8.f;   // running-max slack of the mma.sync kernel's softmax (log2 units)
 
 struct TcParams {
@@ -56,6 +59,8 @@ struct TcParams {
     int pps, nsplit;
     int g_cta, wpg, ncoltiles;
     int stage_bytes;
+    int ring_bytes;  // shared bytes before the mbarriers: the TMA ring, reused for cluster partials
+    int cluster;     // 1: the splits of a row form one cluster and merge their partials on chip
     float scale_log2;
     float* o_part;
     float* ml_part;
@@ -79,8 +84,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     constexpr int KSTEPS = HD / 16;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * p.stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.ring_bytes);
     uint64_t* empty = full + kStages;
+    uint64_t* xbar = empty + kStages;  // cluster merge: [0] partials stored, [1] partials read
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
@@ -100,13 +106,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int ncol = p.chunk * p.ratio;
     const int tile_cols = p.wpg * NTG * 8;
     const int col0 = coltile * tile_cols;
-    if (col0 >= ncol || col0 / p.ratio >= nvalid) return;
-    const int col_last = min(col0 + tile_cols, ncol) - 1;
-    const int j_last = min(col_last / p.ratio, nvalid - 1);
-    const int lmax = start + j_last + 1;
-    const int npages = (lmax + kPage - 1) / kPage;
+    int lmax = 0;
+    if (col0 < ncol && col0 / p.ratio < nvalid) {
+        const int col_last = min(col0 + tile_cols, ncol) - 1;
+        const int j_last = min(col_last / p.ratio, nvalid - 1);
+        lmax = start + j_last + 1;
+    }
+    const int npages = lmax > 0 ? (lmax + kPage - 1) / kPage : 0;
     const int pbeg = split * p.pps;
     const int pend = min(npages, pbeg + p.pps);
+    // splits holding pages of this (sequence, kv-head group, column tile):
+    // ranks 0..nact-1.  A span past the grid (max_limit below some
+    // starts[b] + chunk) is reported and its excess pages are not attended.
+    int nact = (npages + p.pps - 1) / p.pps;
+    if (nact > p.nsplit) {
+        if (threadIdx.x == 0 && split == 0) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+        nact = p.nsplit;
+    }
+    if (p.cluster) {
+        // The cluster is the row's splits.  Barriers for the on-chip merge are
+        // initialised before any CTA of the cluster may signal them, and every
+        // thread of every CTA passes this point before any CTA leaves.
+        if (threadIdx.x == 0 && pbeg < pend && nact > 1) {
+            mbar_init(&xbar[0], nact - 1);
+            mbar_init(&xbar[1], nact - 1);
+            fence_mbar_init();
+        }
+        cluster_sync_all();
+    }
     if (lmax <= 0 || pbeg >= pend) return;
     const int np = pend - pbeg;
     const int row = p.dense ? 0 : p.rows[b];
@@ -365,9 +392,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     }
     __syncthreads();
     pdl_launch_dependents();  // the split merge may be scheduled during the epilogue
-    if (aborted || *s_abort) return;
+    const bool cmerge = p.cluster && nact > 1;
+    if ((aborted || *s_abort) && !cmerge) return;
+    const bool failed = aborted || *s_abort;
+
+    // Cluster merge: partials go to this CTA's shared memory (the ring is
+    // free now), row stride PST floats, then m and l per local column.
+    constexpr int PST = HD + 4;
+    const int ncl = ncons * NTG * 8;
+    float* part = reinterpret_cast<float*>(smem);
+    float* part_m = part + ncl * PST;
+    float* part_l = part_m + ncl;
 
     // Epilogue: finished rows write the output, split rows write partials.
+    if (!failed) {
 #pragma unroll
     for (int nt = 0; nt < NTG; ++nt)
 #pragma unroll
@@ -393,6 +431,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     store_from_f32(p.out, ob + mt * 16 + grp, p.out_dtype, acc[mt][nt][e] * inv);
                     store_from_f32(p.out, ob + mt * 16 + grp + 8, p.out_dtype, acc[mt][nt][2 + e] * inv);
                 }
+            } else if (cmerge) {
+                const int lc = gi * tile_cols + (col - col0);
+                float* op = part + lc * PST;
+#pragma unroll
+                for (int mt = 0; mt < KSTEPS; ++mt) {
+                    op[mt * 16 + grp] = acc[mt][nt][e];
+                    op[mt * 16 + grp + 8] = acc[mt][nt][2 + e];
+                }
+                if (grp == 0) {
+                    part_m[lc] = m_run[nt][e];
+                    part_l[lc] = l;
+                }
             } else {
                 const int64_t idx = (((int64_t)b * p.nsplit + split) * p.chunk + j) * p.Hq + h;
                 float* op = p.o_part + idx * HD;
@@ -407,12 +457,74 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 }
             }
         }
+    }
+    if (!cmerge) return;
+
+    // On-chip merge.  Every active split signals the others once its partials
+    // are stored; split r then merges the local columns lc = r (mod nact)
+    // from all splits' shared memory, and no CTA leaves before every split
+    // has finished reading it.  All waits are bounded.
+    fence_acq_rel_cluster();
+    named_bar_sync(1, ncons * 32);
+    const uint32_t rank = cluster_ctarank();
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < nact; ++r)
+            if (r != (int)rank) mbar_arrive_remote(mapa_shared(smem_u32(&xbar[0]), r));
+    }
+    bool ready = mbar_wait_cluster_bounded(&xbar[0], 0, kWaitLimit);
+    if (!ready && lane == 0) sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
+    if (ready && !failed) {
+        constexpr int DPL = HD / 32;  // head dims per lane
+        for (int lc = (int)rank + warp * nact; lc < ncl; lc += ncons * nact) {
+            const int gi_c = lc / tile_cols;
+            const int col = col0 + lc % tile_cols;
+            if (col >= ncol) continue;
+            const int j = col / p.ratio;
+            if (j >= nvalid) continue;
+            const int L = start + j + 1;
+            const int ns_c = min(nact, ((L + kPage - 1) / kPage + p.pps - 1) / p.pps);
+            if (ns_c <= 1) continue;
+            const uint32_t a_m = smem_u32(part_m + lc), a_l = smem_u32(part_l + lc);
+            const uint32_t a_o = smem_u32(part + lc * PST + lane * DPL);
+            float M = -INFINITY;
+            for (int r = 0; r < ns_c; ++r) M = fmaxf(M, ld_cluster_f32(mapa_shared(a_m, r)));
+            float den = 0.f, o[DPL];
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) o[k] = 0.f;
+#pragma unroll 4
+            for (int r = 0; r < ns_c; ++r) {
+                const float mr_ = ld_cluster_f32(mapa_shared(a_m, r));
+                const float w = mr_ == -INFINITY ? 0.f : ex2_approx(mr_ - M);
+                den = fmaf(w, ld_cluster_f32(mapa_shared(a_l, r)), den);
+                if constexpr (DPL == 4) {
+                    const float4 v = ld_cluster_f32x4(mapa_shared(a_o, r));
+                    o[0] = fmaf(w, v.x, o[0]); o[1] = fmaf(w, v.y, o[1]);
+                    o[2] = fmaf(w, v.z, o[2]); o[3] = fmaf(w, v.w, o[3]);
+                } else {
+                    const float2 v = ld_cluster_f32x2(mapa_shared(a_o, r));
+                    o[0] = fmaf(w, v.x, o[0]); o[1] = fmaf(w, v.y, o[1]);
+                }
+            }
+            const float inv = 1.f / den;
+            const int h = (kvgrp * p.g_cta + gi_c) * p.ratio + col % p.ratio;
+            const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + lane * DPL;
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) store_from_f32(p.out, ob + k, p.out_dtype, o[k] * inv);
+        }
+    }
+    named_bar_sync(1, ncons * 32);  // this CTA's reads of the other splits are done
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < nact; ++r)
+            if (r != (int)rank) mbar_arrive_remote(mapa_shared(smem_u32(&xbar[1]), r));
+        if (!mbar_wait_cluster_bounded(&xbar[1], 0, kWaitLimit)) sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
+    }
 }
 
 // Merge split-K partials (m in log2 units, unnormalised O, l).  One warp per
-// (sequence, chunk row, q head): lanes reduce the split maxima and
-// denominators in parallel, then each lane owns 4 consecutive head dims and
-// keeps 8 splits' loads in flight at once (the merge is latency bound).
+// (sequence, chunk row, q head).  The merge is latency bound, so it takes
+// two dependent rounds of loads: the splits' (m, l) pairs (lane s holds
+// split s, reduced by an online max/sum across lanes), then up to 16 splits'
+// partial rows at once, each lane owning 4 consecutive head dims.
 __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     pdl_wait();  // partials come from the attention launch just before
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -426,50 +538,51 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     const int L = p.starts[b] + j + 1;
     if (L <= 0) return;
     const int np_c = (L + kPage - 1) / kPage;
-    const int ns = (np_c + p.pps - 1) / p.pps;
+    const int ns = min(p.nsplit, (np_c + p.pps - 1) / p.pps);
     if (ns <= 1) return;
     const int64_t idx0 = (((int64_t)b * p.nsplit) * p.chunk + j) * p.Hq + h;
     const int64_t sstride = (int64_t)p.chunk * p.Hq;
-    float M = -INFINITY;
-    for (int s = lane; s < ns; s += 32) M = fmaxf(M, p.ml_part[(idx0 + s * sstride) * 2]);
-    M = warp_max(M);
-    float den = 0.f;
+    // Every split below ns saw at least one key of this row, so each m is finite.
+    float M = -INFINITY, den = 0.f;
     for (int s = lane; s < ns; s += 32) {
-        const float* ml = p.ml_part + (idx0 + s * sstride) * 2;
-        den += exp2f(ml[0] - M) * ml[1];
+        const float2 ml = *reinterpret_cast<const float2*>(p.ml_part + (idx0 + s * sstride) * 2);
+        const float mn = fmaxf(M, ml.x);
+        den = den * ex2_approx(M - mn) + ml.y * ex2_approx(ml.x - mn);
+        M = mn;
     }
-    den = warp_sum(den);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float M2 = __shfl_xor_sync(0xffffffffu, M, off);
+        const float d2 = __shfl_xor_sync(0xffffffffu, den, off);
+        const float mn = fmaxf(M, M2);
+        den = (M == -INFINITY ? 0.f : den * ex2_approx(M - mn)) + (M2 == -INFINITY ? 0.f : d2 * ex2_approx(M2 - mn));
+        M = mn;
+    }
     const float inv = 1.f / den;
     const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh;
     for (int d0 = lane * 4; d0 < hd; d0 += 128) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        int s = 0;
-        for (; s + 8 <= ns; s += 8) {
-            float w[8];
-            float4 o[8];
+        for (int s = 0; s < ns; s += 16) {
+            float w[16];
+            float4 o[16];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int64_t idx = idx0 + (s + t) * sstride;
-                w[t] = p.ml_part[idx * 2];
-                o[t] = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
+            for (int t = 0; t < 16; ++t) {
+                w[t] = -INFINITY;
+                o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (s + t < ns) {
+                    const int64_t idx = idx0 + (s + t) * sstride;
+                    w[t] = p.ml_part[idx * 2];
+                    o[t] = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
+                }
             }
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const float wt = exp2f(w[t] - M);
-                acc.x += wt * o[t].x;
-                acc.y += wt * o[t].y;
-                acc.z += wt * o[t].z;
-                acc.w += wt * o[t].w;
+            for (int t = 0; t < 16; ++t) {
+                const float wt = ex2_approx(w[t] - M);  // 0 for the padding slots
+                acc.x = fmaf(wt, o[t].x, acc.x);
+                acc.y = fmaf(wt, o[t].y, acc.y);
+                acc.z = fmaf(wt, o[t].z, acc.z);
+                acc.w = fmaf(wt, o[t].w, acc.w);
             }
-        }
-        for (; s < ns; ++s) {
-            const int64_t idx = idx0 + s * sstride;
-            const float wt = exp2f(p.ml_part[idx * 2] - M);
-            const float4 o = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
-            acc.x += wt * o.x;
-            acc.y += wt * o.y;
-            acc.z += wt * o.z;
-            acc.w += wt * o.w;
         }
         store_from_f32(p.out, ob + d0, p.out_dtype, acc.x * inv);
         store_from_f32(p.out, ob + d0 + 1, p.out_dtype, acc.y * inv);
@@ -1230,7 +1343,9 @@ struct Plan {
     int ntg = 1, wpg = 1, ncoltiles = 1, g_cta = 1, kvgroups = 1;
     int pps = 1, nsplit = 1;
     int stage_bytes = 0;
-    bool umma = false;  // tcgen05 verify kernel
+    int ring_bytes = 0;    // shared bytes before the mbarriers (ring, or cluster partials when larger)
+    bool cluster = false;  // splits of a row form one cluster and merge on chip
+    bool umma = false;     // tcgen05 verify kernel
     size_t smem = 0;
     size_t ws_bytes = 0;
 };
@@ -1289,6 +1404,74 @@ Plan make_umma_plan(const sdl_attn_args* a) {
     return pl;
 }
 
+// Per-instantiation kernel attributes: the dynamic shared-memory ceiling
+// (raised monotonically), all of the unified L1/shared array as shared memory
+// (the ring buffers, not L1, decide how many CTAs an SM holds) and clusters
+// of up to kMaxClusterSplits CTAs.
+template <int HD, int NTG, typename T>
+int tc_configure(size_t smem) {
+    static std::mutex mu;
+    static size_t configured = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem <= configured) return SDL_OK;
+    auto kern = attn_tc_kernel<HD, NTG, T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    configured = smem;
+    return SDL_OK;
+}
+
+// Whether clusters of `nsplit` CTAs of this kernel can be resident at all
+// (cached per shape; any failure answers no and the plan falls back to the
+// workspace merge).
+template <int HD, int NTG, typename T>
+bool tc_cluster_fits_inst(int nsplit, size_t smem, int threads) {
+    static std::mutex mu;
+    static std::vector<std::pair<uint64_t, bool>> cache;
+    const uint64_t key = ((uint64_t)nsplit << 48) | ((uint64_t)threads << 32) | (uint64_t)smem;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& kv : cache)
+            if (kv.first == key) return kv.second;
+    }
+    bool ok = false;
+    if (tc_configure<HD, NTG, T>(smem) == SDL_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(nsplit, 1, 1);
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = nsplit;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        ok = cudaOccupancyMaxActiveClusters(&n, attn_tc_kernel<HD, NTG, T>, &cfg) == cudaSuccess && n > 0;
+        (void)cudaGetLastError();  // a refused query leaves no sticky error
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache.emplace_back(key, ok);
+    return ok;
+}
+
+bool tc_cluster_fits(int hd, int ntg, int dtype, int nsplit, size_t smem, int threads) {
+    if (dtype == SDL_BF16) {
+        if (hd == 64) return ntg == 2 ? tc_cluster_fits_inst<64, 2, __nv_bfloat16>(nsplit, smem, threads)
+                                      : tc_cluster_fits_inst<64, 1, __nv_bfloat16>(nsplit, smem, threads);
+        return ntg == 2 ? tc_cluster_fits_inst<128, 2, __nv_bfloat16>(nsplit, smem, threads)
+                        : tc_cluster_fits_inst<128, 1, __nv_bfloat16>(nsplit, smem, threads);
+    }
+    if (hd == 64) return ntg == 2 ? tc_cluster_fits_inst<64, 2, __half>(nsplit, smem, threads)
+                                  : tc_cluster_fits_inst<64, 1, __half>(nsplit, smem, threads);
+    return ntg == 2 ? tc_cluster_fits_inst<128, 2, __half>(nsplit, smem, threads)
+                    : tc_cluster_fits_inst<128, 1, __half>(nsplit, smem, threads);
+}
+
 Plan make_plan(const sdl_attn_args* a) {
     if (umma_applicable(a)) return make_umma_plan(a);
     Plan pl;
@@ -1316,12 +1499,32 @@ Plan make_plan(const sdl_attn_args* a) {
     }
     pl.kvgroups = a->Hkv / pl.g_cta;
     pl.stage_bytes = pl.g_cta * head_stage;
-    pl.smem = (size_t)kStages * pl.stage_bytes + 1024 + 2 * kStages * sizeof(uint64_t);
+    const int ncl = pl.g_cta * pl.wpg * pl.ntg * 8;  // query columns of one CTA
+    const int part_bytes = ncl * (a->head_dim + 4) * 4 + 2 * ncl * 4;
+    pl.ring_bytes = std::max(kStages * pl.stage_bytes, part_bytes);
+    pl.smem = (size_t)pl.ring_bytes + 1024 + (2 * kStages + 2) * sizeof(uint64_t);
     const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
     const long base_ctas = (long)a->B * pl.ncoltiles * pl.kvgroups;
     const long target = (long)sm_count() * 4;
     int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
     int pps = a->pages_per_split > 0 ? a->pages_per_split : std::max(4, (max_pages + nsplit_target - 1) / nsplit_target);
+    // On-chip merge (opt-in): the row's splits are one cluster of at most
+    // kMaxClusterSplits CTAs, which must fit the GPU's cluster occupancy.
+    // A cluster is scheduled whole, so the idle splits of short rows hold
+    // slots: on ragged batches the workspace merge is faster.
+    if (a->cluster_merge) {
+        int p2 = pps;
+        if (a->pages_per_split <= 0) p2 = std::max(pps, (max_pages + kMaxClusterSplits - 1) / kMaxClusterSplits);
+        const int ns = (max_pages + p2 - 1) / p2;
+        if (ns > 1 && ns <= kMaxClusterSplits &&
+            tc_cluster_fits(a->head_dim, pl.ntg, a->dtype, ns, pl.smem, (pl.g_cta * pl.wpg + 1) * 32)) {
+            pl.cluster = true;
+            pl.pps = p2;
+            pl.nsplit = ns;
+            pl.ws_bytes = 0;
+            return pl;
+        }
+    }
     for (;;) {
         pl.pps = pps;
         pl.nsplit = (max_pages + pps - 1) / pps;
@@ -1335,20 +1538,12 @@ Plan make_plan(const sdl_attn_args* a) {
 template <int HD, int NTG, typename T>
 int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl, cudaStream_t st) {
     auto kern = attn_tc_kernel<HD, NTG, T>;
-    static size_t configured = 0;
-    if (pl.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
-        // all of the unified L1/shared array as shared memory: the ring buffers,
-        // not L1, decide how many CTAs an SM holds
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared);
-        if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
-        configured = pl.smem;
-    }
+    int rc = tc_configure<HD, NTG, T>(pl.smem);
+    if (rc != SDL_OK) return rc;
     dim3 grid(pl.nsplit, pl.ncoltiles * pl.kvgroups, tp.B);
     dim3 block((pl.g_cta * pl.wpg + 1) * 32);
-    cudaError_t e = sdl::launch_pdl(kern, grid, block, pl.smem, st, mk, mv, tp);
+    cudaError_t e = pl.cluster ? sdl::launch_pdl_cluster(kern, grid, block, pl.smem, st, (unsigned)pl.nsplit, mk, mv, tp)
+                               : sdl::launch_pdl(kern, grid, block, pl.smem, st, mk, mv, tp);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("attn_tc_kernel");
 }
@@ -1473,7 +1668,7 @@ extern "C" int sdl_attention_launches(const sdl_attn_args* args) {
     const bool fused_append = tmp.k_new && pl.tc && !pl.umma && append_fusable(&tmp);
     int n = (tmp.k_new && !fused_append) ? 1 : 0;
     if (!pl.tc) return n + 1;
-    return n + 1 + ((pl.umma || pl.nsplit > 1) ? 1 : 0);
+    return n + 1 + ((pl.umma || (pl.nsplit > 1 && !pl.cluster)) ? 1 : 0);
 }
 
 extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
@@ -1513,6 +1708,8 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.pps = pl.pps; tp.nsplit = pl.nsplit;
         tp.g_cta = pl.g_cta; tp.wpg = pl.wpg; tp.ncoltiles = pl.ncoltiles;
         tp.stage_bytes = pl.stage_bytes;
+        tp.ring_bytes = pl.ring_bytes;
+        tp.cluster = pl.cluster ? 1 : 0;
         tp.scale_log2 = a->scale * 1.4426950408889634f;
         tp.o_part = a->workspace;
         tp.ml_part = a->workspace ? a->workspace + (size_t)a->B * pl.nsplit * a->chunk * a->Hq * a->head_dim : nullptr;
@@ -1544,7 +1741,7 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
             rc = launch_tc_dtype<__half>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
         }
         if (rc != SDL_OK) return rc;
-        if (pl.nsplit > 1 && !pl.umma) {
+        if (pl.nsplit > 1 && !pl.umma && !pl.cluster) {
             const int rows = a->B * a->chunk * a->Hq;
             cudaError_t e = sdl::launch_pdl(attn_combine_kernel, dim3((rows + 3) / 4), dim3(128), 0, st, tp,
                                             (int)a->head_dim);

@@ -114,6 +114,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("force_generic", c_int),
         ("kv_heads_per_cta", c_int),
         ("use_umma", c_int),
+        ("cluster_merge", c_int),
         ("k_new", c_void),
         ("v_new", c_void),
         ("new_row_stride", c_i64),

@@ -82,7 +82,7 @@ def _launch(a: _lib.SdlAttnArgs, device: torch.device, fn: str = "sdl_paged_atte
 
 
 def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0,
-                kv_heads_per_cta=0, use_umma=0) -> _lib.SdlAttnArgs:
+                kv_heads_per_cta=0, use_umma=0, cluster_merge=False) -> _lib.SdlAttnArgs:
     a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
     a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
     mk, mv = kv.tensor_maps()
@@ -98,6 +98,7 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
     a.force_generic = 1 if force_generic else 0
     a.kv_heads_per_cta = int(kv_heads_per_cta)
     a.use_umma = int(use_umma)
+    a.cluster_merge = 1 if cluster_merge else 0
     return a
 
 
@@ -149,6 +150,7 @@ def paged_attention(
     use_umma: int = 0,
     k_new: Optional[torch.Tensor] = None,
     v_new: Optional[torch.Tensor] = None,
+    cluster_merge: bool = False,
 ) -> torch.Tensor:
     """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
 
@@ -157,10 +159,12 @@ def paged_attention(
     (the positions must already be reserved) -- the write-then-attend of a
     decoder layer in one launch on the tensor-core path.
 
-    ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` override the
-    launch plan (pages per split-K CTA, kv heads sharing one CTA of the
-    mma.sync kernel, 1 for the tcgen05 kernel); every plan gives the same
-    result within rounding of the split merge.
+    ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` /
+    ``cluster_merge`` override the launch plan (pages per split-K CTA, kv
+    heads sharing one CTA of the mma.sync kernel, 1 for the tcgen05 kernel,
+    split partials merged on chip within a thread-block cluster instead of by
+    a separate launch); every plan gives the same result within rounding of
+    the split merge.
     """
     _lib.require_cuda(q, "query")
     if q.dim() != 4 or q.shape[3] != kv.head_dim:
@@ -171,7 +175,8 @@ def paged_attention(
         q = q.contiguous()
     if out is None:
         out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
-    a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma)
+    a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma,
+                    cluster_merge)
     keep = _set_new_rows(a, q, kv, k_new, v_new)  # noqa: F841 (keeps copies alive through the launch)
     if batch.max_limit > kv.width * kv.block_size:
         raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))

@@ -156,33 +156,54 @@ def test_paged_attention_matches_oracle(case, generic, umma):
     kv.check_errors()
 
 
-@pytest.mark.parametrize("pps", [1, 3, 0, 64])
-@pytest.mark.parametrize("heads_per_cta,umma", [(0, -1), (1, -1), (0, 1)])
-def test_split_plans_agree(pps, heads_per_cta, umma):
+@pytest.mark.parametrize("pps", [1, 3, 0, 64, 12])
+@pytest.mark.parametrize("heads_per_cta,umma,cluster", [(0, -1, False), (1, -1, False), (0, -1, True),
+                                                         (1, -1, True), (0, 1, False)])
+def test_split_plans_agree(pps, heads_per_cta, umma, cluster):
     """Every launch plan (pages per split-K CTA from 1, i.e. 150+ splits per
     row, to one split; one or two kv heads per CTA of the mma.sync kernel;
-    the tcgen05 kernel, whose 64-token tiles then end inside a split) gives
-    the oracle's result for decode and verify rows."""
+    split partials merged on chip inside a cluster (up to 16 splits) or by a
+    separate launch; the tcgen05 kernel, whose 64-token tiles then end inside
+    a split) gives the oracle's result for decode and verify rows."""
     kv, ref = _build([2500 + 6, 17 + 6, 900 + 6], 2, 128, 16, torch.bfloat16, seed=5)
     for chunk, starts in ((1, [2505, 22, 905]), (6, [2500, 17, 900])):
         q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
         batch = AttnBatch.from_lists(DEV, [0, 1, 2], starts, chunk)
         out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps,
-                              kv_heads_per_cta=heads_per_cta, use_umma=umma)
+                              kv_heads_per_cta=heads_per_cta, use_umma=umma, cluster_merge=cluster)
         exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), starts)
         assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
     kv.check_errors()
 
 
-def test_split_merge_is_deterministic():
-    """The split-K merge has a fixed reduction order: repeated calls give
-    identical bits."""
-    kv, _ = _build([3000, 1500, 40], 2, 128, 16, torch.bfloat16, seed=6)
-    q = torch.randn(3, 1, 12, 128, device=DEV, dtype=torch.bfloat16)
-    batch = AttnBatch.from_lists(DEV, [0, 1, 2], [2999, 1499, 39], 1)
-    first = paged_attention(q, kv, 0, batch, pages_per_split=4)
+@pytest.mark.parametrize("pps,chunk,cluster", [(4, 1, False), (0, 1, False), (0, 6, True), (16, 6, True)])
+def test_split_merge_is_deterministic(pps, chunk, cluster):
+    """The split-K merge (separate launch; on chip in a cluster) has a fixed
+    reduction order: repeated calls give identical bits."""
+    kv, _ = _build([3000 + chunk, 1500 + chunk, 40 + chunk], 2, 128, 16, torch.bfloat16, seed=6)
+    q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
+    batch = AttnBatch.from_lists(DEV, [0, 1, 2], [3000, 1500, 40], chunk)
+    first = paged_attention(q, kv, 0, batch, pages_per_split=pps, cluster_merge=cluster)
     for _ in range(5):
-        assert torch.equal(paged_attention(q, kv, 0, batch, pages_per_split=4), first)
+        assert torch.equal(paged_attention(q, kv, 0, batch, pages_per_split=pps, cluster_merge=cluster), first)
+
+
+def test_cluster_and_separate_merge_agree():
+    """The on-chip cluster merge and the workspace merge launch combine the
+    same partials: results agree to fp32 rounding, and the launch counts
+    differ by the merge launch."""
+    from engine.attention import attention_launches
+    kv, ref = _build([4000 + 6, 2048 + 6, 31 + 6, 700 + 6], 2, 128, 16, torch.bfloat16, seed=8)
+    starts = [4000, 2048, 31, 700]
+    q = torch.randn(4, 6, 12, 128, device=DEV, dtype=torch.bfloat16)
+    batch = AttnBatch.from_lists(DEV, [0, 1, 2, 3], starts, 6)
+    on_chip = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, cluster_merge=True)
+    separate = paged_attention(q, kv, 0, batch, out_dtype=torch.float32)
+    exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(4), starts)
+    scale = np.abs(exact).max()
+    assert np.abs(on_chip.cpu().numpy() - exact).max() <= 2e-3 * scale
+    assert (on_chip - separate).abs().max().item() <= 1e-5 * scale
+    assert attention_launches(q, kv, batch) == 2
 
 
 def test_fp32_pools_use_exact_cuda_core_path():
