@@ -294,12 +294,12 @@ def run_gpu(args, rank: int, world: int, device):
     import torch
 
     from engine import _lib
-    from engine.attention import AttnBatch, attention_launches, paged_attention
+    from engine.attention import AttnBatch, attention_kernel, attention_launches, paged_attention
     from engine.kv import PagedKVCache
     from engine.workloads import c2_layout
 
     c = dict(C2)
-    umma = 1 if args.attn_kernel == "tcgen05" else 0
+    umma = UMMA_FLAG[args.attn_kernel]
     fused = args.append == "fused"
     L = args.layers
     B = args.batch
@@ -450,7 +450,8 @@ def run_gpu(args, rank: int, world: int, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         step_ms, e2e_ms, attn_ms = t.tolist()
     del graph, attn_graph
-    return dict(step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, clocks=clk, h2d=h2d,
+    kern = attention_kernel(q[0], kv, batch, use_umma=umma)
+    return dict(kernel=kern, step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, clocks=clk, h2d=h2d,
                 d2h=d2h, launches=launches_per_step * args.steps, ctx_mean=float(np.mean(ctx)))
 
 
@@ -461,13 +462,13 @@ def run_gpu_c3(args, rank: int, world: int, device):
     import torch
 
     from engine import _lib
-    from engine.attention import AttnBatch, attention_launches, paged_attention
+    from engine.attention import AttnBatch, attention_kernel, attention_launches, paged_attention
     from engine.kv import PagedKVCache
     from engine.workloads import c2_layout
     from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample_logits
 
     c = dict(C3)
-    umma = 1 if args.attn_kernel == "tcgen05" else 0
+    umma = UMMA_FLAG[args.attn_kernel]
     fused = args.append == "fused"
     L, B, gam = args.layers, args.batch, c["gamma"]
     chunk = gam + 1
@@ -669,10 +670,14 @@ def run_gpu_c3(args, rank: int, world: int, device):
         dist.all_reduce(cnt)
         committed, e2e_committed = [int(x) for x in cnt.tolist()]
     del graph, attn_graph
-    return dict(step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, samp_ms=samp_ms,
+    kern = attention_kernel(q[0], kv, batch, use_umma=umma)
+    return dict(kernel=kern, step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, samp_ms=samp_ms,
                 samp_bytes=samp_bytes, clocks=clk, h2d=h2d, d2h=d2h, launches=launches_per_step * args.steps,
                 committed=committed, e2e_committed=e2e_committed, e2e_steps=e2e_steps,
                 tokens_per_round=committed / float(args.steps * B * world))
+
+
+UMMA_FLAG = {"auto": 0, "mma": -1, "tcgen05": 1}
 
 
 def main(argv=None) -> int:
@@ -681,8 +686,9 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--attn-kernel", choices=["mma", "tcgen05"], default="mma",
-                    help="paged attention on the mma.sync kernel (default) or the persistent tcgen05 kernel")
+    ap.add_argument("--attn-kernel", choices=["auto", "mma", "tcgen05"], default="auto",
+                    help="paged attention kernel: the library's automatic choice (default), the mma.sync "
+                         "split-K kernel or the persistent tcgen05 kernel")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="store each layer's new K/V rows inside the attention launch (default) or with a "
                          "separate append launch before it")
@@ -779,10 +785,10 @@ def main(argv=None) -> int:
         "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4),
-                     "traffic": C2_ATTN_TRAFFIC if args.layers == 28 and args.attn_kernel == "mma" else None,
+                     "traffic": C2_ATTN_TRAFFIC if args.layers == 28 and res["kernel"] == "mma" else None,
                      "traffic_source": "ncu --set full capture of attn_tc_kernel on this workload (dram read + "
                                        "write per launch, main kernel only; summary under profiles/)",
-                     "kernel": ("attn_tc_kernel + attn_combine_kernel" if args.attn_kernel == "mma" else
+                     "kernel": ("attn_tc_kernel + attn_combine_kernel" if res["kernel"] == "mma" else
                                 "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
                                " (one paged decode attention op per layer{})".format(
                                    ", new K/V row stored inside it" if args.append == "fused" else ""),
@@ -884,7 +890,7 @@ def main_c3(args) -> int:
         "tokens_per_round": round(res["tokens_per_round"], 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
-                     "kernel": ("attn_tc_kernel (+ attn_combine_kernel when split)" if args.attn_kernel == "mma" else
+                     "kernel": ("attn_tc_kernel (+ attn_combine_kernel when split)" if res["kernel"] == "mma" else
                                 "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
                                ": (gamma+1)-row verify attention{}".format(
                                    ", new K/V rows stored inside it" if args.append == "fused" else ""),

@@ -191,7 +191,9 @@ typedef struct sdl_attn_args {
     int32_t kv_heads_per_cta; /* 0 = automatic; caps kv heads per CTA      */
     int32_t use_umma;         /* 1 = the tcgen05 kernel where it applies
                                  (up to 64 query rows per kv head);
-                                 0 / -1 = the mma.sync kernel              */
+                                 -1 = the mma.sync kernel; 0 = automatic:
+                                 tcgen05 for blocks of more than 16 query
+                                 rows per kv head when max_limit >= 4096  */
     int32_t cluster_merge;    /* mma.sync kernel with split rows: 0 = fp32
                                  partials in the workspace and a separate
                                  merge launch (default); 1 = the splits of
@@ -223,6 +225,11 @@ size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
  * a path that does not write inside the attention kernel.  -1 when `args`
  * is invalid.  No counterpart in the reference. */
 int sdl_attention_launches(const sdl_attn_args* args);
+
+/* Kernel sdl_paged_attention runs for `args`: 0 = CUDA-core (generic),
+ * 1 = mma.sync split-K, 2 = tcgen05 persistent; -1 when `args` is invalid.
+ * No counterpart in the reference. */
+int sdl_attention_kernel(const sdl_attn_args* args);
 
 /* Paged / dense attention for decode, verify (extend) and prefill rows. */
 int sdl_paged_attention(const sdl_attn_args* args, void* stream);

@@ -632,6 +632,7 @@ constexpr uint32_t kUTmemCols = 512;  // S double buffer (2 x 64 columns) + O do
 constexpr int kUOCol = 2 * kUTok;     // TMEM column of O buffer 0; buffer 1 is 128 columns on
 constexpr int kSkMaxPairs = 512;      // (sequence, kv head) pairs one launch may hold
 constexpr int kSkMaxSeqs = 512;       // sequences one launch may hold
+constexpr int kUmmaAutoMinKeys = 4096; // automatic plans: key span from which verify blocks use tcgen05
 
 template <int HD>
 struct USmem {
@@ -1378,11 +1379,18 @@ bool tc_applicable(const sdl_attn_args* a) {
 // kv head and up to 512 (sequence, kv head) pairs.  It runs when asked for
 // (use_umma = 1); the automatic plan keeps the mma.sync kernel.
 bool umma_applicable(const sdl_attn_args* a) {
-    if (a->use_umma <= 0 || !tc_applicable(a)) return false;
+    if (a->use_umma < 0 || !tc_applicable(a)) return false;
     // Q rows are staged with 16-byte async copies
     if (((a->q_sb | a->q_sj | a->q_sh) & 7) || reinterpret_cast<uintptr_t>(a->q) % 16) return false;
     const int rows = a->chunk * (a->Hq / a->Hkv);
-    return rows <= kURows && (long)a->B * a->Hkv <= kSkMaxPairs;
+    if (rows > kURows || (long)a->B * a->Hkv > kSkMaxPairs) return false;
+    if (a->use_umma > 0) return true;
+    // Automatic choice: the mma.sync kernel spends ~330 issue slots per
+    // 8-column warp and page, so blocks of more than two 8-column tiles per
+    // kv head over long contexts are instruction bound there; the tcgen05
+    // kernel issues the products from one thread.  Short contexts keep the
+    // mma.sync kernel, whose split grid starts faster.
+    return rows > 16 && a->max_limit >= kUmmaAutoMinKeys;
 }
 
 // Workspace of the persistent kernel: the per-pair table, then fp32 partials
@@ -1656,6 +1664,15 @@ extern "C" size_t sdl_attention_workspace_bytes(const sdl_attn_args* args) {
     tmp.workspace = nullptr;
     tmp.workspace_bytes = 0;
     return make_plan(&tmp).ws_bytes;
+}
+
+extern "C" int sdl_attention_kernel(const sdl_attn_args* args) {
+    if (validate(args) != SDL_OK) return -1;
+    sdl_attn_args tmp = *args;
+    tmp.workspace = nullptr;
+    tmp.workspace_bytes = 0;
+    const Plan pl = make_plan(&tmp);
+    return !pl.tc ? 0 : pl.umma ? 2 : 1;
 }
 
 extern "C" int sdl_attention_launches(const sdl_attn_args* args) {

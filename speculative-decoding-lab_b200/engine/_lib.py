@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "sdl_make_kv_tensor_map",
     "sdl_attention_workspace_bytes",
     "sdl_attention_launches",
+    "sdl_attention_kernel",
     "sdl_paged_attention",
     "sdl_paged_attention_noalloc",
     "sdl_noalloc_scratch_bytes",
@@ -139,6 +140,7 @@ _SIGS = {
     "sdl_make_kv_tensor_map": (c_int, [c_void, c_void, c_int, c_i64, c_int, c_int]),
     "sdl_attention_workspace_bytes": (c_size, [_P(SdlAttnArgs)]),
     "sdl_attention_launches": (c_int, [_P(SdlAttnArgs)]),
+    "sdl_attention_kernel": (c_int, [_P(SdlAttnArgs)]),
     "sdl_paged_attention": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_paged_attention_noalloc": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_noalloc_scratch_bytes": (c_size, []),

@@ -117,6 +117,20 @@ def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_
     return n
 
 
+KERNEL_NAMES = ("generic", "mma", "tcgen05")
+
+
+def attention_kernel(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0) -> str:
+    """Which kernel ``paged_attention`` runs for these arguments: "generic"
+    (CUDA cores), "mma" (mma.sync split-K) or "tcgen05" (persistent)."""
+    q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
+    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma)
+    n = _lib.load().sdl_attention_kernel(a)
+    if n < 0:
+        raise RuntimeError("sdl_attention_kernel: " + _lib.last_error())
+    return KERNEL_NAMES[n]
+
+
 def _set_new_rows(a: _lib.SdlAttnArgs, q4: torch.Tensor, kv: PagedKVCache, k_new: Optional[torch.Tensor],
                   v_new: Optional[torch.Tensor]):
     """Point ``a`` at the K/V rows to store before attending (fused append)."""

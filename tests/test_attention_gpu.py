@@ -348,3 +348,23 @@ def test_fused_append_rejects_bad_rows():
     with pytest.raises(ValueError):
         paged_attention(q, kv, 0, batch, k_new=torch.zeros(1, 256, device=DEV),
                         v_new=torch.zeros(1, 256, device=DEV))
+
+
+def test_automatic_kernel_choice():
+    """use_umma=0 picks the tcgen05 kernel for verify blocks of more than 16
+    query rows per kv head over spans of 4096+ keys, the mma.sync kernel for
+    decode and short verify, and the CUDA-core kernel for fp32 pools; the
+    explicit flags override it."""
+    from engine.attention import attention_kernel
+    kv, _ = _build([4200 + 7, 300 + 7], 2, 128, 16, torch.bfloat16, seed=31)
+    long_verify = AttnBatch.from_lists(DEV, [0, 1], [4200, 300], 7)
+    short_verify = AttnBatch.from_lists(DEV, [0, 1], [1000, 300], 7)
+    q7 = torch.zeros(2, 7, 16, 128, device=DEV, dtype=torch.bfloat16)
+    q1 = torch.zeros(2, 1, 16, 128, device=DEV, dtype=torch.bfloat16)
+    assert attention_kernel(q7, kv, long_verify) == "tcgen05"
+    assert attention_kernel(q7, kv, long_verify, use_umma=-1) == "mma"
+    assert attention_kernel(q7, kv, short_verify) == "mma"
+    assert attention_kernel(q7, kv, short_verify, use_umma=1) == "tcgen05"
+    assert attention_kernel(q1, kv, AttnBatch.from_lists(DEV, [0, 1], [4206, 306], 1)) == "mma"
+    kv32, _ = _build([40], 2, 16, 4, torch.float32, seed=32)
+    assert attention_kernel(torch.zeros(1, 1, 4, 16, device=DEV), kv32, AttnBatch.from_lists(DEV, [0], [39], 1)) == "generic"
