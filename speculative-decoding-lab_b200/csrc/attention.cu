@@ -527,6 +527,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 // partial rows at once, each lane owning 4 consecutive head dims.
 __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     pdl_wait();  // partials come from the attention launch just before
+    pdl_launch_dependents();  // the next launch may become resident; it waits for this grid to finish
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 4 + warp;
     if (r >= p.B * p.chunk * p.Hq) return;
@@ -1139,6 +1140,7 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 // row), lanes reduce the slot maxima and sums, then own 4 head dims each.
 __global__ void __launch_bounds__(128) attn_sk_combine_kernel(TcParams p, int hd) {
     pdl_wait();
+    pdl_launch_dependents();  // the next launch may become resident; it waits for this grid to finish
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = p.chunk * p.ratio;
     const int wr = blockIdx.x * 4 + warp;
