@@ -634,18 +634,19 @@ constexpr int kUOCol = 2 * kUTok;     // TMEM column of O buffer 0; buffer 1 is 
 constexpr int kSkMaxPairs = 512;      // (sequence, kv head) pairs one launch may hold
 constexpr int kSkMaxSeqs = 512;       // sequences one launch may hold
 constexpr int kUmmaAutoMinKeys = 4096; // automatic plans: key span from which verify blocks use tcgen05
+constexpr uint32_t kPollLimit = 1u << 24;  // idle polls (32 ns apart) of the tcgen05 MMA thread before a timeout
 
 template <int HD>
 struct USmem {
     static constexpr int DO = HD / 64;
-    static constexpr int kNst = 4;                 // K/V ring depth
-    static constexpr int kQ = DO * kURows * 128;   // one Q buffer (8 KB per 64-column half)
-    static constexpr int kHalf = kUTok * 128;      // one 64-column half of a K or V tile
-    static constexpr int kStage = 2 * DO * kHalf;  // K halves then V halves
-    static constexpr int kP = kURows * 128;        // one 64 x 64 16-bit P matrix
-    static constexpr int kOffKV = 2 * kQ;
+    static constexpr int kNst = HD == 128 ? 5 : 8;  // K/V ring depth (fills the shared memory left)
+    static constexpr int kQ = DO * kURows * 128;    // the Q buffer (8 KB per 64-column half)
+    static constexpr int kHalf = kUTok * 128;       // one 64-column half of a K or V tile
+    static constexpr int kStage = 2 * DO * kHalf;   // K halves then V halves
+    static constexpr int kP = kURows * 128;         // one 64 x 64 16-bit P matrix
+    static constexpr int kOffKV = kQ;
     static constexpr int kOffP = kOffKV + kNst * kStage;
-    static constexpr int kBytes = kOffP + 4 * kP;  // P hi / lo, double buffered
+    static constexpr int kBytes = kOffP + 4 * kP;   // P hi / lo, double buffered
 };
 
 // p as a hi + lo pair of 16-bit values (hi = round(p), lo = round(p - hi)),
@@ -786,11 +787,9 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         const int m = 16 * warp + (lane & 15), hq = lane >> 4;
         if (m >= R) {
 #pragma unroll
-            for (int qb = 0; qb < 2; ++qb)
-#pragma unroll
-                for (int cc = hq * (HD / 16); cc < (hq + 1) * (HD / 16); ++cc)
-                    *reinterpret_cast<uint4*>(sQ + qb * L::kQ + (cc >> 3) * (kURows * 128) + m * 128 + (cc & 7) * 16) =
-                        make_uint4(0u, 0u, 0u, 0u);
+            for (int cc = hq * (HD / 16); cc < (hq + 1) * (HD / 16); ++cc)
+                *reinterpret_cast<uint4*>(sQ + (cc >> 3) * (kURows * 128) + m * 128 + (cc & 7) * 16) =
+                    make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
             for (int mm = 0; mm < 4; ++mm)
 #pragma unroll
@@ -882,58 +881,75 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             const uint64_t dV = umma_desc_sw128(aKV + DO * L::kHalf, L::kHalf, 1024);
             int s_issued = 0, pv_issued = 0;
             bool ok = true;
-            // S cursor: pair and segment ordinal of the next S to issue
+            // Cursors (pair, segment ordinal) of the next S and the next PV.
+            // The thread polls both and issues whichever is ready, so a PV
+            // whose P is done never waits behind the next tile's K/V copy.
             int s_idx = sk_pair_of(s_first, npairs, lo), s_seg = 0;
-            auto issue_s = [&](int t) -> bool {
-                const int pos = lo + t;
-                if (pos >= s_first[s_idx + 1]) { s_idx = sk_pair_of(s_first, npairs, pos); ++s_seg; }
-                const int seg_last = min(hi, s_first[s_idx + 1]) - 1;  // last global tile of this segment
-                const int qb = s_seg & 1, st = t % kUNst, sb = t & 1;
-                if (pos == max(lo, s_first[s_idx]) &&
-                    !mbar_wait_bounded(&q_full[qb], (s_seg >> 1) & 1, kWaitLimit)) return false;
-                if (!mbar_wait_bounded(&kv_full[st], (t / kUNst) & 1, kWaitLimit)) return false;
-                if (t >= 2 && !mbar_wait_bounded(&s_free[sb], ((t - 2) >> 1) & 1, kWaitLimit)) return false;
-                tc_fence_after();
-#pragma unroll
-                for (int k = 0; k < SK; ++k) {
-                    const uint32_t qo = qb * L::kQ + (k >> 2) * (kURows * 128) + (k & 3) * 32;
-                    const uint32_t ko = st * L::kStage + (k >> 2) * L::kHalf + (k & 3) * 32;
-                    umma_f16(tmem + sb * kUTok, dQ + (qo >> 4), dK + (ko >> 4), kIdescS, k > 0 ? 1u : 0u);
-                }
-                umma_commit(&s_full[sb]);
-                if (pos == seg_last) umma_commit(&q_free[qb]);  // the segment's Q buffer may be refilled
-                s_issued = t + 1;
-                return true;
-            };
-            int v_idx = s_idx, v_seg = 0;  // PV cursor
-            ok = issue_s(0);
-            for (int i = 0; ok && i < ntl; ++i) {
+            int v_idx = s_idx, v_seg = 0;
+            uint32_t idle = 0;
+            while (pv_issued < ntl) {
                 if (*s_abort) { ok = false; break; }
-                if (i + 1 < ntl && !issue_s(i + 1)) { ok = false; break; }
-                const int pos = lo + i;
-                if (pos >= s_first[v_idx + 1]) { v_idx = sk_pair_of(s_first, npairs, pos); ++v_seg; }
-                const bool first = pos == max(lo, s_first[v_idx]);
-                const int pb = i & 1, st = i % kUNst;
-                if (!mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kWaitLimit)) { ok = false; break; }
-                // O buffer v_seg & 1 was last read by the epilogue of segment v_seg - 2
-                const int ob = v_seg & 1;
-                if (first && v_seg >= 2 && !mbar_wait_bounded(&o_free[ob], ((v_seg - 2) >> 1) & 1, kWaitLimit)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                bool progress = false;
+                if (pv_issued < s_issued) {
+                    // ---- PV(i): O[64 x d] += P_hi V + P_lo V
+                    const int i = pv_issued, pos = lo + i;
+                    int vi = v_idx, vs = v_seg;
+                    if (pos >= s_first[vi + 1]) { vi = sk_pair_of(s_first, npairs, pos); ++vs; }
+                    const bool first = pos == max(lo, s_first[vi]);
+                    const int pb = i & 1, st = i % kUNst;
+                    const int ob = vs & 1;  // O buffer vs & 1 was last read by the epilogue of segment vs - 2
+                    if (mbar_test_wait(&p_full[pb], (i >> 1) & 1) &&
+                        (!first || vs < 2 || mbar_test_wait(&o_free[ob], ((vs - 2) >> 1) & 1))) {
+                        v_idx = vi;
+                        v_seg = vs;
+                        tc_fence_after();
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
+                        for (int h = 0; h < 2; ++h)
 #pragma unroll
-                    for (int k = 0; k < kUTok / 16; ++k) {
-                        const uint32_t po = (2 * pb + h) * L::kP + k * 32;
-                        const uint32_t vo = st * L::kStage + k * 2048;
-                        umma_f16(tmem + kUOCol + ob * 128, dP + (po >> 4), dV + (vo >> 4), kIdescO,
-                                 (!first || h > 0 || k > 0) ? 1u : 0u);
+                            for (int k = 0; k < kUTok / 16; ++k) {
+                                const uint32_t po = (2 * pb + h) * L::kP + k * 32;
+                                const uint32_t vo = st * L::kStage + k * 2048;
+                                umma_f16(tmem + kUOCol + ob * 128, dP + (po >> 4), dV + (vo >> 4), kIdescO,
+                                         (!first || h > 0 || k > 0) ? 1u : 0u);
+                            }
+                        umma_commit(&p_free[pb]);
+                        umma_commit(&kv_empty[st]);
+                        pv_issued = i + 1;
+                        progress = true;
                     }
-                umma_commit(&p_free[pb]);
-                umma_commit(&kv_empty[st]);
-                pv_issued = i + 1;
+                }
+                if (s_issued < ntl) {
+                    // ---- S(t) = Q K^T into TMEM buffer t & 1
+                    const int t = s_issued, pos = lo + t;
+                    int si = s_idx, ss = s_seg;
+                    if (pos >= s_first[si + 1]) { si = sk_pair_of(s_first, npairs, pos); ++ss; }
+                    const bool seg_first = pos == max(lo, s_first[si]);
+                    const int st = t % kUNst, sb = t & 1;
+                    if ((!seg_first || mbar_test_wait(&q_full[0], ss & 1)) &&
+                        mbar_test_wait(&kv_full[st], (t / kUNst) & 1) &&
+                        (t < 2 || mbar_test_wait(&s_free[sb], ((t - 2) >> 1) & 1))) {
+                        s_idx = si;
+                        s_seg = ss;
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < SK; ++k) {
+                            const uint32_t qo = (k >> 2) * (kURows * 128) + (k & 3) * 32;
+                            const uint32_t ko = st * L::kStage + (k >> 2) * L::kHalf + (k & 3) * 32;
+                            umma_f16(tmem + sb * kUTok, dQ + (qo >> 4), dK + (ko >> 4), kIdescS, k > 0 ? 1u : 0u);
+                        }
+                        umma_commit(&s_full[sb]);
+                        // the segment's last S: the Q buffer may be refilled once it completes
+                        if (pos == min(hi, s_first[si + 1]) - 1) umma_commit(&q_free[0]);
+                        s_issued = t + 1;
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    idle = 0;
+                } else {
+                    if (++idle > kPollLimit) { ok = false; break; }
+                    __nanosleep(32);  // leave the issue slots to the softmax warp sharing this sub-partition
+                }
             }
             if (!ok) {
                 sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
@@ -954,9 +970,9 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
         bool ok = true;
 
-        // Q rows of a segment's pair into Q buffer qb (rows >= R stay zero):
+        // Q rows of a segment's pair into the Q buffer (rows >= R stay zero):
         // 16-byte async copies now, published to the MMA thread later.
-        auto issue_q = [&](int idx, int qb) {
+        auto issue_q = [&](int idx) {
             const int b = idx / p.Hkv, head = idx % p.Hkv;
             if (m < R) {
                 const bool live = jr < s_nval[b];
@@ -964,22 +980,22 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                                 (head * p.ratio + hl) * p.q_sh;
 #pragma unroll
                 for (int cc = hc * (HD / 16); cc < (hc + 1) * (HD / 16); ++cc) {
-                    uint8_t* dst = sQ + qb * L::kQ + (cc >> 3) * (kURows * 128) + m * 128 + (((cc & 7) ^ (m & 7)) << 4);
+                    uint8_t* dst = sQ + (cc >> 3) * (kURows * 128) + m * 128 + (((cc & 7) ^ (m & 7)) << 4);
                     if (live) cp_async16(dst, qrow + 8 * cc);
                     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
         };
-        auto publish_q = [&](int qb) {
+        auto publish_q = [&]() {
             cp_async_wait_all();
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&q_full[qb]);
+            if (lane == 0) mbar_arrive(&q_full[0]);
         };
 
         int idx = sk_pair_of(s_first, npairs, lo), seg = 0;
-        issue_q(idx, 0);
-        publish_q(0);
+        issue_q(idx);
+        publish_q();
         int i = 0;
         while (i < ntl && ok) {
             // ---- one segment: tiles [seg_lo, seg_hi) of pair idx (global positions)
@@ -992,15 +1008,8 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             const int lim = live ? start + jr + 1 : 0;  // the row attends positions < lim
             const int lim_eff = min(lim, npg * kPage);
             const int tile0 = seg_lo - s_first[idx];    // first tile of the segment within the pair
-            // the next segment's Q goes into the other buffer once its last user is done
+            // the next segment's Q refills the buffer once this segment's last S is done
             const bool stage_next = seg_hi < hi;
-            const int nqb = (seg + 1) & 1;
-            if (stage_next) {
-                if (seg + 1 >= 2)
-                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&q_free[nqb], ((seg - 1) >> 1) & 1, kWaitLimit));
-                if (!ok) break;
-                issue_q(sk_pair_of(s_first, npairs, seg_hi), nqb);
-            }
             float m_run = -INFINITY, l_run = 0.f;
             for (int pos = seg_lo; pos < seg_hi; ++pos, ++i) {
                 const int sb = i & 1, pb = i & 1;
@@ -1014,6 +1023,12 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_free[sb]);
+                if (stage_next && pos == seg_hi - 1) {
+                    // S of the segment's last tile is done, and with it every read of Q
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&q_free[0], seg & 1, kWaitLimit));
+                    if (!ok) break;
+                    issue_q(sk_pair_of(s_first, npairs, seg_hi));
+                }
 
                 // raw scores; positions at or past the row's limit are masked
                 const int c0 = (tile0 + pos - seg_lo) * kUTok + 32 * hc;
@@ -1077,7 +1092,7 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[pb]);
-                if (stage_next && pos == seg_lo) publish_q(nqb);  // after the segment's first tile
+                if (stage_next && pos == seg_hi - 1) publish_q();  // the copies overlapped this tile's softmax
             }
             if (!ok) break;
             // ---- segment epilogue
