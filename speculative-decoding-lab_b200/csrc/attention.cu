@@ -15,9 +15,11 @@
 //    columns) through a 4-stage mbarrier ring; consumer warps compute
 //    S^T = K_page * Q^T and O^T += V_page^T * P^T with mma.sync m16n8k16
 //    (tokens on the M side so GQA query rows fill the N side), online softmax
-//    in the log2 domain with warp-shuffle column reductions, and P carried
-//    as a hi+lo pair of 16-bit values so the PV product keeps ~16 mantissa
-//    bits.  Splits write fp32 partials; attn_combine_kernel merges them.
+//    in the log2 domain with warp-shuffle column reductions and a lazy
+//    running max; P is carried as a hi+lo pair of 16-bit values for fp32
+//    output (the PV product keeps ~16 mantissa bits) and rounded once for
+//    16-bit output.  Splits write fp32 partials; attn_combine_kernel merges
+//    them.
 //  * attn_generic_kernel (any dtype, any head_dim <= 256, any block size):
 //    one warp per query row on CUDA cores, fp32 arithmetic with expf; used
 //    for fp32 pools and shapes the tensor-core kernel does not cover.
@@ -284,6 +286,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 
     const uint32_t sbase = smem_u32(smem);
     const int mi = lane >> 3, mr = lane & 7;
+    // P as a hi + lo pair for fp32 output (~16 mantissa bits of every weight);
+    // once rounded for 16-bit outputs, whose own rounding bounds the result.
+    const bool p_split = p.out_dtype == SDL_F32;
     bool aborted = false;
     for (int i = 0; i < np; ++i) {
         const int st = i % kStages;
@@ -365,12 +370,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 pv[2 + e] = ex2_approx(fmaf(s[nt][2 + e], p.scale_log2, -muse));
                 l_run[nt][e] += pv[e] + pv[2 + e];
             }
-            const float h0 = round_trip<T>(pv[0]), h1 = round_trip<T>(pv[1]);
-            const float h2 = round_trip<T>(pv[2]), h3 = round_trip<T>(pv[3]);
             pb[nt][0] = movmatrix_trans(pack2<T>(pv[0], pv[1]));
             pb[nt][1] = movmatrix_trans(pack2<T>(pv[2], pv[3]));
-            pl[nt][0] = movmatrix_trans(pack2<T>(pv[0] - h0, pv[1] - h1));
-            pl[nt][1] = movmatrix_trans(pack2<T>(pv[2] - h2, pv[3] - h3));
+            if (p_split) {
+                const float h0 = round_trip<T>(pv[0]), h1 = round_trip<T>(pv[1]);
+                const float h2 = round_trip<T>(pv[2]), h3 = round_trip<T>(pv[3]);
+                pl[nt][0] = movmatrix_trans(pack2<T>(pv[0] - h0, pv[1] - h1));
+                pl[nt][1] = movmatrix_trans(pack2<T>(pv[2] - h2, pv[3] - h3));
+            }
         }
 
         // O^T[d][col] += sum_t V[t][d] P^T[t][col]
@@ -384,7 +391,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
             for (int nt = 0; nt < NTG; ++nt) {
                 mma_16816<T>(acc[mt][nt], a, pb[nt][0], pb[nt][1]);
-                mma_16816<T>(acc[mt][nt], a, pl[nt][0], pl[nt][1]);
+                if (p_split) mma_16816<T>(acc[mt][nt], a, pl[nt][0], pl[nt][1]);
             }
         }
         __syncwarp();
@@ -755,6 +762,10 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int ntl = hi - lo;  // tiles of this CTA
     const int R = p.chunk * p.ratio;
     const int nsoft = (R + 15) / 16;
+    // P as a hi + lo pair of 16-bit values (fp32 output keeps ~16 mantissa bits
+    // of every weight); 16-bit outputs carry P rounded once, as their own
+    // rounding already bounds the result to that precision.
+    const bool p_split = p.out_dtype == SDL_F32;
 
     uint8_t* sQ = smem;
     uint8_t* sKV = smem + L::kOffKV;
@@ -903,8 +914,7 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                         v_idx = vi;
                         v_seg = vs;
                         tc_fence_after();
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
+                        for (int h = 0; h < (p_split ? 2 : 1); ++h)
 #pragma unroll
                             for (int k = 0; k < kUTok / 16; ++k) {
                                 const uint32_t po = (2 * pb + h) * L::kP + k * 32;
@@ -1080,11 +1090,12 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                             const float p0 = ex2_approx(fmaf(sv[8 * k + 2 * e], p.scale_log2, -muse));
                             const float p1 = ex2_approx(fmaf(sv[8 * k + 2 * e + 1], p.scale_log2, -muse));
                             lsum += p0 + p1;
-                            split_pair<T>(p0, p1, hw[e], lw[e]);
+                            if (p_split) split_pair<T>(p0, p1, hw[e], lw[e]);
+                            else hw[e] = pack2<T>(p0, p1);
                         }
                         const int sw = ((4 * hc + k) ^ (m & 7)) << 4;
                         *reinterpret_cast<uint4*>(ph + sw) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                        *reinterpret_cast<uint4*>(pl + sw) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                        if (p_split) *reinterpret_cast<uint4*>(pl + sw) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                     }
                     l_run += lsum;
                 }
