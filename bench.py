@@ -29,6 +29,14 @@ through temperature-1 softmax and the fused rejection sampler with fp32
 uniforms from a seeded stream, and the commit kernel rewinds every block
 table to its accept length.  tokens/s = committed tokens / time.
 
+``--workload c5`` times the attention of one
+long-context round at gamma = 6 per GPU: 16 sequences with contexts
+U[8192, 32768] run 6 draft decode steps over 28 layers of the Qwen2.5-1.5B
+attention shape, then the 7-row verify over 36 layers of the 3B shape
+(16 q heads), each layer one fused append + attention launch; tokens/s =
+batch * 7 verified positions per round / round time, with the verify and
+the decode rooflines reported separately.
+
 Multi-GPU (torchrun): every rank runs its own batch of sequences (weak
 scaling, no data-path collective); a barrier brackets the timed region and the
 slowest rank's time is used.
@@ -61,6 +69,9 @@ C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=
 C2_ATTN_TRAFFIC = 154_140_672 + 4_491_008
 C3 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=32, ctx_lo=256, ctx_hi=2048,
           gamma=5, vocab=151936, temperature=1.0, logit_std=2.0)
+# C5: Qwen2.5-3B-shaped target, 1.5B-shaped draft, 16 sequences per GPU
+C5 = dict(target_layers=36, target_q_heads=16, draft_layers=28, draft_q_heads=12, kv_heads=2, head_dim=128,
+          block_size=16, batch=16, ctx_lo=8192, ctx_hi=32768, gamma=6)
 
 
 def _peaks():
@@ -692,9 +703,11 @@ def main(argv=None) -> int:
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="store each layer's new K/V rows inside the attention launch (default) or with a "
                          "separate append launch before it")
-    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
-                    help="c2: decode attention + KV append (default); c3: verify step at gamma=5")
-    ap.add_argument("--layers", type=int, default=28, help="fewer layers only for profiling captures")
+    ap.add_argument("--workload", choices=["c2", "c3", "c5"], default="c2",
+                    help="c2: decode attention + KV append (default); c3: verify step at gamma=5; "
+                         "c5: the attention of one long-context round at gamma=6 (draft decodes + target verify)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="fewer layers only for profiling captures (default: the workload's model depth)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (C2: 64, C3: 32)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -703,7 +716,11 @@ def main(argv=None) -> int:
     if args.warmup < 3:
         args.warmup = 3
     if args.batch is None:
-        args.batch = C3["batch"] if args.workload == "c3" else C2["batch"]
+        args.batch = {"c2": C2["batch"], "c3": C3["batch"], "c5": C5["batch"]}[args.workload]
+    if args.workload == "c5":
+        return main_c5(args)
+    if args.layers is None:
+        args.layers = 28
     if args.workload == "c3":
         return main_c3(args)
 
@@ -910,6 +927,278 @@ def main_c3(args) -> int:
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu_c5(args, rank: int, world: int, device):
+    """The attention of one C5 round on one GPU: gamma draft decode steps over
+    the draft's layers, then the (gamma+1)-row verify over the target's
+    layers, each layer one fused append + attention launch; both caches are
+    rewound to the context afterwards."""
+    import torch
+
+    from engine import _lib
+    from engine.attention import AttnBatch, attention_kernel, attention_launches, paged_attention
+    from engine.kv import PagedKVCache
+    from engine.workloads import c2_layout
+
+    c = C5
+    umma = UMMA_FLAG[args.attn_kernel]
+    Lt = args.layers or c["target_layers"]
+    Ld = args.layers or c["draft_layers"]
+    B, gam, Hkv, d, bs = args.batch, c["gamma"], c["kv_heads"], c["head_dim"], c["block_size"]
+    Hqt, Hqd = c["target_q_heads"], c["draft_q_heads"]
+    seed = args.seed + rank
+    ctx, _, _ = c2_layout(seed, B, c["ctx_lo"], c["ctx_hi"], bs)
+    sids = list(range(B))
+    gd = torch.Generator(device=device)
+    gd.manual_seed(seed)
+
+    def make_cache(L, extra):
+        cap = sum(-(-(x + extra) // bs) for x in ctx) + B
+        kv = PagedKVCache(L, Hkv, d, cap, bs, device, torch.bfloat16,
+                          max_blocks_per_seq=-(-(c["ctx_hi"] + extra + 1) // bs), max_seqs=B)
+        g = torch.Generator(device="cpu")
+        g.manual_seed(seed + L)
+        kv.allocator._free_stack.copy_(torch.randperm(cap, generator=g).to(torch.int32))
+        for sid in sids:
+            kv.add_sequence(sid)
+        kv.reserve(sids, [0] * B, ctx)
+        kv._k.normal_(generator=gd)
+        kv._v.normal_(generator=gd)
+        return kv
+
+    tgt = make_cache(Lt, gam + 1)
+    dft = make_cache(Ld, gam)
+    bf = torch.bfloat16
+    qt = torch.randn((Lt, B, gam + 1, Hqt, d), generator=gd, device=device).to(bf)
+    kt = torch.randn((Lt, B * (gam + 1), Hkv, d), generator=gd, device=device).to(bf)
+    vt = torch.randn((Lt, B * (gam + 1), Hkv, d), generator=gd, device=device).to(bf)
+    qd = torch.randn((gam, Ld, B, 1, Hqd, d), generator=gd, device=device).to(bf)
+    kd = torch.randn((gam, Ld, B, Hkv, d), generator=gd, device=device).to(bf)
+    vd = torch.randn((gam, Ld, B, Hkv, d), generator=gd, device=device).to(bf)
+    ot = torch.empty_like(qt)
+    od = torch.empty_like(qd)
+    vbatch = AttnBatch.from_lists(device, sids, ctx, gam + 1)
+    dbatches = [AttnBatch.from_lists(device, sids, [x + s for x in ctx], 1) for s in range(gam)]
+    rel = [_lib.REL_TRUNCATE] * B
+
+    def draft_layers():
+        for s in range(gam):
+            for layer in range(Ld):
+                paged_attention(qd[s, layer], dft, layer, dbatches[s], out=od[s, layer], use_umma=umma,
+                                k_new=kd[s, layer], v_new=vd[s, layer])
+
+    def verify_layers():
+        for layer in range(Lt):
+            paged_attention(qt[layer], tgt, layer, vbatch, out=ot[layer], use_umma=umma, k_new=kt[layer],
+                            v_new=vt[layer])
+
+    def reserve():
+        tgt.reserve(sids, ctx, [gam + 1] * B)
+        dft.reserve(sids, ctx, [gam] * B)
+
+    def release():
+        tgt.release(sids, ctx, rel)
+        dft.release(sids, ctx, rel)
+
+    reserve()
+    draft_layers()
+    verify_layers()
+    release()
+    torch.cuda.synchronize(device)
+    g_draft, g_verify = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_draft):
+        draft_layers()
+    with torch.cuda.graph(g_verify):
+        verify_layers()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+
+    def device_step():
+        reserve()
+        g_draft.replay()
+        g_verify.replay()
+        release()
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize(device)
+    tgt.check_errors()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        device_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    step_ms = e0.elapsed_time(e1) / args.steps
+
+    # per-kernel rooflines: the draft decode graph and the verify graph alone
+    reps = max(3, args.steps // 4)
+    reserve()
+    timings = {}
+    for name, gr, n in (("draft", g_draft, gam * Ld), ("verify", g_verify, Lt)):
+        gr.replay()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        a1.record(stream)
+        torch.cuda.synchronize(device)
+        timings[name] = a0.elapsed_time(a1) / (reps * n)
+    release()
+    clk = clocks.stop() if clocks else None
+    tgt.check_errors()
+    dft.check_errors()
+
+    # e2e: the same round through the public per-layer API without graphs,
+    # new Q/K/V rows from pinned host memory, outputs back every round
+    hq = [t.cpu().pin_memory() for t in (qt, kt, vt, qd, kd, vd)]
+    oth = torch.empty(ot.shape, dtype=bf).pin_memory()
+    odh = torch.empty(od.shape, dtype=bf).pin_memory()
+    h2d = sum(t.numel() * 2 for t in hq)
+    d2h = (oth.numel() + odh.numel()) * 2
+
+    def e2e_step():
+        q_t, k_t, v_t, q_d, k_d, v_d = (t.to(device, non_blocking=True) for t in hq)
+        reserve()
+        for s in range(gam):
+            for layer in range(Ld):
+                paged_attention(q_d[s, layer], dft, layer, dbatches[s], out=od[s, layer], use_umma=umma,
+                                k_new=k_d[s, layer], v_new=v_d[s, layer])
+        for layer in range(Lt):
+            paged_attention(q_t[layer], tgt, layer, vbatch, out=ot[layer], use_umma=umma, k_new=k_t[layer],
+                            v_new=v_t[layer])
+        odh.copy_(od, non_blocking=True)
+        oth.copy_(ot, non_blocking=True)
+        release()
+
+    e2e_steps = max(3, args.steps // 4)
+    e2e_step()
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / e2e_steps
+
+    vbytes = sum((x + gam + 1) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * (gam + 1) * Hqt * d * 2 + \
+        sum(-(-(x + gam + 1) // bs) * 4 for x in ctx) + 2 * B * (gam + 1) * 2 * Hkv * d * 2
+    # one draft launch, averaged over the gamma steps (step s attends ctx + s + 1 keys)
+    dbytes = (sum((x + 1 + s) * 2 * Hkv * d * 2 + -(-(x + 1 + s) // bs) * 4 for x in ctx for s in range(gam)) / gam
+              + 2 * B * Hqd * d * 2 + 2 * B * 2 * Hkv * d * 2)
+    launches = 2 + 2 + gam * Ld * attention_launches(qd[0, 0], dft, dbatches[0], use_umma=umma, k_new=kd[0, 0],
+                                                     v_new=vd[0, 0]) + \
+        Lt * attention_launches(qt[0], tgt, vbatch, use_umma=umma, k_new=kt[0], v_new=vt[0])
+    kern = {"verify": attention_kernel(qt[0], tgt, vbatch, use_umma=umma),
+            "draft": attention_kernel(qd[0, 0], dft, dbatches[0], use_umma=umma)}
+    if world > 1:
+        t = torch.tensor([step_ms, e2e_ms, timings["draft"], timings["verify"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, e2e_ms, timings["draft"], timings["verify"] = t.tolist()
+    del g_draft, g_verify
+    return dict(kernel=kern, step_ms=step_ms, e2e_ms=e2e_ms, verify_ms=timings["verify"], draft_ms=timings["draft"],
+                verify_bytes=vbytes, draft_bytes=dbytes, clocks=clk, h2d=h2d, d2h=d2h,
+                launches=launches * args.steps)
+
+
+def main_c5(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    c = C5
+    cfg = {"workload": "C5: attention of one long-context speculative round at gamma=6 "
+                       "(6 draft decode steps x 28 layers of the 1.5B shape, then the 7-row verify x 36 layers "
+                       "of the 3B shape; K/V append fused into every launch)",
+           "target_layers": args.layers or c["target_layers"], "draft_layers": args.layers or c["draft_layers"],
+           "target_q_heads": c["target_q_heads"], "draft_q_heads": c["draft_q_heads"], "kv_heads": c["kv_heads"],
+           "head_dim": c["head_dim"], "block_size": c["block_size"], "gamma": c["gamma"],
+           "batch_per_gpu": args.batch, "global_batch": args.batch * world,
+           "ctx": "U[{},{}] seeded per rank".format(c["ctx_lo"], c["ctx_hi"]),
+           "tokens": "verified positions per round, batch x (gamma+1): the round's upper bound on committed "
+                     "tokens (models and acceptance not modelled)",
+           "block_tables": "random permutation of a pool holding every context",
+           "l2": "no flush needed: every launch reads ~337 MB of K/V (> 126 MB L2)",
+           "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
+           "attention_kernel": args.attn_kernel}
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "metric": METRIC, "config": cfg,
+                              "unavailable": "C5 is not timed on the CPU port (one C5 layer of the numpy port "
+                                             "takes minutes); the C2 and C3 lines carry the CPU baseline"}))
+        return 0
+
+    import torch
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the B200 path has no CPU fallback)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    res = run_gpu_c5(args, rank, world, device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    hbm, peak_kind = _peaks()
+    tokens = args.batch * world * (c["gamma"] + 1)
+    v_gbs = res["verify_bytes"] / (res["verify_ms"] * 1e-3) / 1e9
+    d_gbs = res["draft_bytes"] / (res["draft_ms"] * 1e-3) / 1e9
+    names = {"mma": "attn_tc_kernel (+ attn_combine_kernel)", "tcgen05": "attn_sk_kernel + attn_sk_combine_kernel",
+             "generic": "attn_generic_kernel"}
+    line = {
+        "metric": METRIC,
+        "value": round(tokens / (res["step_ms"] * 1e-3), 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["step_ms"], 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V, U[8192,32768] contexts, random-permutation block tables)",
+        "config": cfg,
+        "roofline": {"bound": "hbm", "achieved": round(v_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(v_gbs / hbm, 4), "traffic": None,
+                     "kernel": names[res["kernel"]["verify"]] + ": 7-row verify attention (3B shape)",
+                     "algorithmic_bytes_per_launch": res["verify_bytes"], "ms_per_launch": round(res["verify_ms"], 5),
+                     "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
+        "decode_roofline": {"achieved": round(d_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(d_gbs / hbm, 4),
+                            "kernel": names[res["kernel"]["draft"]] + ": draft decode attention (1.5B shape)",
+                            "algorithmic_bytes_per_launch": res["draft_bytes"],
+                            "ms_per_launch": round(res["draft_ms"], 5)},
+        "e2e": {"value": round(tokens / (res["e2e_ms"] * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"],
+                "path": "public per-layer API (PagedKVCache.reserve/release + paged_attention with k_new/v_new), "
+                        "no graphs, pinned host Q/K/V in and attention outputs out"},
+        "cpu_baseline": None,
+        "gpu_launches": res["launches"],
+        "clocks": res["clocks"],
+    }
     print(json.dumps(line), flush=True)
     return 0
 

@@ -207,8 +207,8 @@ typedef struct sdl_attn_args {
      * elements, the pool's dtype) are stored at positions starts[b] + j
      * (j below the valid rows) before attending -- the write-then-attend of
      * engine/model.py:143-149 in one call.  The positions' blocks must be
-     * reserved already.  The mma.sync kernel writes them itself; other paths
-     * launch a small append kernel first. */
+     * reserved already.  The mma.sync kernel writes them itself (16-byte
+     * aligned rows); other paths launch a small append kernel first. */
     const void* k_new;
     const void* v_new;
     int64_t new_row_stride;

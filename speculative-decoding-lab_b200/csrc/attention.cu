@@ -79,8 +79,34 @@ struct TcParams {
 
 SDL_DEV uint32_t ld_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Fused append: copies the K and V rows of one kv head for up to kAppendBatch
+// new positions (byte offsets `src` into k_new / v_new and `dst` into the
+// pools; dst < 0 skips a position).  Lanes own 16-byte pieces (K pieces, then
+// V pieces) and issue every load of the batch before any store, so a batch
+// costs one memory round trip.
+constexpr int kAppendBatch = 4;
+template <int HD, typename T>
+SDL_DEV void copy_new_rows(const TcParams& p, int lane, const int64_t (&src)[kAppendBatch],
+                           const int64_t (&dst)[kAppendBatch], int n) {
+    constexpr int kChunks = HD * (int)sizeof(T) / 16;
+    if (lane >= 2 * kChunks) return;
+    const bool isv = lane >= kChunks;
+    const int cb = (lane % kChunks) * 16;
+    const char* s0 = isv ? p.v_new : p.k_new;
+    char* d0 = isv ? p.v_pool : p.k_pool;
+    uint4 v[kAppendBatch];
+#pragma unroll
+    for (int u = 0; u < kAppendBatch; ++u)
+        if (u < n && dst[u] >= 0) v[u] = *reinterpret_cast<const uint4*>(s0 + src[u] + cb);
+#pragma unroll
+    for (int u = 0; u < kAppendBatch; ++u)
+        if (u < n && dst[u] >= 0) *reinterpret_cast<uint4*>(d0 + dst[u] + cb) = v[u];
+}
+
+// 8-column warps: at least two 288-thread CTAs per SM (<= 112 registers), so
+// the 192-thread verify CTAs stay at three per SM.
 template <int HD, int NTG, typename T>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32)
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, NTG == 1 ? 2 : 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const TcParams p) {
     constexpr int DO = HD / 64;
     constexpr int KSTEPS = HD / 16;
@@ -153,35 +179,42 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     if (warp == ncons) {
         // ------------------------------------------------------- producer
         if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
-        if (p.k_new != nullptr) {
-            // Fused append: every new row whose page lies in this CTA's range is
-            // written for this CTA's kv heads (CTAs sharing a page write the same
-            // bytes), then made visible to this CTA's own TMA reads.
-            constexpr int kChunks = HD * (int)sizeof(T) / 16;  // 16-byte pieces of one head row
+        // Fused append: every new row whose page lies in this CTA's range is
+        // written for this CTA's kv heads (CTAs sharing a page write the same
+        // bytes) and made visible to this CTA's own TMA reads, just before the
+        // first page that holds one is issued -- the earlier pages' copies are
+        // in flight meanwhile.
+        const int app_page = p.k_new != nullptr ? max(pbeg, start / kPage) : pend;
+        auto append_rows = [&]() {
             const int row_bytes = p.Hkv * HD * (int)sizeof(T);
-            for (int j = 0; j < nvalid; ++j) {
-                const int pos = start + j, pg = pos / kPage;
-                if (pg < pbeg || pg >= pend) continue;
-                const int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
-                if (phys < 0 || phys >= p.capacity) {
-                    if (lane == 0) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
-                    continue;
+            for (int j0 = 0; j0 < nvalid; j0 += kAppendBatch) {
+                // lane u < kAppendBatch resolves position start + j0 + u: its pool token row, or -1
+                int64_t trow = -1;
+                if (lane < kAppendBatch && j0 + lane < nvalid) {
+                    const int pos = start + j0 + lane, pg = pos / kPage;
+                    if (pg >= pbeg && pg < pend) {
+                        const int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+                        if (phys < 0 || phys >= p.capacity) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+                        else trow = (int64_t)(p.layer * p.capacity + phys) * kPage + pos % kPage;
+                    }
                 }
-                const int64_t dst_row = ((int64_t)(p.layer * p.capacity + phys) * kPage + pos % kPage) * row_bytes;
-                const int64_t src_row = ((int64_t)b * p.chunk + j) * p.new_stride;
+                int64_t tr[kAppendBatch];
+#pragma unroll
+                for (int u = 0; u < kAppendBatch; ++u) tr[u] = __shfl_sync(0xffffffffu, trow, u);
                 for (int gi = 0; gi < p.g_cta; ++gi) {
                     const int hoff = (kvgrp * p.g_cta + gi) * HD * (int)sizeof(T);
-                    if (lane < 2 * kChunks) {
-                        const bool isv = lane >= kChunks;
-                        const int cb = (lane % kChunks) * 16;
-                        const uint4 v = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) + src_row + hoff + cb);
-                        *reinterpret_cast<uint4*>((isv ? p.v_pool : p.k_pool) + dst_row + hoff + cb) = v;
+                    int64_t src[kAppendBatch], dst[kAppendBatch];
+#pragma unroll
+                    for (int u = 0; u < kAppendBatch; ++u) {
+                        src[u] = ((int64_t)b * p.chunk + j0 + u) * p.new_stride + hoff;
+                        dst[u] = tr[u] >= 0 ? tr[u] * row_bytes + hoff : -1;
                     }
+                    copy_new_rows<HD, T>(p, lane, src, dst, min(kAppendBatch, nvalid - j0));
                 }
             }
             asm volatile("fence.proxy.async.global;" ::: "memory");
             __syncwarp();
-        }
+        };
         int issued = 0;
         bool stop = false;
         for (int i0 = 0; i0 < np && !stop; i0 += 32) {
@@ -201,6 +234,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const int t0 = __shfl_sync(0xffffffffu, tok0, k);
                 const int i = i0 + k;
                 const int st = i % kStages;
+                if (pbeg + i == app_page) append_rows();
                 if (i >= kStages) {
                     int ok = 1;
                     if (lane == 0) ok = mbar_wait_bounded(&empty[st], ((i / kStages) - 1) & 1, kWaitLimit) ? 1 : 0;
@@ -1648,7 +1682,7 @@ int validate(const sdl_attn_args* a) {
     return SDL_OK;
 }
 
-// Whether the mma.sync kernel writes the new K/V rows itself (16-byte pieces).
+// Whether the mma.sync kernel may write the new K/V rows itself (16-byte pieces).
 bool append_fusable(const sdl_attn_args* a) {
     const int64_t sb = a->new_row_stride * sdl::dtype_bytes(a->dtype);
     auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
@@ -1723,6 +1757,9 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     cudaStream_t st = sdl::as_stream(stream);
     const int ratio = a->Hq / a->Hkv;
     Plan pl = make_plan(a);
+    // The mma.sync kernel stores the new rows itself (16-byte pieces).  The
+    // tcgen05 kernel does not: a store + proxy fence inside its producer
+    // stalls a deep TMA pipeline longer than a separate append launch costs.
     const bool fused_append = a->k_new && pl.tc && !pl.umma && append_fusable(a);
     if (a->k_new && !fused_append && (rc = launch_append_pos(a, st)) != SDL_OK) return rc;
     if (pl.tc) {

@@ -280,6 +280,9 @@ FUSED_CASES = [
     (14, 2, 64, 5, [0, 31, 1000], None, torch.float16, {"kv_heads_per_cta": 1}),     # fp16, d 64
     (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {}),                      # ragged valid rows
     (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"use_umma": 1}),                # tcgen05: separate append
+    (16, 2, 128, 7, [60, 4200], None, torch.bfloat16, {}),                           # auto tcgen05; rows cross a tile
+    (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {"use_umma": 1}),         # tcgen05, ragged valid rows
+    (14, 2, 64, 5, [0, 31, 1000], None, torch.float16, {"use_umma": 1}),             # tcgen05, fp16, d 64
     (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"force_generic": True}),        # CUDA-core: separate append
     (4, 2, 16, 3, [0, 9, 33], None, torch.float32, {}),                              # fp32 pool: separate append
 ]

@@ -72,7 +72,7 @@ def test_noalloc_refuses_scratch_beyond_its_array():
     rows = torch.arange(64, dtype=torch.int32, device=DEV)
     starts = torch.zeros(64, dtype=torch.int32, device=DEV)
     batch = AttnBatch(rows, starts, 32768)
-    args = _paged_args(q, kv, 0, batch, q)
+    args = _paged_args(q, kv, 0, batch, q, use_umma=-1)  # the mma.sync plan: 64 rows x 32k keys of partials
     assert lib.sdl_attention_workspace_bytes(args) > lib.sdl_noalloc_scratch_bytes()
     rc = lib.sdl_paged_attention_noalloc(ctypes.byref(args), _lib.stream_handle(DEV))
     assert rc == 4  # SDL_ERR_WORKSPACE, refused on the host before any launch
