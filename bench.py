@@ -66,7 +66,7 @@ METRIC = "spec-decode tokens/s (paged KV, 1/2/4/8 GPU); paged-attn HBM GB/s vs 8
 C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=64, ctx_lo=512, ctx_hi=4096)
 # DRAM bytes (read + write) of one C2 attention launch of attn_tc_kernel, from the
 # ncu --set full capture summarised under profiles/ (refreshed when re-profiled).
-C2_ATTN_TRAFFIC = 154_140_672 + 4_491_008
+C2_ATTN_TRAFFIC = 154_166_784 + 4_897_792
 C3 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=32, ctx_lo=256, ctx_hi=2048,
           gamma=5, vocab=151936, temperature=1.0, logit_std=2.0)
 # C5: Qwen2.5-3B-shaped target, 1.5B-shaped draft, 16 sequences per GPU
