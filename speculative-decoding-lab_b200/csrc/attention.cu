@@ -320,6 +320,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 
     const uint32_t sbase = smem_u32(smem);
     const int mi = lane >> 3, mr = lane & 7;
+    // This lane's ldmatrix row offsets within a 2 KB swizzled box: key row t,
+    // 16-byte chunk (2q + h) XOR (t & 7) for the four 16-column steps q of a
+    // 64-column half (K: rows t = mr + 8 (mi & 1), h = mi >> 1; V transposed:
+    // t = mr + 8 (mi >> 1), h = mi & 1).
+    uint32_t koff[4], voff[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int tk = mr + ((mi & 1) << 3), tv = mr + ((mi >> 1) << 3);
+        koff[q] = tk * 128 + (((2 * q + (mi >> 1)) ^ (tk & 7)) << 4);
+        voff[q] = tv * 128 + (((2 * q + (mi & 1)) ^ (tv & 7)) << 4);
+    }
     // P as a hi + lo pair for fp32 output (~16 mantissa bits of every weight);
     // once rounded for 16-bit outputs, whose own rounding bounds the result.
     const bool p_split = p.out_dtype == SDL_F32;
@@ -343,11 +354,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             for (int r = 0; r < 4; ++r) s[nt][r] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < KSTEPS; ++ks) {
-            const int t = mr + ((mi & 1) << 3);
-            const int dd = ks * 16 + ((mi >> 1) << 3);
-            const uint32_t addr = kbase + (dd >> 6) * kBoxBytes + t * 128 + ((((dd & 63) >> 3) ^ (t & 7)) << 4);
             uint32_t a[4];
-            ldmatrix_x4(addr, a[0], a[1], a[2], a[3]);
+            ldmatrix_x4(kbase + koff[ks & 3] + (ks >> 2) * kBoxBytes, a[0], a[1], a[2], a[3]);
 #pragma unroll
             for (int nt = 0; nt < NTG; ++nt) mma_16816<T>(s[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
         }
@@ -417,11 +425,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         // O^T[d][col] += sum_t V[t][d] P^T[t][col]
 #pragma unroll
         for (int mt = 0; mt < KSTEPS; ++mt) {
-            const int t = mr + ((mi >> 1) << 3);
-            const int dd = mt * 16 + ((mi & 1) << 3);
-            const uint32_t addr = vbase + (dd >> 6) * kBoxBytes + t * 128 + ((((dd & 63) >> 3) ^ (t & 7)) << 4);
             uint32_t a[4];
-            ldmatrix_x4_trans(addr, a[0], a[1], a[2], a[3]);
+            ldmatrix_x4_trans(vbase + voff[mt & 3] + (mt >> 2) * kBoxBytes, a[0], a[1], a[2], a[3]);
 #pragma unroll
             for (int nt = 0; nt < NTG; ++nt) {
                 mma_16816<T>(acc[mt][nt], a, pb[nt][0], pb[nt][1]);
