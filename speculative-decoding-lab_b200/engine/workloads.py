@@ -89,6 +89,34 @@ def c2_layout(seed: int = 0, batch: int = 64, ctx_lo: int = 512, ctx_hi: int = 4
 C3 = dict(gamma=5, batch=32, ctx_lo=256, ctx_hi=2048, temperature=1.0, logit_std=2.0, vocab=151936,
           target="qwen2.5-1.5b", draft="qwen2.5-0.5b")
 
+# --------------------------------------------------------------------- C4
+C4 = dict(gamma=4, prompt_mu=6.0, prompt_sigma=0.8, prompt_cap=4096, out_lo=64, out_hi=512, arrival_rate=64.0,
+          pool_fraction=0.8, temperature=1.0, vocab=151936, target="qwen2.5-1.5b", draft="qwen2.5-0.5b")
+
+
+def c4_requests(seed: int = 0, n: int = 2048, mean_gap_steps: float = 1.0, vocab: int = 151936):
+    """C4 requests: prompt length floor(lognormal(6, 0.8)) capped at 4096 (at
+    least 1), ids U[0, vocab), output length U[64, 512], Poisson arrivals.
+
+    The reference's scheduler clock is the step (one speculative round), so
+    the arrival process is Poisson in steps with mean gap ``mean_gap_steps``
+    (the caller maps the config's 64 requests/s per GPU onto rounds).
+    Returns ``(prompt_ids, max_new_tokens, arrive_step)`` triples in arrival
+    order.
+    """
+    c = C4
+    rng = np.random.default_rng(seed)
+    t = 0.0
+    out = []
+    for _ in range(n):
+        length = int(min(c["prompt_cap"], max(1, np.floor(rng.lognormal(c["prompt_mu"], c["prompt_sigma"])))))
+        ids = rng.integers(0, vocab, size=length)
+        new = int(rng.integers(c["out_lo"], c["out_hi"] + 1))
+        out.append(([int(x) for x in ids], new, int(t)))
+        t += float(rng.exponential(mean_gap_steps))
+    return out
+
+
 # --------------------------------------------------------------------- C5
 C5 = dict(gamma=6, batch_per_gpu=16, ctx_lo=8192, ctx_hi=32768, temperature=0.8, new_tokens=256,
           target="qwen2.5-3b", draft="qwen2.5-1.5b")
