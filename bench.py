@@ -708,6 +708,7 @@ def main(argv=None) -> int:
                          "c4: continuous-batching spec scheduler end to end; "
                          "c5: the attention of one long-context round at gamma=6 (draft decodes + target verify)")
     ap.add_argument("--requests", type=int, default=64, help="c4: requests per GPU (the config's 2048 take minutes)")
+    ap.add_argument("--eager", action="store_true", help="c4: run the model forwards eagerly instead of CUDA graphs")
     ap.add_argument("--layers", type=int, default=None,
                     help="fewer layers only for profiling captures (default: the workload's model depth)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (C2: 64, C3: 32)")
@@ -1229,6 +1230,7 @@ def main_c4(args) -> int:
            "prompts": "floor(lognormal(6, 0.8)) capped at 4096, ids U[0, 151936)",
            "outputs": "U[64, 512] new tokens", "arrivals": "Poisson, mean gap {} round(s)".format(gap),
            "kv_pool": "80% of free HBM after weights, block_size 16, target and draft pools",
+           "forwards": "eager" if args.eager else "CUDA-graph replays (batch buckets)",
            "parallelism": "dp{} (request-sharded, independent engines)".format(world)}
     if args.impl == "reference":
         if rank == 0:
@@ -1268,8 +1270,13 @@ def main_c4(args) -> int:
                               draft.num_layers * draft.num_kv_heads * draft.head_dim)
     blocks = int(c["pool_fraction"] * free / per_block)
     ecfg = EngineConfig(block_size=16, max_num_blocks=blocks, max_batch=args.requests)
-    kv = build_kv(target, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=args.requests + 8)
-    dkv = build_kv(draft, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=args.requests + 8)
+    # table rows for every sequence id the warm-up and the timed run create
+    rows = 2 * args.requests + 16
+    kv = build_kv(target, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=rows)
+    dkv = build_kv(draft, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=rows)
+    if not args.eager:
+        target.enable_cuda_graphs()
+        draft.enable_cuda_graphs()
     sched = SpeculativePagedScheduler(target, kv, draft, dkv, ecfg, SpecSampling(temperature=c["temperature"]),
                                       c["gamma"])
 
@@ -1280,9 +1287,10 @@ def main_c4(args) -> int:
                                        arrive_time=t))
         return out
 
-    # warm-up: a short run through every path (prefill, draft steps, verify, sampler, commit)
-    for _ in range(max(1, min(args.warmup, 3))):
-        sched.run_spec_continuous(reqs(4, 1000 + rank, cap_new=16), seed=1, measure=False)
+    # warm-up: the same requests with 8 new tokens each -- every path (prefill,
+    # draft steps, verify, sampler, commit) and, with graphs, the captures of
+    # the batch buckets and key spans the timed run starts with
+    sched.run_spec_continuous(reqs(args.requests, args.seed * 7919 + rank, cap_new=8), seed=1, measure=False)
     torch.cuda.synchronize(device)
     if dist:
         dist.barrier()
@@ -1313,7 +1321,7 @@ def main_c4(args) -> int:
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": res.steps,
-        "warmup": max(1, min(args.warmup, 3)),
+        "warmup": 1,
         "ms_per_step": round(ms / max(1, res.steps), 4),
         "higher_is_better": True,
         "scaling": "weak",

@@ -353,6 +353,33 @@ int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj,
 int sdl_get_error(int32_t* err_word, int32_t* out_host, int32_t clear,
                   void* stream);
 
+/* ---------------------------------------------------------------------
+ * Fused elementwise ops of a decoder layer (16-bit models; no counterpart
+ * as a function in the reference, which chains framework ops:
+ * engine/model.py:41-72 RMSNorm / rotate_half / apply_rotary,
+ * engine/qwen.py:43-75 SwiGLU).  Each rounds to the model dtype where the
+ * reference's chain rounds.
+ * ------------------------------------------------------------------- */
+
+/* out = T((xf / sqrt(mean(xf^2) + eps)) * w) per row, xf = x as fp32.  With
+ * delta != NULL the residual add comes first: x_out = T(x + delta) and the
+ * norm is taken of x_out.  Strides are in elements, rows of `dim`. */
+int sdl_rmsnorm(const void* x, int64_t x_stride, const void* delta, int64_t delta_stride,
+                void* x_out, int64_t x_out_stride, const void* weight, void* out,
+                int64_t out_stride, int32_t rows, int32_t dim, float eps,
+                int32_t dtype, void* stream);
+
+/* In-place rotate-half RoPE of `rows` rows of `heads` x `head_dim`:
+ * x' = T(T(x * cos) + T(rotate_half(x) * sin)), one cos / sin row of
+ * head_dim per x row (engine/model.py:50-56). */
+int sdl_rope(void* x, int64_t x_row_stride, int32_t rows, int32_t heads,
+             int32_t head_dim, const void* cos, int64_t cos_row_stride,
+             const void* sin, int64_t sin_row_stride, int32_t dtype, void* stream);
+
+/* out = T(T(silu(gate)) * up), silu(g) = g / (1 + exp(-g)) (engine/qwen.py:49-50). */
+int sdl_silu_mul(const void* gate, const void* up, void* out, int64_t n,
+                 int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

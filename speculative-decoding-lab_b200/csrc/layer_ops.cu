@@ -1,0 +1,156 @@
+// Fused elementwise ops of a decoder layer (engine/model.py:41-72,
+// engine/qwen.py:43-75) for 16-bit models: RMSNorm (optionally after the
+// residual add), rotate-half RoPE of q and k in place, and the SwiGLU gate.
+// Each replaces a chain of small framework kernels with one launch and
+// reproduces the chain's rounding: every elementwise step of the chain rounds
+// to the model dtype exactly where the chain does.
+//
+//   rmsnorm:  xf = float(x); r = sqrt(mean(xf^2) + eps); out = T((xf / r) * float(w))
+//             (engine/model.py RMSNorm.forward).  The mean is a fixed-order
+//             block sum times fl(1/dim), so it may differ from another sum
+//             order in the last fp32 bit.
+//   add_rmsnorm: h' = T(float(h) + float(d)) (the residual add), then rmsnorm(h').
+//   rope:     x' = T(T(x * c) + T(rh(x) * s)), rh(x) = (-x[d/2:], x[:d/2])
+//             (engine/model.py:50-56: apply_rotary = x*cos + rotate_half(x)*sin).
+//   silu_mul: out = T(float(T(silu(g))) * float(u)), silu(g) = g / (1 + exp(-g))
+//             (engine/qwen.py:49-50).
+#include "sdl_common.cuh"
+
+#include <algorithm>
+
+namespace {
+
+constexpr int kNormThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restrict__ x, int64_t xs,
+                                                               const T* __restrict__ delta, int64_t ds,
+                                                               T* __restrict__ x_out, int64_t xos,
+                                                               const T* __restrict__ w, T* __restrict__ out,
+                                                               int64_t os, int dim, float eps) {
+    __shared__ float s_red[32];
+    const int64_t row = blockIdx.x;
+    const T* xr = x + row * xs;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim; i += kNormThreads) {
+        float v = to_f32<T>(xr[i]);
+        if (delta != nullptr) {
+            const T h = from_f32<T>(__fadd_rn(v, to_f32<T>(delta[row * ds + i])));
+            x_out[row * xos + i] = h;
+            v = to_f32<T>(h);
+        }
+        ss = __fmaf_rn(v, v, ss);
+    }
+    ss = block_sum<float>(ss, s_red);
+    // the mean as sum * fl(1/dim), the form of a mean reduction's final scale
+    const float r = __fsqrt_rn(__fadd_rn(__fmul_rn(ss, __frcp_rn((float)dim)), eps));
+    const T* hr = delta != nullptr ? x_out + row * xos : xr;
+    for (int i = threadIdx.x; i < dim; i += kNormThreads) {
+        const float v = to_f32<T>(hr[i]);
+        out[row * os + i] = from_f32<T>(__fmul_rn(__fdiv_rn(v, r), to_f32<T>(w[i])));
+    }
+}
+
+// One thread per (row, head, i < d/2) pair of rotated elements.
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ x, int64_t xs, int heads, int d, const T* __restrict__ cs,
+                            int64_t cs_stride, const T* __restrict__ sn, int64_t sn_stride, int rows) {
+    const int half = d / 2;
+    const int64_t n = (int64_t)rows * heads * half;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(t % half);
+        const int64_t rh = t / half;
+        const int h = (int)(rh % heads);
+        const int64_t r = rh / heads;
+        T* p = x + r * xs + (int64_t)h * d;
+        const float x1 = to_f32<T>(p[i]), x2 = to_f32<T>(p[i + half]);
+        const T* c = cs + r * cs_stride;
+        const T* s = sn + r * sn_stride;
+        const float c1 = to_f32<T>(c[i]), c2 = to_f32<T>(c[i + half]);
+        const float s1 = to_f32<T>(s[i]), s2 = to_f32<T>(s[i + half]);
+        // rotate_half(x) = (-x2, x1): each product and the sum round to T
+        const float a1 = round_trip<T>(__fmul_rn(x1, c1)), b1 = round_trip<T>(__fmul_rn(-x2, s1));
+        const float a2 = round_trip<T>(__fmul_rn(x2, c2)), b2 = round_trip<T>(__fmul_rn(x1, s2));
+        p[i] = from_f32<T>(__fadd_rn(a1, b1));
+        p[i + half] = from_f32<T>(__fadd_rn(a2, b2));
+    }
+}
+
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float gv = to_f32<T>(g[i]);
+        const float sv = round_trip<T>(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))));
+        out[i] = from_f32<T>(__fmul_rn(sv, to_f32<T>(u[i])));
+    }
+}
+
+int grid_for(int64_t n, int threads) {
+    const int64_t b = (n + threads - 1) / threads;
+    return (int)std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 16);
+}
+
+}  // namespace
+
+extern "C" int sdl_rmsnorm(const void* x, int64_t x_stride, const void* delta, int64_t delta_stride, void* x_out,
+                           int64_t x_out_stride, const void* weight, void* out, int64_t out_stride, int32_t rows,
+                           int32_t dim, float eps, int32_t dtype, void* stream) {
+    if (!x || !weight || !out || rows < 0 || dim < 1 || (delta && !x_out))
+        return sdl::fail(SDL_ERR_INVALID, "sdl_rmsnorm: bad arguments");
+    if (rows == 0) return SDL_OK;
+    cudaStream_t st = sdl::as_stream(stream);
+    if (dtype == SDL_BF16) {
+        using T = __nv_bfloat16;
+        rmsnorm_kernel<T><<<rows, kNormThreads, 0, st>>>((const T*)x, x_stride, (const T*)delta, delta_stride,
+                                                         (T*)x_out, x_out_stride, (const T*)weight, (T*)out,
+                                                         out_stride, dim, eps);
+    } else if (dtype == SDL_F16) {
+        using T = __half;
+        rmsnorm_kernel<T><<<rows, kNormThreads, 0, st>>>((const T*)x, x_stride, (const T*)delta, delta_stride,
+                                                         (T*)x_out, x_out_stride, (const T*)weight, (T*)out,
+                                                         out_stride, dim, eps);
+    } else {
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_rmsnorm: 16-bit dtypes only");
+    }
+    return sdl::check_launch("rmsnorm_kernel");
+}
+
+extern "C" int sdl_rope(void* x, int64_t x_row_stride, int32_t rows, int32_t heads, int32_t head_dim,
+                        const void* cos, int64_t cos_row_stride, const void* sin, int64_t sin_row_stride,
+                        int32_t dtype, void* stream) {
+    if (!x || !cos || !sin || rows < 0 || heads < 1 || head_dim < 2 || head_dim % 2)
+        return sdl::fail(SDL_ERR_INVALID, "sdl_rope: bad arguments");
+    if (rows == 0) return SDL_OK;
+    cudaStream_t st = sdl::as_stream(stream);
+    const int64_t n = (int64_t)rows * heads * (head_dim / 2);
+    const int grid = grid_for(n, 256);
+    if (dtype == SDL_BF16) {
+        using T = __nv_bfloat16;
+        rope_kernel<T><<<grid, 256, 0, st>>>((T*)x, x_row_stride, heads, head_dim, (const T*)cos, cos_row_stride,
+                                              (const T*)sin, sin_row_stride, rows);
+    } else if (dtype == SDL_F16) {
+        using T = __half;
+        rope_kernel<T><<<grid, 256, 0, st>>>((T*)x, x_row_stride, heads, head_dim, (const T*)cos, cos_row_stride,
+                                              (const T*)sin, sin_row_stride, rows);
+    } else {
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_rope: 16-bit dtypes only");
+    }
+    return sdl::check_launch("rope_kernel");
+}
+
+extern "C" int sdl_silu_mul(const void* gate, const void* up, void* out, int64_t n, int32_t dtype, void* stream) {
+    if (!gate || !up || !out || n < 0) return sdl::fail(SDL_ERR_INVALID, "sdl_silu_mul: bad arguments");
+    if (n == 0) return SDL_OK;
+    cudaStream_t st = sdl::as_stream(stream);
+    const int grid = grid_for(n, 256);
+    if (dtype == SDL_BF16) {
+        using T = __nv_bfloat16;
+        silu_mul_kernel<T><<<grid, 256, 0, st>>>((const T*)gate, (const T*)up, (T*)out, n);
+    } else if (dtype == SDL_F16) {
+        using T = __half;
+        silu_mul_kernel<T><<<grid, 256, 0, st>>>((const T*)gate, (const T*)up, (T*)out, n);
+    } else {
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_silu_mul: 16-bit dtypes only");
+    }
+    return sdl::check_launch("silu_mul_kernel");
+}

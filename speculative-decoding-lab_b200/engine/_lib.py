@@ -69,6 +69,9 @@ EXPORTED_SYMBOLS = (
     "sdl_sample_logits_rows",
     "sdl_spec_sample_logits",
     "sdl_get_error",
+    "sdl_rmsnorm",
+    "sdl_rope",
+    "sdl_silu_mul",
 )
 
 
@@ -164,6 +167,10 @@ _SIGS = {
                                        c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void, c_void,
                                        c_size, c_void, c_void]),
     "sdl_get_error": (c_int, [c_void, c_void, c_int, c_void]),
+    "sdl_rmsnorm": (c_int, [c_void, c_i64, c_void, c_i64, c_void, c_i64, c_void, c_void, c_i64, c_int, c_int, c_float,
+                            c_int, c_void]),
+    "sdl_rope": (c_int, [c_void, c_i64, c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_int, c_void]),
+    "sdl_silu_mul": (c_int, [c_void, c_void, c_void, c_i64, c_int, c_void]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None

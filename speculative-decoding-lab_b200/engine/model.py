@@ -30,7 +30,7 @@ from torch import nn
 
 from .attention import AttnBatch, paged_attention
 from .kv import PagedKVCache
-from . import _lib
+from . import _lib, layer_ops
 from .utils import setup_logger
 
 logger = setup_logger(__name__)
@@ -56,6 +56,14 @@ def apply_rotary(x: torch.Tensor, sin: torch.Tensor, cos: torch.Tensor) -> torch
     return x * cos + rotate_half(x) * sin
 
 
+def apply_rotary_(x: torch.Tensor, sin: torch.Tensor, cos: torch.Tensor) -> torch.Tensor:
+    """``apply_rotary`` that may overwrite ``x`` (a fresh projection output):
+    one fused in-place launch for 16-bit CUDA tensors with contiguous rows."""
+    if layer_ops.fusable(x) and x.is_contiguous():
+        return layer_ops.rope_(x, sin, cos)
+    return apply_rotary(x, sin, cos)
+
+
 # --------------------------------------------------------------------- norms
 class RMSNorm(nn.Module):
     def __init__(self, dim: int, eps: float = 1e-6) -> None:
@@ -64,6 +72,8 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if layer_ops.fusable(x):  # one fused launch for 16-bit models
+            return layer_ops.rmsnorm(x, self.weight, self.eps)
         input_dtype = x.dtype
         xf = x.float()
         rms = torch.sqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
@@ -246,8 +256,117 @@ class ToyConfig:
     seed: int = 0
 
 
+class _GraphedForward:
+    """One captured paged forward (embedding to logits) for a fixed cache,
+    rows per position (``chunk``) and padded batch size.
+
+    Static device inputs (token ids, block-table rows, start positions) are
+    refilled before each replay; rows beyond the real batch repeat row 0, so
+    they store the same K/V bytes at the same positions and their logits are
+    discarded.  Reservation of the positions and sampling stay outside the
+    graph.
+    """
+
+    __slots__ = ("graph", "ids", "rows", "starts", "logits", "keep", "table_ptr")
+
+    def __init__(self, graph, ids, rows, starts, logits, keep, table_ptr) -> None:
+        self.graph = graph
+        self.ids = ids
+        self.rows = rows
+        self.starts = starts
+        self.logits = logits
+        self.keep = keep  # every other tensor the captured kernels read (must outlive the graph)
+        self.table_ptr = table_ptr  # the block table the graph reads; a grown (moved) table needs a new capture
+
+
 class PagedLMMixin:
-    """prefill / decode / decode_block over a stack of layers with ``forward_plan``."""
+    """prefill / decode / decode_block over a stack of layers with ``forward_plan``.
+
+    ``enable_cuda_graphs()`` switches decode / decode_block to CUDA-graph
+    replays of the whole forward (one capture per cache, chunk and batch
+    bucket) -- the host issues a handful of copies and one replay instead of
+    ~25 launches per layer.  The kernels are the same; a padded batch may
+    change the GEMM library's and the split-K merge's reduction order, so
+    logits agree with the eager path to rounding, not bit for bit.
+    """
+
+    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
+
+    def enable_cuda_graphs(self, enabled: bool = True) -> None:
+        self._graphs_enabled = bool(enabled)
+        if not enabled:
+            self._graphs = {}
+
+    def _graph_bucket(self, batch: int) -> Optional[int]:
+        if not getattr(self, "_graphs_enabled", False):
+            return None
+        for b in self.GRAPH_BUCKETS:
+            if b >= batch:
+                return b
+        return None
+
+    def _graph_forward(self, input_ids_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
+                       starts: Sequence[int], bucket: int) -> torch.Tensor:
+        """Logits ``(B, chunk, V)`` of positions ``starts[b] + j`` (already
+        reserved) through the captured forward for ``bucket`` rows."""
+        B, chunk = input_ids_2d.shape
+        graphs = self.__dict__.setdefault("_graphs", {})
+        # key span bucket: the attention plan (split size, kernel choice) is
+        # fixed at capture, so graphs are kept per power-of-two bound of the
+        # rows' key span rather than per the whole table width
+        span_cap = kv.width * kv.block_size
+        need = max(int(x) for x in starts) + chunk
+        span = 1024
+        while span < need:
+            span *= 2
+        span = min(span, span_cap)
+        key = (id(kv), chunk, bucket, span)
+        g = graphs.get(key)
+        if g is not None and g.table_ptr != kv._table.data_ptr():
+            # the cache grew its block table (more sequence rows): recapture
+            del graphs[key]
+            g = None
+        meta = _lib.i32([int(x) for x in seq_ids] + [int(x) for x in starts], self.device)
+        ids = input_ids_2d.to(self.device)
+
+        def fill(dst_ids, dst_rows, dst_starts):
+            dst_ids[:B].copy_(ids)
+            dst_rows[:B].copy_(meta[:B])
+            dst_starts[:B].copy_(meta[B:])
+            if bucket > B:
+                dst_ids[B:].copy_(ids[:1].expand(bucket - B, chunk))
+                dst_rows[B:].copy_(meta[:1].expand(bucket - B))
+                dst_starts[B:].copy_(meta[B:B + 1].expand(bucket - B))
+
+        if g is None:
+            s_ids = torch.zeros((bucket, chunk), dtype=torch.long, device=self.device)
+            s_rows = torch.zeros(bucket, dtype=torch.int32, device=self.device)
+            s_starts = torch.zeros(bucket, dtype=torch.int32, device=self.device)
+            fill(s_ids, s_rows, s_starts)
+            batch = AttnBatch(s_rows, s_starts, span)
+            steps = torch.arange(chunk, device=self.device)
+
+            def run() -> torch.Tensor:
+                positions = s_starts.long().unsqueeze(1) + steps.unsqueeze(0)
+                plan = ForwardPlan(None, batch, positions, chunk)
+                hidden = self.embed_tokens(s_ids)
+                cos, sin = self._rope(positions)
+                hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+                return self._logits(hidden)
+
+            # one eager pass sizes every workspace and stores this call's K/V;
+            # the replay below stores the same bytes again
+            run()
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = run()
+            g = _GraphedForward(graph, s_ids, s_rows, s_starts, logits, (steps, batch, kv), kv._table.data_ptr())
+            graphs[key] = g
+        else:
+            fill(g.ids, g.rows, g.starts)
+        g.graph.replay()
+        return g.logits[:B]
 
     def _rope(self, positions: torch.Tensor):
         cs = self._rope_table()[positions]
@@ -279,6 +398,12 @@ class PagedLMMixin:
         ``slots`` (optional) are positions already reserved by a commit kernel.
         """
         self.forward_calls += 1
+        bucket = self._graph_bucket(len(seq_ids))
+        if bucket is not None:
+            ctx = [int(c) for c in ctx_lengths]
+            if slots is None:
+                kv.reserve(seq_ids, ctx, [1] * len(ctx))
+            return self._graph_forward(input_ids.reshape(-1, 1), kv, seq_ids, ctx, bucket)[:, 0]
         plan = plan_decode(kv, seq_ids, ctx_lengths, slots)
         hidden = self.embed_tokens(input_ids.to(self.device).reshape(-1))
         cos, sin = self._rope(plan.positions[:, 0])
@@ -290,6 +415,11 @@ class PagedLMMixin:
         """``chunk`` consecutive tokens per row; returns ``(B, chunk, V)``."""
         self.forward_calls += 1
         B, chunk = input_ids_2d.shape
+        bucket = self._graph_bucket(B)
+        if bucket is not None:
+            starts = [int(x) for x in start_positions]
+            kv.reserve(seq_ids, starts, [chunk] * B)
+            return self._graph_forward(input_ids_2d, kv, seq_ids, starts, bucket)
         plan = plan_block(kv, seq_ids, start_positions, chunk)
         hidden = self.embed_tokens(input_ids_2d.to(self.device))
         cos, sin = self._rope(plan.positions)

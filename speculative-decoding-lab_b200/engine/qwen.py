@@ -21,7 +21,8 @@ from typing import Any, Dict, List, Optional, Sequence
 import torch
 from torch import nn
 
-from .model import IdTokenizer, PagedLMMixin, RMSNorm, apply_rotary, make_rotary_cache, paged_attend
+from . import layer_ops
+from .model import IdTokenizer, PagedLMMixin, RMSNorm, apply_rotary, apply_rotary_, make_rotary_cache, paged_attend
 from .utils import setup_logger
 
 logger = setup_logger(__name__)
@@ -48,6 +49,8 @@ class QwenMLP(nn.Module):
         self.down_proj = nn.Linear(intermediate, hidden, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if layer_ops.fusable(x):
+            return self.down_proj(layer_ops.silu_mul(self.gate_proj(x), self.up_proj(x)))
         return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -66,11 +69,16 @@ class QwenDecoderLayer(nn.Module):
         attn = self.self_attn
         lead = tuple(hidden.shape[:-1])
         x = self.input_layernorm(hidden)
-        q = apply_rotary(attn.q_proj(x).view(*lead, attn.num_heads, attn.head_dim), sin, cos)
-        k = apply_rotary(attn.k_proj(x).view(*lead, attn.num_kv_heads, attn.head_dim), sin, cos)
+        q = apply_rotary_(attn.q_proj(x).view(*lead, attn.num_heads, attn.head_dim), sin, cos)
+        k = apply_rotary_(attn.k_proj(x).view(*lead, attn.num_kv_heads, attn.head_dim), sin, cos)
         v = attn.v_proj(x).view(*lead, attn.num_kv_heads, attn.head_dim)
         out = paged_attend(q, k, v, kv, layer_index, plan)
-        hidden = hidden + attn.o_proj(out.reshape(*lead, -1))
+        o = attn.o_proj(out.reshape(*lead, -1))
+        if layer_ops.fusable(hidden):  # residual add + post-attention norm in one launch
+            norm = self.post_attention_layernorm
+            hidden, x2 = layer_ops.add_rmsnorm(hidden, o, norm.weight, norm.eps)
+            return hidden + self.mlp(x2)
+        hidden = hidden + o
         return hidden + self.mlp(self.post_attention_layernorm(hidden))
 
 
