@@ -44,6 +44,7 @@ constexpr int kBoxBytes = kPage * 128;  // one [16 tokens][64 cols] 16-bit box
 constexpr uint32_t kWaitLimit = 1u << 20;
 constexpr int kMaxClusterSplits = 16;  // splits of one row merged on chip (non-portable cluster size)
 constexpr float kLazyLog2 = 8.f;   // running-max slack of the mma.sync kernel's softmax (log2 units)
+constexpr int kCombineOneRound = 16;  // split merge: splits whose partials one round of loads covers
 
 struct TcParams {
     const void* q;
@@ -567,10 +568,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 }
 
 // Merge split-K partials (m in log2 units, unnormalised O, l).  One warp per
-// (sequence, chunk row, q head).  The merge is latency bound, so it takes
-// two dependent rounds of loads: the splits' (m, l) pairs (lane s holds
-// split s, reduced by an online max/sum across lanes), then up to 16 splits'
-// partial rows at once, each lane owning 4 consecutive head dims.
+// (sequence, chunk row, q head), each lane owning 4 consecutive head dims.
+// The merge is latency bound: up to kCombineOneRound splits take one round
+// of loads (every split's m, l and partial row at once); more take two
+// dependent rounds, the splits' (m, l) pairs (lane s holds split s, reduced
+// by an online max/sum across lanes), then 16 partial rows at a time.
 __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     pdl_wait();  // partials come from the attention launch just before
     pdl_launch_dependents();  // the next launch may become resident; it waits for this grid to finish
@@ -589,7 +591,48 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     if (ns <= 1) return;
     const int64_t idx0 = (((int64_t)b * p.nsplit) * p.chunk + j) * p.Hq + h;
     const int64_t sstride = (int64_t)p.chunk * p.Hq;
+    const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh;
     // Every split below ns saw at least one key of this row, so each m is finite.
+    if (ns <= kCombineOneRound && hd <= 128) {
+        // One round of loads: every split's (m, l) (the same addresses in
+        // every lane) and this lane's 4 head dims of every split's row.
+        const int d0 = lane * 4;
+        const bool mine = d0 < hd;
+        float2 ml[kCombineOneRound];
+        float4 o[kCombineOneRound];
+#pragma unroll
+        for (int t = 0; t < kCombineOneRound; ++t) {
+            ml[t] = make_float2(-INFINITY, 0.f);
+            o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < ns) {
+                const int64_t idx = idx0 + t * sstride;
+                ml[t] = *reinterpret_cast<const float2*>(p.ml_part + idx * 2);
+                if (mine) o[t] = *reinterpret_cast<const float4*>(p.o_part + idx * hd + d0);
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < kCombineOneRound; ++t) M = fmaxf(M, ml[t].x);
+        float den = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int t = 0; t < kCombineOneRound; ++t) {
+            const float w = ex2_approx(ml[t].x - M);  // 0 for the padding slots
+            den = fmaf(w, ml[t].y, den);
+            acc.x = fmaf(w, o[t].x, acc.x);
+            acc.y = fmaf(w, o[t].y, acc.y);
+            acc.z = fmaf(w, o[t].z, acc.z);
+            acc.w = fmaf(w, o[t].w, acc.w);
+        }
+        if (mine) {
+            const float inv = 1.f / den;
+            store_from_f32(p.out, ob + d0, p.out_dtype, acc.x * inv);
+            store_from_f32(p.out, ob + d0 + 1, p.out_dtype, acc.y * inv);
+            store_from_f32(p.out, ob + d0 + 2, p.out_dtype, acc.z * inv);
+            store_from_f32(p.out, ob + d0 + 3, p.out_dtype, acc.w * inv);
+        }
+        return;
+    }
     float M = -INFINITY, den = 0.f;
     for (int s = lane; s < ns; s += 32) {
         const float2 ml = *reinterpret_cast<const float2*>(p.ml_part + (idx0 + s * sstride) * 2);
@@ -606,7 +649,6 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
         M = mn;
     }
     const float inv = 1.f / den;
-    const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh;
     for (int d0 = lane * 4; d0 < hd; d0 += 128) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int s = 0; s < ns; s += 16) {
@@ -1202,7 +1244,11 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 }
 
 // Merge the partials of pairs split across CTAs: one warp per (pair, query
-// row), lanes reduce the slot maxima and sums, then own 4 head dims each.
+// row), each lane owning 4 head dims.  Up to kCombineOneRound slots take one
+// round of loads (every slot's m, l and this lane's dims of its row at once);
+// more take a reduction of the slot maxima and sums across lanes, then the
+// rows slot by slot.  A slot whose tiles lie past the row's key limit holds
+// m = -inf and weighs 0.
 __global__ void __launch_bounds__(128) attn_sk_combine_kernel(TcParams p, int hd) {
     pdl_wait();
     pdl_launch_dependents();  // the next launch may become resident; it waits for this grid to finish
@@ -1219,6 +1265,45 @@ __global__ void __launch_bounds__(128) attn_sk_combine_kernel(TcParams p, int hd
     const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
     if (j >= nvalid) return;
     const int64_t base = (int64_t)t.z * R + m;  // partial of slot t.z, row m
+    if (cnt <= kCombineOneRound && hd <= 128) {
+        const int d0 = lane * 4;
+        const bool mine = d0 < hd;
+        float2 ml[kCombineOneRound];
+        float4 o[kCombineOneRound];
+#pragma unroll
+        for (int s = 0; s < kCombineOneRound; ++s) {
+            ml[s] = make_float2(-INFINITY, 0.f);
+            o[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (s < cnt) {
+                const int64_t row = base + (int64_t)s * R;
+                ml[s] = *reinterpret_cast<const float2*>(p.ml_part + row * 2);
+                if (mine) o[s] = *reinterpret_cast<const float4*>(p.o_part + row * hd + d0);
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < kCombineOneRound; ++s) M = fmaxf(M, ml[s].x);
+        float den = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < kCombineOneRound; ++s) {
+            const float w = ex2_approx(ml[s].x - M);  // 0 for -inf maxima and the padding slots
+            den = fmaf(w, ml[s].y, den);
+            acc.x = fmaf(w, o[s].x, acc.x);
+            acc.y = fmaf(w, o[s].y, acc.y);
+            acc.z = fmaf(w, o[s].z, acc.z);
+            acc.w = fmaf(w, o[s].w, acc.w);
+        }
+        if (mine) {
+            const float inv = 1.f / den;
+            const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + d0;
+            store_from_f32(p.out, ob, p.out_dtype, acc.x * inv);
+            store_from_f32(p.out, ob + 1, p.out_dtype, acc.y * inv);
+            store_from_f32(p.out, ob + 2, p.out_dtype, acc.z * inv);
+            store_from_f32(p.out, ob + 3, p.out_dtype, acc.w * inv);
+        }
+        return;
+    }
     float M = -INFINITY;
     for (int s = lane; s < cnt; s += 32) M = fmaxf(M, p.ml_part[(base + (int64_t)s * R) * 2]);
     M = warp_max(M);
