@@ -119,10 +119,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
-    // Launched as a programmatic dependent: everything below may read what
-    // the preceding kernel (K/V append, block-table reserve) wrote.
-    pdl_wait();
-
     const int b = blockIdx.z;
     const int split = blockIdx.x;
     const int coltile = blockIdx.y % p.ncoltiles;
@@ -130,6 +126,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ncons = p.g_cta * p.wpg;
 
+    // Launched as a programmatic dependent, so this CTA may start while the
+    // preceding kernel runs.  The row metadata (starts, valid_rows, rows) and
+    // the block table are read before griddepcontrol.wait: no kernel of this
+    // library that lets its dependents start early (attention, split merge,
+    // K/V append, sampler) writes them, and the kernels that do (reserve,
+    // release, commit) run to completion before a dependent starts.  Q, the
+    // new K/V rows and the pool pages are read only after the wait.
     const int start = p.starts[b];
     const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
     const int ncol = p.chunk * p.ratio;
@@ -166,6 +169,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     if (lmax <= 0 || pbeg >= pend) return;
     const int np = pend - pbeg;
     const int row = p.dense ? 0 : p.rows[b];
+    // Pool token row of page pbeg + i (producer lanes; out-of-range entries raise and read row 0).
+    auto page_tok = [&](int i) -> int {
+        const int pg = pbeg + i;
+        if (p.dense) return b * p.kv_len + pg * kPage;
+        int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+        if (phys < 0 || phys >= p.capacity) { sdl_raise(p.err, SDL_DEVERR_BAD_INDEX); phys = 0; }
+        return (p.layer * p.capacity + phys) * kPage;
+    };
+    const int tok_first = (warp == ncons && lane < np) ? page_tok(lane) : 0;  // the first 32 pages
 
     if (threadIdx.x == 0) {
         *s_abort = 0;
@@ -175,6 +187,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
         fence_mbar_init();
     }
+    pdl_wait();
     __syncthreads();
 
     if (warp == ncons) {
@@ -219,17 +232,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         int issued = 0;
         bool stop = false;
         for (int i0 = 0; i0 < np && !stop; i0 += 32) {
-            int tok0 = 0;
-            if (i0 + lane < np) {
-                int pg = pbeg + i0 + lane;
-                if (p.dense) {
-                    tok0 = b * p.kv_len + pg * kPage;
-                } else {
-                    int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
-                    if (phys < 0 || phys >= p.capacity) { sdl_raise(p.err, SDL_DEVERR_BAD_INDEX); phys = 0; }
-                    tok0 = (p.layer * p.capacity + phys) * kPage;
-                }
-            }
+            const int tok0 = i0 == 0 ? tok_first : (i0 + lane < np ? page_tok(i0 + lane) : 0);
             const int cnt = min(32, np - i0);
             for (int k = 0; k < cnt; ++k) {
                 const int t0 = __shfl_sync(0xffffffffu, tok0, k);
@@ -792,12 +795,16 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
-    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int npairs = p.B * p.Hkv;
     const int G = gridDim.x, c = blockIdx.x;
 
-    // --- per-sequence data, tile prefix over the pairs, tiles per CTA, slots
+    // --- per-sequence data, tile prefix over the pairs, tiles per CTA, slots.
+    // Computed before griddepcontrol.wait, while the preceding kernel may
+    // still run: no kernel of this library that lets its dependents start
+    // early writes starts, valid_rows, rows or the block table.  The pair
+    // table in the workspace, which the preceding split merge may still
+    // read, is written only after the wait.
     for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
         s_start[b] = p.starts[b];
         s_nval[b] = sk_nvalid(p, b);
@@ -831,13 +838,18 @@ attn_sk_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
         int tot;
         const int ex = block_exclusive_scan<int>(cnt, s_red, &tot);
-        if (idx < npairs) {
-            s_slot[idx] = nslots + ex;
-            if (c == 0) p.sk_table[idx] = make_int4(s_first[idx], s_first[idx + 1] - s_first[idx], nslots + ex, cnt);
-        }
+        if (idx < npairs) s_slot[idx] = nslots + ex;
         nslots += tot;
     }
     __syncthreads();
+    pdl_wait();
+    if (c == 0) {
+        for (int idx = threadIdx.x; idx < npairs; idx += blockDim.x) {
+            const int f = s_first[idx], n = s_first[idx + 1] - f;
+            const int cnt = n > 0 ? (f + n - 1) / tpc - f / tpc + 1 : 0;
+            p.sk_table[idx] = make_int4(f, n, s_slot[idx], cnt);
+        }
+    }
     const int lo = c * tpc, hi = min(total, lo + tpc);
     if (lo >= hi) return;
     const int ntl = hi - lo;  // tiles of this CTA
