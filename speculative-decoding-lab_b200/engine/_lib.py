@@ -208,7 +208,13 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: Optional[torch.device] = None) -> int:
+    """cudaStream_t of the current stream of ``device`` (as an int)."""
+    if _raw_stream is not None and device is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
