@@ -202,6 +202,12 @@ typedef struct sdl_attn_args {
                                  memory, no workspace, when the split count
                                  allows (<= 16).  Slower on ragged batches:
                                  a cluster holds its idle splits' slots    */
+    int64_t key_count;        /* 0, or the host's count of keys the call
+                                 attends, sum over b of starts[b] + chunk:
+                                 the mma.sync plan then sizes its split-K
+                                 grid to one wave of resident CTAs.  Only
+                                 the launch shape depends on it, never the
+                                 result (the grid still covers max_limit) */
     /* Fused K/V append (paged pools only): when k_new != NULL the rows
      * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
      * elements, the pool's dtype) are stored at positions starts[b] + j

@@ -1644,6 +1644,52 @@ bool tc_cluster_fits(int hd, int ntg, int dtype, int nsplit, size_t smem, int th
                     : tc_cluster_fits_inst<128, 1, __half>(nsplit, smem, threads);
 }
 
+// Resident CTAs per SM of one instantiation at this shared-memory size and
+// block (cached per shape; 0 when the query fails).
+template <int HD, int NTG, typename T>
+int tc_occupancy_inst(size_t smem, int threads) {
+    static std::mutex mu;
+    static std::vector<std::pair<uint64_t, int>> cache;
+    const uint64_t key = ((uint64_t)threads << 32) | (uint64_t)smem;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& kv : cache)
+            if (kv.first == key) return kv.second;
+    }
+    int n = 0;
+    if (tc_configure<HD, NTG, T>(smem) != SDL_OK ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_tc_kernel<HD, NTG, T>, threads, smem) != cudaSuccess) {
+        (void)cudaGetLastError();  // a refused query leaves no sticky error
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache.emplace_back(key, n);
+    return n;
+}
+
+int tc_occupancy(int hd, int ntg, int dtype, size_t smem, int threads) {
+    if (dtype == SDL_BF16) {
+        if (hd == 64) return ntg == 2 ? tc_occupancy_inst<64, 2, __nv_bfloat16>(smem, threads)
+                                      : tc_occupancy_inst<64, 1, __nv_bfloat16>(smem, threads);
+        return ntg == 2 ? tc_occupancy_inst<128, 2, __nv_bfloat16>(smem, threads)
+                        : tc_occupancy_inst<128, 1, __nv_bfloat16>(smem, threads);
+    }
+    if (hd == 64) return ntg == 2 ? tc_occupancy_inst<64, 2, __half>(smem, threads)
+                                  : tc_occupancy_inst<64, 1, __half>(smem, threads);
+    return ntg == 2 ? tc_occupancy_inst<128, 2, __half>(smem, threads)
+                    : tc_occupancy_inst<128, 1, __half>(smem, threads);
+}
+
+constexpr int kMinSplitPages = 4;  // fewest pages per split-K CTA the automatic plan chooses
+// Fill of the resident CTA slots the key-count plan aims at, measured on
+// B200 over split sizes.  Decode (one query row per sequence; 64 rows
+// U[512,4096], 144 rows U[200,1500], 16 rows U[8k,32k]) is bandwidth bound
+// and fastest at 86-90 % (fewer, equal CTAs per SM); verify blocks (6-7 rows
+// per sequence) are issue bound and fastest at 95-97 % (more resident warps).
+// Fuller grids spill CTAs into a second wave.
+constexpr double kOneWaveFillDecode = 0.89;
+constexpr double kOneWaveFillBlock = 0.96;
+
 Plan make_plan(const sdl_attn_args* a) {
     if (umma_applicable(a)) return make_umma_plan(a);
     Plan pl;
@@ -1680,6 +1726,21 @@ Plan make_plan(const sdl_attn_args* a) {
     const long target = (long)sm_count() * 4;
     int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
     int pps = a->pages_per_split > 0 ? a->pages_per_split : std::max(4, (max_pages + nsplit_target - 1) / nsplit_target);
+    if (a->pages_per_split <= 0 && a->key_count > 0) {
+        // With the host's key count: the fewest pages per split whose grid
+        // fills about kOneWaveFill* of the resident CTA slots.  Each (row, kv
+        // group, column tile) holds about key_count / B keys and leaves on
+        // average half a split of remainder; a second wave for a few CTAs
+        // costs more than the per-SM balance that smaller splits buy.
+        const int occ = tc_occupancy(a->head_dim, pl.ntg, a->dtype, pl.smem, (pl.g_cta * pl.wpg + 1) * 32);
+        if (occ > 0) {
+            const double slots = (a->chunk == 1 ? kOneWaveFillDecode : kOneWaveFillBlock) * sm_count() * occ;
+            const double row_pages = (double)a->key_count / ((double)a->B * kPage) + 0.5;
+            int p2 = kMinSplitPages;
+            while (p2 < max_pages && (double)base_ctas * (row_pages / p2 + 0.5) > slots) ++p2;
+            pps = std::min(p2, max_pages);
+        }
+    }
     // On-chip merge (opt-in): the row's splits are one cluster of at most
     // kMaxClusterSplits CTAs, which must fit the GPU's cluster occupancy.
     // A cluster is scheduled whole, so the idle splits of short rows hold

@@ -119,6 +119,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("kv_heads_per_cta", c_int),
         ("use_umma", c_int),
         ("cluster_merge", c_int),
+        ("key_count", c_i64),
         ("k_new", c_void),
         ("v_new", c_void),
         ("new_row_stride", c_i64),

@@ -39,14 +39,17 @@ class AttnBatch:
     bound of ``starts[b] + chunk`` used to size the launch grid.
     """
 
-    __slots__ = ("rows", "starts", "max_limit", "valid_rows")
+    __slots__ = ("rows", "starts", "max_limit", "valid_rows", "key_count")
 
     def __init__(self, rows: torch.Tensor, starts: torch.Tensor, max_limit: int,
-                 valid_rows: Optional[torch.Tensor] = None) -> None:
+                 valid_rows: Optional[torch.Tensor] = None, key_count: int = 0) -> None:
         self.rows = rows
         self.starts = starts
         self.max_limit = int(max_limit)
         self.valid_rows = valid_rows
+        # host count of attended keys (sum of starts[b] + chunk), 0 = unknown:
+        # sizes the split-K grid only, never changes the result
+        self.key_count = int(key_count)
 
     @classmethod
     def from_lists(cls, device: torch.device, seq_ids: Sequence[int], starts: Sequence[int], chunk: int) -> "AttnBatch":
@@ -55,7 +58,7 @@ class AttnBatch:
         n = len(seq_ids)
         packed = _lib.i32(seq_ids + starts, device)
         max_limit = (max(starts) + chunk) if n else chunk
-        return cls(packed[:n], packed[n:], max_limit)
+        return cls(packed[:n], packed[n:], max_limit, key_count=sum(starts) + n * chunk)
 
 
 def _args_common(q: torch.Tensor, out: torch.Tensor, Hkv: int, err: Optional[torch.Tensor]) -> _lib.SdlAttnArgs:
@@ -96,6 +99,7 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
     a.starts = batch.starts.data_ptr()
     a.valid_rows = batch.valid_rows.data_ptr() if batch.valid_rows is not None else None
     a.max_limit = batch.max_limit
+    a.key_count = batch.key_count
     a.pages_per_split = int(pages_per_split)
     a.force_generic = 1 if force_generic else 0
     a.kv_heads_per_cta = int(kv_heads_per_cta)
@@ -235,7 +239,8 @@ def paged_attention(
     # Everything the launch plan and the struct's fixed fields depend on,
     # including the pointer alignments the plan tests.
     key = (id(kv), kv._table.data_ptr(), kv._k.data_ptr(), batch.rows.data_ptr(), batch.starts.data_ptr(),
-           vr.data_ptr() if vr is not None else 0, batch.max_limit, tuple(q.shape), q.stride(), q.dtype,
+           vr.data_ptr() if vr is not None else 0, batch.max_limit, batch.key_count, tuple(q.shape), q.stride(),
+           q.dtype,
            q.data_ptr() % 16, out.stride(), out.dtype, force_generic, pages_per_split, kv_heads_per_cta,
            use_umma, cluster_merge, -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16), threading.get_ident())
     ent = _ARGS_CACHE.get(key)

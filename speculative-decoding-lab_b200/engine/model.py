@@ -139,7 +139,7 @@ def plan_prefill(kv: PagedKVCache, seq_ids: Sequence[int], seq_lengths: Sequence
         grid[mask] = slots
         slots = grid
     packed = _lib.i32([int(s) for s in seq_ids] + [0] * B + lengths, kv.device)
-    batch = AttnBatch(packed[:B], packed[B:2 * B], chunk, packed[2 * B:])
+    batch = AttnBatch(packed[:B], packed[B:2 * B], chunk, packed[2 * B:], key_count=sum(lengths))
     pos = torch.arange(chunk, device=kv.device).unsqueeze(0).expand(B, chunk)
     return ForwardPlan(slots, batch, pos, chunk)
 
@@ -343,7 +343,9 @@ class PagedLMMixin:
             s_rows = torch.zeros(bucket, dtype=torch.int32, device=self.device)
             s_starts = torch.zeros(bucket, dtype=torch.int32, device=self.device)
             fill(s_ids, s_rows, s_starts)
-            batch = AttnBatch(s_rows, s_starts, span)
+            # the launch shapes follow this capture's lengths (padded rows repeat row 0)
+            keys = sum(int(x) for x in starts) + (bucket - B) * int(starts[0]) + bucket * chunk
+            batch = AttnBatch(s_rows, s_starts, span, key_count=keys)
             steps = torch.arange(chunk, device=self.device)
 
             def run() -> torch.Tensor:
