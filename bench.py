@@ -67,6 +67,14 @@ C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=
 # DRAM bytes (read + write) of one C2 attention launch of attn_tc_kernel, from the
 # ncu --set full capture summarised under profiles/ (refreshed when re-profiled).
 C2_ATTN_TRAFFIC = 154_166_784 + 4_897_792
+
+# kernel names of the attention op per attention_kernel() answer
+ATTN_KERNELS = {
+    "mma": "attn_tc_kernel (+ attn_combine_kernel when split)",
+    "mma_rows": "attn_rows_kernel (+ attn_combine_kernel when split)",
+    "tcgen05": "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)",
+    "generic": "attn_generic_kernel",
+}
 C3 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=32, ctx_lo=256, ctx_hi=2048,
           gamma=5, vocab=151936, temperature=1.0, logit_std=2.0)
 # C5: Qwen2.5-3B-shaped target, 1.5B-shaped draft, 16 sequences per GPU
@@ -837,8 +845,7 @@ def main(argv=None) -> int:
                      "traffic": C2_ATTN_TRAFFIC if args.layers == 28 and res["kernel"] == "mma" else None,
                      "traffic_source": "ncu --set full capture of attn_tc_kernel on this workload (dram read + "
                                        "write per launch, main kernel only; summary under profiles/)",
-                     "kernel": ("attn_tc_kernel + attn_combine_kernel" if res["kernel"] == "mma" else
-                                "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
+                     "kernel": ATTN_KERNELS[res["kernel"]] +
                                " (one paged decode attention op per layer{})".format(
                                    ", new K/V row stored inside it" if args.append == "fused" else ""),
                      "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
@@ -941,8 +948,7 @@ def main_c3(args) -> int:
         "tokens_per_round": round(res["tokens_per_round"], 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
-                     "kernel": ("attn_tc_kernel (+ attn_combine_kernel when split)" if res["kernel"] == "mma" else
-                                "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)") +
+                     "kernel": ATTN_KERNELS[res["kernel"]] +
                                ": (gamma+1)-row verify attention{}".format(
                                    ", new K/V rows stored inside it" if args.append == "fused" else ""),
                      "algorithmic_bytes_per_launch": res["attn_bytes"], "ms_per_launch": round(res["attn_ms"], 5),
@@ -1200,8 +1206,7 @@ def main_c5(args) -> int:
     tokens = args.batch * world * (c["gamma"] + 1)
     v_gbs = res["verify_bytes"] / (res["verify_ms"] * 1e-3) / 1e9
     d_gbs = res["draft_bytes"] / (res["draft_ms"] * 1e-3) / 1e9
-    names = {"mma": "attn_tc_kernel (+ attn_combine_kernel)", "tcgen05": "attn_sk_kernel + attn_sk_combine_kernel",
-             "generic": "attn_generic_kernel"}
+    names = ATTN_KERNELS
     line = {
         "metric": METRIC,
         "value": round(tokens / (res["step_ms"] * 1e-3), 2),

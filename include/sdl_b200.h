@@ -208,6 +208,12 @@ typedef struct sdl_attn_args {
                                  grid to one wave of resident CTAs.  Only
                                  the launch shape depends on it, never the
                                  result (the grid still covers max_limit) */
+    int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
+                                 on the MMA M dimension for blocks of at
+                                 least 16 query rows per kv head, keys on M
+                                 below that), 1 = keys on M (query columns
+                                 on N: the decode layout), 2 = query rows
+                                 on M (FlashAttention-2 register layout)   */
     /* Fused K/V append (paged pools only): when k_new != NULL the rows
      * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
      * elements, the pool's dtype) are stored at positions starts[b] + j
@@ -233,7 +239,8 @@ size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
 int sdl_attention_launches(const sdl_attn_args* args);
 
 /* Kernel sdl_paged_attention runs for `args`: 0 = CUDA-core (generic),
- * 1 = mma.sync split-K, 2 = tcgen05 persistent; -1 when `args` is invalid.
+ * 1 = mma.sync split-K with keys on M, 2 = tcgen05 persistent, 3 = mma.sync
+ * split-K with query rows on M; -1 when `args` is invalid.
  * No counterpart in the reference. */
 int sdl_attention_kernel(const sdl_attn_args* args);
 

@@ -683,6 +683,370 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
     }
 }
 
+// ---------------------------------------------- rows-on-M mma.sync kernel
+// attn_rows_kernel: paged attention for blocks of query rows -- the
+// (gamma+1)-token verify block and prefill chunks -- in the FlashAttention-2
+// register layout.  Row r = token j * ratio + head offset (the GQA rows of
+// one kv head); a warp owns 16 rows on the MMA M dimension and walks 32-key
+// tiles:
+//   S[16 x 32] = Q K^T   Q fragments held in registers, K by ldmatrix;
+//   P = 2^(S * scale * log2(e) - m) per row: the row max takes two quad
+//       shuffles, and O and l are rescaled only when it grows by more than
+//       2^kLazyLog2 (so P <= 2^kLazyLog2);
+//   O[16 x d] += P V     the S accumulators re-packed in place as the A
+//       operand (no transposes), V by ldmatrix.trans.
+// Against the keys-on-M kernel above this needs about a fifth of the
+// instructions per key and row, which is what verify blocks are bound by.
+// A producer warp streams tiles of two 16-token pages of K and V (2 KB
+// 128-byte-swizzled boxes) through a TMA ring, first storing the call's new
+// K/V rows that fall in its pages (fused append), as attn_tc_kernel does.
+// CTA = (split, row tile x kv head, sequence); rows whose pages span several
+// splits leave fp32 partials (same layout) for attn_combine_kernel.
+constexpr int kRowWarps = 4;                 // consumer warps of a full row tile
+constexpr int kRowTile = 16 * kRowWarps;     // query rows per CTA
+constexpr int kTilePages = 2;                // 16-token pages per ring stage (32-key tiles)
+constexpr int kRowStages = 4;                // ring depth
+
+template <int HD>
+constexpr int rows_stage_bytes() { return kTilePages * 2 * (HD / 64) * kBoxBytes; }
+
+template <int HD, typename T>
+__global__ void __launch_bounds__((kRowWarps + 1) * 32, 2)
+attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const TcParams p) {
+    constexpr int DO = HD / 64;
+    constexpr int KS = HD / 16;                   // k-steps of S = Q K^T
+    constexpr int ON = HD / 8;                    // n-tiles (8 head dims) of O
+    constexpr int SN = kTilePages * kPage / 8;    // n-tiles (8 keys) of S
+    constexpr int PAGE_BYTES = 2 * DO * kBoxBytes;
+    constexpr int STAGE_BYTES = rows_stage_bytes<HD>();
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRowStages * STAGE_BYTES);
+    uint64_t* empty = full + kRowStages;
+    __shared__ int s_abort_flag;
+    volatile int* s_abort = &s_abort_flag;
+
+    const int b = blockIdx.z, split = blockIdx.x;
+    const int g = blockIdx.y % p.Hkv, rt = blockIdx.y / p.Hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ncons = (int)(blockDim.x >> 5) - 1;
+    const int R = p.chunk * p.ratio;
+
+    // Row metadata and the first page-table batch are read before
+    // griddepcontrol.wait, under the same rule as attn_tc_kernel; Q, the new
+    // K/V rows and the pool pages only after it.
+    const int start = p.starts[b];
+    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
+    const int r_lo = rt * kRowTile;
+    const int r_hi = min(R, r_lo + kRowTile);
+    int lmax = 0;
+    if (r_lo < R && r_lo / p.ratio < nvalid) lmax = start + min((r_hi - 1) / p.ratio, nvalid - 1) + 1;
+    const int npages = lmax > 0 ? (lmax + kPage - 1) / kPage : 0;
+    const int pbeg = split * p.pps;  // pps is a multiple of kTilePages
+    const int pend = min(npages, pbeg + p.pps);
+    // A span past the grid (max_limit below some starts[b] + chunk) is
+    // reported and its excess pages are not attended.
+    if ((npages + p.pps - 1) / p.pps > p.nsplit && threadIdx.x == 0 && split == 0)
+        sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+    if (lmax <= 0 || pbeg >= pend) return;
+    const int np = pend - pbeg;
+    const int ntile = (np + kTilePages - 1) / kTilePages;
+    const int row = p.dense ? 0 : p.rows[b];
+    // Pool token row of page pg (out-of-range entries raise and read row 0).
+    auto page_tok = [&](int pg) -> int {
+        if (p.dense) return b * p.kv_len + pg * kPage;
+        int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+        if (phys < 0 || phys >= p.capacity) { sdl_raise(p.err, SDL_DEVERR_BAD_INDEX); phys = 0; }
+        return (p.layer * p.capacity + phys) * kPage;
+    };
+    const int tok_first = (warp == ncons && lane < np) ? page_tok(pbeg + lane) : 0;
+
+    if (threadIdx.x == 0) {
+        *s_abort = 0;
+        for (int s = 0; s < kRowStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ncons);
+        }
+        fence_mbar_init();
+    }
+    pdl_wait();
+    __syncthreads();
+
+    if (warp == ncons) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
+        // first page of this split that holds a new row (-1: no append)
+        const int app_page = p.k_new != nullptr && max(pbeg, start / kPage) < pend ? max(pbeg, start / kPage) : -1;
+        // Fused append of kv head g's slice of every new row whose page lies
+        // in [pbeg, pend), before the tile holding the first of them is issued.
+        auto append_rows = [&]() {
+            const int row_bytes = p.Hkv * HD * (int)sizeof(T);
+            const int hoff = g * HD * (int)sizeof(T);
+            for (int j0 = 0; j0 < nvalid; j0 += kAppendBatch) {
+                int64_t trow = -1;
+                if (lane < kAppendBatch && j0 + lane < nvalid) {
+                    const int pos = start + j0 + lane, pg = pos / kPage;
+                    if (pg >= pbeg && pg < pend) {
+                        const int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+                        if (phys < 0 || phys >= p.capacity) sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);
+                        else trow = (int64_t)(p.layer * p.capacity + phys) * kPage + pos % kPage;
+                    }
+                }
+                int64_t src[kAppendBatch], dst[kAppendBatch];
+#pragma unroll
+                for (int u = 0; u < kAppendBatch; ++u) {
+                    const int64_t tr = __shfl_sync(0xffffffffu, trow, u);
+                    src[u] = ((int64_t)b * p.chunk + j0 + u) * p.new_stride + hoff;
+                    dst[u] = tr >= 0 ? tr * row_bytes + hoff : -1;
+                }
+                copy_new_rows<HD, T>(p, lane, src, dst, min(kAppendBatch, nvalid - j0));
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __syncwarp();
+        };
+        int issued = 0;
+        bool stop = false;
+        for (int i0 = 0; i0 < np && !stop; i0 += 32) {  // 32 pages (16 tiles) per table batch
+            const int tok = i0 == 0 ? tok_first : (i0 + lane < np ? page_tok(pbeg + i0 + lane) : 0);
+            const int cnt = min(32, np - i0);
+            for (int k = 0; k < cnt; k += kTilePages) {
+                const int i = (i0 + k) / kTilePages;
+                const int st = i % kRowStages;
+                const int t0 = __shfl_sync(0xffffffffu, tok, k);
+                // a lone last page is loaded twice: its second copy's keys lie
+                // past every row's limit and are masked
+                const int t1 = __shfl_sync(0xffffffffu, tok, min(k + 1, cnt - 1));
+                const int pg0 = pbeg + i0 + k;
+                if (app_page >= pg0 && app_page < pg0 + kTilePages) append_rows();  // app_page < pend
+                if (i >= kRowStages) {
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait_bounded(&empty[st], ((i / kRowStages) - 1) & 1, kWaitLimit) ? 1 : 0;
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok || *s_abort) {
+                        if (lane == 0 && !ok) { sdl_raise(p.err, SDL_DEVERR_TIMEOUT); *s_abort = 1; }
+                        stop = true;
+                        break;
+                    }
+                }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[st], STAGE_BYTES);
+                    uint8_t* sbuf = smem + st * STAGE_BYTES;
+#pragma unroll
+                    for (int q = 0; q < kTilePages; ++q) {
+                        const int tq = q == 0 ? t0 : t1;
+#pragma unroll
+                        for (int dd = 0; dd < DO; ++dd) {
+                            tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[st], 0, dd, g, tq);
+                            tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[st], 0, dd, g, tq);
+                        }
+                    }
+                }
+                __syncwarp();
+                issued = i + 1;
+            }
+        }
+        __syncthreads();
+        // Drain: never leave the CTA with bulk copies still landing in smem.
+        if (lane == 0 && *s_abort) {
+            for (int i = max(0, issued - kRowStages); i < issued; ++i)
+                (void)mbar_wait_bounded(&full[i % kRowStages], (i / kRowStages) & 1, kWaitLimit);
+        }
+        pdl_launch_dependents();
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int t4 = lane & 3, gq = lane >> 2;
+    const int r0 = r_lo + warp * 16;
+    const int ra = r0 + gq, rb = ra + 8;
+    const int ja = ra / p.ratio, jb = rb / p.ratio;
+    const bool va = ra < r_hi && ja < nvalid, vb = rb < r_hi && jb < nvalid;
+    const bool active = r0 < r_hi && r0 / p.ratio < nvalid;  // rows ascend: the warp's first row decides
+    // key limits (rows that are not attended get the tile's limit: finite values, never stored)
+    const int lim_a = va ? start + ja + 1 : lmax, lim_b = vb ? start + jb + 1 : lmax;
+    const int lim_min = __reduce_min_sync(0xffffffffu, min(lim_a, lim_b));
+
+    uint32_t qa[KS][4];
+    {
+        const T* q0 = reinterpret_cast<const T*>(p.q) + b * p.q_sb;
+        const T* qpa = q0 + ja * p.q_sj + (g * p.ratio + ra % p.ratio) * p.q_sh;
+        const T* qpb = q0 + jb * p.q_sj + (g * p.ratio + rb % p.ratio) * p.q_sh;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            qa[ks][0] = va ? ld_u32(qpa + ks * 16 + 2 * t4) : 0u;
+            qa[ks][1] = vb ? ld_u32(qpb + ks * 16 + 2 * t4) : 0u;
+            qa[ks][2] = va ? ld_u32(qpa + ks * 16 + 8 + 2 * t4) : 0u;
+            qa[ks][3] = vb ? ld_u32(qpb + ks * 16 + 8 + 2 * t4) : 0u;
+        }
+    }
+    float o[ON][4];
+#pragma unroll
+    for (int dn = 0; dn < ON; ++dn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[dn][e] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+
+    // ldmatrix lane offsets inside a stage (128-byte swizzle: 16-byte chunk
+    // c of token row t sits at chunk c ^ (t & 7); here t & 7 = lane & 7).
+    // K (S's B operand): matrix m = lane / 8 holds keys 8 nt + (lane & 7),
+    // head-dim chunk 2 ks + m (two k-steps per x4).  V (P V's B operand,
+    // transposed): keys 16 kk + 8 (m & 1) + (lane & 7), dim chunk dn + m / 2.
+    const int sw = lane & 7, mq = lane >> 3;
+    uint32_t kofs[SN];
+#pragma unroll
+    for (int nt = 0; nt < SN; ++nt) kofs[nt] = (nt >> 1) * PAGE_BYTES + ((nt & 1) * 8 + sw) * 128;
+    const uint32_t vrow = ((mq & 1) * 8 + sw) * 128;
+    const int vch = mq >> 1;
+    const bool p_split = p.out_dtype == SDL_F32;
+    const uint32_t sbase = smem_u32(smem);
+    bool aborted = false;
+
+    for (int i = 0; i < ntile; ++i) {
+        const int st = i % kRowStages;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (i / kRowStages) & 1, kWaitLimit));
+        if (!ok) {
+            if (lane == 0) { sdl_raise(p.err, SDL_DEVERR_TIMEOUT); *s_abort = 1; }
+            aborted = true;
+            break;
+        }
+        if (active) {
+            const uint32_t sb = sbase + st * STAGE_BYTES;
+            float s[SN][4];
+#pragma unroll
+            for (int nt = 0; nt < SN; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) s[nt][e] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks += 2) {
+                const int c = 2 * ks + mq;
+                const uint32_t co = (c >> 3) * kBoxBytes + (((c & 7) ^ sw) << 4);
+#pragma unroll
+                for (int nt = 0; nt < SN; ++nt) {
+                    uint32_t b0, b1, b2, b3;
+                    ldmatrix_x4(sb + kofs[nt] + co, b0, b1, b2, b3);
+                    mma_16816<T>(s[nt], qa[ks], b0, b1);
+                    mma_16816<T>(s[nt], qa[ks + 1], b2, b3);
+                }
+            }
+            // causal mask (tiles wholly below every row's limit skip it) and row maxima
+            const int pos0 = (pbeg + i * kTilePages) * kPage;
+            const bool whole = pos0 + kTilePages * kPage <= lim_min;
+            float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < SN; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    if (!whole) {
+                        const int key = pos0 + nt * 8 + 2 * t4 + e;
+                        if (key >= lim_a) s[nt][e] = -INFINITY;
+                        if (key >= lim_b) s[nt][2 + e] = -INFINITY;
+                    }
+                    mxa = fmaxf(mxa, s[nt][e]);
+                    mxb = fmaxf(mxb, s[nt][2 + e]);
+                }
+            mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+            mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+            mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+            mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+            mxa *= p.scale_log2;
+            mxb *= p.scale_log2;
+            const bool na = mxa > m_a + kLazyLog2, nb = mxb > m_b + kLazyLog2;
+            if (__any_sync(0xffffffffu, na || nb)) {
+                if (na) {
+                    const float alpha = ex2_approx(m_a - mxa);  // 0 on the first keys
+                    m_a = mxa;
+                    l_a *= alpha;
+#pragma unroll
+                    for (int dn = 0; dn < ON; ++dn) { o[dn][0] *= alpha; o[dn][1] *= alpha; }
+                }
+                if (nb) {
+                    const float alpha = ex2_approx(m_b - mxb);
+                    m_b = mxb;
+                    l_b *= alpha;
+#pragma unroll
+                    for (int dn = 0; dn < ON; ++dn) { o[dn][2] *= alpha; o[dn][3] *= alpha; }
+                }
+            }
+            // P as the A operand of P V: k-step kk takes S n-tiles 2 kk (keys
+            // 2t, 2t+1 of rows g, g+8) and 2 kk + 1 (keys 8 + 2t, 9 + 2t)
+            const float ua = m_a == -INFINITY ? 0.f : m_a, ub = m_b == -INFINITY ? 0.f : m_b;
+            uint32_t pa[SN / 2][4], pl[SN / 2][4];
+#pragma unroll
+            for (int nt = 0; nt < SN; ++nt) {
+                const float p0 = ex2_approx(fmaf(s[nt][0], p.scale_log2, -ua));
+                const float p1 = ex2_approx(fmaf(s[nt][1], p.scale_log2, -ua));
+                const float p2 = ex2_approx(fmaf(s[nt][2], p.scale_log2, -ub));
+                const float p3 = ex2_approx(fmaf(s[nt][3], p.scale_log2, -ub));
+                l_a += p0 + p1;
+                l_b += p2 + p3;
+                const int kk = nt >> 1, hf = (nt & 1) * 2;
+                pa[kk][hf] = pack2<T>(p0, p1);
+                pa[kk][hf + 1] = pack2<T>(p2, p3);
+                if (p_split) {
+                    pl[kk][hf] = pack2<T>(p0 - round_trip<T>(p0), p1 - round_trip<T>(p1));
+                    pl[kk][hf + 1] = pack2<T>(p2 - round_trip<T>(p2), p3 - round_trip<T>(p3));
+                }
+            }
+#pragma unroll
+            for (int kk = 0; kk < SN / 2; ++kk) {
+#pragma unroll
+                for (int dn = 0; dn < ON; dn += 2) {
+                    const int c = dn + vch;
+                    uint32_t v0, v1, v2, v3;
+                    ldmatrix_x4_trans(sb + kk * PAGE_BYTES + (DO + (c >> 3)) * kBoxBytes + vrow + (((c & 7) ^ sw) << 4),
+                                      v0, v1, v2, v3);
+                    mma_16816<T>(o[dn], pa[kk], v0, v1);
+                    mma_16816<T>(o[dn + 1], pa[kk], v2, v3);
+                    if (p_split) {
+                        mma_16816<T>(o[dn], pl[kk], v0, v1);
+                        mma_16816<T>(o[dn + 1], pl[kk], v2, v3);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    __syncthreads();
+    pdl_launch_dependents();  // the split merge may be scheduled during the epilogue
+    if (aborted || *s_abort || !active) return;
+
+    // Epilogue: rows whose keys all lie in this split write the output,
+    // split rows write partials.
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+        const bool v = hr ? vb : va;
+        if (!v) continue;
+        const int r = hr ? rb : ra;
+        const int j = hr ? jb : ja;
+        const int h = g * p.ratio + r % p.ratio;
+        const int np_c = (start + j + 1 + kPage - 1) / kPage;
+        if (pbeg >= np_c) continue;  // no key of this row in this split
+        const float l = hr ? l_b : l_a;
+        const int ns_c = (np_c + p.pps - 1) / p.pps;
+        if (ns_c == 1) {
+            const float inv = 1.f / l;
+            const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + 2 * t4;
+#pragma unroll
+            for (int dn = 0; dn < ON; ++dn) {
+                store_from_f32(p.out, ob + dn * 8, p.out_dtype, o[dn][2 * hr] * inv);
+                store_from_f32(p.out, ob + dn * 8 + 1, p.out_dtype, o[dn][2 * hr + 1] * inv);
+            }
+        } else {
+            const int64_t idx = (((int64_t)b * p.nsplit + split) * p.chunk + j) * p.Hq + h;
+            float* op = p.o_part + idx * HD + 2 * t4;
+#pragma unroll
+            for (int dn = 0; dn < ON; ++dn)
+                *reinterpret_cast<float2*>(op + dn * 8) = make_float2(o[dn][2 * hr], o[dn][2 * hr + 1]);
+            if (t4 == 0) *reinterpret_cast<float2*>(p.ml_part + idx * 2) = make_float2(hr ? m_b : m_a, l);
+        }
+    }
+}
+
 // ------------------------------------------------------ tcgen05 verify path
 // attn_sk_kernel: paged attention for blocks of up to 64 query rows per kv
 // head (decode and the (gamma+1)-row verify) on the 5th-generation tensor
@@ -1510,6 +1874,7 @@ struct Plan {
     int stage_bytes = 0;
     int ring_bytes = 0;    // shared bytes before the mbarriers (ring, or cluster partials when larger)
     bool cluster = false;  // splits of a row form one cluster and merge on chip
+    bool rows = false;     // rows-on-M mma.sync kernel (ncoltiles = row tiles, wpg = consumer warps)
     bool umma = false;     // tcgen05 verify kernel
     size_t smem = 0;
     size_t ws_bytes = 0;
@@ -1689,9 +2054,113 @@ constexpr int kMinSplitPages = 4;  // fewest pages per split-K CTA the automatic
 // Fuller grids spill CTAs into a second wave.
 constexpr double kOneWaveFillDecode = 0.89;
 constexpr double kOneWaveFillBlock = 0.96;
+constexpr int kRowsMinRows = 16;   // automatic plans: query rows per kv head from which the rows-on-M kernel runs
+
+template <int HD, typename T>
+int rows_configure(size_t smem) {
+    static std::mutex mu;
+    static size_t configured = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem <= configured) return SDL_OK;
+    auto kern = attn_rows_kernel<HD, T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    configured = smem;
+    return SDL_OK;
+}
+
+template <int HD, typename T>
+int rows_occupancy_inst(size_t smem, int threads) {
+    static std::mutex mu;
+    static std::vector<std::pair<uint64_t, int>> cache;
+    const uint64_t key = ((uint64_t)threads << 32) | (uint64_t)smem;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& kv : cache)
+            if (kv.first == key) return kv.second;
+    }
+    int n = 0;
+    if (rows_configure<HD, T>(smem) != SDL_OK ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_rows_kernel<HD, T>, threads, smem) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache.emplace_back(key, n);
+    return n;
+}
+
+int rows_occupancy(int hd, int dtype, size_t smem, int threads) {
+    if (dtype == SDL_BF16)
+        return hd == 64 ? rows_occupancy_inst<64, __nv_bfloat16>(smem, threads)
+                        : rows_occupancy_inst<128, __nv_bfloat16>(smem, threads);
+    return hd == 64 ? rows_occupancy_inst<64, __half>(smem, threads) : rows_occupancy_inst<128, __half>(smem, threads);
+}
+
+// Pages per split-K CTA: without a key count, enough splits for ~4 CTAs per
+// SM if every row spanned max_limit; with one, the fewest pages per split
+// whose grid fills about kOneWaveFill* of the resident CTA slots (`occ` per
+// SM).  Each work item holds about key_count / B keys and leaves on average
+// half a split of remainder; a second wave for a few CTAs costs more than
+// the per-SM balance smaller splits buy.
+int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) {
+    if (a->pages_per_split > 0) return a->pages_per_split;
+    const long target = (long)sm_count() * 4;
+    const int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
+    int pps = std::max(kMinSplitPages, (max_pages + nsplit_target - 1) / nsplit_target);
+    if (a->key_count > 0 && occ > 0) {
+        const double slots = (a->chunk == 1 ? kOneWaveFillDecode : kOneWaveFillBlock) * sm_count() * occ;
+        const double row_pages = (double)a->key_count / ((double)a->B * kPage) + 0.5;
+        int p2 = kMinSplitPages;
+        while (p2 < max_pages && (double)base_ctas * (row_pages / p2 + 0.5) > slots) ++p2;
+        pps = std::min(p2, max_pages);
+    }
+    return pps;
+}
+
+// Splits covering max_limit and their workspace; without enough caller
+// workspace the split doubles until the partials fit.
+void finish_split_plan(const sdl_attn_args* a, Plan& pl, int pps, int max_pages, int align) {
+    for (;;) {
+        pps = (pps + align - 1) / align * align;
+        pl.pps = pps;
+        pl.nsplit = (max_pages + pps - 1) / pps;
+        pl.ws_bytes = pl.nsplit > 1 ? (size_t)a->B * pl.nsplit * a->chunk * a->Hq * (a->head_dim + 2) * sizeof(float) : 0;
+        if (a->pages_per_split > 0 || pl.ws_bytes <= a->workspace_bytes || pl.nsplit == 1 || !a->workspace) break;
+        pps *= 2;
+    }
+}
+
+bool rows_applicable(const sdl_attn_args* a) {
+    if (a->mma_layout == 1 || a->cluster_merge || !tc_applicable(a)) return false;
+    if (a->mma_layout == 2) return true;
+    return a->chunk * (a->Hq / a->Hkv) >= kRowsMinRows;
+}
+
+Plan make_rows_plan(const sdl_attn_args* a) {
+    Plan pl;
+    pl.tc = true;
+    pl.rows = true;
+    const int R = a->chunk * (a->Hq / a->Hkv);
+    pl.ncoltiles = (R + kRowTile - 1) / kRowTile;
+    pl.wpg = (std::min(R, kRowTile) + 15) / 16;
+    pl.g_cta = 1;
+    pl.kvgroups = a->Hkv;
+    pl.stage_bytes = a->head_dim == 128 ? rows_stage_bytes<128>() : rows_stage_bytes<64>();
+    pl.ring_bytes = kRowStages * pl.stage_bytes;
+    pl.smem = (size_t)pl.ring_bytes + 1024 + 2 * kRowStages * sizeof(uint64_t);
+    const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
+    const long base_ctas = (long)a->B * pl.ncoltiles * pl.kvgroups;
+    const int occ = a->key_count > 0 ? rows_occupancy(a->head_dim, a->dtype, pl.smem, (pl.wpg + 1) * 32) : 0;
+    finish_split_plan(a, pl, split_pages(a, base_ctas, max_pages, occ), max_pages, kTilePages);
+    return pl;
+}
 
 Plan make_plan(const sdl_attn_args* a) {
     if (umma_applicable(a)) return make_umma_plan(a);
+    if (rows_applicable(a)) return make_rows_plan(a);
     Plan pl;
     pl.tc = tc_applicable(a);
     if (!pl.tc) return pl;
@@ -1723,24 +2192,9 @@ Plan make_plan(const sdl_attn_args* a) {
     pl.smem = (size_t)pl.ring_bytes + 1024 + (2 * kStages + 2) * sizeof(uint64_t);
     const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
     const long base_ctas = (long)a->B * pl.ncoltiles * pl.kvgroups;
-    const long target = (long)sm_count() * 4;
-    int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
-    int pps = a->pages_per_split > 0 ? a->pages_per_split : std::max(4, (max_pages + nsplit_target - 1) / nsplit_target);
-    if (a->pages_per_split <= 0 && a->key_count > 0) {
-        // With the host's key count: the fewest pages per split whose grid
-        // fills about kOneWaveFill* of the resident CTA slots.  Each (row, kv
-        // group, column tile) holds about key_count / B keys and leaves on
-        // average half a split of remainder; a second wave for a few CTAs
-        // costs more than the per-SM balance that smaller splits buy.
-        const int occ = tc_occupancy(a->head_dim, pl.ntg, a->dtype, pl.smem, (pl.g_cta * pl.wpg + 1) * 32);
-        if (occ > 0) {
-            const double slots = (a->chunk == 1 ? kOneWaveFillDecode : kOneWaveFillBlock) * sm_count() * occ;
-            const double row_pages = (double)a->key_count / ((double)a->B * kPage) + 0.5;
-            int p2 = kMinSplitPages;
-            while (p2 < max_pages && (double)base_ctas * (row_pages / p2 + 0.5) > slots) ++p2;
-            pps = std::min(p2, max_pages);
-        }
-    }
+    const int occ = a->key_count > 0
+                        ? tc_occupancy(a->head_dim, pl.ntg, a->dtype, pl.smem, (pl.g_cta * pl.wpg + 1) * 32) : 0;
+    const int pps = split_pages(a, base_ctas, max_pages, occ);
     // On-chip merge (opt-in): the row's splits are one cluster of at most
     // kMaxClusterSplits CTAs, which must fit the GPU's cluster occupancy.
     // A cluster is scheduled whole, so the idle splits of short rows hold
@@ -1758,13 +2212,7 @@ Plan make_plan(const sdl_attn_args* a) {
             return pl;
         }
     }
-    for (;;) {
-        pl.pps = pps;
-        pl.nsplit = (max_pages + pps - 1) / pps;
-        pl.ws_bytes = pl.nsplit > 1 ? (size_t)a->B * pl.nsplit * a->chunk * a->Hq * (a->head_dim + 2) * sizeof(float) : 0;
-        if (a->pages_per_split > 0 || pl.ws_bytes <= a->workspace_bytes || pl.nsplit == 1 || !a->workspace) break;
-        pps *= 2;
-    }
+    finish_split_plan(a, pl, pps, max_pages, 1);
     return pl;
 }
 
@@ -1779,6 +2227,23 @@ int launch_tc_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams&
                                : sdl::launch_pdl(kern, grid, block, pl.smem, st, mk, mv, tp);
     if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
     return sdl::check_launch("attn_tc_kernel");
+}
+
+template <int HD, typename T>
+int launch_rows_inst(const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl, cudaStream_t st) {
+    auto kern = attn_rows_kernel<HD, T>;
+    int rc = rows_configure<HD, T>(pl.smem);
+    if (rc != SDL_OK) return rc;
+    dim3 grid(pl.nsplit, pl.ncoltiles * pl.kvgroups, tp.B);
+    cudaError_t e = sdl::launch_pdl(kern, grid, dim3((pl.wpg + 1) * 32), pl.smem, st, mk, mv, tp);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("attn_rows_kernel");
+}
+
+template <typename T>
+int launch_rows_dtype(int hd, const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl,
+                      cudaStream_t st) {
+    return hd == 64 ? launch_rows_inst<64, T>(mk, mv, tp, pl, st) : launch_rows_inst<128, T>(mk, mv, tp, pl, st);
 }
 
 template <int HD, typename T>
@@ -1897,7 +2362,7 @@ extern "C" int sdl_attention_kernel(const sdl_attn_args* args) {
     tmp.workspace = nullptr;
     tmp.workspace_bytes = 0;
     const Plan pl = make_plan(&tmp);
-    return !pl.tc ? 0 : pl.umma ? 2 : 1;
+    return !pl.tc ? 0 : pl.umma ? 2 : pl.rows ? 3 : 1;
 }
 
 extern "C" int sdl_attention_launches(const sdl_attn_args* args) {
@@ -1980,6 +2445,9 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         if (pl.umma) {
             if (a->dtype == SDL_BF16) rc = launch_umma_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
             else rc = launch_umma_dtype<__half>(a->head_dim, mk, mv, tp, pl, st);
+        } else if (pl.rows) {
+            if (a->dtype == SDL_BF16) rc = launch_rows_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
+            else rc = launch_rows_dtype<__half>(a->head_dim, mk, mv, tp, pl, st);
         } else if (a->dtype == SDL_BF16) {
             rc = launch_tc_dtype<__nv_bfloat16>(a->head_dim, pl.ntg, mk, mv, tp, pl, st);
         } else {

@@ -120,6 +120,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("use_umma", c_int),
         ("cluster_merge", c_int),
         ("key_count", c_i64),
+        ("mma_layout", c_int),
         ("k_new", c_void),
         ("v_new", c_void),
         ("new_row_stride", c_i64),

@@ -87,7 +87,7 @@ def _launch(a: _lib.SdlAttnArgs, device: torch.device, fn: str = "sdl_paged_atte
 
 
 def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0,
-                kv_heads_per_cta=0, use_umma=0, cluster_merge=False) -> _lib.SdlAttnArgs:
+                kv_heads_per_cta=0, use_umma=0, cluster_merge=False, mma_layout=0) -> _lib.SdlAttnArgs:
     a = _args_common(q, out, kv.num_kv_heads, kv.err_word)
     a.k_pool, a.v_pool = kv._k.data_ptr(), kv._v.data_ptr()
     mk, mv = kv.tensor_maps()
@@ -105,17 +105,19 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
     a.kv_heads_per_cta = int(kv_heads_per_cta)
     a.use_umma = int(use_umma)
     a.cluster_merge = 1 if cluster_merge else 0
+    a.mma_layout = int(mma_layout)
     return a
 
 
 def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
-                       k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None) -> int:
+                       k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
+                       mma_layout: int = 0) -> int:
     """Kernel launches one ``paged_attention`` call with these arguments
     makes: the attention launch, the split-K merge when the plan splits a
     row's pages across CTAs, and a positional append when ``k_new`` is given
     to a plan that does not write inside the attention kernel."""
     q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
-    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma)
+    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma, mma_layout=mma_layout)
     keep = _set_new_rows(a, q4, kv, k_new, v_new)  # noqa: F841 (keeps copies alive)
     n = _lib.load().sdl_attention_launches(a)
     if n < 0:
@@ -123,14 +125,17 @@ def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_
     return n
 
 
-KERNEL_NAMES = ("generic", "mma", "tcgen05")
+KERNEL_NAMES = ("generic", "mma", "tcgen05", "mma_rows")
 
 
-def attention_kernel(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0) -> str:
+def attention_kernel(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
+                     mma_layout: int = 0) -> str:
     """Which kernel ``paged_attention`` runs for these arguments: "generic"
-    (CUDA cores), "mma" (mma.sync split-K) or "tcgen05" (persistent)."""
+    (CUDA cores), "mma" (mma.sync split-K, keys on the MMA M dimension),
+    "mma_rows" (mma.sync split-K, query rows on M) or "tcgen05"
+    (persistent)."""
     q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
-    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma)
+    a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma, mma_layout=mma_layout)
     n = _lib.load().sdl_attention_kernel(a)
     if n < 0:
         raise RuntimeError("sdl_attention_kernel: " + _lib.last_error())
@@ -206,6 +211,7 @@ def paged_attention(
     k_new: Optional[torch.Tensor] = None,
     v_new: Optional[torch.Tensor] = None,
     cluster_merge: bool = False,
+    mma_layout: int = 0,
 ) -> torch.Tensor:
     """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
 
@@ -215,11 +221,12 @@ def paged_attention(
     decoder layer in one launch on the tensor-core path.
 
     ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` /
-    ``cluster_merge`` override the launch plan (pages per split-K CTA, kv
-    heads sharing one CTA of the mma.sync kernel, 1 for the tcgen05 kernel,
-    split partials merged on chip within a thread-block cluster instead of by
-    a separate launch); every plan gives the same result within rounding of
-    the split merge.
+    ``cluster_merge`` / ``mma_layout`` override the launch plan (pages per
+    split-K CTA, kv heads sharing one CTA of the mma.sync kernel, 1 for the
+    tcgen05 kernel, split partials merged on chip within a thread-block
+    cluster instead of by a separate launch, 1 / 2 for the mma.sync kernel
+    with keys / query rows on the MMA M dimension); every plan gives the same
+    result within rounding of the split merge.
     """
     _lib.require_cuda(q, "query")
     if q.dim() != 4 or q.shape[3] != kv.head_dim:
@@ -240,13 +247,13 @@ def paged_attention(
     # including the pointer alignments the plan tests.
     key = (id(kv), kv._table.data_ptr(), kv._k.data_ptr(), batch.rows.data_ptr(), batch.starts.data_ptr(),
            vr.data_ptr() if vr is not None else 0, batch.max_limit, batch.key_count, tuple(q.shape), q.stride(),
-           q.dtype,
-           q.data_ptr() % 16, out.stride(), out.dtype, force_generic, pages_per_split, kv_heads_per_cta,
-           use_umma, cluster_merge, -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16), threading.get_ident())
+           q.dtype, q.data_ptr() % 16, out.stride(), out.dtype, force_generic, pages_per_split, kv_heads_per_cta,
+           use_umma, cluster_merge, mma_layout,
+           -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16), threading.get_ident())
     ent = _ARGS_CACHE.get(key)
     if ent is None or ent.kv() is not kv:
         a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma,
-                        cluster_merge)
+                        cluster_merge, mma_layout)
         if kn is not None:
             a.k_new, a.v_new, a.new_row_stride = kn.data_ptr(), vn.data_ptr(), kn.stride(0)
         need = int(_lib.load().sdl_attention_workspace_bytes(a))

@@ -141,25 +141,29 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", range(len(CASES)))
-@pytest.mark.parametrize("generic,umma", [(False, 0), (False, 1), (False, -1), (True, 0)])
-def test_paged_attention_matches_oracle(case, generic, umma):
-    """Every kernel (tcgen05, mma.sync, CUDA-core) against the oracle."""
+@pytest.mark.parametrize("generic,umma,layout", [(False, 0, 0), (False, 1, 0), (False, -1, 1), (False, -1, 2),
+                                                 (True, 0, 0)])
+def test_paged_attention_matches_oracle(case, generic, umma, layout):
+    """Every kernel (tcgen05, mma.sync with keys or query rows on the MMA M
+    dimension, CUDA-core) against the oracle."""
     Hq, Hkv, d, chunk, starts, bs, dtype = CASES[case]
     kv, ref = _build([s + chunk for s in starts], Hkv, d, bs, dtype, seed=100 + case)
     rng = np.random.default_rng(case)
     q = torch.from_numpy(rng.standard_normal((len(starts), chunk, Hq, d)).astype(np.float32)).to(DEV, dtype)
     batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
-    out = paged_attention(q, kv, 0, batch, force_generic=generic, use_umma=umma)
-    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, force_generic=generic, use_umma=umma)
+    kw = dict(force_generic=generic, use_umma=umma, mma_layout=layout)
+    out = paged_attention(q, kv, 0, batch, **kw)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, **kw)
     exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(len(starts)), starts)
     _check_bf16(out.float().cpu().numpy(), out32.cpu().numpy(), exact)
     kv.check_errors()
 
 
 @pytest.mark.parametrize("pps", [1, 3, 0, 64, 12])
-@pytest.mark.parametrize("heads_per_cta,umma,cluster", [(0, -1, False), (1, -1, False), (0, -1, True),
-                                                         (1, -1, True), (0, 1, False)])
-def test_split_plans_agree(pps, heads_per_cta, umma, cluster):
+@pytest.mark.parametrize("heads_per_cta,umma,cluster,layout", [(0, -1, False, 1), (1, -1, False, 1),
+                                                                (0, -1, True, 1), (1, -1, True, 1),
+                                                                (0, 1, False, 0), (0, -1, False, 2)])
+def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
     """Every launch plan (pages per split-K CTA from 1, i.e. 150+ splits per
     row, to one split; one or two kv heads per CTA of the mma.sync kernel;
     split partials merged on chip inside a cluster (up to 16 splits) or by a
@@ -170,13 +174,15 @@ def test_split_plans_agree(pps, heads_per_cta, umma, cluster):
         q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
         batch = AttnBatch.from_lists(DEV, [0, 1, 2], starts, chunk)
         out = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, pages_per_split=pps,
-                              kv_heads_per_cta=heads_per_cta, use_umma=umma, cluster_merge=cluster)
+                              kv_heads_per_cta=heads_per_cta, use_umma=umma, cluster_merge=cluster,
+                              mma_layout=layout)
         exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(3), starts)
         assert np.abs(out.cpu().numpy() - exact).max() <= 2e-3 * np.abs(exact).max()
     kv.check_errors()
 
 
-@pytest.mark.parametrize("pps,chunk,cluster", [(4, 1, False), (0, 1, False), (0, 6, True), (16, 6, True)])
+@pytest.mark.parametrize("pps,chunk,cluster", [(4, 1, False), (0, 1, False), (0, 6, True), (16, 6, True),
+                                               (0, 6, False), (4, 6, False)])
 def test_split_merge_is_deterministic(pps, chunk, cluster):
     """The split-K merge (separate launch; on chip in a cluster) has a fixed
     reduction order: repeated calls give identical bits."""
@@ -283,6 +289,11 @@ FUSED_CASES = [
     (16, 2, 128, 7, [60, 4200], None, torch.bfloat16, {}),                           # auto tcgen05; rows cross a tile
     (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {"use_umma": 1}),         # tcgen05, ragged valid rows
     (14, 2, 64, 5, [0, 31, 1000], None, torch.float16, {"use_umma": 1}),             # tcgen05, fp16, d 64
+    (12, 2, 128, 6, [0, 5, 250, 2047], None, torch.bfloat16, {"mma_layout": 1}),     # keys-on-M kernel, verify
+    (12, 2, 128, 22, [3, 700], None, torch.bfloat16, {"mma_layout": 1}),             # keys on M: 3 col tiles
+    (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {"mma_layout": 1}),       # keys on M, ragged rows
+    (12, 2, 128, 24, [0, 37, 500], [24, 5, 17], torch.bfloat16, {"mma_layout": 2}),   # rows on M: 3 row tiles
+    (12, 2, 128, 1, [15, 16, 1029], None, torch.bfloat16, {"mma_layout": 2}),        # rows on M, decode
     (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"force_generic": True}),        # CUDA-core: separate append
     (4, 2, 16, 3, [0, 9, 33], None, torch.float32, {}),                              # fp32 pool: separate append
 ]
@@ -355,9 +366,9 @@ def test_fused_append_rejects_bad_rows():
 
 def test_automatic_kernel_choice():
     """use_umma=0 picks the tcgen05 kernel for verify blocks of more than 16
-    query rows per kv head over spans of 4096+ keys, the mma.sync kernel for
-    decode and short verify, and the CUDA-core kernel for fp32 pools; the
-    explicit flags override it."""
+    query rows per kv head over spans of 4096+ keys, the rows-on-M mma.sync
+    kernel for shorter verify blocks, the keys-on-M one for decode, and the
+    CUDA-core kernel for fp32 pools; the explicit flags override it."""
     from engine.attention import attention_kernel
     kv, _ = _build([4200 + 7, 300 + 7], 2, 128, 16, torch.bfloat16, seed=31)
     long_verify = AttnBatch.from_lists(DEV, [0, 1], [4200, 300], 7)
@@ -365,9 +376,11 @@ def test_automatic_kernel_choice():
     q7 = torch.zeros(2, 7, 16, 128, device=DEV, dtype=torch.bfloat16)
     q1 = torch.zeros(2, 1, 16, 128, device=DEV, dtype=torch.bfloat16)
     assert attention_kernel(q7, kv, long_verify) == "tcgen05"
-    assert attention_kernel(q7, kv, long_verify, use_umma=-1) == "mma"
-    assert attention_kernel(q7, kv, short_verify) == "mma"
+    assert attention_kernel(q7, kv, long_verify, use_umma=-1) == "mma_rows"
+    assert attention_kernel(q7, kv, short_verify) == "mma_rows"
+    assert attention_kernel(q7, kv, short_verify, mma_layout=1) == "mma"
     assert attention_kernel(q7, kv, short_verify, use_umma=1) == "tcgen05"
     assert attention_kernel(q1, kv, AttnBatch.from_lists(DEV, [0, 1], [4206, 306], 1)) == "mma"
+    assert attention_kernel(q1, kv, AttnBatch.from_lists(DEV, [0, 1], [4206, 306], 1), mma_layout=2) == "mma_rows"
     kv32, _ = _build([40], 2, 16, 4, torch.float32, seed=32)
     assert attention_kernel(torch.zeros(1, 1, 4, 16, device=DEV), kv32, AttnBatch.from_lists(DEV, [0], [39], 1)) == "generic"
