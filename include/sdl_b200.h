@@ -210,10 +210,11 @@ typedef struct sdl_attn_args {
                                  result (the grid still covers max_limit) */
     int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
                                  on the MMA M dimension for blocks of at
-                                 least 16 query rows per kv head, keys on M
-                                 below that), 1 = keys on M (query columns
-                                 on N: the decode layout), 2 = query rows
-                                 on M (FlashAttention-2 register layout)   */
+                                 least 48 query rows per kv head, 16 at
+                                 head_dim 64; keys on M below that), 1 =
+                                 keys on M (query columns on N: the decode
+                                 layout), 2 = query rows on M
+                                 (FlashAttention-2 register layout)        */
     /* Fused K/V append (paged pools only): when k_new != NULL the rows
      * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
      * elements, the pool's dtype) are stored at positions starts[b] + j

@@ -2054,7 +2054,13 @@ constexpr int kMinSplitPages = 4;  // fewest pages per split-K CTA the automatic
 // Fuller grids spill CTAs into a second wave.
 constexpr double kOneWaveFillDecode = 0.89;
 constexpr double kOneWaveFillBlock = 0.96;
-constexpr int kRowsMinRows = 16;   // automatic plans: query rows per kv head from which the rows-on-M kernel runs
+// Automatic plans: query rows per kv head from which the rows-on-M kernel
+// runs.  Measured on B200: it wins for head_dim 64 verify blocks (42 rows:
+// 15.1 against 18.5 us), 56-row verify (100 against 116 us) and prefill;
+// 36-row head_dim-128 verify is latency bound in both and the keys-on-M
+// kernel, with more warps per SM, is 3 % faster there.
+constexpr int kRowsMinRows64 = 16;
+constexpr int kRowsMinRows128 = 48;
 
 template <int HD, typename T>
 int rows_configure(size_t smem) {
@@ -2136,7 +2142,7 @@ void finish_split_plan(const sdl_attn_args* a, Plan& pl, int pps, int max_pages,
 bool rows_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->mma_layout == 2) return true;
-    return a->chunk * (a->Hq / a->Hkv) >= kRowsMinRows;
+    return a->chunk * (a->Hq / a->Hkv) >= (a->head_dim == 64 ? kRowsMinRows64 : kRowsMinRows128);
 }
 
 Plan make_rows_plan(const sdl_attn_args* a) {
