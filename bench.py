@@ -318,7 +318,7 @@ def run_gpu(args, rank: int, world: int, device):
     from engine.workloads import c2_layout
 
     c = dict(C2)
-    umma = UMMA_FLAG[args.attn_kernel]
+    akw = dict(use_umma=UMMA_FLAG[args.attn_kernel], mma_layout=LAYOUT_FLAG[args.mma_layout])
     fused = args.append == "fused"
     L = args.layers
     B = args.batch
@@ -351,12 +351,12 @@ def run_gpu(args, rank: int, world: int, device):
     def step_layers(with_append=True):
         for layer in range(L):
             if with_append and fused:  # store the new K/V row inside the attention launch
-                paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma, k_new=knew[layer],
+                paged_attention(q[layer], kv, layer, batch, out=out[layer], **akw, k_new=knew[layer],
                                 v_new=vnew[layer])
                 continue
             if with_append:
                 kv.append(layer, slots_static, knew[layer], vnew[layer])
-            paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma)
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], **akw)
 
     # warm up every code path once outside capture (attributes, workspace)
     slots_static.copy_(kv.reserve(sids, ctx, [1] * B))
@@ -449,11 +449,11 @@ def run_gpu(args, rank: int, world: int, device):
         b2 = AttnBatch.from_lists(device, sids, ctx, 1)
         for layer in range(L):
             if fused:
-                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma, k_new=kd[layer],
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], **akw, k_new=kd[layer],
                                 v_new=vd[layer])
             else:
                 kv.append(layer, slots, kd[layer], vd[layer])
-                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma)
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], **akw)
         kv.release(sids, ctx, rel_flags)
         out_ready[i].record(comp)
         with torch.cuda.stream(copy_stream):
@@ -487,16 +487,16 @@ def run_gpu(args, rank: int, world: int, device):
     attn_bytes = sum((x + 1) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * Hq * d * 2 + sum(-(-(x + 1) // bs) * 4 for x in ctx)
     if fused:  # the op also reads the new K/V rows and writes them into their pages
         attn_bytes += 2 * (B * 2 * Hkv * d * 2)
-        per_layer = attention_launches(q[0], kv, batch, use_umma=umma, k_new=knew[0], v_new=vnew[0])
+        per_layer = attention_launches(q[0], kv, batch, **akw, k_new=knew[0], v_new=vnew[0])
     else:
-        per_layer = 1 + attention_launches(q[0], kv, batch, use_umma=umma)  # append + attention (+ merge)
+        per_layer = 1 + attention_launches(q[0], kv, batch, **akw)  # append + attention (+ merge)
     launches_per_step = 2 + L * per_layer  # + reserve + release
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         step_ms, e2e_ms, attn_ms = t.tolist()
     del graph, attn_graph
-    kern = attention_kernel(q[0], kv, batch, use_umma=umma)
+    kern = attention_kernel(q[0], kv, batch, **akw)
     return dict(kernel=kern, step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, clocks=clk, h2d=h2d,
                 d2h=d2h, launches=launches_per_step * args.steps, ctx_mean=float(np.mean(ctx)))
 
@@ -514,7 +514,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
     from specdec.sampler import UniformStream, probs_rows, sample_rows, spec_sample_logits
 
     c = dict(C3)
-    umma = UMMA_FLAG[args.attn_kernel]
+    akw = dict(use_umma=UMMA_FLAG[args.attn_kernel], mma_layout=LAYOUT_FLAG[args.mma_layout])
     fused = args.append == "fused"
     L, B, gam = args.layers, args.batch, c["gamma"]
     chunk = gam + 1
@@ -558,12 +558,12 @@ def run_gpu_c3(args, rank: int, world: int, device):
     def verify_layers(with_append=True):
         for layer in range(L):
             if with_append and fused:  # store the round's K/V rows inside the attention launch
-                paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma, k_new=knew[layer],
+                paged_attention(q[layer], kv, layer, batch, out=out[layer], **akw, k_new=knew[layer],
                                 v_new=vnew[layer])
                 continue
             if with_append:
                 kv.append(layer, slots_static, knew[layer], vnew[layer])
-            paged_attention(q[layer], kv, layer, batch, out=out[layer], use_umma=umma)
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], **akw)
 
     def sample_commit():
         spec_sample_logits(p_logits, q_logits, T, proposals, ustream, err=kv.err_word, out=(tokens, n_out))
@@ -669,11 +669,11 @@ def run_gpu_c3(args, rank: int, world: int, device):
         od = torch.empty_like(out)
         for layer in range(L):
             if fused:
-                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma, k_new=kd[layer],
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], **akw, k_new=kd[layer],
                                 v_new=vd[layer])
             else:
                 kv.append(layer, slots, kd[layer], vd[layer])
-                paged_attention(qd[layer], kv, layer, b2, out=od[layer], use_umma=umma)
+                paged_attention(qd[layer], kv, layer, b2, out=od[layer], **akw)
         toks, no = spec_sample_logits(pld, qld, T, prd, ustream, err=kv.err_word)
         _lib.check(lib.sdl_spec_commit(meta, None, B, packed.data_ptr(), no.data_ptr(), toks.data_ptr(), chunk,
                                        packed.data_ptr() + 4 * B, -1, packed.data_ptr() + 8 * B, outs[0].data_ptr(),
@@ -704,9 +704,9 @@ def run_gpu_c3(args, rank: int, world: int, device):
     launches_sampler = 4  # statistics, accept walk, draw sums, draw
     if fused:  # the op also reads the new K/V rows and writes them into their pages
         attn_bytes += 2 * (B * chunk * 2 * Hkv * d * 2)
-        per_layer = attention_launches(q[0], kv, batch, use_umma=umma, k_new=knew[0], v_new=vnew[0])
+        per_layer = attention_launches(q[0], kv, batch, **akw, k_new=knew[0], v_new=vnew[0])
     else:
-        per_layer = 1 + attention_launches(q[0], kv, batch, use_umma=umma)
+        per_layer = 1 + attention_launches(q[0], kv, batch, **akw)
     launches_per_step = 1 + L * per_layer + launches_sampler + 1  # reserve, layers, sampler, commit
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, attn_ms, samp_ms], device=device)
@@ -716,7 +716,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
         dist.all_reduce(cnt)
         committed, e2e_committed = [int(x) for x in cnt.tolist()]
     del graph, attn_graph
-    kern = attention_kernel(q[0], kv, batch, use_umma=umma)
+    kern = attention_kernel(q[0], kv, batch, **akw)
     return dict(kernel=kern, step_ms=step_ms, e2e_ms=e2e_ms, attn_ms=attn_ms, attn_bytes=attn_bytes, samp_ms=samp_ms,
                 samp_bytes=samp_bytes, clocks=clk, h2d=h2d, d2h=d2h, launches=launches_per_step * args.steps,
                 committed=committed, e2e_committed=e2e_committed, e2e_steps=e2e_steps,
@@ -724,6 +724,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
 
 
 UMMA_FLAG = {"auto": 0, "mma": -1, "tcgen05": 1}
+LAYOUT_FLAG = {"auto": 0, "keys": 1, "rows": 2}
 
 
 def main(argv=None) -> int:
@@ -735,6 +736,9 @@ def main(argv=None) -> int:
     ap.add_argument("--attn-kernel", choices=["auto", "mma", "tcgen05"], default="auto",
                     help="paged attention kernel: the library's automatic choice (default), the mma.sync "
                          "split-K kernel or the persistent tcgen05 kernel")
+    ap.add_argument("--mma-layout", choices=["auto", "keys", "rows"], default="auto",
+                    help="mma.sync kernel layout: the library's automatic choice (default), keys or query rows "
+                         "on the MMA M dimension")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="store each layer's new K/V rows inside the attention launch (default) or with a "
                          "separate append launch before it")
@@ -774,7 +778,7 @@ def main(argv=None) -> int:
            "block_tables": "random permutation of a pool holding every context",
            "l2": "no flush needed: each attention launch reads ~151 MB of K/V (> 126 MB L2), layers disjoint",
            "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
-           "attention_kernel": args.attn_kernel, "kv_append": args.append}
+           "attention_kernel": args.attn_kernel, "mma_layout": args.mma_layout, "kv_append": args.append}
 
     if args.impl == "reference":
         if rank != 0:
@@ -879,7 +883,7 @@ def main_c3(args) -> int:
            "block_tables": "random permutation of a pool holding every context",
            "l2": "no flush needed: a step streams ~1.06 GB of K/V over 28 disjoint layers and 214 MB of logits",
            "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
-           "attention_kernel": args.attn_kernel, "kv_append": args.append}
+           "attention_kernel": args.attn_kernel, "mma_layout": args.mma_layout, "kv_append": args.append}
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -984,7 +988,7 @@ def run_gpu_c5(args, rank: int, world: int, device):
     from engine.workloads import c2_layout
 
     c = C5
-    umma = UMMA_FLAG[args.attn_kernel]
+    akw = dict(use_umma=UMMA_FLAG[args.attn_kernel], mma_layout=LAYOUT_FLAG[args.mma_layout])
     Lt = args.layers or c["target_layers"]
     Ld = args.layers or c["draft_layers"]
     B, gam, Hkv, d, bs = args.batch, c["gamma"], c["kv_heads"], c["head_dim"], c["block_size"]
@@ -1027,12 +1031,12 @@ def run_gpu_c5(args, rank: int, world: int, device):
     def draft_layers():
         for s in range(gam):
             for layer in range(Ld):
-                paged_attention(qd[s, layer], dft, layer, dbatches[s], out=od[s, layer], use_umma=umma,
+                paged_attention(qd[s, layer], dft, layer, dbatches[s], out=od[s, layer], **akw,
                                 k_new=kd[s, layer], v_new=vd[s, layer])
 
     def verify_layers():
         for layer in range(Lt):
-            paged_attention(qt[layer], tgt, layer, vbatch, out=ot[layer], use_umma=umma, k_new=kt[layer],
+            paged_attention(qt[layer], tgt, layer, vbatch, out=ot[layer], **akw, k_new=kt[layer],
                             v_new=vt[layer])
 
     def reserve():
@@ -1115,10 +1119,10 @@ def run_gpu_c5(args, rank: int, world: int, device):
         reserve()
         for s in range(gam):
             for layer in range(Ld):
-                paged_attention(q_d[s, layer], dft, layer, dbatches[s], out=od[s, layer], use_umma=umma,
+                paged_attention(q_d[s, layer], dft, layer, dbatches[s], out=od[s, layer], **akw,
                                 k_new=k_d[s, layer], v_new=v_d[s, layer])
         for layer in range(Lt):
-            paged_attention(q_t[layer], tgt, layer, vbatch, out=ot[layer], use_umma=umma, k_new=k_t[layer],
+            paged_attention(q_t[layer], tgt, layer, vbatch, out=ot[layer], **akw, k_new=k_t[layer],
                             v_new=v_t[layer])
         odh.copy_(od, non_blocking=True)
         oth.copy_(ot, non_blocking=True)
@@ -1140,11 +1144,11 @@ def run_gpu_c5(args, rank: int, world: int, device):
     # one draft launch, averaged over the gamma steps (step s attends ctx + s + 1 keys)
     dbytes = (sum((x + 1 + s) * 2 * Hkv * d * 2 + -(-(x + 1 + s) // bs) * 4 for x in ctx for s in range(gam)) / gam
               + 2 * B * Hqd * d * 2 + 2 * B * 2 * Hkv * d * 2)
-    launches = 2 + 2 + gam * Ld * attention_launches(qd[0, 0], dft, dbatches[0], use_umma=umma, k_new=kd[0, 0],
+    launches = 2 + 2 + gam * Ld * attention_launches(qd[0, 0], dft, dbatches[0], **akw, k_new=kd[0, 0],
                                                      v_new=vd[0, 0]) + \
-        Lt * attention_launches(qt[0], tgt, vbatch, use_umma=umma, k_new=kt[0], v_new=vt[0])
-    kern = {"verify": attention_kernel(qt[0], tgt, vbatch, use_umma=umma),
-            "draft": attention_kernel(qd[0, 0], dft, dbatches[0], use_umma=umma)}
+        Lt * attention_launches(qt[0], tgt, vbatch, **akw, k_new=kt[0], v_new=vt[0])
+    kern = {"verify": attention_kernel(qt[0], tgt, vbatch, **akw),
+            "draft": attention_kernel(qd[0, 0], dft, dbatches[0], **akw)}
     if world > 1:
         t = torch.tensor([step_ms, e2e_ms, timings["draft"], timings["verify"]], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1173,7 +1177,7 @@ def main_c5(args) -> int:
            "block_tables": "random permutation of a pool holding every context",
            "l2": "no flush needed: every launch reads ~337 MB of K/V (> 126 MB L2)",
            "parallelism": "dp{} (request-sharded, independent KV pools)".format(world),
-           "attention_kernel": args.attn_kernel}
+           "attention_kernel": args.attn_kernel, "mma_layout": args.mma_layout}
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps({"impl": "reference", "metric": METRIC, "config": cfg,
