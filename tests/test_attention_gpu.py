@@ -106,11 +106,14 @@ def test_fp32_attention_matches_reference_fixture(tag):
 
 
 @pytest.mark.parametrize("tag", ["dec_bf16_d128", "ext_bf16_d128", "dec_bf16_d64_r7"])
-def test_bf16_attention_matches_reference_fixture(tag):
+@pytest.mark.parametrize("layout", [0, 1, 2])
+def test_bf16_attention_matches_reference_fixture(tag, layout):
+    """The reference's own outputs, on the automatic kernel and on both
+    mma.sync layouts (keys / query rows on the MMA M dimension)."""
     kv, q, starts, chunk, Hq, ref = _golden_case(tag)
     batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
-    out = paged_attention(q, kv, 0, batch)
-    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32)
+    out = paged_attention(q, kv, 0, batch, mma_layout=layout)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, mma_layout=layout)
     # exact value from the fp64 oracle on the same bf16 inputs
     a = load_npz("attention.npz")
     okvc = okv.PagedKVCache(1, kv.num_kv_heads, kv.head_dim, kv.capacity, kv.block_size)
@@ -181,17 +184,20 @@ def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
     kv.check_errors()
 
 
-@pytest.mark.parametrize("pps,chunk,cluster", [(4, 1, False), (0, 1, False), (0, 6, True), (16, 6, True),
-                                               (0, 6, False), (4, 6, False)])
-def test_split_merge_is_deterministic(pps, chunk, cluster):
+@pytest.mark.parametrize("pps,chunk,cluster,layout", [(4, 1, False, 0), (0, 1, False, 0), (0, 6, True, 0),
+                                                      (16, 6, True, 0), (0, 6, False, 0), (4, 6, False, 0),
+                                                      (0, 6, False, 2), (4, 6, False, 2), (0, 1, False, 2)])
+def test_split_merge_is_deterministic(pps, chunk, cluster, layout):
     """The split-K merge (separate launch; on chip in a cluster) has a fixed
-    reduction order: repeated calls give identical bits."""
+    reduction order: repeated calls give identical bits, on both mma.sync
+    layouts."""
     kv, _ = _build([3000 + chunk, 1500 + chunk, 40 + chunk], 2, 128, 16, torch.bfloat16, seed=6)
     q = torch.randn(3, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
     batch = AttnBatch.from_lists(DEV, [0, 1, 2], [3000, 1500, 40], chunk)
-    first = paged_attention(q, kv, 0, batch, pages_per_split=pps, cluster_merge=cluster)
+    kw = dict(pages_per_split=pps, cluster_merge=cluster, mma_layout=layout)
+    first = paged_attention(q, kv, 0, batch, **kw)
     for _ in range(5):
-        assert torch.equal(paged_attention(q, kv, 0, batch, pages_per_split=pps, cluster_merge=cluster), first)
+        assert torch.equal(paged_attention(q, kv, 0, batch, **kw), first)
 
 
 def test_cluster_and_separate_merge_agree():
