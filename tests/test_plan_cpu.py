@@ -1,0 +1,91 @@
+"""Launch-plan logic of the attention entry points, on the host (no GPU).
+
+``sdl_attention_kernel`` / ``sdl_attention_launches`` /
+``sdl_attention_workspace_bytes`` only read the scalar arguments and the
+alignment of the pointers, so they run without a device: the pointers below
+are aligned stand-ins that are never dereferenced.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from engine import _lib
+
+KERNELS = {0: "generic", 1: "mma", 2: "tcgen05", 3: "mma_rows"}
+
+
+def _args(B, chunk, Hq, Hkv, d, max_limit, dtype=_lib.SDL_BF16, **kw):
+    a = _lib.SdlAttnArgs()
+    a.q, a.out = 0x100000, 0x200000
+    a.q_sb, a.q_sj, a.q_sh = chunk * Hq * d, Hq * d, d
+    a.o_sb, a.o_sj, a.o_sh = chunk * Hq * d, Hq * d, d
+    a.dtype = a.out_dtype = dtype
+    a.k_pool, a.v_pool, a.block_table = 0x300000, 0x400000, 0x500000
+    a.rows, a.starts = 0x600000, 0x700000
+    a.width, a.capacity, a.num_layers, a.layer, a.block_size = 4096, 100000, 1, 0, 16
+    a.B, a.chunk, a.Hq, a.Hkv, a.head_dim = B, chunk, Hq, Hkv, d
+    a.max_limit = max_limit
+    a.scale = d ** -0.5
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def _kernel(a):
+    n = _lib.load().sdl_attention_kernel(ctypes.byref(a))
+    assert n >= 0, _lib.last_error()
+    return KERNELS[n]
+
+
+@pytest.mark.parametrize("shape,flags,want", [
+    ((64, 1, 12, 2, 128, 4096), {}, "mma"),                       # C2 decode: keys on M
+    ((32, 6, 12, 2, 128, 2048), {}, "mma"),                       # C3 verify, 36 rows: keys on M
+    ((32, 8, 12, 2, 128, 2048), {}, "mma_rows"),                  # 48 rows per kv head
+    ((32, 5, 14, 2, 64, 2048), {}, "mma_rows"),                   # d 64, 35 rows
+    ((16, 7, 16, 2, 128, 32768), {}, "tcgen05"),                  # C5 verify: long span
+    ((16, 7, 16, 2, 128, 32768), {"use_umma": -1}, "mma_rows"),   # mma.sync forced
+    ((16, 7, 16, 2, 128, 32768), {"use_umma": -1, "mma_layout": 1}, "mma"),
+    ((64, 1, 12, 2, 128, 4096), {"mma_layout": 2}, "mma_rows"),
+    ((32, 8, 12, 2, 128, 2048), {"cluster_merge": 1}, "mma"),     # the cluster merge is keys-on-M only
+    ((1, 512, 12, 2, 128, 512), {}, "mma_rows"),                  # prefill chunk
+    ((8, 1, 4, 2, 16, 100), {"dtype": _lib.SDL_F32}, "generic"),  # fp32 pool
+    ((32, 6, 12, 2, 128, 2048), {"force_generic": 1}, "generic"),
+])
+def test_kernel_choice(shape, flags, want):
+    assert _kernel(_args(*shape, **flags)) == want
+
+
+def test_launch_counts_and_workspace():
+    lib = _lib.load()
+    # split decode rows: attention + merge, partials in the workspace
+    a = _args(64, 1, 12, 2, 128, 4096)
+    assert lib.sdl_attention_launches(ctypes.byref(a)) == 2
+    assert lib.sdl_attention_workspace_bytes(ctypes.byref(a)) > 0
+    # one page per split would need far more partial rows than 64 pages per split
+    big = _args(64, 1, 12, 2, 128, 4096, pages_per_split=1)
+    small = _args(64, 1, 12, 2, 128, 4096, pages_per_split=64)
+    assert lib.sdl_attention_workspace_bytes(ctypes.byref(big)) > lib.sdl_attention_workspace_bytes(ctypes.byref(small))
+    # one split per row: a single launch, no workspace
+    one = _args(2000, 1, 12, 2, 128, 64)
+    assert lib.sdl_attention_launches(ctypes.byref(one)) == 1
+    assert lib.sdl_attention_workspace_bytes(ctypes.byref(one)) == 0
+    # the rows-on-M kernel's splits are whole 32-key tiles: an odd request rounds up
+    r1 = _args(32, 8, 12, 2, 128, 2048, pages_per_split=1)
+    r2 = _args(32, 8, 12, 2, 128, 2048, pages_per_split=2)
+    assert lib.sdl_attention_workspace_bytes(ctypes.byref(r1)) == lib.sdl_attention_workspace_bytes(ctypes.byref(r2))
+    # a positional append launch is added only where the kernel does not store the rows itself
+    fused = _args(64, 1, 12, 2, 128, 4096, k_new=0x800000, v_new=0x900000, new_row_stride=2 * 128)
+    assert lib.sdl_attention_launches(ctypes.byref(fused)) == 2
+    sep = _args(16, 7, 16, 2, 128, 32768, k_new=0x800000, v_new=0x900000, new_row_stride=2 * 128)
+    assert lib.sdl_attention_launches(ctypes.byref(sep)) == 3  # append + tcgen05 + its merge
+
+
+def test_invalid_arguments_are_refused():
+    lib = _lib.load()
+    a = _args(4, 1, 12, 5, 128, 100)  # Hq not a multiple of Hkv
+    assert lib.sdl_attention_kernel(ctypes.byref(a)) == -1
+    assert lib.sdl_attention_launches(ctypes.byref(a)) == -1
+    assert lib.sdl_attention_workspace_bytes(ctypes.byref(a)) == 0
