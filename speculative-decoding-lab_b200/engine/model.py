@@ -279,6 +279,24 @@ class _GraphedForward:
         self.table_ptr = table_ptr  # the block table the graph reads; a grown (moved) table needs a new capture
 
 
+class _GraphedPrefill:
+    """One captured prefill of a single prompt, padded to a power-of-two
+    length bucket.  Static inputs (token ids, block-table row, prompt length,
+    last position) are refilled before each replay; positions past the prompt
+    are computed but never stored (the attention's valid-row count) and their
+    hidden states are dropped."""
+
+    __slots__ = ("graph", "ids", "meta", "logits", "keep", "table_ptr")
+
+    def __init__(self, graph, ids, meta, logits, keep, table_ptr) -> None:
+        self.graph = graph
+        self.ids = ids
+        self.meta = meta  # (block-table row, prompt length, last position) as device tensors
+        self.logits = logits
+        self.keep = keep  # every other tensor the captured kernels read (must outlive the graph)
+        self.table_ptr = table_ptr
+
+
 class PagedLMMixin:
     """prefill / decode / decode_block over a stack of layers with ``forward_plan``.
 
@@ -380,11 +398,84 @@ class PagedLMMixin:
             hidden = layer.forward_plan(hidden, kv, index, plan, cos, sin)
         return hidden
 
+    PREFILL_MIN_BUCKET = 64
+
+    def _prefill_bucket(self, kv: PagedKVCache, B: int, chunk: int, length: int) -> Optional[int]:
+        """Length bucket of a graphed prefill, or None for the eager path:
+        graphs on, one prompt without padding, a 16-bit model (fp32 models
+        keep eager prefills, whose reductions the parity runs pin), and a
+        bucket the block table and the rotary table both cover."""
+        if not getattr(self, "_graphs_enabled", False) or B != 1 or chunk != length:
+            return None
+        if self.embed_tokens.weight.dtype not in (torch.bfloat16, torch.float16):
+            return None
+        cb = self.PREFILL_MIN_BUCKET
+        while cb < chunk:
+            cb *= 2
+        if cb > kv.width * kv.block_size or cb > self._rope_table().shape[0]:
+            return None
+        return cb
+
+    def _graph_prefill(self, prompt_2d: torch.Tensor, kv: PagedKVCache, sid: int, length: int,
+                       cb: int) -> torch.Tensor:
+        """First-token logits ``(1, V)`` of one prompt (positions already
+        reserved) through the captured prefill of bucket ``cb``."""
+        graphs = self.__dict__.setdefault("_graphs", {})
+        key = (id(kv), "prefill", cb)
+        g = graphs.get(key)
+        if g is not None and g.table_ptr != kv._table.data_ptr():
+            del graphs[key]  # the block table grew (moved): recapture
+            g = None
+        meta = _lib.i32([int(sid), int(length), int(length) - 1], self.device)
+        ids = prompt_2d.to(self.device)
+
+        def fill(dst_ids, dst_meta):
+            dst_ids[:, :length].copy_(ids)
+            dst_ids[:, length:].zero_()
+            dst_meta.copy_(meta)
+
+        if g is None:
+            s_ids = torch.zeros((1, cb), dtype=torch.long, device=self.device)
+            s_meta = torch.zeros(3, dtype=torch.int32, device=self.device)
+            fill(s_ids, s_meta)
+            s_starts = torch.zeros(1, dtype=torch.int32, device=self.device)
+            batch = AttnBatch(s_meta[0:1], s_starts, cb, s_meta[1:2], key_count=cb)
+            positions = torch.arange(cb, device=self.device).unsqueeze(0)
+
+            def run() -> torch.Tensor:
+                plan = ForwardPlan(None, batch, positions, cb)
+                hidden = self.embed_tokens(s_ids)
+                cos, sin = self._rope(positions)
+                hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+                h_last = hidden.index_select(1, s_meta[2:3].long())[:, 0]
+                return self._logits(h_last)
+
+            # one eager pass sizes every workspace and stores this prompt's
+            # K/V; the replay below stores the same bytes again
+            run()
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = run()
+            g = _GraphedPrefill(graph, s_ids, s_meta, logits, (s_starts, positions, batch, kv), kv._table.data_ptr())
+            graphs[key] = g
+        else:
+            fill(g.ids, g.meta)
+        g.graph.replay()
+        return g.logits
+
     def prefill(self, prompt_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
                 seq_lengths: Sequence[int]) -> torch.Tensor:
-        """Prefill ragged prompts; return first-token logits ``(B, V)``."""
+        """Prefill ragged prompts; return first-token logits ``(B, V)``.
+
+        With CUDA graphs enabled, a single unpadded prompt of a 16-bit model
+        replays a captured prefill padded to a power-of-two length bucket."""
         self.forward_calls += 1
         B, chunk = prompt_2d.shape
+        cb = self._prefill_bucket(kv, B, chunk, int(seq_lengths[0]) if B == 1 else -1)
+        if cb is not None:
+            kv.reserve(seq_ids, [0], [chunk])
+            return self._graph_prefill(prompt_2d, kv, seq_ids[0], chunk, cb)
         plan = plan_prefill(kv, seq_ids, seq_lengths, chunk)
         hidden = self.embed_tokens(prompt_2d.to(self.device))
         cos, sin = self._rope(plan.positions)

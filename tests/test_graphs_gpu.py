@@ -14,6 +14,7 @@ import torch
 
 from conftest import load_json
 from engine import workloads
+from engine.attention import gather_ctx
 from engine.config import EngineConfig, WorkloadRequest
 from engine.qwen import build_random_model
 from engine.scheduler import build_kv
@@ -93,3 +94,40 @@ def test_c1_runs_reproduce_with_graphs(label):
     assert res.tokens_per_round == run["tokens_per_round"]
     kv.check_errors()
     dkv.check_errors()
+
+
+def test_graph_prefill_matches_eager():
+    """A 16-bit model with graphs on prefills a single prompt through a
+    captured forward padded to a power-of-two length bucket: first-token
+    logits and the stored K/V agree with the eager prefill to bf16 rounding,
+    on the capture, on a replay with another length in the same bucket and in
+    a second bucket; fp32 models keep the eager prefill."""
+    eager = _model("c1-target", 3, torch.bfloat16)
+    graphed = _model("c1-target", 3, torch.bfloat16)
+    graphed.enable_cuda_graphs()
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (40, 57, 130)]
+    kvs = [build_kv(m, EngineConfig(block_size=16, max_num_blocks=256), DEV, max_seqs=4) for m in (eager, graphed)]
+    for sid, p in enumerate(prompts):
+        outs = []
+        for m, kv in zip((eager, graphed), kvs):
+            kv.add_sequence(sid)
+            outs.append(m.prefill(torch.tensor([p], device=DEV), kv, [sid], [len(p)]).float())
+        le, lg = outs
+        assert le.shape == lg.shape == (1, 1024)
+        assert (le - lg).abs().max().item() <= 5e-2 * le.abs().max().item(), sid
+        for layer in (0, eager.num_layers - 1):
+            ke = gather_ctx(kvs[0], layer, sid, len(p))
+            kg = gather_ctx(kvs[1], layer, sid, len(p))
+            for a, b in zip(ke, kg):
+                assert (a.float() - b.float()).abs().max().item() <= 5e-2 * a.float().abs().max().item()
+    assert kvs[0].block_tables == kvs[1].block_tables
+    assert sorted(k[2] for k in graphed._graphs if k[1] == "prefill") == [64, 256]
+    fp32 = _model("c1-target", 3)
+    fp32.enable_cuda_graphs()
+    kv32 = build_kv(fp32, EngineConfig(block_size=16, max_num_blocks=64), DEV, max_seqs=1)
+    kv32.add_sequence(0)
+    fp32.prefill(torch.tensor([prompts[0]], device=DEV), kv32, [0], [len(prompts[0])])
+    assert not any(k[1] == "prefill" for k in getattr(fp32, "_graphs", {}))
+    for kv in kvs + [kv32]:
+        kv.check_errors()
