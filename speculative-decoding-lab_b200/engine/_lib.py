@@ -237,6 +237,14 @@ def dtype_code(dtype: torch.dtype) -> int:
     raise TypeError("unsupported dtype {} (float32, bfloat16, float16)".format(dtype))
 
 
+def to_device(values, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """Host values -> CUDA tensor without waiting for the stream: built on
+    the host and copied with ``non_blocking`` (the copy is queued behind the
+    stream's work), where ``torch.tensor(values, device=...)`` would wait for
+    every queued kernel first."""
+    return torch.tensor(values, dtype=dtype).to(device, non_blocking=True)
+
+
 def i32(values, device: torch.device) -> torch.Tensor:
     """Host list -> contiguous int32 CUDA tensor (one H2D copy)."""
     if isinstance(values, torch.Tensor):

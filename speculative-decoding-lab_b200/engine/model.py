@@ -134,7 +134,7 @@ def plan_prefill(kv: PagedKVCache, seq_ids: Sequence[int], seq_lengths: Sequence
     slots = kv.reserve(seq_ids, [0] * B, lengths)
     if any(ln != chunk for ln in lengths):
         grid = torch.full((B * chunk,), -1, dtype=torch.int32, device=kv.device)
-        lens_t = torch.tensor(lengths, device=kv.device)
+        lens_t = _lib.to_device(lengths, torch.long, kv.device)
         mask = (torch.arange(chunk, device=kv.device).unsqueeze(0) < lens_t.unsqueeze(1)).reshape(-1)
         grid[mask] = slots
         slots = grid
@@ -480,7 +480,7 @@ class PagedLMMixin:
         hidden = self.embed_tokens(prompt_2d.to(self.device))
         cos, sin = self._rope(plan.positions)
         hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
-        last = torch.tensor([int(x) - 1 for x in seq_lengths], device=self.device)
+        last = _lib.to_device([int(x) - 1 for x in seq_lengths], torch.long, self.device)
         h_last = hidden[torch.arange(B, device=self.device), last]
         return self._logits(h_last)
 

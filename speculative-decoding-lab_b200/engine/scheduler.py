@@ -192,7 +192,7 @@ class PagedScheduler:
     def _prefill_one(self, seq: Sequence, result: SchedulerResult, stream: Optional[UniformStream]) -> Optional[float]:
         watch = Stopwatch()
         with watch:
-            ids = torch.tensor([list(seq.prompt_ids)], dtype=torch.long, device=self.model.device)
+            ids = _lib.to_device([list(seq.prompt_ids)], torch.long, self.model.device)
             logits = self.model.prefill(ids, self.kv, [seq.sid], [len(seq.prompt_ids)])
             token = int(self._next_tokens(logits, stream)[0].item())
             seq.generated.append(token)
@@ -203,7 +203,7 @@ class PagedScheduler:
     def _decode_active(self, running: Seq[Sequence], result: SchedulerResult,
                        stream: Optional[UniformStream]) -> None:
         model = self.model
-        ids = torch.tensor([seq.generated[-1] for seq in running], dtype=torch.long, device=model.device)
+        ids = _lib.to_device([seq.generated[-1] for seq in running], torch.long, model.device)
         ctx = [self.kv.seq_len(seq.sid) for seq in running]
         logits = model.decode(ids, self.kv, [s.sid for s in running], ctx)
         tokens = self._next_tokens(logits, stream).tolist()
@@ -283,12 +283,12 @@ class PagedScheduler:
             while any(not s.done for s in all_seqs):
                 living = [b for b, s in enumerate(all_seqs) if not s.done]
                 if living:
-                    ids = torch.tensor([s.generated[-1] if s.generated else 0 for s in all_seqs],
-                                       dtype=torch.long, device=device)
+                    ids = _lib.to_device([s.generated[-1] if s.generated else 0 for s in all_seqs], torch.long,
+                                         device)
                     ctx = [self.kv.seq_len(s.sid) for s in all_seqs]
                     logits = self.model.decode(ids, self.kv, [s.sid for s in all_seqs], ctx)
                     result.total_forwards += 1
-                    rows = torch.tensor(living, device=device)
+                    rows = _lib.to_device(living, torch.long, device)
                     tokens = self._next_tokens(logits.index_select(0, rows), stream).tolist()
                     for token, b in zip(tokens, living):
                         s = all_seqs[b]

@@ -79,7 +79,7 @@ def batch_accept(
     p = torch.stack([p_by_sid[s].float() for s in sids]).contiguous()
     q = torch.stack([torch.stack([r.float() for r in q_by_sid[s]]) for s in sids]).contiguous()
     gamma = q.shape[1]
-    props = torch.tensor([list(proposals_by_sid[s]) for s in sids], dtype=torch.int32, device=p.device)
+    props = _lib.to_device([list(proposals_by_sid[s]) for s in sids], torch.int32, p.device)
     if isinstance(generator, UniformStream):
         stream = generator
     else:
@@ -129,7 +129,7 @@ class SpeculativePagedScheduler(PagedScheduler):
                           stream: Optional[UniformStream]) -> Optional[float]:
         watch = Stopwatch()
         with watch:
-            ids = torch.tensor([list(seq.prompt_ids)], dtype=torch.long, device=self.model.device)
+            ids = _lib.to_device([list(seq.prompt_ids)], torch.long, self.model.device)
             logits = self.model.prefill(ids, self.kv, [seq.sid], [len(seq.prompt_ids)])
             tok = self._next_tokens(logits, stream)
             self.draft_model.prefill(ids, self.draft_kv, [seq.sid], [len(seq.prompt_ids)])
@@ -218,7 +218,7 @@ class SpeculativePagedScheduler(PagedScheduler):
         q_probs = None
         if not greedy:
             stream.reserve(gamma * B)
-        cur = torch.tensor([s.generated[-1] for s in running], dtype=torch.long, device=device)
+        cur = _lib.to_device([s.generated[-1] for s in running], torch.long, device)
         fused = False
         for t in range(gamma):
             q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0])
@@ -247,7 +247,7 @@ class SpeculativePagedScheduler(PagedScheduler):
             cur = prop_t.long()
 
         # ---- 2. target verifies [pending] + proposals in one forward
-        rows = torch.cat((torch.tensor([[s.generated[-1]] for s in running], dtype=torch.long, device=device),
+        rows = torch.cat((_lib.to_device([[s.generated[-1]] for s in running], torch.long, device),
                           proposals.long()), dim=1)
         p_logits = model.decode_block(rows, self.kv, sids, starts)  # (B, chunk, V)
 
@@ -337,7 +337,7 @@ class SpeculativePagedScheduler(PagedScheduler):
 
         # ---- 6. draft catch-up for fully accepted rounds (engine/spec_scheduler.py:308-319)
         if catch_sids:
-            ids = torch.tensor(catch_tok, dtype=torch.long, device=device)
+            ids = _lib.to_device(catch_tok, torch.long, device)
             slots = _lib.i32(catch_slot, device)
             draft.decode(ids, self.draft_kv, catch_sids, catch_pos, slots=slots)
 
