@@ -236,7 +236,9 @@ def paged_attention(
     if q.stride(3) != 1:
         q = q.contiguous()
     if out is None:
-        out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device)
+        # rows past valid_rows are left unwritten by the kernels and read as zero
+        alloc = torch.empty if batch.valid_rows is None else torch.zeros
+        out = alloc(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     if batch.max_limit > kv.width * kv.block_size:
         raise RuntimeError("attention span {} exceeds the block-table width".format(batch.max_limit))
     kn = vn = None

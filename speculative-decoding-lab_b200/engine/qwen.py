@@ -40,6 +40,22 @@ class QwenAttention(nn.Module):
         self.v_proj = nn.Linear(hidden, num_kv_heads * head_dim, bias=attention_bias)
         self.o_proj = nn.Linear(num_q_heads * head_dim, hidden, bias=False)
 
+    def qkv_fused(self, x: torch.Tensor) -> torch.Tensor:
+        """q, k and v projections as one GEMM over the concatenated weights:
+        rows of ``[q heads | k heads | v heads] x head_dim``.  The
+        concatenation is cached and rebuilt when a projection's storage or
+        in-place version changes."""
+        parts = [self.q_proj, self.k_proj, self.v_proj]
+        params = [m.weight for m in parts] + [m.bias for m in parts if m.bias is not None]
+        key = tuple((t.data_ptr(), t._version, t.dtype) for t in params)
+        if self.__dict__.get("_qkv_key") != key:
+            w = torch.cat([m.weight for m in parts], 0)
+            b = torch.cat([m.bias for m in parts], 0) if all(m.bias is not None for m in parts) else None
+            self.__dict__["_qkv"] = (w, b)
+            self.__dict__["_qkv_key"] = key
+        w, b = self.__dict__["_qkv"]
+        return torch.nn.functional.linear(x, w, b)
+
 
 class QwenMLP(nn.Module):
     def __init__(self, hidden: int, intermediate: int) -> None:
@@ -69,9 +85,18 @@ class QwenDecoderLayer(nn.Module):
         attn = self.self_attn
         lead = tuple(hidden.shape[:-1])
         x = self.input_layernorm(hidden)
-        q = apply_rotary_(attn.q_proj(x).view(*lead, attn.num_heads, attn.head_dim), sin, cos)
-        k = apply_rotary_(attn.k_proj(x).view(*lead, attn.num_kv_heads, attn.head_dim), sin, cos)
-        v = attn.v_proj(x).view(*lead, attn.num_kv_heads, attn.head_dim)
+        d, hq, hkv = attn.head_dim, attn.num_heads, attn.num_kv_heads
+        if layer_ops.fusable(x):
+            # 16-bit models: one projection GEMM, and one RoPE launch over the
+            # q and k heads, which sit side by side in each row of its output
+            qkv = attn.qkv_fused(x)
+            qk = layer_ops.rope_(qkv[..., :(hq + hkv) * d].view(*lead, hq + hkv, d), sin, cos)
+            q, k = qk[..., :hq, :], qk[..., hq:, :]
+            v = qkv[..., (hq + hkv) * d:].view(*lead, hkv, d)
+        else:
+            q = apply_rotary_(attn.q_proj(x).view(*lead, hq, d), sin, cos)
+            k = apply_rotary_(attn.k_proj(x).view(*lead, hkv, d), sin, cos)
+            v = attn.v_proj(x).view(*lead, hkv, d)
         out = paged_attend(q, k, v, kv, layer_index, plan)
         o = attn.o_proj(out.reshape(*lead, -1))
         if layer_ops.fusable(hidden):  # residual add + post-attention norm in one launch
