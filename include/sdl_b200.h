@@ -394,6 +394,13 @@ int sdl_rope(void* x, int64_t x_row_stride, int32_t rows, int32_t heads,
 int sdl_silu_mul(const void* gate, const void* up, void* out, int64_t n,
                  int32_t dtype, void* stream);
 
+/* The same gate on the output of one GEMM over the concatenated gate and up
+ * weights: row r of x holds gate[r][0..inter) then up[r][0..inter) (row
+ * stride x_row_stride elements); out[r][i] = T(T(silu(gate)) * up)
+ * (engine/qwen.py:49-50 with the two projections fused). */
+int sdl_swiglu(const void* x, int64_t x_row_stride, void* out, int64_t out_row_stride,
+               int32_t rows, int32_t inter, int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,44 @@ __global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u
     }
 }
 
+// SwiGLU gate over fused rows [gate | up]: one thread per (row, i).
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ x, int64_t xs, T* __restrict__ out, int64_t os, int rows,
+                              int inter) {
+    const int64_t n = (int64_t)rows * inter;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = t / inter;
+        const int i = (int)(t - r * inter);
+        const T* xr = x + r * xs;
+        const float gv = to_f32<T>(xr[i]);
+        const float sv = round_trip<T>(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))));
+        out[r * os + i] = from_f32<T>(__fmul_rn(sv, to_f32<T>(xr[inter + i])));
+    }
+}
+
+// The same on pairs of columns: one row per blockIdx.y, 4-byte accesses
+// (even inter and row strides, 4-byte aligned rows).
+template <typename T> struct Pair2;
+template <> struct Pair2<__nv_bfloat16> { using type = __nv_bfloat162; };
+template <> struct Pair2<__half> { using type = __half2; };
+
+template <typename T>
+__global__ void swiglu_pair_kernel(const T* __restrict__ x, int64_t xs, T* __restrict__ out, int64_t os, int inter) {
+    using T2 = typename Pair2<T>::type;
+    const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= inter) return;
+    const T* xr = x + (int64_t)blockIdx.y * xs;
+    const T2 g = *reinterpret_cast<const T2*>(xr + i);
+    const T2 u = *reinterpret_cast<const T2*>(xr + inter + i);
+    const float g0 = to_f32<T>(g.x), g1 = to_f32<T>(g.y);
+    const float s0 = round_trip<T>(__fdiv_rn(g0, __fadd_rn(1.f, expf(-g0))));
+    const float s1 = round_trip<T>(__fdiv_rn(g1, __fadd_rn(1.f, expf(-g1))));
+    T2 y;
+    y.x = from_f32<T>(__fmul_rn(s0, to_f32<T>(u.x)));
+    y.y = from_f32<T>(__fmul_rn(s1, to_f32<T>(u.y)));
+    *reinterpret_cast<T2*>(out + (int64_t)blockIdx.y * os + i) = y;
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t b = (n + threads - 1) / threads;
     return (int)std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 16);
@@ -153,4 +191,36 @@ extern "C" int sdl_silu_mul(const void* gate, const void* up, void* out, int64_t
         return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_silu_mul: 16-bit dtypes only");
     }
     return sdl::check_launch("silu_mul_kernel");
+}
+
+extern "C" int sdl_swiglu(const void* x, int64_t x_row_stride, void* out, int64_t out_row_stride, int32_t rows,
+                          int32_t inter, int32_t dtype, void* stream) {
+    if (!x || !out || rows < 0 || inter < 1 || x_row_stride < 2 * (int64_t)inter || out_row_stride < inter)
+        return sdl::fail(SDL_ERR_INVALID, "sdl_swiglu: bad arguments");
+    if (rows == 0) return SDL_OK;
+    cudaStream_t st = sdl::as_stream(stream);
+    auto al4 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 4 == 0; };
+    if (inter % 2 == 0 && x_row_stride % 2 == 0 && out_row_stride % 2 == 0 && al4(x) && al4(out) && rows <= 65535 &&
+        (dtype == SDL_BF16 || dtype == SDL_F16)) {
+        const dim3 grid((inter / 2 + 255) / 256, rows);
+        if (dtype == SDL_BF16) {
+            using T = __nv_bfloat16;
+            swiglu_pair_kernel<T><<<grid, 256, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, inter);
+        } else {
+            using T = __half;
+            swiglu_pair_kernel<T><<<grid, 256, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, inter);
+        }
+        return sdl::check_launch("swiglu_pair_kernel");
+    }
+    const int grid = grid_for((int64_t)rows * inter, 256);
+    if (dtype == SDL_BF16) {
+        using T = __nv_bfloat16;
+        swiglu_kernel<T><<<grid, 256, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, rows, inter);
+    } else if (dtype == SDL_F16) {
+        using T = __half;
+        swiglu_kernel<T><<<grid, 256, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, rows, inter);
+    } else {
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_swiglu: 16-bit dtypes only");
+    }
+    return sdl::check_launch("swiglu_kernel");
 }

@@ -72,6 +72,7 @@ EXPORTED_SYMBOLS = (
     "sdl_rmsnorm",
     "sdl_rope",
     "sdl_silu_mul",
+    "sdl_swiglu",
 )
 
 
@@ -173,6 +174,7 @@ _SIGS = {
                             c_int, c_void]),
     "sdl_rope": (c_int, [c_void, c_i64, c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_int, c_void]),
     "sdl_silu_mul": (c_int, [c_void, c_void, c_void, c_i64, c_int, c_void]),
+    "sdl_swiglu": (c_int, [c_void, c_i64, c_void, c_i64, c_int, c_int, c_int, c_void]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None

@@ -86,3 +86,19 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         "sdl_silu_mul",
     )
     return out
+
+
+def swiglu(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
+    """``silu(gate) * up`` on rows ``[gate | up]`` of one fused projection
+    (``inter`` columns each), with ``silu_mul``'s two roundings."""
+    x = gate_up.reshape(-1, gate_up.shape[-1])
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    out = torch.empty((x.shape[0], inter), dtype=x.dtype, device=x.device)
+    _lib.check(
+        _lib.load().sdl_swiglu(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), x.shape[0], int(inter),
+                               _lib.dtype_code(x.dtype), _lib.stream_handle(x.device)),
+        "sdl_swiglu",
+    )
+    return out.reshape(*gate_up.shape[:-1], inter)
+

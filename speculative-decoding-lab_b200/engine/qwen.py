@@ -64,9 +64,19 @@ class QwenMLP(nn.Module):
         self.up_proj = nn.Linear(hidden, intermediate, bias=False)
         self.down_proj = nn.Linear(intermediate, hidden, bias=False)
 
+    def gate_up_fused(self, x: torch.Tensor) -> torch.Tensor:
+        """gate and up projections as one GEMM over the concatenated weights
+        (rows ``[gate | up]``); the concatenation is cached and rebuilt when a
+        projection's storage or in-place version changes."""
+        key = tuple((t.data_ptr(), t._version, t.dtype) for t in (self.gate_proj.weight, self.up_proj.weight))
+        if self.__dict__.get("_gu_key") != key:
+            self.__dict__["_gu"] = torch.cat([self.gate_proj.weight, self.up_proj.weight], 0)
+            self.__dict__["_gu_key"] = key
+        return torch.nn.functional.linear(x, self.__dict__["_gu"])
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if layer_ops.fusable(x):
-            return self.down_proj(layer_ops.silu_mul(self.gate_proj(x), self.up_proj(x)))
+        if layer_ops.fusable(x):  # 16-bit models: one gate/up GEMM, one gate launch
+            return self.down_proj(layer_ops.swiglu(self.gate_up_fused(x), self.gate_proj.out_features))
         return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
 
 

@@ -68,3 +68,15 @@ def test_rmsnorm_matches_the_chain(dtype, dim):
     assert torch.equal(h, x + delta)
     u = _ulps(normed, chain(x + delta), dtype)
     assert u.max().item() <= 1 and (u == 0).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_swiglu_on_fused_rows_equals_silu_mul(dtype):
+    """The gate over rows [gate | up] of one fused projection gives silu_mul's
+    bits on the two halves."""
+    g = torch.Generator(device=DEV).manual_seed(3)
+    for inter in (4864, 77):  # even: column pairs; odd: one column per thread
+        gu = (torch.randn((37, 2 * inter), generator=g, device=DEV) * 3).to(dtype)
+        want = layer_ops.silu_mul(gu[:, :inter], gu[:, inter:])
+        assert torch.equal(layer_ops.swiglu(gu, inter), want)
+
