@@ -72,6 +72,7 @@ C2_ATTN_TRAFFIC = 154_166_784 + 4_897_792
 ATTN_KERNELS = {
     "mma": "attn_tc_kernel (+ attn_combine_kernel when split)",
     "mma_rows": "attn_rows_kernel (+ attn_combine_kernel when split)",
+    "mma_direct": "attn_direct_kernel (+ attn_combine_kernel when split)",
     "tcgen05": "attn_sk_kernel + attn_sk_combine_kernel (persistent tcgen05)",
     "generic": "attn_generic_kernel",
 }
@@ -743,7 +744,7 @@ def run_gpu_c3(args, rank: int, world: int, device):
 
 
 UMMA_FLAG = {"auto": 0, "mma": -1, "tcgen05": 1}
-LAYOUT_FLAG = {"auto": 0, "keys": 1, "rows": 2}
+LAYOUT_FLAG = {"auto": 0, "keys": 1, "rows": 2, "direct": 3}
 
 
 def main(argv=None) -> int:
@@ -755,7 +756,7 @@ def main(argv=None) -> int:
     ap.add_argument("--attn-kernel", choices=["auto", "mma", "tcgen05"], default="auto",
                     help="paged attention kernel: the library's automatic choice (default), the mma.sync "
                          "split-K kernel or the persistent tcgen05 kernel")
-    ap.add_argument("--mma-layout", choices=["auto", "keys", "rows"], default="auto",
+    ap.add_argument("--mma-layout", choices=["auto", "keys", "rows", "direct"], default="auto",
                     help="mma.sync kernel layout: the library's automatic choice (default), keys or query rows "
                          "on the MMA M dimension")
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",

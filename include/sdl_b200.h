@@ -211,10 +211,17 @@ typedef struct sdl_attn_args {
     int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
                                  on the MMA M dimension for blocks of at
                                  least 48 query rows per kv head, 16 at
-                                 head_dim 64; keys on M below that), 1 =
+                                 head_dim 64; keys on M below that, with
+                                 register-direct loads (3) for head_dim-64
+                                 decode), 1 =
                                  keys on M (query columns on N: the decode
                                  layout), 2 = query rows on M
-                                 (FlashAttention-2 register layout)        */
+                                 (FlashAttention-2 register layout), 3 =
+                                 keys on M with K/V loaded from the pool
+                                 straight into the MMA fragments (blocks
+                                 of at most 8 query columns per kv head
+                                 over 16-byte aligned K/V; others keep
+                                 the automatic choice)                    */
     /* Fused K/V append (paged pools only): when k_new != NULL the rows
      * k_new/v_new [B*chunk][Hkv*head_dim] (row stride new_row_stride
      * elements, the pool's dtype) are stored at positions starts[b] + j

@@ -75,6 +75,8 @@ struct TcParams {
     const char* k_new;
     const char* v_new;
     int64_t new_stride;  // bytes between consecutive new rows
+    const char* k_src;   // K and V rows attended (the pool, or the dense tensors): register-direct kernel
+    const char* v_src;
     int32_t* err;
 };
 
@@ -567,6 +569,336 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         for (int r = 0; r < nact; ++r)
             if (r != (int)rank) mbar_arrive_remote(mapa_shared(smem_u32(&xbar[1]), r));
         if (!mbar_wait_cluster_bounded(&xbar[1], 0, kWaitLimit)) sdl_raise(p.err, SDL_DEVERR_TIMEOUT);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Register-direct decode kernel: keys on the MMA M dimension like
+// attn_tc_kernel, but each thread loads its mma.sync fragment elements
+// straight from the pool rows as 16-byte pieces -- no TMA, no shared-memory
+// ring, no barrier inside the page loop.  One CTA per (split, group of
+// g_cta kv heads, sequence) for blocks of at most kDirCols query columns per
+// kv head; warp w attends kv head w % g_cta, the kDirWarps / g_cta warps of
+// a head take the split's pages round-robin, each with its own online
+// softmax, and merge through shared memory at the end.  With g_cta = Hkv
+// the heads' halves of a token row are read together by sibling warps.
+//
+// Fragment layout (m16n8k16, g = lane / 4, c = lane % 4):
+//  * S^T = K Q^T.  The head dimension is summed over, so it is permuted the
+//    same way in K (A) and Q (B): k-step 2j + h takes, for this thread, dims
+//    32j + 8c + 4h + {0,1} (fragment columns 2c, 2c+1) and + {2,3} (columns
+//    2c+8, 2c+9).  One 16-byte piece of a K row (dims 32j + 8c .. +8) then
+//    feeds two k-steps, and a quad of lanes reads 64 contiguous bytes.
+//  * O^T += V^T P^T.  The M rows of O^T are head dims, permuted so that M
+//    tile 4u + w, rows g and g + 8, are dims 64u + 8g + 2w and + 1: word w of
+//    the 16-byte piece (dims 64u + 8g .. +8) of a V row holds both.  The A
+//    fragment pairs two keys per register, so the words of keys 2c, 2c+1
+//    (and 2c+8, 2c+9) are interleaved with byte permutes.
+// The next page's K (after this page's S) and V (after this page's P V) are
+// loaded while the current page is computed.
+constexpr int kDirWarps = 4;
+constexpr int kDirCols = 8;  // query columns (chunk * ratio) one CTA covers
+
+template <int I> SDL_DEV uint32_t u4_word(const uint4& v) {
+    if constexpr (I == 0) return v.x;
+    else if constexpr (I == 1) return v.y;
+    else if constexpr (I == 2) return v.z;
+    else return v.w;
+}
+
+// Three CTAs per SM at head_dim 128 (the two pages in flight need ~140
+// registers), four at 64.
+template <int HD, typename T>
+__global__ void __launch_bounds__(kDirWarps * 32, HD == 128 ? 3 : 4)
+attn_direct_kernel(const TcParams p) {
+    constexpr int KC = HD / 32;              // 16-byte K pieces per key row and thread
+    constexpr int VC = HD / 64;              // 16-byte V pieces per key and thread
+    constexpr int MT = HD / 16;              // k-steps of S^T = M tiles of O^T
+    constexpr int RB = HD * (int)sizeof(T);  // bytes of one kv head's row
+    __shared__ __align__(16) float s_part[kDirWarps][kDirCols][HD + 4];
+    __shared__ float s_m[kDirWarps][kDirCols], s_l[kDirWarps][kDirCols];
+
+    const int split = blockIdx.x, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tq = lane & 3, grp = lane >> 2;
+    const int G = p.g_cta, WH = kDirWarps / G;  // kv heads per CTA, warps per head
+    const int gi = warp % G, wi = warp / G;
+    const int g = blockIdx.y * G + gi;
+
+    // Row metadata and the block table are read before griddepcontrol.wait
+    // (as in attn_tc_kernel: no early-starting kernel of this library writes
+    // them); Q, the new rows and the pool pages after it.
+    const int start = p.starts[b];
+    const int nvalid = p.valid_rows ? min(p.valid_rows[b], p.chunk) : p.chunk;
+    const int ncol = p.chunk * p.ratio;
+    const int lmax = nvalid > 0 ? start + nvalid : 0;
+    if (lmax <= 0) return;
+    const int npages = (lmax + kPage - 1) / kPage;
+    if (split == 0 && threadIdx.x == 0 && (npages + p.pps - 1) / p.pps > p.nsplit)
+        sdl_raise(p.err, SDL_DEVERR_BAD_INDEX);  // span past the grid: the excess pages are not attended
+    const int pbeg = split * p.pps;
+    const int pend = min(npages, pbeg + p.pps);
+    if (pbeg >= pend) return;
+    const int np = pend - pbeg;
+    const int my_n = wi < np ? (np - wi + WH - 1) / WH : 0;
+    const int row = p.dense ? 0 : p.rows[b];
+    const int klim = p.dense ? min(lmax, p.kv_len) : lmax;  // keys loaded (the rest read as zero)
+    const int64_t rs = (int64_t)p.Hkv * RB;                  // bytes of one token row
+    // Pool token row of this warp's k-th page (out-of-range entries raise and read row 0).
+    auto page_tok = [&](int k) -> int {
+        const int pg = pbeg + wi + k * WH;
+        if (p.dense) return b * p.kv_len + pg * kPage;
+        int phys = pg < p.width ? p.table[(int64_t)row * p.width + pg] : -1;
+        if (phys < 0 || phys >= p.capacity) { sdl_raise(p.err, SDL_DEVERR_BAD_INDEX); phys = 0; }
+        return (p.layer * p.capacity + phys) * kPage;
+    };
+    int tok_l = lane < my_n ? page_tok(lane) : 0;  // lane l: this warp's page l (then l + 32, ...)
+
+    pdl_wait();
+
+    // Q as B fragments: column grp of this warp, dims permuted as above.
+    uint32_t qf[MT][2];
+    {
+        const int col = grp;
+        const bool ok = col < ncol && col / p.ratio < nvalid;
+        const T* qp = nullptr;
+        if (ok) {
+            const int j = col / p.ratio, h = g * p.ratio + col % p.ratio;
+            qp = reinterpret_cast<const T*>(p.q) + b * p.q_sb + j * p.q_sj + h * p.q_sh;
+        }
+#pragma unroll
+        for (int j = 0; j < KC; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                qf[2 * j + h][0] = ok ? ld_u32(qp + 32 * j + 8 * tq + 4 * h) : 0u;
+                qf[2 * j + h][1] = ok ? ld_u32(qp + 32 * j + 8 * tq + 4 * h + 2) : 0u;
+            }
+    }
+    int lim[2];
+    float m_run[2], l_run[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const int col = 2 * tq + e;
+        const int j = col / p.ratio;
+        lim[e] = (col < ncol && j < nvalid) ? start + j + 1 : lmax;
+        m_run[e] = -INFINITY;
+        l_run[e] = 0.f;
+    }
+    const int lim_min = __reduce_min_sync(0xffffffffu, min(lim[0], lim[1]));
+    float acc[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[mt][r] = 0.f;
+
+    // Fused append: the warp that attends page pg first stores this kv
+    // head's new rows that fall in it (lanes own 16-byte pieces, K then V);
+    // __syncwarp orders those stores before the warp's own loads of the page.
+    auto append_page = [&](int pg, int t0) {
+        constexpr int PC = RB / 16;
+        const int lo = max(start, pg * kPage), hi = min(start + nvalid, (pg + 1) * kPage);
+        for (int pos = lo; pos < hi; ++pos) {
+            const int64_t src = ((int64_t)b * p.chunk + (pos - start)) * p.new_stride + g * RB;
+            const int64_t dst = (int64_t)(t0 + pos - pg * kPage) * rs + g * RB;
+            if (lane < 2 * PC) {
+                const bool isv = lane >= PC;
+                const int cb = (lane % PC) * 16;
+                const uint4 v = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) + src + cb);
+                *reinterpret_cast<uint4*>((isv ? p.v_pool : p.k_pool) + dst + cb) = v;
+            }
+        }
+        __syncwarp();
+    };
+    uint4 kr[2][KC];  // key rows grp, grp + 8
+    uint4 vr[4][VC];  // keys 2tq, 2tq + 1, 2tq + 8, 2tq + 9
+    auto load_k = [&](int t0, int pos0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int key = grp + 8 * r;
+            const bool ok = pos0 + key < klim;
+            const char* src = p.k_src + (int64_t)(t0 + key) * rs + g * RB + tq * 16;
+#pragma unroll
+            for (int j = 0; j < KC; ++j)
+                kr[r][j] = ok ? *reinterpret_cast<const uint4*>(src + j * 64) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    auto load_v = [&](int t0, int pos0) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int key = 2 * tq + (r & 1) + 8 * (r >> 1);
+            const bool ok = pos0 + key < klim;
+            const char* src = p.v_src + (int64_t)(t0 + key) * rs + g * RB + grp * 16;
+#pragma unroll
+            for (int u = 0; u < VC; ++u)
+                vr[r][u] = ok ? *reinterpret_cast<const uint4*>(src + u * 128) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+
+    const bool p_split = p.out_dtype == SDL_F32;
+    const bool append = p.k_new != nullptr;
+    if (my_n > 0) {
+        const int t0 = __shfl_sync(0xffffffffu, tok_l, 0);
+        const int pg = pbeg + wi;
+        if (append) append_page(pg, t0);
+        load_k(t0, pg * kPage);
+        load_v(t0, pg * kPage);
+    }
+    for (int k = 0; k < my_n; ++k) {
+        const int pg = pbeg + wi + k * WH;
+        // S^T[key][col] over this page's 16 keys
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < KC; ++j) {
+            uint32_t a0[4] = {u4_word<0>(kr[0][j]), u4_word<0>(kr[1][j]), u4_word<1>(kr[0][j]), u4_word<1>(kr[1][j])};
+            mma_16816<T>(s, a0, qf[2 * j][0], qf[2 * j][1]);
+            uint32_t a1[4] = {u4_word<2>(kr[0][j]), u4_word<2>(kr[1][j]), u4_word<3>(kr[0][j]), u4_word<3>(kr[1][j])};
+            mma_16816<T>(s, a1, qf[2 * j + 1][0], qf[2 * j + 1][1]);
+        }
+        const bool more = k + 1 < my_n;
+        int t_next = 0;
+        if (more) {
+            if (((k + 1) & 31) == 0) tok_l = k + 1 + lane < my_n ? page_tok(k + 1 + lane) : 0;
+            t_next = __shfl_sync(0xffffffffu, tok_l, (k + 1) & 31);
+            if (append) append_page(pg + WH, t_next);
+            load_k(t_next, (pg + WH) * kPage);
+        }
+
+        // Online softmax per query column, log2 domain, lazy running max
+        // (m_run moves only when a page's max exceeds it by 2^kLazyLog2).
+        const int pos_lo = pg * kPage + grp, pos_hi = pos_lo + 8;
+        const bool whole = (pg + 1) * kPage <= lim_min;
+        float mx[2];
+        bool need = false;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            if (!whole) {
+                if (pos_lo >= lim[e]) s[e] = -INFINITY;
+                if (pos_hi >= lim[e]) s[2 + e] = -INFINITY;
+            }
+            float m = fmaxf(s[e], s[2 + e]);
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            mx[e] = m * p.scale_log2;
+            need |= mx[e] > m_run[e] + kLazyLog2;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                if (!(mx[e] > m_run[e] + kLazyLog2)) continue;
+                const float alpha = ex2_approx(m_run[e] - mx[e]);  // 0 on the first page
+                m_run[e] = mx[e];
+                l_run[e] *= alpha;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    acc[mt][e] *= alpha;
+                    acc[mt][2 + e] *= alpha;
+                }
+            }
+        }
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const float muse = m_run[e] == -INFINITY ? 0.f : m_run[e];
+            pv[e] = ex2_approx(fmaf(s[e], p.scale_log2, -muse));
+            pv[2 + e] = ex2_approx(fmaf(s[2 + e], p.scale_log2, -muse));
+            l_run[e] += pv[e] + pv[2 + e];
+        }
+        // P^T as B fragments: keys 2c, 2c+1 (and 2c+8, 2c+9) of column g.
+        const uint32_t pb0 = movmatrix_trans(pack2<T>(pv[0], pv[1]));
+        const uint32_t pb1 = movmatrix_trans(pack2<T>(pv[2], pv[3]));
+        uint32_t pl0 = 0u, pl1 = 0u;
+        if (p_split) {
+            pl0 = movmatrix_trans(pack2<T>(pv[0] - round_trip<T>(pv[0]), pv[1] - round_trip<T>(pv[1])));
+            pl1 = movmatrix_trans(pack2<T>(pv[2] - round_trip<T>(pv[2]), pv[3] - round_trip<T>(pv[3])));
+        }
+
+        // O^T[dim][col] += sum_key V[key][dim] P^T[key][col]
+#pragma unroll
+        for (int u = 0; u < VC; ++u) {
+#define SDL_DIRECT_PV(W)                                                                             \
+    {                                                                                                \
+        const uint32_t x0 = u4_word<W>(vr[0][u]), x1 = u4_word<W>(vr[1][u]);                         \
+        const uint32_t x2 = u4_word<W>(vr[2][u]), x3 = u4_word<W>(vr[3][u]);                         \
+        uint32_t a[4] = {__byte_perm(x0, x1, 0x5410), __byte_perm(x0, x1, 0x7632),                   \
+                         __byte_perm(x2, x3, 0x5410), __byte_perm(x2, x3, 0x7632)};                  \
+        mma_16816<T>(acc[4 * u + W], a, pb0, pb1);                                                   \
+        if (p_split) mma_16816<T>(acc[4 * u + W], a, pl0, pl1);                                      \
+    }
+            SDL_DIRECT_PV(0)
+            SDL_DIRECT_PV(1)
+            SDL_DIRECT_PV(2)
+            SDL_DIRECT_PV(3)
+#undef SDL_DIRECT_PV
+        }
+        if (more) load_v(t_next, (pg + WH) * kPage);
+    }
+    pdl_launch_dependents();  // the split merge may be scheduled during the epilogue
+
+    // Each warp's (m, l, O) to shared memory, columns 2tq + e.
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        float l = l_run[e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        const int col = 2 * tq + e;
+        if (grp == 0) {
+            s_m[warp][col] = m_run[e];
+            s_l[warp][col] = l;
+        }
+#pragma unroll
+        for (int u = 0; u < VC; ++u)
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+                *reinterpret_cast<float2*>(&s_part[warp][col][64 * u + 8 * grp + 2 * w]) =
+                    make_float2(acc[4 * u + w][e], acc[4 * u + w][2 + e]);
+    }
+    __syncthreads();
+
+    // Merge each head's warps: thread -> (head, column, 4 head dims).  A
+    // column with a key in this split saw it in the first page of the
+    // head's warp wi = 0, so M is finite.
+    constexpr int NQ = HD / 4;
+    for (int idx = threadIdx.x; idx < G * kDirCols * NQ; idx += kDirWarps * 32) {
+        const int hg = idx / (kDirCols * NQ);
+        const int col = (idx / NQ) % kDirCols, d0 = (idx % NQ) * 4;
+        if (col >= ncol) continue;
+        const int j = col / p.ratio;
+        if (j >= nvalid) continue;
+        const int L = start + j + 1;
+        const int np_c = (L + kPage - 1) / kPage;
+        if (pbeg >= np_c) continue;
+        const int ns_c = (np_c + p.pps - 1) / p.pps;
+        float M = -INFINITY;
+        for (int w = hg; w < kDirWarps; w += G) M = fmaxf(M, s_m[w][col]);
+        float den = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = hg; w < kDirWarps; w += G) {
+            const float mw = s_m[w][col];
+            if (mw == -INFINITY) continue;  // a warp with no key of this column
+            const float wt = ex2_approx(mw - M);
+            den = fmaf(wt, s_l[w][col], den);
+            const float4 v = *reinterpret_cast<const float4*>(&s_part[w][col][d0]);
+            o.x = fmaf(wt, v.x, o.x); o.y = fmaf(wt, v.y, o.y);
+            o.z = fmaf(wt, v.z, o.z); o.w = fmaf(wt, v.w, o.w);
+        }
+        const int h = (blockIdx.y * G + hg) * p.ratio + col % p.ratio;
+        if (ns_c == 1) {
+            const float inv = 1.f / den;
+            const int64_t ob = b * p.o_sb + j * p.o_sj + h * p.o_sh + d0;
+            store_from_f32(p.out, ob, p.out_dtype, o.x * inv);
+            store_from_f32(p.out, ob + 1, p.out_dtype, o.y * inv);
+            store_from_f32(p.out, ob + 2, p.out_dtype, o.z * inv);
+            store_from_f32(p.out, ob + 3, p.out_dtype, o.w * inv);
+        } else {
+            const int64_t pidx = (((int64_t)b * p.nsplit + split) * p.chunk + j) * p.Hq + h;
+            *reinterpret_cast<float4*>(p.o_part + pidx * HD + d0) = o;
+            if (d0 == 0) {
+                p.ml_part[pidx * 2] = M;
+                p.ml_part[pidx * 2 + 1] = den;
+            }
+        }
     }
 }
 
@@ -1876,6 +2208,7 @@ struct Plan {
     bool cluster = false;  // splits of a row form one cluster and merge on chip
     bool rows = false;     // rows-on-M mma.sync kernel (ncoltiles = row tiles, wpg = consumer warps)
     bool umma = false;     // tcgen05 verify kernel
+    bool direct = false;   // register-direct decode kernel (one CTA per split, kv head and sequence)
     size_t smem = 0;
     size_t ws_bytes = 0;
 };
@@ -2164,8 +2497,68 @@ Plan make_rows_plan(const sdl_attn_args* a) {
     return pl;
 }
 
+template <int HD, typename T>
+int direct_occupancy_inst() {
+    static int n = -1;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (n < 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_direct_kernel<HD, T>, kDirWarps * 32, 0) !=
+            cudaSuccess) {
+            (void)cudaGetLastError();
+            return 0;  // not cached: a later call asks again
+        }
+    }
+    return n;
+}
+
+int direct_occupancy(int hd, int dtype) {
+    if (dtype == SDL_BF16)
+        return hd == 64 ? direct_occupancy_inst<64, __nv_bfloat16>() : direct_occupancy_inst<128, __nv_bfloat16>();
+    return hd == 64 ? direct_occupancy_inst<64, __half>() : direct_occupancy_inst<128, __half>();
+}
+
+// The register-direct kernel covers blocks of at most kDirCols query columns
+// per kv head over 16-byte aligned K/V.  It runs when asked for
+// (mma_layout = 3) and, automatically, for head_dim-64 decode, where it
+// measured faster on B200 (0.5B-shaped draft, 64 rows of 200-1500 keys:
+// 11.4-11.9 against 13.1 us).  At head_dim 128 the TMA ring keeps more bytes
+// in flight per SM than the registers can (C2 decode 30.1 against 33.4 us).
+bool direct_applicable(const sdl_attn_args* a) {
+    if (a->mma_layout == 1 || a->mma_layout == 2 || a->cluster_merge || !tc_applicable(a)) return false;
+    if (a->chunk * (a->Hq / a->Hkv) > kDirCols) return false;
+    const void* k = a->k_pool ? a->k_pool : a->k_dense;
+    const void* v = a->k_pool ? a->v_pool : a->v_dense;
+    if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) return false;
+    return a->mma_layout == 3 || (a->chunk == 1 && a->head_dim == 64);
+}
+
+Plan make_direct_plan(const sdl_attn_args* a) {
+    Plan pl;
+    pl.tc = true;
+    pl.direct = true;
+    // kv heads per CTA: one unless kv_heads_per_cta asks for more (the
+    // most dividing Hkv and kDirWarps up to it).  Reading a token row's
+    // heads together measured no faster (C2 decode 33.9 against 34.4 us,
+    // long-context decode 65.1 against 62.8 us).
+    for (int gc = std::min(a->Hkv, kDirWarps); gc >= 1; --gc) {
+        if (a->Hkv % gc || kDirWarps % gc) continue;
+        if (gc > std::max(1, a->kv_heads_per_cta)) continue;
+        pl.g_cta = gc;
+        break;
+    }
+    pl.kvgroups = a->Hkv / pl.g_cta;
+    pl.wpg = kDirWarps / pl.g_cta;
+    const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
+    const long base_ctas = (long)a->B * pl.kvgroups;
+    const int occ = a->key_count > 0 ? direct_occupancy(a->head_dim, a->dtype) : 0;
+    finish_split_plan(a, pl, split_pages(a, base_ctas, max_pages, occ), max_pages, 1);
+    return pl;
+}
+
 Plan make_plan(const sdl_attn_args* a) {
     if (umma_applicable(a)) return make_umma_plan(a);
+    if (direct_applicable(a)) return make_direct_plan(a);
     if (rows_applicable(a)) return make_rows_plan(a);
     Plan pl;
     pl.tc = tc_applicable(a);
@@ -2250,6 +2643,15 @@ template <typename T>
 int launch_rows_dtype(int hd, const CUtensorMap& mk, const CUtensorMap& mv, const TcParams& tp, const Plan& pl,
                       cudaStream_t st) {
     return hd == 64 ? launch_rows_inst<64, T>(mk, mv, tp, pl, st) : launch_rows_inst<128, T>(mk, mv, tp, pl, st);
+}
+
+template <typename T>
+int launch_direct_dtype(int hd, const TcParams& tp, const Plan& pl, cudaStream_t st) {
+    const dim3 grid(pl.nsplit, pl.kvgroups, tp.B), block(kDirWarps * 32);
+    const cudaError_t e = hd == 64 ? sdl::launch_pdl(attn_direct_kernel<64, T>, grid, block, 0, st, tp)
+                                   : sdl::launch_pdl(attn_direct_kernel<128, T>, grid, block, 0, st, tp);
+    if (e != cudaSuccess) return sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    return sdl::check_launch("attn_direct_kernel");
 }
 
 template <int HD, typename T>
@@ -2368,7 +2770,7 @@ extern "C" int sdl_attention_kernel(const sdl_attn_args* args) {
     tmp.workspace = nullptr;
     tmp.workspace_bytes = 0;
     const Plan pl = make_plan(&tmp);
-    return !pl.tc ? 0 : pl.umma ? 2 : pl.rows ? 3 : 1;
+    return !pl.tc ? 0 : pl.umma ? 2 : pl.rows ? 3 : pl.direct ? 4 : 1;
 }
 
 extern "C" int sdl_attention_launches(const sdl_attn_args* args) {
@@ -2399,8 +2801,10 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     if (pl.tc) {
         if (pl.ws_bytes > 0 && (!a->workspace || a->workspace_bytes < pl.ws_bytes))
             return sdl::fail(SDL_ERR_WORKSPACE, "sdl_paged_attention: workspace too small");
-        CUtensorMap mk, mv;
-        if (a->k_pool) {
+        CUtensorMap mk = {}, mv = {};
+        if (pl.direct) {
+            // plain loads: no tensor maps
+        } else if (a->k_pool) {
             if (a->tmap_k && a->tmap_v) {
                 memcpy(&mk, a->tmap_k, sizeof(CUtensorMap));
                 memcpy(&mv, a->tmap_v, sizeof(CUtensorMap));
@@ -2433,6 +2837,8 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.k_pool = tp.v_pool = nullptr;
         tp.k_new = tp.v_new = nullptr;
         tp.new_stride = 0;
+        tp.k_src = static_cast<const char*>(a->k_pool ? a->k_pool : a->k_dense);
+        tp.v_src = static_cast<const char*>(a->k_pool ? a->v_pool : a->v_dense);
         if (fused_append) {
             tp.k_pool = static_cast<char*>(const_cast<void*>(a->k_pool));
             tp.v_pool = static_cast<char*>(const_cast<void*>(a->v_pool));
@@ -2451,6 +2857,9 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         if (pl.umma) {
             if (a->dtype == SDL_BF16) rc = launch_umma_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
             else rc = launch_umma_dtype<__half>(a->head_dim, mk, mv, tp, pl, st);
+        } else if (pl.direct) {
+            if (a->dtype == SDL_BF16) rc = launch_direct_dtype<__nv_bfloat16>(a->head_dim, tp, pl, st);
+            else rc = launch_direct_dtype<__half>(a->head_dim, tp, pl, st);
         } else if (pl.rows) {
             if (a->dtype == SDL_BF16) rc = launch_rows_dtype<__nv_bfloat16>(a->head_dim, mk, mv, tp, pl, st);
             else rc = launch_rows_dtype<__half>(a->head_dim, mk, mv, tp, pl, st);

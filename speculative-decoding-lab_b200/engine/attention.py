@@ -125,14 +125,15 @@ def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_
     return n
 
 
-KERNEL_NAMES = ("generic", "mma", "tcgen05", "mma_rows")
+KERNEL_NAMES = ("generic", "mma", "tcgen05", "mma_rows", "mma_direct")
 
 
 def attention_kernel(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
                      mma_layout: int = 0) -> str:
     """Which kernel ``paged_attention`` runs for these arguments: "generic"
     (CUDA cores), "mma" (mma.sync split-K, keys on the MMA M dimension),
-    "mma_rows" (mma.sync split-K, query rows on M) or "tcgen05"
+    "mma_rows" (mma.sync split-K, query rows on M), "mma_direct" (keys on M,
+    K/V loaded straight into registers; decode) or "tcgen05"
     (persistent)."""
     q4 = q if q.dim() == 4 else q.reshape(q.shape[0], 1, q.shape[-2], q.shape[-1])
     a = _paged_args(q4, kv, 0, batch, q4, use_umma=use_umma, mma_layout=mma_layout)
@@ -225,7 +226,8 @@ def paged_attention(
     split-K CTA, kv heads sharing one CTA of the mma.sync kernel, 1 for the
     tcgen05 kernel, split partials merged on chip within a thread-block
     cluster instead of by a separate launch, 1 / 2 for the mma.sync kernel
-    with keys / query rows on the MMA M dimension); every plan gives the same
+    with keys / query rows on the MMA M dimension, 3 for keys on M with K/V
+    loaded straight into registers); every plan gives the same
     result within rounding of the split merge.
     """
     _lib.require_cuda(q, "query")

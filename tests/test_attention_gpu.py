@@ -106,10 +106,11 @@ def test_fp32_attention_matches_reference_fixture(tag):
 
 
 @pytest.mark.parametrize("tag", ["dec_bf16_d128", "ext_bf16_d128", "dec_bf16_d64_r7"])
-@pytest.mark.parametrize("layout", [0, 1, 2])
+@pytest.mark.parametrize("layout", [0, 1, 2, 3])
 def test_bf16_attention_matches_reference_fixture(tag, layout):
-    """The reference's own outputs, on the automatic kernel and on both
-    mma.sync layouts (keys / query rows on the MMA M dimension)."""
+    """The reference's own outputs, on the automatic kernel and on every
+    mma.sync layout (keys / query rows on the MMA M dimension, keys on M with
+    register-direct loads)."""
     kv, q, starts, chunk, Hq, ref = _golden_case(tag)
     batch = AttnBatch.from_lists(DEV, list(range(len(starts))), starts, chunk)
     out = paged_attention(q, kv, 0, batch, mma_layout=layout)
@@ -145,7 +146,7 @@ CASES = [
 
 @pytest.mark.parametrize("case", range(len(CASES)))
 @pytest.mark.parametrize("generic,umma,layout", [(False, 0, 0), (False, 1, 0), (False, -1, 1), (False, -1, 2),
-                                                 (True, 0, 0)])
+                                                 (False, -1, 3), (True, 0, 0)])
 def test_paged_attention_matches_oracle(case, generic, umma, layout):
     """Every kernel (tcgen05, mma.sync with keys or query rows on the MMA M
     dimension, CUDA-core) against the oracle."""
@@ -165,7 +166,8 @@ def test_paged_attention_matches_oracle(case, generic, umma, layout):
 @pytest.mark.parametrize("pps", [1, 3, 0, 64, 12])
 @pytest.mark.parametrize("heads_per_cta,umma,cluster,layout", [(0, -1, False, 1), (1, -1, False, 1),
                                                                 (0, -1, True, 1), (1, -1, True, 1),
-                                                                (0, 1, False, 0), (0, -1, False, 2)])
+                                                                (0, 1, False, 0), (0, -1, False, 2),
+                                                                (0, -1, False, 3), (2, -1, False, 3)])
 def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
     """Every launch plan (pages per split-K CTA from 1, i.e. 150+ splits per
     row, to one split; one or two kv heads per CTA of the mma.sync kernel;
@@ -186,7 +188,8 @@ def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
 
 @pytest.mark.parametrize("pps,chunk,cluster,layout", [(4, 1, False, 0), (0, 1, False, 0), (0, 6, True, 0),
                                                       (16, 6, True, 0), (0, 6, False, 0), (4, 6, False, 0),
-                                                      (0, 6, False, 2), (4, 6, False, 2), (0, 1, False, 2)])
+                                                      (0, 6, False, 2), (4, 6, False, 2), (0, 1, False, 2),
+                                                      (4, 1, False, 3), (0, 1, False, 3)])
 def test_split_merge_is_deterministic(pps, chunk, cluster, layout):
     """The split-K merge (separate launch; on chip in a cluster) has a fixed
     reduction order: repeated calls give identical bits, on both mma.sync
@@ -300,6 +303,11 @@ FUSED_CASES = [
     (12, 2, 128, 9, [0, 40, 91], [9, 3, 6], torch.bfloat16, {"mma_layout": 1}),       # keys on M, ragged rows
     (12, 2, 128, 24, [0, 37, 500], [24, 5, 17], torch.bfloat16, {"mma_layout": 2}),   # rows on M: 3 row tiles
     (12, 2, 128, 1, [15, 16, 1029], None, torch.bfloat16, {"mma_layout": 2}),        # rows on M, decode
+    (12, 2, 128, 1, [15, 16, 17, 1029, 4095], None, torch.bfloat16, {"mma_layout": 3}),  # register-direct decode
+    (14, 2, 64, 1, [0, 31, 1000], None, torch.float16, {"mma_layout": 3, "kv_heads_per_cta": 2}),  # fp16, d 64
+    (8, 8, 128, 3, [14, 300], None, torch.bfloat16, {"mma_layout": 3, "pages_per_split": 1,
+                                                      "kv_heads_per_cta": 4}),  # rows span 2 splits, 4 heads/CTA
+    (4, 2, 64, 4, [0, 13, 90], [4, 1, 3], torch.bfloat16, {"mma_layout": 3}),        # register-direct, ragged rows
     (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"force_generic": True}),        # CUDA-core: separate append
     (4, 2, 16, 3, [0, 9, 33], None, torch.float32, {}),                              # fp32 pool: separate append
 ]

@@ -14,7 +14,7 @@ import pytest
 
 from engine import _lib
 
-KERNELS = {0: "generic", 1: "mma", 2: "tcgen05", 3: "mma_rows"}
+KERNELS = {0: "generic", 1: "mma", 2: "tcgen05", 3: "mma_rows", 4: "mma_direct"}
 
 
 def _args(B, chunk, Hq, Hkv, d, max_limit, dtype=_lib.SDL_BF16, **kw):
@@ -49,6 +49,13 @@ def _kernel(a):
     ((16, 7, 16, 2, 128, 32768), {"use_umma": -1}, "mma_rows"),   # mma.sync forced
     ((16, 7, 16, 2, 128, 32768), {"use_umma": -1, "mma_layout": 1}, "mma"),
     ((64, 1, 12, 2, 128, 4096), {"mma_layout": 2}, "mma_rows"),
+    ((64, 1, 12, 2, 128, 4096), {"mma_layout": 3}, "mma_direct"),  # register-direct decode
+    ((64, 1, 14, 2, 64, 4096), {"mma_layout": 3}, "mma_direct"),   # 7 columns, d 64
+    ((64, 1, 14, 2, 64, 1500), {}, "mma_direct"),                  # 0.5B draft decode: automatic at d 64
+    ((64, 1, 14, 2, 64, 1500), {"mma_layout": 1}, "mma"),
+    ((64, 2, 14, 2, 64, 1500), {}, "mma"),                         # 14 columns
+    ((32, 6, 12, 2, 128, 2048), {"mma_layout": 3}, "mma"),         # 36 columns: beyond one 8-column tile
+    ((64, 1, 12, 2, 128, 4096), {"mma_layout": 3, "k_pool": 0x300008}, "mma"),  # pool not 16-byte aligned
     ((32, 8, 12, 2, 128, 2048), {"cluster_merge": 1}, "mma"),     # the cluster merge is keys-on-M only
     ((1, 512, 12, 2, 128, 512), {}, "mma_rows"),                  # prefill chunk
     ((8, 1, 4, 2, 16, 100), {"dtype": _lib.SDL_F32}, "generic"),  # fp32 pool
