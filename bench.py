@@ -66,7 +66,7 @@ METRIC = "spec-decode tokens/s (paged KV, 1/2/4/8 GPU); paged-attn HBM GB/s vs 8
 C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=64, ctx_lo=512, ctx_hi=4096)
 # DRAM bytes (read + write) of one C2 attention launch of attn_tc_kernel, from the
 # ncu --set full capture summarised under profiles/ (refreshed when re-profiled).
-C2_ATTN_TRAFFIC = 154_166_784 + 4_897_792
+C2_ATTN_TRAFFIC = 154_167_040 + 3_741_184
 
 # kernel names of the attention op per attention_kernel() answer
 ATTN_KERNELS = {
