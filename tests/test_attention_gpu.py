@@ -254,6 +254,25 @@ def test_decode_api_and_full_attention_match_oracle():
         np.testing.assert_allclose(fo.cpu().numpy(), exact[sid], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("ctx", [1, 15, 16, 37, 1029])
+@pytest.mark.parametrize("d", [64, 128])
+def test_full_attention_dense_16bit_matches_fp32_torch(ctx, d):
+    """Dense K/V of a length that is not a multiple of 16 (``full_attention``;
+    at head_dim 64 the register-direct kernel, which must not load keys past
+    the tensor's end) against plain fp32 torch attention with GQA 7:1."""
+    g = torch.Generator().manual_seed(ctx * 7 + d)
+    q = torch.randn(14, d, generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn(ctx, 2, d, generator=g).to(DEV, torch.bfloat16)
+    v = torch.randn(ctx, 2, d, generator=g).to(DEV, torch.bfloat16)
+    out = full_attention(q, k, v, 14).float()
+    qf = q.float().view(2, 7, d)
+    kf, vf = k.float().permute(1, 0, 2), v.float().permute(1, 0, 2)  # (2, ctx, d)
+    p = torch.softmax(qf @ kf.transpose(1, 2) * d ** -0.5, dim=-1)
+    ref = (p @ vf).reshape(14, d)
+    assert torch.isfinite(out).all()
+    assert (out - ref).abs().max().item() <= 2.0 ** -7 * ref.abs().max().item() + 2e-3
+
+
 @pytest.mark.parametrize("dtype,d", [(torch.float32, 8), (torch.bfloat16, 128), (torch.bfloat16, 64)])
 def test_prefill_chunk_matches_oracle_and_zeroes_padding(dtype, d):
     Hq, Hkv = (4, 2) if d == 8 else (12, 2)
