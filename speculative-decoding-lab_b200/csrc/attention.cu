@@ -1420,7 +1420,8 @@ constexpr uint32_t kUTmemCols = 512;  // S double buffer (2 x 64 columns) + O do
 constexpr int kUOCol = 2 * kUTok;     // TMEM column of O buffer 0; buffer 1 is 128 columns on
 constexpr int kSkMaxPairs = 512;      // (sequence, kv head) pairs one launch may hold
 constexpr int kSkMaxSeqs = 512;       // sequences one launch may hold
-constexpr int kUmmaAutoMinKeys = 4096; // automatic plans: key span from which verify blocks use tcgen05
+constexpr int kUmmaAutoMinKeys = 4096; // automatic plans: mean keys per sequence from which blocks use tcgen05
+constexpr int kUmmaAutoMinRows = 48;   // ... and query rows per kv head
 constexpr uint32_t kPollLimit = 1u << 24;  // idle polls (32 ns apart) of the tcgen05 MMA thread before a timeout
 
 template <int HD>
@@ -2247,12 +2248,16 @@ bool umma_applicable(const sdl_attn_args* a) {
     const int rows = a->chunk * (a->Hq / a->Hkv);
     if (rows > kURows || (long)a->B * a->Hkv > kSkMaxPairs) return false;
     if (a->use_umma > 0) return true;
-    // Automatic choice: the mma.sync kernel spends ~330 issue slots per
-    // 8-column warp and page, so blocks of more than two 8-column tiles per
-    // kv head over long contexts are instruction bound there; the tcgen05
-    // kernel issues the products from one thread.  Short contexts keep the
-    // mma.sync kernel, whose split grid starts faster.
-    return rows > 16 && a->max_limit >= kUmmaAutoMinKeys;
+    // Automatic choice: the mma.sync kernels spend many issue slots per
+    // page, so large blocks over long contexts are instruction bound there;
+    // the tcgen05 kernel issues the products from one thread.  Measured on
+    // B200: 56 rows per kv head over 8k-32k keys (C5 verify) 87.7 us against
+    // 100 (rows on M) / 116 (keys on M); 30 rows over 8k-32k keys 93.7
+    // against 75.1 (keys on M); 30 rows over mostly short rows with one of
+    // 4200 keys 42.0 against 25.8 (rows on M).  The mean span decides (the
+    // key count when given), not the longest row.
+    const long mean_keys = a->key_count > 0 ? (long)(a->key_count / std::max(1, a->B)) : (long)a->max_limit;
+    return rows >= kUmmaAutoMinRows && mean_keys >= kUmmaAutoMinKeys;
 }
 
 // Workspace of the persistent kernel: the per-pair table, then fp32 partials
@@ -2391,9 +2396,15 @@ constexpr double kOneWaveFillBlock = 0.96;
 // runs.  Measured on B200: it wins for head_dim 64 verify blocks (42 rows:
 // 15.1 against 18.5 us), 56-row verify (100 against 116 us) and prefill;
 // 36-row head_dim-128 verify is latency bound in both and the keys-on-M
-// kernel, with more warps per SM, is 3 % faster there.
+// kernel, with more warps per SM, is 3 % faster there (32 rows of 256-2048
+// keys).  Over short rows the balance turns: 30-row blocks of 64 sequences
+// with a mean of ~700 keys take 24-26 us on rows on M against 32-33 us on
+// keys on M, so head_dim-128 blocks of 24+ rows take rows on M when the key
+// count puts the mean span below kRowsShortKeys.
 constexpr int kRowsMinRows64 = 16;
 constexpr int kRowsMinRows128 = 48;
+constexpr int kRowsMinRows128Short = 24;
+constexpr int kRowsShortKeys = 1024;
 
 template <int HD, typename T>
 int rows_configure(size_t smem) {
@@ -2475,7 +2486,10 @@ void finish_split_plan(const sdl_attn_args* a, Plan& pl, int pps, int max_pages,
 bool rows_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->mma_layout == 2) return true;
-    return a->chunk * (a->Hq / a->Hkv) >= (a->head_dim == 64 ? kRowsMinRows64 : kRowsMinRows128);
+    const int rows = a->chunk * (a->Hq / a->Hkv);
+    if (rows >= (a->head_dim == 64 ? kRowsMinRows64 : kRowsMinRows128)) return true;
+    return a->head_dim == 128 && rows >= kRowsMinRows128Short && a->key_count > 0 &&
+           a->key_count < (int64_t)kRowsShortKeys * a->B;
 }
 
 Plan make_rows_plan(const sdl_attn_args* a) {

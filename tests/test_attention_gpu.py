@@ -398,14 +398,15 @@ def test_fused_append_rejects_bad_rows():
 
 
 def test_automatic_kernel_choice():
-    """use_umma=0 picks the tcgen05 kernel for verify blocks of more than 16
-    query rows per kv head over spans of 4096+ keys, the rows-on-M mma.sync
-    kernel for shorter blocks of 48+ rows per kv head (16+ at head_dim 64),
-    the keys-on-M one for decode and smaller blocks, and the CUDA-core kernel
-    for fp32 pools; the explicit flags override it."""
+    """use_umma=0 picks the tcgen05 kernel for verify blocks of 48+ query
+    rows per kv head over a mean span of 4096+ keys, the rows-on-M mma.sync
+    kernel for shorter blocks of 48+ rows per kv head (16+ at head_dim 64;
+    24+ at head_dim 128 over a mean span below 1024 keys), the keys-on-M one
+    for decode and smaller blocks, and the CUDA-core kernel for fp32 pools;
+    the explicit flags override it."""
     from engine.attention import attention_kernel
-    kv, _ = _build([4200 + 7, 300 + 7], 2, 128, 16, torch.bfloat16, seed=31)
-    long_verify = AttnBatch.from_lists(DEV, [0, 1], [4200, 300], 7)
+    kv, _ = _build([4200 + 7, 4100 + 7], 2, 128, 16, torch.bfloat16, seed=31)
+    long_verify = AttnBatch.from_lists(DEV, [0, 1], [4200, 4100], 7)
     short_verify = AttnBatch.from_lists(DEV, [0, 1], [1000, 300], 7)
     q7 = torch.zeros(2, 7, 16, 128, device=DEV, dtype=torch.bfloat16)
     q1 = torch.zeros(2, 1, 16, 128, device=DEV, dtype=torch.bfloat16)
@@ -415,7 +416,9 @@ def test_automatic_kernel_choice():
     assert attention_kernel(q7, kv, short_verify, mma_layout=1) == "mma"
     assert attention_kernel(q7, kv, short_verify, use_umma=1) == "tcgen05"
     q6 = torch.zeros(2, 6, 12, 128, device=DEV, dtype=torch.bfloat16)            # 36 rows: keys on M
-    assert attention_kernel(q6, kv, AttnBatch.from_lists(DEV, [0, 1], [1000, 300], 6)) == "mma"
+    assert attention_kernel(q6, kv, AttnBatch.from_lists(DEV, [0, 1], [1400, 1100], 6)) == "mma"
+    assert attention_kernel(q6, kv, AttnBatch.from_lists(DEV, [0, 1], [1000, 300], 6)) == "mma_rows"  # short spans
+    assert attention_kernel(q7, kv, AttnBatch.from_lists(DEV, [0, 1], [4200, 300], 7)) == "mma_rows"  # mean 2257
     assert attention_kernel(q1, kv, AttnBatch.from_lists(DEV, [0, 1], [4206, 306], 1)) == "mma"
     assert attention_kernel(q1, kv, AttnBatch.from_lists(DEV, [0, 1], [4206, 306], 1), mma_layout=2) == "mma_rows"
     kv32, _ = _build([40], 2, 16, 4, torch.float32, seed=32)

@@ -46,6 +46,10 @@ def _kernel(a):
     ((32, 8, 12, 2, 128, 2048), {}, "mma_rows"),                  # 48 rows per kv head
     ((32, 5, 14, 2, 64, 2048), {}, "mma_rows"),                   # d 64, 35 rows
     ((16, 7, 16, 2, 128, 32768), {}, "tcgen05"),                  # C5 verify: long span
+    ((16, 7, 16, 2, 128, 32768), {"key_count": 16 * 20000}, "tcgen05"),
+    ((16, 5, 12, 2, 128, 32768), {"key_count": 16 * 20000}, "mma"),   # 30 rows: keys on M
+    ((64, 5, 12, 2, 128, 4200), {"key_count": 64 * 700}, "mma_rows"),  # C4 verify: short mean span
+    ((32, 6, 12, 2, 128, 2048), {"key_count": 32 * 1152}, "mma"),  # C3 verify: mean 1152 keys
     ((16, 7, 16, 2, 128, 32768), {"use_umma": -1}, "mma_rows"),   # mma.sync forced
     ((16, 7, 16, 2, 128, 32768), {"use_umma": -1, "mma_layout": 1}, "mma"),
     ((64, 1, 12, 2, 128, 4096), {"mma_layout": 2}, "mma_rows"),
