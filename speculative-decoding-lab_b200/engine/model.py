@@ -394,8 +394,12 @@ class PagedLMMixin:
 
     def _run_layers(self, hidden: torch.Tensor, kv: PagedKVCache, plan: ForwardPlan,
                     cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        # A layer may hand on its residual stream as a pair (hidden, delta):
+        # the next layer's input norm adds delta in the same launch.
         for index, layer in enumerate(self.layers):
             hidden = layer.forward_plan(hidden, kv, index, plan, cos, sin)
+        if isinstance(hidden, tuple):
+            hidden = hidden[0] + hidden[1]
         return hidden
 
     PREFILL_MIN_BUCKET = 64

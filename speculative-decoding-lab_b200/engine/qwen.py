@@ -92,9 +92,17 @@ class QwenDecoderLayer(nn.Module):
         self.mlp = QwenMLP(hidden, intermediate)
 
     def forward_plan(self, hidden, kv, layer_index, plan, cos, sin):
+        """One decoder layer.  16-bit models return the residual stream as a
+        pair ``(hidden, mlp_out)`` whose sum the next layer's input norm forms
+        in its own launch (the same bf16 rounding as ``hidden + mlp_out``);
+        ``hidden`` may arrive as such a pair."""
         attn = self.self_attn
+        if isinstance(hidden, tuple):
+            norm = self.input_layernorm
+            hidden, x = layer_ops.add_rmsnorm(hidden[0], hidden[1], norm.weight, norm.eps)
+        else:
+            x = self.input_layernorm(hidden)
         lead = tuple(hidden.shape[:-1])
-        x = self.input_layernorm(hidden)
         d, hq, hkv = attn.head_dim, attn.num_heads, attn.num_kv_heads
         if layer_ops.fusable(x):
             # 16-bit models: one projection GEMM, and one RoPE launch over the
@@ -112,7 +120,7 @@ class QwenDecoderLayer(nn.Module):
         if layer_ops.fusable(hidden):  # residual add + post-attention norm in one launch
             norm = self.post_attention_layernorm
             hidden, x2 = layer_ops.add_rmsnorm(hidden, o, norm.weight, norm.eps)
-            return hidden + self.mlp(x2)
+            return hidden, self.mlp(x2)
         hidden = hidden + o
         return hidden + self.mlp(self.post_attention_layernorm(hidden))
 
