@@ -49,7 +49,7 @@ def test_silu_mul_is_bit_exact(dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("dim", [200, 256, 896, 1536, 2048, 4096])
+@pytest.mark.parametrize("dim", [200, 256, 896, 1025, 1536, 2048, 4096, 4097, 5000])
 def test_rmsnorm_matches_the_chain(dtype, dim):
     g = torch.Generator(device=DEV).manual_seed(dim)
     x = (torch.randn((67, dim), generator=g, device=DEV) * 2).to(dtype)
