@@ -192,8 +192,10 @@ typedef struct sdl_attn_args {
     int32_t use_umma;         /* 1 = the tcgen05 kernel where it applies
                                  (up to 64 query rows per kv head);
                                  -1 = the mma.sync kernel; 0 = automatic:
-                                 tcgen05 for blocks of more than 16 query
-                                 rows per kv head when max_limit >= 4096  */
+                                 tcgen05 for blocks of at least 48 query
+                                 rows per kv head over a mean span of at
+                                 least 4096 keys (key_count / B, or
+                                 max_limit without a key count)           */
     int32_t cluster_merge;    /* mma.sync kernel with split rows: 0 = fp32
                                  partials in the workspace and a separate
                                  merge launch (default); 1 = the splits of
@@ -211,9 +213,12 @@ typedef struct sdl_attn_args {
     int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
                                  on the MMA M dimension for blocks of at
                                  least 48 query rows per kv head, 16 at
-                                 head_dim 64; keys on M below that, with
+                                 head_dim 64, 24 at head_dim 128 when
+                                 key_count gives a mean span below 1024
+                                 keys; keys on M below that, with
                                  register-direct loads (3) for head_dim-64
-                                 decode), 1 =
+                                 decode when key_count gives a mean span
+                                 of at most 1280 keys), 1 =
                                  keys on M (query columns on N: the decode
                                  layout), 2 = query rows on M
                                  (FlashAttention-2 register layout), 3 =

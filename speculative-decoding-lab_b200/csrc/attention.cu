@@ -2534,17 +2534,21 @@ int direct_occupancy(int hd, int dtype) {
 
 // The register-direct kernel covers blocks of at most kDirCols query columns
 // per kv head over 16-byte aligned K/V.  It runs when asked for
-// (mma_layout = 3) and, automatically, for head_dim-64 decode, where it
+// (mma_layout = 3) and, automatically, for head_dim-64 decode over short
+// rows (a key count with a mean span of at most kDirAutoMaxKeys), where it
 // measured faster on B200 (0.5B-shaped draft, 64 rows of 200-1500 keys:
-// 11.4-11.9 against 13.1 us).  At head_dim 128 the TMA ring keeps more bytes
+// 11.4-11.9 against 13.0 us).  Over 1000-3000 keys the TMA kernel is ahead
+// (18.5 against 21.1 us), and at head_dim 128 the TMA ring keeps more bytes
 // in flight per SM than the registers can (C2 decode 30.1 against 33.4 us).
+constexpr int kDirAutoMaxKeys = 1280;
 bool direct_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->mma_layout == 2 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->chunk * (a->Hq / a->Hkv) > kDirCols) return false;
     const void* k = a->k_pool ? a->k_pool : a->k_dense;
     const void* v = a->k_pool ? a->v_pool : a->v_dense;
     if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) return false;
-    return a->mma_layout == 3 || (a->chunk == 1 && a->head_dim == 64);
+    return a->mma_layout == 3 || (a->chunk == 1 && a->head_dim == 64 && a->key_count > 0 &&
+                                  a->key_count <= (int64_t)kDirAutoMaxKeys * a->B);
 }
 
 Plan make_direct_plan(const sdl_attn_args* a) {

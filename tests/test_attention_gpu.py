@@ -327,6 +327,8 @@ FUSED_CASES = [
     (8, 8, 128, 3, [14, 300], None, torch.bfloat16, {"mma_layout": 3, "pages_per_split": 1,
                                                       "kv_heads_per_cta": 4}),  # rows span 2 splits, 4 heads/CTA
     (4, 2, 64, 4, [0, 13, 90], [4, 1, 3], torch.bfloat16, {"mma_layout": 3}),        # register-direct, ragged rows
+    (14, 2, 64, 1, [0, 15, 16, 700, 2047], None, torch.bfloat16, {"key_count": 2783}),  # 12-warp unsplit variant
+    (14, 2, 64, 1, [3, 40, 1000], [1, 0, 1], torch.float16, {"key_count": 1045}),   # unsplit, an idle row
     (12, 2, 128, 6, [5, 250], None, torch.bfloat16, {"force_generic": True}),        # CUDA-core: separate append
     (4, 2, 16, 3, [0, 9, 33], None, torch.float32, {}),                              # fp32 pool: separate append
 ]
@@ -334,6 +336,8 @@ FUSED_CASES = [
 
 def _fused_pair(case, layers=2, layer=1, misalign=False):
     Hq, Hkv, d, chunk, starts, valid, dtype, kw = FUSED_CASES[case]
+    kw = dict(kw)
+    key_count = kw.pop("key_count", 0)
     B = len(starts)
     valid = valid or [chunk] * B
     bs = 4 if dtype == torch.float32 else 16
@@ -347,7 +351,7 @@ def _fused_pair(case, layers=2, layer=1, misalign=False):
     k_new = torch.randn(B * chunk, width, generator=g).to(DEV, dtype)[:, (2 if misalign else 0):]
     v_new = torch.randn(B * chunk, width, generator=g).to(DEV, dtype)[:, (2 if misalign else 0):]
     packed = _lib_i32(list(range(B)) + starts + valid)
-    batch = AttnBatch(packed[:B], packed[B:2 * B], max(s + chunk for s in starts), packed[2 * B:])
+    batch = AttnBatch(packed[:B], packed[B:2 * B], max(s + chunk for s in starts), packed[2 * B:], key_count)
     keep = torch.cat([torch.arange(b * chunk, b * chunk + valid[b]) for b in range(B)]).to(DEV)
     pair[0].append(layer, slots[0], k_new[keep].reshape(-1, Hkv, d), v_new[keep].reshape(-1, Hkv, d))
     sep = paged_attention(q, pair[0], layer, batch, **kw)

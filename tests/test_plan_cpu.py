@@ -55,7 +55,9 @@ def _kernel(a):
     ((64, 1, 12, 2, 128, 4096), {"mma_layout": 2}, "mma_rows"),
     ((64, 1, 12, 2, 128, 4096), {"mma_layout": 3}, "mma_direct"),  # register-direct decode
     ((64, 1, 14, 2, 64, 4096), {"mma_layout": 3}, "mma_direct"),   # 7 columns, d 64
-    ((64, 1, 14, 2, 64, 1500), {}, "mma_direct"),                  # 0.5B draft decode: automatic at d 64
+    ((64, 1, 14, 2, 64, 1500), {"key_count": 64 * 700}, "mma_direct"),  # 0.5B draft decode, short rows
+    ((64, 1, 14, 2, 64, 3000), {"key_count": 64 * 2000}, "mma"),   # longer rows: the TMA kernel
+    ((64, 1, 14, 2, 64, 1500), {}, "mma"),                         # no key count: the TMA kernel
     ((64, 1, 14, 2, 64, 1500), {"mma_layout": 1}, "mma"),
     ((64, 2, 14, 2, 64, 1500), {}, "mma"),                         # 14 columns
     ((32, 6, 12, 2, 128, 2048), {"mma_layout": 3}, "mma"),         # 36 columns: beyond one 8-column tile
