@@ -253,7 +253,8 @@ int sdl_attention_launches(const sdl_attn_args* args);
 
 /* Kernel sdl_paged_attention runs for `args`: 0 = CUDA-core (generic),
  * 1 = mma.sync split-K with keys on M, 2 = tcgen05 persistent, 3 = mma.sync
- * split-K with query rows on M; -1 when `args` is invalid.
+ * split-K with query rows on M, 4 = mma.sync split-K with keys on M and K/V
+ * loaded straight into the MMA fragments; -1 when `args` is invalid.
  * No counterpart in the reference. */
 int sdl_attention_kernel(const sdl_attn_args* args);
 
