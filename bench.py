@@ -309,6 +309,132 @@ class CpuC3:
         }
 
 
+class _Budget(Exception):
+    pass
+
+
+class CpuC4:
+    """The reference algorithm (numpy oracle port) on a bounded sample of C4.
+
+    The oracle's speculative scheduler (engine/spec_scheduler.py:110-322
+    restated: prefill on admission, gamma draft decodes, the gamma+1-row
+    verify, batch_accept, rewind / catch-up / clear) serves the first
+    ``batch`` requests of the C4 stream, all admitted at once, with both
+    models cut to one decoder layer (Qwen2.5-1.5B and 0.5B shapes, full
+    151,936-row vocab heads, weights N(0, 0.02), embeddings tied to the
+    heads to halve host memory) until ``seconds`` of host time are spent.  The time inside
+    the decoder layers is scaled to the full depth (28 and 24 layers).
+    Prefill is charged per request in proportion to the share of its output
+    the sample produced: tokens/s = tokens / (round time + prefill time x
+    tokens / requested tokens).
+    """
+
+    def __init__(self, seed: int = 0, threads: int = 0, batch: int = 8) -> None:
+        from engine import workloads
+        from engine.weights import qwen_numpy_state
+        from oracle.model import NumpyPagedLM, rotary_table
+
+        assert 151936 % 128 == 0
+
+        c = workloads.C4
+        self.c = c
+        self.batch = batch
+        self.threads = threads or (os.cpu_count() or 1)
+        self.models = []
+        self.depth = []
+        for name, s in ((c["target"], 1), (c["draft"], 2)):
+            full = workloads.shape_config(name)
+            cfg = workloads.shape_config(name, num_hidden_layers=1, tie_word_embeddings=True)
+            # the vocab rows repeat one random block of 1187 rows (151936 = 128 x 1187): the same
+            # arithmetic as distinct rows, without drawing 10^8 normals per model
+            V, H = cfg.vocab_size, cfg.hidden_size
+            cfg_small = workloads.shape_config(name, num_hidden_layers=1, tie_word_embeddings=True,
+                                               vocab_size=V // 128)
+            st = qwen_numpy_state(cfg_small, seed * 2 + s, 0.02)
+            st["embed_tokens.weight"] = np.tile(st["embed_tokens.weight"], (128, 1))
+            st["lm_head.weight"] = st["embed_tokens.weight"]
+            rope = rotary_table(cfg.head_dim, cfg.rope_theta, c["prompt_cap"] + c["out_hi"] + 16)
+            m = NumpyPagedLM(st, 1, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, rope, "qwen")
+            self.models.append(m)
+            self.depth.append(int(full.num_hidden_layers))
+        self.reqs = workloads.c4_requests(seed, batch, 1.0, c["vocab"])
+
+    def measure(self, seconds: float):
+        from oracle import kv as okv
+        from oracle import sampler as osm
+        from oracle import scheduler as osched
+
+        c = self.c
+        acc = {"layers": [0.0, 0.0], "prefill": 0.0, "prefill_layers": [0.0, 0.0]}
+        state = {"in_prefill": False}
+        for i, m in enumerate(self.models):
+            layer_fn = type(m)._layer
+            prefill_fn = type(m).prefill
+
+            def timed_layer(*a, _f=layer_fn, _m=m, _i=i, **k):
+                t = time.perf_counter()
+                try:
+                    return _f(_m, *a, **k)
+                finally:
+                    key = "prefill_layers" if state["in_prefill"] else "layers"
+                    acc[key][_i] += time.perf_counter() - t
+
+            def timed_prefill(*a, _f=prefill_fn, _m=m, **k):
+                t = time.perf_counter()
+                state["in_prefill"] = True
+                try:
+                    return _f(_m, *a, **k)
+                finally:
+                    state["in_prefill"] = False
+                    acc["prefill"] += time.perf_counter() - t
+
+            m._layer = timed_layer
+            m.prefill = timed_prefill
+        tgt, dft = self.models
+        cap_t = sum(-(-(len(ids) + new + 16) // 16) for ids, new, _ in self.reqs) + 8
+        kv_t = okv.PagedKVCache(1, tgt.nkv, tgt.d, cap_t, 16)
+        kv_d = okv.PagedKVCache(1, dft.nkv, dft.d, cap_t, 16)
+        us = np.random.default_rng(12345).random(1 << 20, dtype=np.float32)
+        reqs = [osched.Req(list(ids), new, 0) for ids, new, _ in self.reqs]
+        res = osched.RunResult()
+        t0 = time.perf_counter()
+
+        def hook():
+            if time.perf_counter() - t0 >= seconds:
+                raise _Budget()
+
+        try:
+            osched.run_spec_continuous(tgt, kv_t, dft, kv_d, reqs, c["gamma"], c["temperature"],
+                                       stream=osm.UniformStream(us), round_hook=hook, result=res)
+        except _Budget:
+            pass
+        wall = time.perf_counter() - t0
+        tokens = sum(len(s.generated) for s in res.sequences)
+        requested = sum(s.max_new_tokens for s in res.sequences)
+        rounds = len(res.tokens_per_round) // max(1, len(res.sequences))
+        lt, ld = acc["layers"]
+        plt, pld = acc["prefill_layers"]
+        scale_t, scale_d = self.depth[0], self.depth[1]
+        prefill_scaled = acc["prefill"] + plt * (scale_t - 1) + pld * (scale_d - 1)
+        round_wall = wall - acc["prefill"]
+        round_scaled = round_wall + lt * (scale_t - 1) + ld * (scale_d - 1)
+        charged = round_scaled + prefill_scaled * tokens / max(1, requested)
+        value = tokens / charged
+        return {
+            "value": round(value, 4),
+            "unit": "tokens/s",
+            "cores": self.threads,
+            "kind": "port",
+            "sample": "oracle speculative scheduler (numpy: fp32 GEMMs on {} BLAS threads, fp64 attention) "
+                      "serving the first {} C4 requests with both models cut to 1 decoder layer: {:.2f} s of "
+                      "host time ({:.2f} s prefill, ~{} rounds), {} tokens of {} requested; decoder-layer time "
+                      "scaled to 28 / 24 layers and prefill charged in proportion to the output produced, "
+                      "{:.1f} s charged".format(self.threads, len(res.sequences), wall, acc["prefill"], rounds,
+                                               tokens, requested, charged),
+            "sample_seconds": round(wall, 3),
+        }
+
+
 # --------------------------------------------------------------- GPU arm
 def run_gpu(args, rank: int, world: int, device):
     import torch
@@ -750,8 +876,9 @@ LAYOUT_FLAG = {"auto": 0, "keys": 1, "rows": 2, "direct": 3}
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: c4 20 slices of the request stream, c2/c3/c5 400)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed warm-up steps (default: c4 3, others 10)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--attn-kernel", choices=["auto", "mma", "tcgen05"], default="auto",
                     help="paged attention kernel: the library's automatic choice (default), the mma.sync "
@@ -762,11 +889,12 @@ def main(argv=None) -> int:
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="store each layer's new K/V rows inside the attention launch (default) or with a "
                          "separate append launch before it")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
-                    help="c2: decode attention + KV append (default); c3: verify step at gamma=5; "
-                         "c4: continuous-batching spec scheduler end to end; "
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c4",
+                    help="c4: continuous-batching spec scheduler end to end (default, the spec-decode "
+                         "tokens/s headline); c2: decode attention + KV append; c3: verify step at gamma=5; "
                          "c5: the attention of one long-context round at gamma=6 (draft decodes + target verify)")
-    ap.add_argument("--requests", type=int, default=64, help="c4: requests per GPU (the config's 2048 take minutes)")
+    ap.add_argument("--requests", type=int, default=2048,
+                    help="c4: requests in the whole job's arrival stream (the config's 2048)")
     ap.add_argument("--eager", action="store_true", help="c4: run the model forwards eagerly instead of CUDA graphs")
     ap.add_argument("--layers", type=int, default=None,
                     help="fewer layers only for profiling captures (default: the workload's model depth)")
@@ -775,6 +903,10 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
+    if args.steps is None:
+        args.steps = 20 if args.workload == "c4" else 400
+    if args.warmup is None:
+        args.warmup = 3 if args.workload == "c4" else 10
     if args.warmup < 3:
         args.warmup = 3
     if args.batch is None:
@@ -813,9 +945,11 @@ def main(argv=None) -> int:
                 vals.append(r["value"])
         value = float(np.mean(vals))
         line = {"metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * args.batch / value, 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": cfg, "impl": "reference",
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * per, 3),
+                "step_meaning": "one bounded host sample of the workload ({:.2f} s; see cpu_baseline.sample); "
+                                "a whole C2 step would take {:.0f} ms on the host".format(per, 1000.0 * args.batch / value),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (numpy port)",
+                "data": "synthetic", "config": cfg, "impl": "reference",
                 "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                                  "sample": r["sample"]},
                 "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -917,9 +1051,10 @@ def main_c3(args) -> int:
                 vals.append(r["value"])
         value = float(np.mean(vals))
         line = {"metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": cfg, "impl": "reference",
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * per, 3),
+                "step_meaning": "one bounded host sample of the workload ({:.2f} s; see cpu_baseline.sample)".format(per),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (attention f64)",
+                "data": "synthetic", "config": cfg, "impl": "reference",
                 "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                                  "sample": r["sample"]},
                 "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -1267,41 +1402,143 @@ def main_c5(args) -> int:
     return 0
 
 
+def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps):
+    """One attention op as a model forward launches it -- the K/V rows of
+    ``chunk`` new positions stored inside the paged attention launch -- over
+    contexts ``ctx`` (a random-permutation pool of exactly those pages), timed
+    with CUDA events over ``reps`` replays of a graph of ``layers`` launches.
+    Returns the kernel name, ms per launch and algorithmic bytes per launch."""
+    import torch
+
+    from engine.attention import AttnBatch, attention_kernel, attention_launches, paged_attention
+    from engine.kv import PagedKVCache
+
+    bs = 16
+    B = len(ctx)
+    cap = sum(-(-(x + chunk) // bs) for x in ctx) + B
+    width = max(-(-(x + chunk) // bs) for x in ctx) + 1
+    kv = PagedKVCache(layers, Hkv, d, cap, bs, device, torch.bfloat16, max_blocks_per_seq=width, max_seqs=B)
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    kv.allocator._free_stack.copy_(torch.randperm(cap, generator=g).to(torch.int32))
+    sids = list(range(B))
+    for sid in sids:
+        kv.add_sequence(sid)
+    kv.reserve(sids, [0] * B, ctx)
+    gd = torch.Generator(device=device)
+    gd.manual_seed(seed)
+    kv._k.normal_(generator=gd)
+    kv._v.normal_(generator=gd)
+    bf = torch.bfloat16
+    q = torch.randn((layers, B, chunk, Hq, d), generator=gd, device=device).to(bf)
+    kn = torch.randn((layers, B * chunk, Hkv, d), generator=gd, device=device).to(bf)
+    vn = torch.randn((layers, B * chunk, Hkv, d), generator=gd, device=device).to(bf)
+    out = torch.empty_like(q)
+    batch = AttnBatch.from_lists(device, sids, ctx, chunk)
+    kv.reserve(sids, ctx, [chunk] * B)
+
+    def run():
+        for layer in range(layers):
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], k_new=kn[layer], v_new=vn[layer])
+
+    run()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    stream = torch.cuda.current_stream(device)
+    graph.replay()
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    kv.check_errors()
+    ms = e0.elapsed_time(e1) / (reps * layers)
+    nbytes = (sum((x + chunk) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * chunk * Hq * d * 2
+              + sum(-(-(x + chunk) // bs) * 4 for x in ctx) + 2 * (B * chunk * 2 * Hkv * d * 2))
+    kern = attention_kernel(q[0], kv, batch)
+    launches = attention_launches(q[0], kv, batch, k_new=kn[0], v_new=vn[0])
+    del graph
+    return {"kernel": kern, "ms": ms, "bytes": nbytes, "launches_per_op": launches, "batch": B,
+            "mean_ctx": round(sum(ctx) / max(1, B), 1)}
+
+
 def main_c4(args) -> int:
-    """C4: the continuous-batching speculative scheduler end to end on random-
-    init Qwen2.5-1.5B (target) / 0.5B (draft) shaped bf16 models, gamma=4,
-    temperature 1.0, KV pools sized to 80 % of the free HBM.  The reference's
-    own metric: generated tokens / makespan (engine/scheduler.py:81-84)."""
+    """C4: the continuous-batching speculative
+    scheduler end to end on random-init Qwen2.5-1.5B (target) / 0.5B (draft)
+    shaped bf16 models, gamma=4, temperature 1.0, KV pools sized to 80 % of
+    the free HBM.  The metric is the reference's own: generated tokens /
+    makespan (engine/scheduler.py:81-84), summed over ranks / slowest rank.
+
+    One global stream of ``--requests`` (2048) requests with Poisson arrivals
+    at 64 requests/s per GPU is sharded round-robin over the ranks
+    (``engine.distributed.shard_requests``) and served by one continuous run
+    per rank: a request is admitted at the first round boundary after its
+    wall-clock arrival, and the run ends when the last request finishes.  A
+    *step* is one of ``--steps`` equal slices of that stream (the timed
+    region serves all of them back to back, without draining in between, as
+    a server would), so ms_per_step = makespan / steps.  Before timing: every
+    CUDA graph is captured up front (``capture_graphs``, independent of the
+    requests) and ``--warmup`` slices' worth of a different request stream
+    is served."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     from engine import workloads
 
     c = workloads.C4
-    # The scheduler's clock is the round: the config's 64 requests/s per GPU
-    # is mapped to one arrival per round on average (a round of this engine
-    # at these shapes takes ~10-20 ms, so the batch fills within tens of
-    # rounds as it would at 64 requests/s).
-    gap = 1.0
+    total = args.requests
+    K, W = args.steps, args.warmup
+    rate = c["arrival_rate"] * world
     cfg = {"workload": "C4: continuous-batching speculative scheduler, gamma=4, T=1.0 (Qwen2.5-1.5B target / "
                        "0.5B draft shapes, random-init bf16 weights)",
-           "requests_per_gpu": args.requests, "global_requests": args.requests * world,
+           "global_requests": total,
+           "requests_per_step": "{}/{} (a step is a slice of the one arrival stream; the stream is served by one "
+                                "continuous run per rank, sharded round-robin)".format(total, K),
            "prompts": "floor(lognormal(6, 0.8)) capped at 4096, ids U[0, 151936)",
-           "outputs": "U[64, 512] new tokens", "arrivals": "Poisson, mean gap {} round(s)".format(gap),
+           "outputs": "U[64, 512] new tokens",
+           "arrivals": "Poisson, 64 requests/s per GPU ({:g}/s for the whole job), wall clock: a request is "
+                       "admitted at the first round boundary after its arrival".format(rate),
            "kv_pool": "80% of free HBM after weights, block_size 16, target and draft pools",
-           "forwards": "eager" if args.eager else "CUDA-graph replays (batch buckets)",
-           "parallelism": "dp{} (request-sharded, independent engines)".format(world)}
+           "forwards": "eager" if args.eager else "CUDA-graph replays (batch x key-span buckets, all captured "
+                                                  "before the warm-up)",
+           "warmup": "{} requests of a different stream (seed {})".format(max(1, (total * W) // K), args.seed + 1000003),
+           "l2": "no flush needed: weights (4.1 GB) and the KV pages of a round are far larger than L2",
+           "parallelism": "dp{} (request-sharded, independent engines and KV pools)".format(world)}
     if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "metric": METRIC, "config": cfg,
-                              "unavailable": "C4 is not timed on the CPU port (a 1.5B-shaped model step takes "
-                                             "seconds on the host cores); the C2 and C3 lines carry the CPU "
-                                             "baseline"}))
+        if rank != 0:
+            return 0
+        threads = os.cpu_count() or 1
+        per = max(2.0, min(args.cpu_seconds, 150.0 / max(1, K + W)))
+        base = CpuC4(seed=args.seed, threads=threads)
+        vals, samples = [], []
+        for i in range(W + K):
+            r = base.measure(per)
+            if i >= W:
+                vals.append(r["value"])
+                samples.append(r["sample_seconds"])
+        value = float(np.mean(vals))
+        line = {"metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "n_gpus": world,
+                "steps": K, "warmup": W, "ms_per_step": round(1000.0 * float(np.mean(samples)), 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32 (attention f64)", "data": "synthetic", "config": cfg, "impl": "reference",
+                "step_meaning": "one bounded host sample of the C4 scheduler (see cpu_baseline.sample); "
+                                "ms_per_step is the host time a sample took",
+                "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return 0
 
     import torch
 
+    from engine import _lib
     from engine.config import EngineConfig, WorkloadRequest
+    from engine.distributed import gather_results, init_from_env, shard_requests
     from engine.qwen import build_random_model
     from engine.scheduler import build_kv
     from engine.spec_scheduler import SpeculativePagedScheduler
@@ -1311,100 +1548,191 @@ def main_c4(args) -> int:
         raise SystemExit("bench.py needs a CUDA device (the B200 path has no CPU fallback)")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    init_from_env("nccl" if world > 1 else None, timeout_s=600.0)
     dist = None
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
-
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     bf = torch.bfloat16
     tcfg = workloads.shape_config(c["target"], max_position_embeddings=8192)
     dcfg = workloads.shape_config(c["draft"], max_position_embeddings=8192)
-    target = build_random_model(tcfg, device, bf, seed=1 + 2 * rank)
-    draft = build_random_model(dcfg, device, bf, seed=2 + 2 * rank)
+    target = build_random_model(tcfg, device, bf, seed=1)
+    draft = build_random_model(dcfg, device, bf, seed=2)
+
+    def stream_of(seed, n):
+        """This rank's share of an ``n``-request arrival stream (global arrival times)."""
+        return shard_requests(workloads.c4_requests_wall(seed, n, rate, c["vocab"]), rank, world, "round_robin")
+
+    timed = stream_of(args.seed, total)
+    warm = stream_of(args.seed + 1000003, max(1, (total * W) // K))
+    per_run = max(len(timed), len(warm))
     free, _ = torch.cuda.mem_get_info(device)
     per_block = 16 * 2 * 2 * (target.num_layers * target.num_kv_heads * target.head_dim +
                               draft.num_layers * draft.num_kv_heads * draft.head_dim)
     blocks = int(c["pool_fraction"] * free / per_block)
-    ecfg = EngineConfig(block_size=16, max_num_blocks=blocks, max_batch=args.requests)
-    # table rows for every sequence id the warm-up and the timed run create
-    rows = 2 * args.requests + 16
-    kv = build_kv(target, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=rows)
-    dkv = build_kv(draft, ecfg, device, max_blocks_per_seq=(4096 + 512 + 16) // 16 + 2, max_seqs=rows)
+    ecfg = EngineConfig(block_size=16, max_num_blocks=blocks, max_batch=per_run)
+    width = (c["prompt_cap"] + c["out_hi"] + 16) // 16 + 2
+    kv = build_kv(target, ecfg, device, max_blocks_per_seq=width, max_seqs=per_run + 2)
+    dkv = build_kv(draft, ecfg, device, max_blocks_per_seq=width, max_seqs=per_run + 2)
     if not args.eager:
         target.enable_cuda_graphs()
         draft.enable_cuda_graphs()
     sched = SpeculativePagedScheduler(target, kv, draft, dkv, ecfg, SpecSampling(temperature=c["temperature"]),
                                       c["gamma"])
+    t_cap = time.perf_counter()
+    n_graphs = sched.capture_graphs()
+    cap_s = time.perf_counter() - t_cap
+    first_sid = sched._next_sid  # rows from here on serve requests; every slice reuses them
 
-    def reqs(n, seed, cap_new=None):
+    rounds = {"n": 0, "rows": 0, "max": None}
+
+    def hook(sids, starts, d0):
+        rounds["n"] += 1
+        rounds["rows"] += len(sids)
+        best = rounds["max"]
+        if best is None or len(sids) * (1 + sum(starts) / len(sids)) > best[0]:
+            rounds["max"] = (len(sids) * (1 + sum(starts) / len(sids)), list(starts), list(d0))
+
+    def requests_of(part, staged):
         out = []
-        for ids, new, t in workloads.c4_requests(seed, n, gap, c["vocab"]):
-            out.append(WorkloadRequest(prompt=ids, max_new_tokens=min(new, cap_new) if cap_new else new,
-                                       arrive_time=t))
+        for ids, new, t in part:
+            prompt = torch.tensor(ids, dtype=torch.long).to(device) if staged else ids
+            out.append(WorkloadRequest(prompt=prompt, max_new_tokens=new, arrive_time=t))
         return out
 
-    # warm-up: the same requests at their full lengths under another sampling
-    # seed -- every path (prefill, draft steps, verify, sampler, commit) and,
-    # with graphs, the captures of the batch buckets and key spans a run of
-    # this shape goes through, as a server captures its graphs at start-up
-    warm = sched.run_spec_continuous(reqs(args.requests, args.seed * 7919 + rank), seed=1, measure=False)
+    def serve(reqs, seed):
+        """One continuous run over ``reqs`` (wall-clock arrivals); returns generated tokens."""
+        assert kv.num_allocated_blocks == 0 and dkv.num_allocated_blocks == 0
+        sched._next_sid = first_sid
+        return sched.run_spec_continuous(reqs, seed=seed, measure=False, arrival_clock="wall").generated_tokens
+
+    serve(requests_of(warm, False), 7000)
+    torch.cuda.synchronize(device)
+    kv.check_errors()
+    dkv.check_errors()
+
+    # timed: prompts staged in HBM before the region (the "inputs resident" figure)
+    staged = requests_of(timed, True)
     torch.cuda.synchronize(device)
     if dist:
         dist.barrier()
     clocks = ClockSampler(device.index if device.index is not None else 0) if rank == 0 else None
     if clocks:
         clocks.start()
-    res = sched.run_spec_continuous(reqs(args.requests, args.seed * 7919 + rank), seed=args.seed + rank,
-                                    measure=True)
+    stream = torch.cuda.current_stream(device)
+    calls0 = _lib.calls()
+    sched.round_hook = hook
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    tokens = serve(staged, 100)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    sched.round_hook = None
+    calls = _lib.calls() - calls0
     clk = clocks.stop() if clocks else None
     kv.check_errors()
     dkv.check_errors()
-    tokens, ms = res.generated_tokens, res.makespan_ms
-    prompt_bytes = sum(len(r.prompt) * 8 for r in reqs(args.requests, args.seed * 7919 + rank))
+    n_rounds, n_rows = rounds["n"], rounds["rows"]
+
+    # e2e: the same public call with host prompt lists (copied up at admission)
+    # over the same stream; token lists come back every round
+    host = requests_of(timed, False)
+    h2d = sum(len(r.prompt) * 8 for r in host)
+    rounds_e = {"n": 0, "rows": 0}
+    torch.cuda.synchronize(device)
     if dist:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        n = torch.tensor([tokens], device=device, dtype=torch.float64)
-        dist.all_reduce(n)
-        ms, tokens = float(t.item()), int(n.item())
+        dist.barrier()
+    t0 = time.perf_counter()
+    sched.round_hook = lambda s, a, b: (rounds_e.__setitem__("n", rounds_e["n"] + 1),
+                                        rounds_e.__setitem__("rows", rounds_e["rows"] + len(s)))
+    e2e_tokens = serve(host, 100)
+    torch.cuda.synchronize(device)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0
+    sched.round_hook = None
+    chunk = c["gamma"] + 1
+    d2h = (rounds_e["rows"] * (chunk + 3) + 2 * rounds_e["n"]) * 4
+
+    # kernel rooflines on the heaviest round's shapes (after freeing the pools)
+    _, starts_max, d0_max = rounds["max"]
+    del sched, kv, dkv
+    torch.cuda.synchronize(device)
+    torch.cuda.empty_cache()
+    reps = 5
+    draft_op = _time_attention_op(device, d0_max, 1, dcfg.num_attention_heads, dcfg.num_key_value_heads,
+                                  dcfg.head_dim, dcfg.num_hidden_layers, args.seed + 5, reps)
+    verify_op = _time_attention_op(device, starts_max, chunk, tcfg.num_attention_heads, tcfg.num_key_value_heads,
+                                   tcfg.head_dim, tcfg.num_hidden_layers, args.seed + 6, reps)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuC4(seed=args.seed).measure(args.cpu_seconds)
+    payload = {"tokens": tokens, "ms": ms, "e2e_tokens": e2e_tokens, "e2e_ms": e2e_ms, "rounds": n_rounds,
+               "rows": n_rows, "calls": calls, "draft_ms": draft_op["ms"], "verify_ms": verify_op["ms"]}
+    allp = gather_results(payload)
+    if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    value = tokens / (ms * 1e-3)
+    ms_max = max(p["ms"] for p in allp)
+    tok_sum = sum(p["tokens"] for p in allp)
+    e2e_max = max(p["e2e_ms"] for p in allp)
+    e2e_sum = sum(p["e2e_tokens"] for p in allp)
+    value = tok_sum / (ms_max * 1e-3)
+    hbm, peak_kind = _peaks()
+    d_ms = max(p["draft_ms"] for p in allp)
+    v_ms = max(p["verify_ms"] for p in allp)
+    d_gbs = draft_op["bytes"] / (d_ms * 1e-3) / 1e9
+    v_gbs = verify_op["bytes"] / (v_ms * 1e-3) / 1e9
+    names = ATTN_KERNELS
     line = {
         "metric": METRIC,
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": res.steps,
-        "warmup": warm.steps,  # rounds of the warm-up run
-        "ms_per_step": round(ms / max(1, res.steps), 4),
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms_max / K, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded prompts and lengths, random-init weights)",
+        "data": "synthetic (seeded prompts, lengths and arrivals; random-init weights)",
         "config": cfg,
-        "generated_tokens": tokens,
-        "makespan_ms": round(ms, 2),
-        "mean_tokens_per_round": round(res.mean_tokens_per_round or 0.0, 4),
-        "mean_acceptance": round(res.mean_acceptance or 0.0, 4),
-        "kv_peak_blocks": res.kv_peak_blocks,
-        "pool_blocks": blocks,
-        "roofline": None,
-        "roofline_note": "end-to-end scheduler run (GEMMs, attention, sampler, host orchestration); the kernel "
-                         "rooflines are on the c2, c3 and c5 lines",
-        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": round(prompt_bytes / max(1, res.steps)),
-                "d2h_bytes_per_step": round(tokens * 8 / max(1, res.steps)),
-                "path": "the value itself: SpeculativePagedScheduler.run_spec_continuous with host prompts in and "
-                        "host token lists out"},
-        "gpu_launches": None,
+        "step_meaning": "one of {} equal slices of the arrival stream (served by one continuous run)".format(K),
+        "generated_tokens": tok_sum,
+        "makespan_ms": round(ms_max, 2),
+        "per_rank": [{"tokens": p["tokens"], "ms": round(p["ms"], 1), "rounds": p["rounds"],
+                      "mean_batch": round(p["rows"] / max(1, p["rounds"]), 2)} for p in allp],
+        "graphs_captured": n_graphs,
+        "graph_capture_s": round(cap_s, 2),
+        "roofline": {"bound": "hbm", "achieved": round(d_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(d_gbs / hbm, 4), "traffic": None,
+                     "kernel": names[draft_op["kernel"]] + ": draft decode attention (0.5B shape, 24 layers), "
+                               "K/V append fused, on the heaviest round's draft contexts",
+                     "batch": draft_op["batch"], "mean_ctx": draft_op["mean_ctx"],
+                     "algorithmic_bytes_per_launch": draft_op["bytes"], "ms_per_launch": round(d_ms, 5),
+                     "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
+        "verify_roofline": {"bound": "hbm", "achieved": round(v_gbs, 1), "peak": hbm, "unit": "GB/s",
+                            "frac": round(v_gbs / hbm, 4),
+                            "kernel": names[verify_op["kernel"]] + ": 5-row verify attention (1.5B shape, 28 "
+                                      "layers), K/V append fused, on the heaviest round's target contexts",
+                            "batch": verify_op["batch"], "mean_ctx": verify_op["mean_ctx"],
+                            "algorithmic_bytes_per_launch": verify_op["bytes"], "ms_per_launch": round(v_ms, 5)},
+        "e2e": {"value": round(e2e_sum / (e2e_max * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": round(h2d / K), "d2h_bytes_per_step": round(d2h / K),
+                "path": "SpeculativePagedScheduler.run_spec_continuous over the same stream with host prompt "
+                        "lists (copied up at admission) and host token lists out (one packed read per round), "
+                        "host wall clock"},
+        "gpu_launches": calls,
+        "gpu_launches_note": "library entry calls in the timed region (graph replays counted with the calls "
+                             "they captured); each launches one or two of this library's kernels",
         "clocks": clk,
     }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return 0
 

@@ -12,7 +12,7 @@
  * host reads that word at its per-round sync and raises.
  *
  * The host-side drop-in (Python package engine/, specdec/) binds these
- * symbols with ctypes; see INTEGRATION.md for the binding.
+ * symbols with ctypes (engine/_lib.py).
  *
  * Reference interfaces each entry point replaces are cited as
  * <file>:<line> inside sup-zzj/speculative-decoding-lab.
@@ -266,8 +266,10 @@ int sdl_paged_attention(const sdl_attn_args* args, void* stream);
  * in: a runtime whose pool allocator owns all HBM, or an FFI host that only
  * owns its input/output buffers.  args->workspace is ignored; split-K
  * partials go to a static 8 MiB device array (sdl_noalloc_scratch_bytes())
- * that every GPU loading the library keeps until exit.  Calls whose plan
- * needs more scratch return SDL_ERR_WORKSPACE without launching.  The first
+ * that every GPU loading the library keeps until exit.  The automatic split
+ * size grows until the partials fit the array; calls whose plan still needs
+ * more (an explicit pages_per_split, the tcgen05 kernel) return
+ * SDL_ERR_WORKSPACE without launching.  The first
  * call on a device looks up the array's address (cudaGetSymbolAddress), so
  * make that first call before any stream capture.  All calls share the one
  * array: calls that overlap on the GPU (other streams, other threads) race. */
@@ -346,7 +348,11 @@ size_t sdl_spec_sample_scratch_bytes(int32_t B);
  * p_i from the same logits; sdl_logits_to_probs (temperature mode) writes
  * exactly those values.  Draws use the integer rule of sdl_sample_rows.
  * Workspaces must be 256-byte aligned and at least
- * sdl_sampler_workspace_bytes(rows, vocab) bytes, rows = logit rows read. */
+ * sdl_sampler_workspace_bytes(rows, vocab) bytes, rows = logit rows read;
+ * their first 64 KB are a control block of the one-launch speculative
+ * sampler that must be zero before a workspace's first use (the library
+ * keeps it consistent afterwards; after a call that set an error bit, zero
+ * it again). */
 size_t sdl_sampler_workspace_bytes(int32_t rows, int32_t vocab);
 
 /* sample_token (specdec/sampler.py:59-69) applied to logits_to_probs
@@ -361,11 +367,16 @@ int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t row_stride
                            size_t workspace_bytes, int32_t* err, void* stream);
 
 /* batch_accept (engine/spec_scheduler.py:46-88) from target logits
- * [B][gamma+1][V] and draft logits [B][gamma][V] (same dtype) in four
- * launches (row statistics, accept walk, per-chunk draw sums, draw) without
+ * [B][gamma+1][V] and draft logits [B][gamma][V] (same dtype) without
  * materialising probability rows: equal to sdl_logits_to_probs on both
  * blocks followed by sdl_spec_sample (sampling mode), including the uniform
- * consumption and *u_base update. */
+ * consumption and *u_base update.  Five launches by default (statistics,
+ * merge, accept walk, per-slice draw sums, draw); with
+ * sdl_set_spec_sampler_mode(1), one launch (a thread-block cluster per
+ * sequence: row statistics, the fp64 accept tests in the reference's
+ * uniform order, the (p-q)+ residual or bonus draw) wherever the batch's
+ * clusters can all be resident at once and vocab <= 1048576.  Both give
+ * the same bits. */
 int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj,
                            const void* q_logits, int64_t q_sb, int64_t q_sj,
                            int32_t dtype, float temperature, float eps,
@@ -374,6 +385,11 @@ int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj,
                            int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
                            int32_t* tokens, int32_t* n_out, void* workspace,
                            size_t workspace_bytes, int32_t* err, void* stream);
+
+/* 0 (default): sdl_spec_sample_logits runs its five-launch chain; 1: its
+ * one-launch kernel wherever that applies.  Process-wide.  No counterpart in
+ * the reference. */
+int sdl_set_spec_sampler_mode(int32_t mode);
 
 /* Copy the device error word to *out (stream-ordered D2H; *out is valid
  * after the stream synchronises) and optionally clear it. */

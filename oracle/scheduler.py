@@ -105,8 +105,11 @@ def run_continuous(model: NumpyPagedLM, kv: PagedKVCache, requests: Sequence[Req
 def run_spec_continuous(target: NumpyPagedLM, kv: PagedKVCache, draft: NumpyPagedLM, draft_kv: PagedKVCache,
                         requests: Sequence[Req], gamma: int, temperature: float,
                         stream: Optional[UniformStream] = None, eos: Optional[int] = None,
-                        top_k: int = 0, top_p: float = 1.0, round_hook=None) -> RunResult:
-    res = RunResult()
+                        top_k: int = 0, top_p: float = 1.0, round_hook=None,
+                        result: Optional[RunResult] = None) -> RunResult:
+    """``result`` (optional) is filled in place, so a caller whose
+    ``round_hook`` stops the run early by raising still sees the rounds done."""
+    res = result if result is not None else RunResult()
     arrivals = sorted(requests, key=lambda r: r.arrive_time)
     step = 0
     next_sid = 0

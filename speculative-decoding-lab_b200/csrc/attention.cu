@@ -2955,10 +2955,15 @@ extern "C" size_t sdl_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes;
 extern "C" int sdl_paged_attention_noalloc(const sdl_attn_args* args, void* stream) {
     int rc = validate(args);
     if (rc != SDL_OK) return rc;
+    // The plan is made against the static array, so an automatic split
+    // size grows until the partials fit it; only a plan that cannot shrink
+    // (an explicit pages_per_split, the tcgen05 kernel) can still need more.
+    float* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch)) != SDL_OK) return rc;
     sdl_attn_args a = *args;
-    a.workspace = nullptr;
-    a.workspace_bytes = 0;
-    const size_t need = sdl_attention_workspace_bytes(&a);
+    a.workspace = scratch;
+    a.workspace_bytes = kNoAllocScratchBytes;
+    const size_t need = make_plan(&a).ws_bytes;
     if (need > kNoAllocScratchBytes) {
         char msg[256];
         snprintf(msg, sizeof(msg),
@@ -2966,12 +2971,6 @@ extern "C" int sdl_paged_attention_noalloc(const sdl_attn_args* args, void* stre
                  "%zu-byte static scratch; pass a workspace to sdl_paged_attention instead",
                  need, kNoAllocScratchBytes);
         return sdl::fail(SDL_ERR_WORKSPACE, msg);
-    }
-    if (need > 0) {
-        float* scratch = nullptr;
-        if ((rc = noalloc_scratch(&scratch)) != SDL_OK) return rc;
-        a.workspace = scratch;
-        a.workspace_bytes = kNoAllocScratchBytes;
     }
     return sdl_paged_attention(&a, stream);
 }

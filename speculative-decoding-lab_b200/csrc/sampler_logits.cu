@@ -27,6 +27,9 @@
 // 2^62), exact u64 sums), so splitting a row across CTAs cannot change them.
 #include "sdl_common.cuh"
 
+#include <map>
+#include <mutex>
+
 namespace {
 
 constexpr int kChunk = 8192;   // elements per statistics chunk
@@ -537,6 +540,330 @@ __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> 
     }
 }
 
+// -------------------------------------------- fused rejection sampling
+// spec_fused_kernel: the whole speculative sampling step of a round in one
+// launch -- softmax statistics of every p and q row, the fp64 accept tests
+// with the reference's uniform consumption, and the residual / bonus draw --
+// with the same operations as the stats -> merge -> accept -> wsum -> finish
+// chain above, so tokens, accept lengths and the stream counter are
+// bit-identical to it.
+//
+// One thread-block cluster of up to kFuseCluster CTAs (two 256-thread
+// groups each, working on separate chunks) per sequence b:
+//  1. the cluster's CTAs take the (row, 8192-chunk) statistics of the
+//     sequence's 2*gamma+1 logit rows (chunk_stats) into the workspace;
+//  2. after a cluster barrier, CTA 0 merges each row (merge_kernel's order),
+//     computes min(1, p/q) for its gamma proposals (accept_logits_kernel's
+//     arithmetic), publishes them and a flag, then waits -- bounded -- for
+//     the flags of sequences 0..b-1 and walks their accept tests in order
+//     to find where this sequence's uniforms start in the stream (the
+//     reference draws them sequence after sequence); the last sequence also
+//     advances the stream counter;
+//  3. the cluster's CTAs sum the integer weights W of the drawn
+//     distribution -- (p_r - q_r)+ after a rejection at r, else p_gamma --
+//     per 2048-element slice; CTA 0 finds the slice and the token
+//     (finish_kernel's rule).
+// The only wait on another cluster is step 2's, and only on lower sequence
+// numbers; the host launches this kernel only when every cluster of the
+// grid can be resident at once, so that wait always ends (it is bounded
+// all the same).  Flags carry a launch epoch kept in the workspace's
+// control block with a done counter; the last cluster to finish advances
+// the epoch, so the flags never need clearing.
+constexpr int kFuseCluster = 8;
+constexpr size_t kCtrlBytes = 64 * 1024;              // control block at the start of the sampler workspace
+constexpr int kCtrlWords = 16;                        // [0] epoch, [1] done counter
+constexpr int kMaxFusedSeqs = (int)(kCtrlBytes / 4) - kCtrlWords;
+constexpr uint32_t kFlagWaitLimit = 1u << 22;          // polls, 64 ns apart
+constexpr int kMaxFusedRows = 65;                       // 2 * gamma + 1 for gamma <= 32
+constexpr int kFuseGroups = 2;                          // 256-thread groups per CTA (chunk tasks in flight)
+constexpr int kFuseThreads = kFuseGroups * kGroup;
+constexpr int kFuseMaxDrawChunks = kFuseThreads;        // draw slices CTA 0 scans with one value per thread
+
+struct FusedWs {
+    float2* stats;    // [B][R][nchunks]
+    float2* rowstat;  // [B][R] (m, 1/s)
+    double* acc;      // [B][gamma]
+    uint64_t* wsum;   // [B][ndc]
+    uint64_t* wsum_p; // [B][ndc] (residual fallback)
+    int* ctrl;        // [0] epoch, [1] done, then flags[B] from kCtrlWords
+};
+
+SDL_DEV int ld_acquire_i32(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+SDL_DEV void st_release_i32(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+SDL_DEV int ld_cluster_i32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFuseThreads, 2) spec_fused_kernel(Rows<T> A, Rows<T> Q, int V, float temp,
+                                                            const int* __restrict__ prop, int B, int gamma,
+                                                            const float* __restrict__ uniforms, int64_t nu,
+                                                            int64_t* u_base, int64_t u_skip, int* tokens, int* n_out,
+                                                            FusedWs w, int nchunks, int ndc, int* err) {
+    extern __shared__ double s_walk[];  // CTA 0: acceptance of sequences 0..b, then their uniforms
+    __shared__ float red[kFuseGroups][8];
+    __shared__ uint64_t s_wg[kFuseGroups][8];
+    __shared__ float2 s_rs[kMaxFusedRows];
+    __shared__ uint64_t s_w[32];
+    __shared__ int s_tok, s_chunk, s_r, s_ok, s_epoch;
+    __shared__ float s_u;
+    __shared__ uint64_t s_target;
+    __shared__ int64_t s_base;
+    pdl_wait();
+    const int cs = gridDim.x;  // CTAs per sequence (the cluster)
+    const int rank = (int)cluster_ctarank();
+    const int b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = tid / kGroup, g = tid % kGroup;  // the CTA's 256-thread groups work on separate chunks
+    const int R = 2 * gamma + 1;
+    int* flags = w.ctrl + kCtrlWords;
+    if (rank == 0 && tid == 0) {
+        // read before any cluster of this launch can change them: the epoch
+        // moves and the counter is written only after every cluster is done
+        s_epoch = ld_acquire_i32(w.ctrl);
+        s_base = (u_base ? *u_base : 0) + u_skip;
+    }
+
+    // 1. chunk statistics of the sequence's rows: p rows 0..gamma, then q rows
+    for (int t = rank * kFuseGroups + grp; t < R * nchunks; t += cs * kFuseGroups) {
+        const int row = t / nchunks, c = t % nchunks;
+        const T* x = row <= gamma ? A.row(b * (gamma + 1) + row) : Q.row(b * gamma + row - gamma - 1);
+        const float2 st = chunk_stats<T>(x, c * kChunk, min(V, (c + 1) * kChunk), temp, g, 1 + grp, red[grp]);
+        if (g == 0) w.stats[((int64_t)b * R + row) * nchunks + c] = st;
+    }
+    __threadfence();
+    cluster_sync_all();
+
+    if (rank == 0) {
+        // 2a. row statistics (m, 1/s): merge_kernel's operations, one warp per row
+        for (int row = warp; row < R; row += kFuseThreads / 32) {
+            const float2* st = w.stats + ((int64_t)b * R + row) * nchunks;
+            float m = -INFINITY;
+            for (int c = lane; c < nchunks; c += 32) m = fmaxf(m, __ldcg(st + c).x);
+            m = warp_max(m);
+            float s = 0.f;
+            if (m != -INFINITY) {
+                for (int c0 = 0; c0 < nchunks; c0 += 32) {
+                    const float2 v = c0 + lane < nchunks ? __ldcg(st + c0 + lane) : make_float2(-INFINITY, 0.f);
+                    const float f = v.x != -INFINITY ? expf(__fsub_rn(v.x, m)) : 0.f;
+                    const int n = min(32, nchunks - c0);
+                    for (int k = 0; k < n; ++k) {  // chunk order, as merge_kernel's thread 0
+                        const float vx = __shfl_sync(0xffffffffu, v.x, k);
+                        const float vy = __shfl_sync(0xffffffffu, v.y, k);
+                        const float fk = __shfl_sync(0xffffffffu, f, k);
+                        if (vx != -INFINITY) s = __fmaf_rn(vy, fk, s);
+                    }
+                }
+            }
+            if (lane == 0) {
+                const float2 rs = make_float2(m, __frcp_rn(s));
+                s_rs[row] = rs;
+                w.rowstat[(int64_t)b * R + row] = rs;
+            }
+        }
+        __syncthreads();
+        // 2b. min(1, p/q) of this sequence's proposals (accept_logits_kernel's arithmetic)
+        if (tid < gamma) {
+            const int x = prop[b * gamma + tid];
+            double acc;
+            if (x < 0 || x >= V) {  // a proposal outside the vocabulary is rejected
+                sdl_raise(err, SDL_DEVERR_BAD_INDEX);
+                acc = 0.0;
+            } else {
+                const float2 sp = s_rs[tid], sq = s_rs[gamma + 1 + tid];
+                const double pv = prob_of(scaled(to_f32<T>(A.row(b * (gamma + 1) + tid)[x]), temp), sp.x, sp.y);
+                const double qv = prob_of(scaled(to_f32<T>(Q.row(b * gamma + tid)[x]), temp), sq.x, sq.y);
+                if (qv <= 1e-12) acc = pv > 1e-12 ? 1.0 : 0.0;
+                else acc = fmin(1.0, pv / qv);
+            }
+            w.acc[(int64_t)b * gamma + tid] = acc;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            st_release_i32(flags + b, s_epoch + 1);
+        }
+        // 2c. where this sequence's uniforms start: the tests of sequences
+        // 0..b-1 (bounded wait for their flags), walked in order
+        int ok = 1;
+        for (int bp = tid; bp < b && ok; bp += kFuseThreads) {
+            uint32_t n = 0;
+            while (ld_acquire_i32(flags + bp) != s_epoch + 1) {
+                if (++n > kFlagWaitLimit) { ok = 0; break; }
+                __nanosleep(64);
+            }
+        }
+        ok = __syncthreads_and(ok);
+        double* a_s = s_walk;                                                      // [(b+1) * gamma]
+        float* u_s = reinterpret_cast<float*>(s_walk + (size_t)(b + 1) * gamma);  // [(b+1) * (gamma+1)]
+        const int64_t base = s_base;
+        if (ok) {
+            for (int i = tid; i < (b + 1) * gamma; i += kFuseThreads) a_s[i] = __ldcg(w.acc + i);
+            for (int i = tid; i < (b + 1) * (gamma + 1); i += kFuseThreads) {
+                const int64_t ui = base + i;
+                u_s[i] = (ui >= 0 && ui < nu) ? uniforms[ui] : __int_as_float(0x7fc00000);
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int off = 0, r = 0;
+            float uf = 0.5f;
+            bool bad_u = false;
+            if (ok) {
+                for (int bb = 0; bb <= b; ++bb) {
+                    bool reject = false;
+                    if (lane < gamma) {
+                        const float u = u_s[off + lane];
+                        if (u != u) bad_u = true;
+                        reject = !((double)u < a_s[bb * gamma + lane]);
+                    }
+                    const unsigned rj = __ballot_sync(0xffffffffu, reject);
+                    r = rj ? __ffs(rj) - 1 : gamma;
+                    const int consumed = r < gamma ? r + 2 : gamma + 1;
+                    uf = u_s[off + consumed - 1];
+                    if (uf != uf) bad_u = true;
+                    off += consumed;
+                }
+            }
+            bad_u = __any_sync(0xffffffffu, bad_u);
+            if (lane == 0) {
+                if (!ok) sdl_raise(err, SDL_DEVERR_TIMEOUT);
+                if (bad_u) sdl_raise(err, SDL_DEVERR_UNIFORMS);
+                s_r = ok ? r : 0;
+                s_u = uf;
+                s_ok = ok;
+                if (ok && b == B - 1 && u_base) *u_base = base + off;
+            }
+        }
+    }
+    cluster_sync_all();  // r and u (and the row statistics) for the whole cluster
+    int r;
+    float u;
+    if (rank == 0) {
+        r = s_r;
+        u = s_u;
+    } else {
+        r = ld_cluster_i32(mapa_shared(smem_u32(&s_r), 0));
+        u = ld_cluster_f32(mapa_shared(smem_u32(&s_u), 0));
+    }
+
+    // 3. the draw: integer weight sums of its distribution per 2048-element
+    // slice (wsum_kernel's operations), over the cluster's CTAs
+    const int prow = r;                                 // p row r of the sequence
+    const int qrow = r < gamma ? gamma + 1 + r : -1;    // q row r, or none after a full accept
+    const float2 sp = __ldcg(w.rowstat + (int64_t)b * R + prow);
+    const float2 sq = qrow >= 0 ? __ldcg(w.rowstat + (int64_t)b * R + qrow) : make_float2(0.f, 1.f);
+    const T* xp = A.row(b * (gamma + 1) + r);
+    const T* xq = qrow >= 0 ? Q.row(b * gamma + r) : nullptr;
+    for (int c = rank * kFuseGroups + grp; c < ndc; c += cs * kFuseGroups) {
+        const int lo = c * kDrawChunk, hi = min(V, lo + kDrawChunk);
+        float vp[kDrawPerThread], vq[kDrawPerThread];
+        const bool vecp = row_vec_ok<T>(xp);
+#pragma unroll
+        for (int k = 0; k < kDrawPerThread / 4; ++k) load4<T>(xp, lo + 4 * g + 1024 * k, hi, vecp, vp + 4 * k);
+        if (xq) {
+            const bool vecq = row_vec_ok<T>(xq);
+#pragma unroll
+            for (int k = 0; k < kDrawPerThread / 4; ++k) load4<T>(xq, lo + 4 * g + 1024 * k, hi, vecq, vq + 4 * k);
+        }
+        uint64_t wt = 0;
+        if (xq) {
+#pragma unroll
+            for (int e = 0; e < kDrawPerThread; ++e) {
+                const float p = prob_of(scaled(vp[e], temp), sp.x, sp.y);
+                const float q = prob_of(scaled(vq[e], temp), sq.x, sq.y);
+                wt += wfix(fmaxf(__fsub_rn(p, q), 0.f));
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < kDrawPerThread; ++e) wt += wfix(prob_of(scaled(vp[e], temp), sp.x, sp.y));
+        }
+        wt = warp_sum_u64(wt);
+        if (lane == 0) s_wg[grp][g >> 5] = wt;
+        group_sync(1 + grp);
+        if (g == 0) {
+            uint64_t a = 0;
+            for (int i = 0; i < kGroup / 32; ++i) a += s_wg[grp][i];
+            w.wsum[(int64_t)b * ndc + c] = a;
+        }
+        group_sync(1 + grp);
+    }
+    __threadfence();
+    cluster_sync_all();
+    if (rank != 0) return;
+
+    // CTA 0: the slice holding the target and the token in it (finish_kernel's rule)
+    const uint64_t* ws = w.wsum + (int64_t)b * ndc;
+    const int c = tid;
+    uint64_t wc = c < ndc ? __ldcg(ws + c) : 0ull;
+    uint64_t S;
+    uint64_t incl = block_incl_scan_u64(wc, s_w, &S);
+    bool usep = false;
+    if (qrow >= 0 && (double)S / kTwo62 <= 1e-12) {
+        // residual mass <= 1e-12 (rare): draw from p; its slice sums, one warp per slice
+        usep = true;
+        for (int sl = warp; sl < ndc; sl += kFuseThreads / 32) {
+            const int lo = sl * kDrawChunk, hi = min(V, lo + kDrawChunk);
+            uint64_t a = 0;
+            for (int i = lo + lane; i < hi; i += 32) a += wfix(prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y));
+            a = warp_sum_u64(a);
+            if (lane == 0) w.wsum_p[(int64_t)b * ndc + sl] = a;
+        }
+        __threadfence_block();
+        __syncthreads();
+        wc = c < ndc ? w.wsum_p[(int64_t)b * ndc + c] : 0ull;
+        incl = block_incl_scan_u64(wc, s_w, &S);
+    }
+    if (tid == 0) s_chunk = -1;
+    __syncthreads();
+    const uint64_t target = S != 0 ? __umul64hi(ufix(u), S) : 0ull;
+    if (S != 0 && wc != 0 && incl - wc <= target && target < incl) {
+        s_chunk = c;
+        s_target = target - (incl - wc);
+    }
+    __syncthreads();
+    const int chunk = s_chunk;
+    int tok = -1;
+    if (chunk >= 0) {
+        const int lo = chunk * kDrawChunk, hi = min(V, lo + kDrawChunk);
+        if (xq && !usep) {
+            tok = block_find(
+                [&](int i) {
+                    const float p = prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y);
+                    const float q = prob_of(scaled(to_f32<T>(xq[i]), temp), sq.x, sq.y);
+                    return fmaxf(__fsub_rn(p, q), 0.f);
+                },
+                lo, hi, s_target, s_w, &s_tok);
+        } else {
+            tok = block_find([&](int i) { return prob_of(scaled(to_f32<T>(xp[i]), temp), sp.x, sp.y); }, lo, hi,
+                             s_target, s_w, &s_tok);
+        }
+    }
+    if (tid == 0) {
+        if (tok < 0) { sdl_raise(err, SDL_DEVERR_BAD_SAMPLE); tok = 0; }
+        for (int j = 0; j < r; ++j) tokens[b * (gamma + 1) + j] = prop[b * gamma + j];
+        tokens[b * (gamma + 1) + r] = tok;
+        n_out[b] = r + 1;
+        // launch bookkeeping: the last cluster to get here moves the epoch on
+        __threadfence();
+        if (atomicAdd(w.ctrl + 1, 1) == B - 1) {
+            w.ctrl[1] = 0;
+            __threadfence();
+            st_release_i32(w.ctrl, s_epoch + 1);
+        }
+    }
+}
+
 // ------------------------------------------------------------ host side
 struct Ws {
     float2* stats;
@@ -550,10 +877,13 @@ struct Ws {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Every sampler workspace starts with the fused kernel's control block
+// (launch epoch, done counter, per-sequence flags), which must be zero before
+// a workspace's first use; no kernel of the chain touches it.
 Ws carve(void* base, int stat_rows, int draws, int nchunks, int ndc) {
     Ws w;
     char* p = static_cast<char*>(base);
-    size_t o = 0;
+    size_t o = kCtrlBytes;
     w.stats = reinterpret_cast<float2*>(p + o);
     o = align256(o + (size_t)stat_rows * nchunks * sizeof(float2));
     w.rowstat = reinterpret_cast<float2*>(p + o);
@@ -594,10 +924,121 @@ int sample_logits_t(const T* logits, int64_t row_stride, int rows, int V, float 
     return sdl::check_launch("sample_logits");
 }
 
+FusedWs carve_fused(void* base, int B, int gamma, int nchunks, int ndc, size_t* bytes) {
+    FusedWs w;
+    char* p = static_cast<char*>(base);
+    const int R = 2 * gamma + 1;
+    size_t o = 0;
+    w.ctrl = reinterpret_cast<int*>(p);
+    o = kCtrlBytes;
+    w.stats = reinterpret_cast<float2*>(p + o);
+    o = align256(o + (size_t)B * R * nchunks * sizeof(float2));
+    w.rowstat = reinterpret_cast<float2*>(p + o);
+    o = align256(o + (size_t)B * R * sizeof(float2));
+    w.acc = reinterpret_cast<double*>(p + o);
+    o = align256(o + (size_t)B * gamma * sizeof(double));
+    w.wsum = reinterpret_cast<uint64_t*>(p + o);
+    o = align256(o + (size_t)B * ndc * sizeof(uint64_t));
+    w.wsum_p = reinterpret_cast<uint64_t*>(p + o);
+    o = align256(o + (size_t)B * ndc * sizeof(uint64_t));
+    if (bytes) *bytes = o;
+    return w;
+}
+
+size_t fused_walk_smem(int B, int gamma) {
+    return (size_t)B * gamma * sizeof(double) + (size_t)B * (gamma + 1) * sizeof(float);
+}
+
+// 0 (default): the five-launch chain; 1: the one-launch kernel where it
+// applies.  Measured on B200 at C3 (32 sequences, gamma 5, vocab 151,936,
+// fp32 logits): 76 us for the one-launch kernel against 63 us for the
+// chain, whose statistics launch spreads 6,688 CTAs over every SM while
+// the clusters hold 1-2 CTAs per SM and serialise their phases.
+int g_sampler_mode = 0;
+
+// Clusters of `cs` CTAs of spec_fused_kernel<T> resident at once with
+// `smem` bytes of dynamic shared memory (0 when the query fails).
+template <typename T>
+int fused_active_clusters(int cs, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(cs, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs, 1, 1);
+    cfg.blockDim = dim3(kFuseThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, spec_fused_kernel<T>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    cache[key] = n;
+    return n;
+}
+
+// Launches the fused kernel when it applies (returns 1), else returns 0
+// and launches nothing; a negative value is an error status.
+template <typename T>
+int spec_fused_try(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t q_sb, int64_t q_sj, float temp,
+                   const int* prop, int B, int gamma, int V, const float* uniforms, int64_t nu, int64_t* u_base,
+                   int64_t u_skip, int* tokens, int* n_out, void* ws_base, size_t ws_bytes, int* err,
+                   cudaStream_t st) {
+    if (g_sampler_mode != 1) return 0;
+    const int nchunks = (V + kChunk - 1) / kChunk;
+    const int ndc = (V + kDrawChunk - 1) / kDrawChunk;
+    if (B > kMaxFusedSeqs || ndc > kFuseMaxDrawChunks || 2 * gamma + 1 > kMaxFusedRows) return 0;
+    size_t need = 0;
+    (void)carve_fused(nullptr, B, gamma, nchunks, ndc, &need);
+    if (need > ws_bytes) return 0;
+    const size_t smem = fused_walk_smem(B, gamma);
+    if (smem > 200 * 1024) return 0;
+    static std::mutex mu;
+    static size_t configured = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > 48 * 1024 && smem > configured) {
+            if (cudaFuncSetAttribute(spec_fused_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess) {
+                (void)cudaGetLastError();
+                return 0;
+            }
+            configured = smem;
+        }
+    }
+    // the largest cluster whose grid is resident at once (the look-back wait
+    // of step 2 needs every lower-numbered sequence running or done)
+    int cs = kFuseCluster;
+    while (cs >= 1 && fused_active_clusters<T>(cs, smem) < B) cs /= 2;
+    if (cs < 1) return 0;
+    FusedWs w = carve_fused(ws_base, B, gamma, nchunks, ndc, nullptr);
+    Rows<T> A{pl, p_sb, p_sj, gamma + 1, B * (gamma + 1)};
+    Rows<T> Q{ql, q_sb, q_sj, gamma, B * gamma};
+    cudaError_t e = sdl::launch_pdl_cluster(spec_fused_kernel<T>, dim3(cs, B), dim3(kFuseThreads), smem, st,
+                                            (unsigned)cs, A, Q, V, temp, prop, B, gamma, uniforms, nu, u_base, u_skip,
+                                            tokens, n_out, w, nchunks, ndc, err);
+    if (e != cudaSuccess) return -sdl::fail(SDL_ERR_CUDA, cudaGetErrorString(e));
+    const int rc = sdl::check_launch("spec_fused_kernel");
+    return rc == SDL_OK ? 1 : -rc;
+}
+
 template <typename T>
 int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t q_sb, int64_t q_sj, float temp,
                   const int* prop, int B, int gamma, int V, const float* uniforms, int64_t nu, int64_t* u_base,
-                  int64_t u_skip, int* tokens, int* n_out, void* ws_base, int* err, cudaStream_t st) {
+                  int64_t u_skip, int* tokens, int* n_out, void* ws_base, size_t ws_bytes, int* err,
+                  cudaStream_t st) {
+    const int fused = spec_fused_try<T>(pl, p_sb, p_sj, ql, q_sb, q_sj, temp, prop, B, gamma, V, uniforms, nu, u_base,
+                                        u_skip, tokens, n_out, ws_base, ws_bytes, err, st);
+    if (fused != 0) return fused > 0 ? SDL_OK : -fused;
     const int nchunks = (V + kChunk - 1) / kChunk;
     const int ndc = (V + kDrawChunk - 1) / kDrawChunk;
     const int prow = B * (gamma + 1), qrow = B * gamma;
@@ -715,14 +1156,21 @@ extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_
     if (dtype == SDL_F32)
         return spec_logits_t<float>((const float*)p_logits, p_sb, p_sj, (const float*)q_logits, q_sb, q_sj, t,
                                     proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens, n_out,
-                                    workspace, err, st);
+                                    workspace, workspace_bytes, err, st);
     if (dtype == SDL_BF16)
         return spec_logits_t<__nv_bfloat16>((const __nv_bfloat16*)p_logits, p_sb, p_sj,
                                             (const __nv_bfloat16*)q_logits, q_sb, q_sj, t, proposals, B, gamma, vocab,
-                                            uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace, err, st);
+                                            uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace,
+                                            workspace_bytes, err, st);
     if (dtype == SDL_F16)
         return spec_logits_t<__half>((const __half*)p_logits, p_sb, p_sj, (const __half*)q_logits, q_sb, q_sj, t,
                                      proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens,
-                                     n_out, workspace, err, st);
+                                     n_out, workspace, workspace_bytes, err, st);
     return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: dtype");
+}
+
+extern "C" int sdl_set_spec_sampler_mode(int32_t mode) {
+    if (mode != 0 && mode != 1) return sdl::fail(SDL_ERR_INVALID, "sdl_set_spec_sampler_mode: mode must be 0 or 1");
+    g_sampler_mode = mode;
+    return SDL_OK;
 }

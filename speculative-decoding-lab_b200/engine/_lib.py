@@ -68,6 +68,7 @@ EXPORTED_SYMBOLS = (
     "sdl_sampler_workspace_bytes",
     "sdl_sample_logits_rows",
     "sdl_spec_sample_logits",
+    "sdl_set_spec_sampler_mode",
     "sdl_get_error",
     "sdl_rmsnorm",
     "sdl_rope",
@@ -169,6 +170,7 @@ _SIGS = {
     "sdl_spec_sample_logits": (c_int, [c_void, c_i64, c_i64, c_void, c_i64, c_i64, c_int, c_float, c_float, c_void,
                                        c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void, c_void,
                                        c_size, c_void, c_void]),
+    "sdl_set_spec_sampler_mode": (c_int, [c_int]),
     "sdl_get_error": (c_int, [c_void, c_void, c_int, c_void]),
     "sdl_rmsnorm": (c_int, [c_void, c_i64, c_void, c_i64, c_void, c_i64, c_void, c_void, c_i64, c_int, c_int, c_float,
                             c_int, c_void]),
@@ -203,7 +205,23 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
+# Entry calls into the library made from this process (each launches one or
+# more of its kernels); CUDA-graph replays add the calls their capture made.
+_CALLS = [0]
+
+
+def calls() -> int:
+    """Library entry calls so far (``check`` counts every one)."""
+    return _CALLS[0]
+
+
+def count_calls(n: int) -> None:
+    """Add ``n`` calls replayed inside a CUDA graph."""
+    _CALLS[0] += int(n)
+
+
 def check(rc: int, what: str) -> None:
+    _CALLS[0] += 1
     if rc != 0:
         raise RuntimeError("{} failed (status {}): {}".format(what, rc, last_error()))
 
@@ -258,7 +276,9 @@ class Workspace:
     """Per-device growable fp32 scratch (split-K attention partials under the
     default tag, sampler statistics under ``"sampler"``).
 
-    A buffer that is outgrown is kept alive rather than freed: CUDA graphs
+    Buffers start zeroed: a sampler workspace begins with the fused
+    sampler's control block, which must be zero before its first use.  A
+    buffer that is outgrown is kept alive rather than freed: CUDA graphs
     captured earlier still hold its address.
     """
 
@@ -273,6 +293,6 @@ class Workspace:
         if buf is None or buf.numel() < need:
             if buf is not None:
                 cls._retired.append(buf)
-            buf = torch.empty(int(need * 1.25) + 1024, dtype=torch.float32, device=device)
+            buf = torch.zeros(int(need * 1.25) + 1024, dtype=torch.float32, device=device)
             cls._bufs[key] = buf
         return buf

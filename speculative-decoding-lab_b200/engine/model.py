@@ -267,10 +267,11 @@ class _GraphedForward:
     graph.
     """
 
-    __slots__ = ("graph", "ids", "rows", "starts", "logits", "keep", "table_ptr")
+    __slots__ = ("graph", "ids", "rows", "starts", "logits", "keep", "table_ptr", "calls")
 
-    def __init__(self, graph, ids, rows, starts, logits, keep, table_ptr) -> None:
+    def __init__(self, graph, ids, rows, starts, logits, keep, table_ptr, calls=0) -> None:
         self.graph = graph
+        self.calls = calls  # library entry calls captured (counted again at every replay)
         self.ids = ids
         self.rows = rows
         self.starts = starts
@@ -280,16 +281,17 @@ class _GraphedForward:
 
 
 class _GraphedPrefill:
-    """One captured prefill of a single prompt, padded to a power-of-two
-    length bucket.  Static inputs (token ids, block-table row, prompt length,
+    """One captured prefill of a single prompt, padded to a length bucket
+    (``prefill_bucket_of``).  Static inputs (token ids, block-table row, prompt length,
     last position) are refilled before each replay; positions past the prompt
     are computed but never stored (the attention's valid-row count) and their
     hidden states are dropped."""
 
-    __slots__ = ("graph", "ids", "meta", "logits", "keep", "table_ptr")
+    __slots__ = ("graph", "ids", "meta", "logits", "keep", "table_ptr", "calls")
 
-    def __init__(self, graph, ids, meta, logits, keep, table_ptr) -> None:
+    def __init__(self, graph, ids, meta, logits, keep, table_ptr, calls=0) -> None:
         self.graph = graph
+        self.calls = calls  # library entry calls captured (counted again at every replay)
         self.ids = ids
         self.meta = meta  # (block-table row, prompt length, last position) as device tensors
         self.logits = logits
@@ -308,12 +310,34 @@ class PagedLMMixin:
     logits agree with the eager path to rounding, not bit for bit.
     """
 
-    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
+    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256)
 
     def enable_cuda_graphs(self, enabled: bool = True) -> None:
         self._graphs_enabled = bool(enabled)
         if not enabled:
             self._graphs = {}
+
+    def _graph_pool(self):
+        """One memory pool shared by all of this model's live graphs: their
+        intermediates are dead between replays, which never overlap (one
+        stream), so later captures may reuse what earlier ones freed.  The
+        pool is a live graph's (a pool whose graphs were all released cannot
+        take new captures); with none alive, a fresh one."""
+        for g in self.__dict__.get("_graphs", {}).values():
+            return g.graph.pool()
+        return torch.cuda.graph_pool_handle()
+
+    def _graph_logits_buffer(self, chunk: int, bucket: int) -> torch.Tensor:
+        """``(bucket, chunk, vocab)`` view of the one logits buffer the graphs
+        of ``chunk`` rows per sequence share (sized for the largest bucket):
+        a replay's logits are consumed before the next replay of this model."""
+        bufs = self.__dict__.setdefault("_logits_bufs", {})
+        buf = bufs.get(chunk)
+        w = self.lm_head.weight
+        if buf is None:
+            buf = torch.empty((self.GRAPH_BUCKETS[-1], chunk, w.shape[0]), dtype=w.dtype, device=w.device)
+            bufs[chunk] = buf
+        return buf[:bucket]
 
     def _graph_bucket(self, batch: int) -> Optional[int]:
         if not getattr(self, "_graphs_enabled", False):
@@ -366,27 +390,83 @@ class PagedLMMixin:
             batch = AttnBatch(s_rows, s_starts, span, key_count=keys)
             steps = torch.arange(chunk, device=self.device)
 
+            logits_out = self._graph_logits_buffer(chunk, bucket)
+
             def run() -> torch.Tensor:
                 positions = s_starts.long().unsqueeze(1) + steps.unsqueeze(0)
                 plan = ForwardPlan(None, batch, positions, chunk)
                 hidden = self.embed_tokens(s_ids)
                 cos, sin = self._rope(positions)
                 hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
-                return self._logits(hidden)
+                # the head writes into the logits buffer every graph of this chunk shares
+                return torch.matmul(self.norm(hidden), self.lm_head.weight.t(), out=logits_out)
 
             # one eager pass sizes every workspace and stores this call's K/V;
             # the replay below stores the same bytes again
             run()
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            c0 = _lib.calls()
+            with torch.cuda.graph(graph, pool=self._graph_pool()):
                 logits = run()
-            g = _GraphedForward(graph, s_ids, s_rows, s_starts, logits, (steps, batch, kv), kv._table.data_ptr())
+            g = _GraphedForward(graph, s_ids, s_rows, s_starts, logits, (steps, batch, kv), kv._table.data_ptr(),
+                                _lib.calls() - c0)
             graphs[key] = g
         else:
             fill(g.ids, g.rows, g.starts)
         g.graph.replay()
+        _lib.count_calls(g.calls)
         return g.logits[:B]
+
+    @staticmethod
+    def graph_spans(kv: PagedKVCache) -> List[int]:
+        """The key-span buckets ``_graph_forward`` keys its graphs by for
+        ``kv``: powers of two from 1024, the last one capped at the table's
+        width in tokens."""
+        cap = kv.width * kv.block_size
+        spans, s = [], 1024
+        while True:
+            spans.append(min(s, cap))
+            if s >= cap:
+                return spans
+            s *= 2
+
+    def capture_graphs(self, kv: PagedKVCache, sid: int, chunk: int, prefill: bool = True,
+                       buckets: Optional[Sequence[int]] = None) -> int:
+        """Capture, before serving, every forward graph a run can replay for
+        ``kv``: ``chunk`` positions per row (1 = decode, gamma+1 = verify) at
+        every batch bucket and key-span bucket, and with ``prefill`` every
+        prompt-length bucket.  A serving process does this at start-up, so no
+        capture (an eager pass plus a capture, tens of milliseconds) falls
+        inside a run, whatever its requests.
+
+        ``sid`` is a registered, empty block-table row used as scratch: its
+        positions are reserved, written and released here.  Each span bucket
+        is captured at a span just inside it (55 % of the bucket, and above
+        the previous bucket), which sets the captured attention plans' split
+        sizes.  Returns the number of graphs captured."""
+        if not getattr(self, "_graphs_enabled", False):
+            return 0
+        graphs = self.__dict__.setdefault("_graphs", {})
+        n0 = len(graphs)
+        buckets = list(buckets) if buckets is not None else list(self.GRAPH_BUCKETS)
+        ids = torch.zeros((1, chunk), dtype=torch.long, device=self.device)
+        prev = 0
+        for span in self.graph_spans(kv):
+            need = max(prev + 1, int(0.55 * span), chunk)
+            prev = span
+            kv.reserve([sid], [0], [need])
+            for b in buckets:
+                self._graph_forward(ids, kv, [sid], [need - chunk], b)
+            kv.clear(sid)
+        if prefill:
+            cb = self.PREFILL_MIN_BUCKET
+            while self._prefill_bucket(kv, 1, cb, cb) == cb:
+                self.prefill(torch.zeros((1, cb), dtype=torch.long, device=self.device), kv, [sid], [cb])
+                kv.clear(sid)
+                cb = self.prefill_bucket_of(cb + 1)
+        torch.cuda.synchronize(self.device)
+        return len(graphs) - n0
 
     def _rope(self, positions: torch.Tensor):
         cs = self._rope_table()[positions]
@@ -404,6 +484,23 @@ class PagedLMMixin:
 
     PREFILL_MIN_BUCKET = 64
 
+    @classmethod
+    def prefill_bucket_of(cls, n: int) -> int:
+        """Padded length of a graphed prefill of ``n`` tokens: 64, then
+        multiples of 128 up to 1024, of 256 up to 4096, then powers of two
+        (the padded positions cost GEMM rows, so the steps stay fine where
+        prompts are common)."""
+        if n <= cls.PREFILL_MIN_BUCKET:
+            return cls.PREFILL_MIN_BUCKET
+        if n <= 1024:
+            return -(-n // 128) * 128
+        if n <= 4096:
+            return -(-n // 256) * 256
+        cb = 4096
+        while cb < n:
+            cb *= 2
+        return cb
+
     def _prefill_bucket(self, kv: PagedKVCache, B: int, chunk: int, length: int) -> Optional[int]:
         """Length bucket of a graphed prefill, or None for the eager path:
         graphs on, one prompt without padding, a 16-bit model (fp32 models
@@ -413,9 +510,7 @@ class PagedLMMixin:
             return None
         if self.embed_tokens.weight.dtype not in (torch.bfloat16, torch.float16):
             return None
-        cb = self.PREFILL_MIN_BUCKET
-        while cb < chunk:
-            cb *= 2
+        cb = self.prefill_bucket_of(chunk)
         if cb > kv.width * kv.block_size or cb > self._rope_table().shape[0]:
             return None
         return cb
@@ -459,13 +554,16 @@ class PagedLMMixin:
             run()
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            c0 = _lib.calls()
+            with torch.cuda.graph(graph, pool=self._graph_pool()):
                 logits = run()
-            g = _GraphedPrefill(graph, s_ids, s_meta, logits, (s_starts, positions, batch, kv), kv._table.data_ptr())
+            g = _GraphedPrefill(graph, s_ids, s_meta, logits, (s_starts, positions, batch, kv), kv._table.data_ptr(),
+                                _lib.calls() - c0)
             graphs[key] = g
         else:
             fill(g.ids, g.meta)
         g.graph.replay()
+        _lib.count_calls(g.calls)
         return g.logits
 
     def prefill(self, prompt_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
@@ -473,7 +571,7 @@ class PagedLMMixin:
         """Prefill ragged prompts; return first-token logits ``(B, V)``.
 
         With CUDA graphs enabled, a single unpadded prompt of a 16-bit model
-        replays a captured prefill padded to a power-of-two length bucket."""
+        replays a captured prefill padded to a length bucket (``prefill_bucket_of``)."""
         self.forward_calls += 1
         B, chunk = prompt_2d.shape
         cb = self._prefill_bucket(kv, B, chunk, int(seq_lengths[0]) if B == 1 else -1)

@@ -27,7 +27,8 @@ catch-up decode for sequences that accepted everything plus the bonus.
 from __future__ import annotations
 
 import ctypes
-from typing import Any, Dict, List, Optional, Sequence as Seq
+import time
+from typing import Any, Callable, Dict, List, Optional, Sequence as Seq
 
 import torch
 
@@ -104,6 +105,9 @@ class SpeculativePagedScheduler(PagedScheduler):
         if not 1 <= self.gamma <= 32:
             raise ValueError("gamma must be within [1, 32]")
         self._q_buf: Optional[torch.Tensor] = None
+        # optional observer of every round: called with (sequence ids, target
+        # start positions, draft lengths) before the round's first launch
+        self.round_hook: Optional[Callable[[List[int], List[int], List[int]], None]] = None
 
     # ------------------------------------------------------------ admission
     def _flush_arrivals(self, arrivals: List[WorkloadRequest], when: int, result: SchedulerResult,
@@ -112,7 +116,9 @@ class SpeculativePagedScheduler(PagedScheduler):
         for request in arrivals:
             seq = Sequence(
                 sid=self._next_sid,
-                prompt_ids=self.model.encode(request.prompt),
+                # a CUDA tensor of ids is taken as is (prompts staged in HBM)
+                prompt_ids=(request.prompt if isinstance(request.prompt, torch.Tensor)
+                            else self.model.encode(request.prompt)),
                 max_new_tokens=request.max_new_tokens,
                 arrive_time=request.arrive_time,
                 admit_step=when,
@@ -129,7 +135,10 @@ class SpeculativePagedScheduler(PagedScheduler):
                           stream: Optional[UniformStream]) -> Optional[float]:
         watch = Stopwatch()
         with watch:
-            ids = _lib.to_device([list(seq.prompt_ids)], torch.long, self.model.device)
+            if isinstance(seq.prompt_ids, torch.Tensor):  # prompt ids already in HBM
+                ids = seq.prompt_ids.to(self.model.device, torch.long).reshape(1, -1)
+            else:
+                ids = _lib.to_device([list(seq.prompt_ids)], torch.long, self.model.device)
             logits = self.model.prefill(ids, self.kv, [seq.sid], [len(seq.prompt_ids)])
             tok = self._next_tokens(logits, stream)
             self.draft_model.prefill(ids, self.draft_kv, [seq.sid], [len(seq.prompt_ids)])
@@ -137,8 +146,37 @@ class SpeculativePagedScheduler(PagedScheduler):
         seq.prefilled = True
         return watch.elapsed_ms
 
+    # ------------------------------------------------------------ start-up
+    def capture_graphs(self) -> int:
+        """Capture every CUDA graph the models can replay in a run (draft
+        decode, target verify of gamma+1 rows, both models' prefill, at every
+        batch and key-span bucket) before serving, on a scratch sequence id.
+        A no-op unless the models have CUDA graphs enabled.  Returns the
+        number of graphs captured."""
+        sid = self._next_sid
+        self._next_sid += 1
+        n = 0
+        for model, kv, chunk in ((self.draft_model, self.draft_kv, 1), (self.model, self.kv, self.gamma + 1)):
+            if not hasattr(model, "capture_graphs"):
+                continue
+            kv.add_sequence(sid)
+            n += model.capture_graphs(kv, sid, chunk)
+        return n
+
     # ------------------------------------------------------------ spec loop
-    def run_spec_continuous(self, requests: Seq[WorkloadRequest], seed: int, measure: bool = True) -> SchedulerResult:
+    def run_spec_continuous(self, requests: Seq[WorkloadRequest], seed: int, measure: bool = True,
+                            arrival_clock: str = "step") -> SchedulerResult:
+        """Serve ``requests`` to completion (engine/spec_scheduler.py:166-222).
+
+        ``arrival_clock="step"`` (the reference's): ``arrive_time`` counts
+        scheduler rounds.  ``"wall"``: ``arrive_time`` is in seconds from the
+        start of the run, and a request is admitted at the first round
+        boundary at or after its arrival; with nothing to run the scheduler
+        waits for the next arrival (that idle time is part of the makespan).
+        """
+        if arrival_clock not in ("step", "wall"):
+            raise ValueError("arrival_clock must be 'step' or 'wall'")
+        wall = arrival_clock == "wall"
         result = SchedulerResult(mode="spec-continuous", sampling=self.sampling.describe())
         stream = self._make_stream(seed)
         device = self.model.device
@@ -149,8 +187,14 @@ class SpeculativePagedScheduler(PagedScheduler):
             torch.cuda.reset_peak_memory_stats(device)
         stopwatch = Stopwatch()
         with stopwatch:
-            due = [r for r in arrivals if r.arrive_time <= step]
-            pending = [r for r in arrivals if r.arrive_time > step]
+            t0 = time.perf_counter()
+
+            def clock():
+                return (time.perf_counter() - t0) if wall else step
+
+            now = clock()
+            due = [r for r in arrivals if r.arrive_time <= now]
+            pending = [r for r in arrivals if r.arrive_time > now]
             self._flush_arrivals(due, step, result, stream)
             running = [s for s in result.sequences if not s.finished]
             while running or pending:
@@ -158,9 +202,12 @@ class SpeculativePagedScheduler(PagedScheduler):
                 if running:
                     self._spec_step(running, result, stream)
                     result.total_forwards += 1
+                elif wall and pending:
+                    time.sleep(max(0.0, pending[0].arrive_time - clock()))
                 step += 1
-                due = [r for r in pending if r.arrive_time <= step]
-                pending = [r for r in pending if r.arrive_time > step]
+                now = clock()
+                due = [r for r in pending if r.arrive_time <= now]
+                pending = [r for r in pending if r.arrive_time > now]
                 if due:
                     self._flush_arrivals(due, step, result, stream)
                 running = [s for s in result.sequences if not s.finished]
@@ -212,6 +259,8 @@ class SpeculativePagedScheduler(PagedScheduler):
         B = len(running)
         starts = [self.kv.seq_len(sid) for sid in sids]
         d0 = [self.draft_kv.seq_len(sid) for sid in sids]
+        if self.round_hook is not None:
+            self.round_hook(sids, starts, d0)
 
         # ---- 1. draft proposes gamma tokens per sequence
         proposals = torch.empty((B, gamma), dtype=torch.int32, device=device)

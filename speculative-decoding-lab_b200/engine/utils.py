@@ -1,15 +1,6 @@
-"""Re-export the shared utilities from ``specdec.utils``."""
+"""The engine's helpers are the ones in ``specdec.utils`` (same module path as
+the reference's ``engine/utils.py`` import sites)."""
 
 from __future__ import annotations
 
-from specdec.utils import (  # noqa: F401
-    Stopwatch,
-    human_bytes,
-    mean_std,
-    sanitize_for_json,
-    save_json,
-    set_seed,
-    setup_logger,
-    sync_device,
-    timestamp,
-)
+from specdec.utils import Stopwatch, mean_std, setup_logger, sync_device  # noqa: F401

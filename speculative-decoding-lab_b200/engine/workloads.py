@@ -117,6 +117,41 @@ def c4_requests(seed: int = 0, n: int = 2048, mean_gap_steps: float = 1.0, vocab
     return out
 
 
+def c4_requests_wall(seed: int = 0, n: int = 2048, rate_per_s: float = 64.0, vocab: int = 151936):
+    """The C4 request stream with Poisson arrivals in seconds: the same draws
+    as :func:`c4_requests` (prompt length, ids, output length, then the gap),
+    with exponential gaps of mean ``1 / rate_per_s`` seconds.
+
+    Returns ``(prompt_ids, max_new_tokens, arrive_seconds)`` triples in
+    arrival order (the first at 0.0).
+    """
+    c = C4
+    rng = np.random.default_rng(seed)
+    t = 0.0
+    out = []
+    for _ in range(n):
+        length = int(min(c["prompt_cap"], max(1, np.floor(rng.lognormal(c["prompt_mu"], c["prompt_sigma"])))))
+        ids = rng.integers(0, vocab, size=length)
+        new = int(rng.integers(c["out_lo"], c["out_hi"] + 1))
+        out.append(([int(x) for x in ids], new, t))
+        t += float(rng.exponential(1.0 / rate_per_s))
+    return out
+
+
+def c4_slices(requests, steps: int):
+    """Cut an arrival-ordered request stream into ``steps`` consecutive
+    slices of (nearly) equal size, each slice's arrival times rebased so its
+    first request arrives at 0."""
+    n = len(requests)
+    out = []
+    for k in range(steps):
+        lo, hi = (k * n) // steps, ((k + 1) * n) // steps
+        part = requests[lo:hi]
+        t0 = part[0][2] if part else 0.0
+        out.append([(ids, new, t - t0) for ids, new, t in part])
+    return out
+
+
 # --------------------------------------------------------------------- C5
 C5 = dict(gamma=6, batch_per_gpu=16, ctx_lo=8192, ctx_hi=32768, temperature=0.8, new_tokens=256,
           target="qwen2.5-3b", draft="qwen2.5-1.5b")

@@ -3,15 +3,7 @@
 from __future__ import annotations
 
 from dataclasses import asdict, dataclass
-from typing import Any, Dict, Tuple
-
-DEFAULT_PROMPTS: Tuple[str, ...] = (
-    "The key idea behind speculative decoding is",
-    "In a distributed system, exactly-once semantics requires",
-    "Photosynthesis converts light energy into chemical energy by",
-)
-
-DEFAULT_GAMMAS: Tuple[int, ...] = (1, 2, 3, 4, 5, 6, 8, 10, 12)
+from typing import Any, Dict
 
 
 @dataclass
@@ -44,20 +36,6 @@ class SamplingConfig:
         payload = asdict(self)
         payload["mode"] = "greedy" if self.is_greedy else "sampling"
         return payload
-
-
-@dataclass
-class ModelConfig:
-    """Which draft/target pair to load and where."""
-
-    draft_model: str = "Qwen/Qwen2.5-0.5B"
-    target_model: str = "Qwen/Qwen2.5-1.5B"
-    device: str = "auto"
-    dtype: str = "auto"
-    cache_dir: str = "models"
-
-    def to_dict(self) -> Dict[str, Any]:
-        return asdict(self)
 
 
 def validate_gamma(gamma: int) -> int:

@@ -47,7 +47,8 @@ def _load_by_path(name: str, path: str):
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SDL_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SDL_REFERENCE"), required="SDL_REFERENCE" not in os.environ,
+                    help="checkout of the reference project (or set SDL_REFERENCE)")
     args = ap.parse_args(argv)
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)

@@ -98,7 +98,7 @@ def test_c1_runs_reproduce_with_graphs(label):
 
 def test_graph_prefill_matches_eager():
     """A 16-bit model with graphs on prefills a single prompt through a
-    captured forward padded to a power-of-two length bucket: first-token
+    captured forward padded to a length bucket (64, then multiples of 128): first-token
     logits and the stored K/V agree with the eager prefill to bf16 rounding,
     on the capture, on a replay with another length in the same bucket and in
     a second bucket; fp32 models keep the eager prefill."""
@@ -131,3 +131,61 @@ def test_graph_prefill_matches_eager():
     assert not any(k[1] == "prefill" for k in getattr(fp32, "_graphs", {}))
     for kv in kvs + [kv32]:
         kv.check_errors()
+
+
+@pytest.mark.parametrize("label", ["greedy", "t1"])
+def test_precaptured_graphs_and_wall_clock_admission_reproduce_c1(label):
+    """Every graph captured up front (``capture_graphs``, on a scratch
+    sequence, before any request) and the wall-clock admission path with all
+    arrivals at time 0: the C1 runs still reproduce the reference token for
+    token and round for round, and the run captures nothing new."""
+    g = load_json("c1_spec.json")
+    run = g["runs"][label]
+    C1 = workloads.C1
+    target = _model("c1-target", C1["target_seed"])
+    draft = _model("c1-draft", C1["draft_seed"])
+    target.enable_cuda_graphs()
+    draft.enable_cuda_graphs()
+    cfg = EngineConfig(block_size=C1["block_size"], max_num_blocks=g["capacity"])
+    kv = build_kv(target, cfg, DEV, max_seqs=16)
+    dkv = build_kv(draft, cfg, DEV, max_seqs=16)
+    sched = SpeculativePagedScheduler(target, kv, draft, dkv, cfg, SpecSampling(temperature=run["temperature"]),
+                                      C1["gamma"], uniforms=torch.from_numpy(workloads.c1_uniforms(0)))
+    n = sched.capture_graphs()
+    spans = len(target.graph_spans(kv))
+    assert n == spans * len(target.GRAPH_BUCKETS) * 2  # draft decode + target verify; fp32: no prefill graphs
+    assert kv.num_allocated_blocks == 0 and dkv.num_allocated_blocks == 0
+    before = (len(target._graphs), len(draft._graphs))
+    sched._next_sid = 0  # the scratch row is empty again: the run's sequence ids start at 0 as in the reference
+    reqs = [WorkloadRequest(prompt=ids, max_new_tokens=n_, arrive_time=0.0)
+            for ids, n_, _ in workloads.c1_requests(0)]
+    res = sched.run_spec_continuous(reqs, seed=0, measure=False, arrival_clock="wall")
+    assert [s.generated for s in res.sequences] == run["generated"]
+    assert res.tokens_per_round == run["tokens_per_round"]
+    assert (len(target._graphs), len(draft._graphs)) == before
+    kv.check_errors()
+    dkv.check_errors()
+
+
+def test_wall_clock_admission_waits_for_arrivals():
+    """Requests arriving 0.3 s and 0.6 s into the run are admitted at a round
+    boundary no earlier than their arrival; the run waits when idle."""
+    import time as _time
+
+    C1 = workloads.C1
+    target = _model("c1-target", C1["target_seed"])
+    draft = _model("c1-draft", C1["draft_seed"])
+    cfg = EngineConfig(block_size=16, max_num_blocks=256)
+    kv = build_kv(target, cfg, DEV)
+    dkv = build_kv(draft, cfg, DEV)
+    sched = SpeculativePagedScheduler(target, kv, draft, dkv, cfg, SpecSampling(temperature=0.0), C1["gamma"])
+    reqs = [WorkloadRequest(prompt=ids, max_new_tokens=4, arrive_time=t)
+            for (ids, _, _), t in zip(workloads.c1_requests(0)[:3], (0.0, 0.3, 0.6))]
+    t0 = _time.perf_counter()
+    res = sched.run_spec_continuous(reqs, seed=0, measure=True, arrival_clock="wall")
+    assert _time.perf_counter() - t0 >= 0.6
+    assert res.makespan_ms >= 600.0
+    assert [len(s.generated) for s in res.sequences] == [4, 4, 4]
+    assert [s.arrive_time for s in res.sequences] == [0.0, 0.3, 0.6]
+    with pytest.raises(ValueError):
+        sched.run_spec_continuous(reqs, seed=0, arrival_clock="tick")

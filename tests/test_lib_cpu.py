@@ -94,3 +94,33 @@ def test_ctypes_structs_match_the_header_layout(tmp_path):
         for fname, _ in cls._fields_:
             assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
 
+
+
+def test_c4_wall_clock_stream_draws_like_the_step_stream():
+    """The wall-clock C4 stream draws prompts and output lengths in the same
+    order as the step-clock one; arrivals are Poisson gaps in seconds (mean
+    1/rate); slices cover the stream in order, each rebased to start at 0."""
+    import numpy as np
+
+    from engine import workloads
+
+    a = workloads.c4_requests(3, 200, 1.0)
+    b = workloads.c4_requests_wall(3, 200, 64.0)
+    assert [x[0] for x in a] == [x[0] for x in b] and [x[1] for x in a] == [x[1] for x in b]
+    t = np.array([x[2] for x in b])
+    assert t[0] == 0.0 and np.all(np.diff(t) >= 0)
+    assert 0.5 / 64 < np.diff(t).mean() < 2.0 / 64
+    parts = workloads.c4_slices(b, 7)
+    assert sum(len(p) for p in parts) == 200 and all(p[0][2] == 0.0 for p in parts)
+    assert [x[0] for p in parts for x in p] == [x[0] for x in b]
+
+
+def test_prefill_buckets_are_fine_where_prompts_are_common():
+    """Graphed prefills pad a prompt to 64, a multiple of 128 up to 1024, of
+    256 up to 4096, then a power of two; every bucket holds its prompt."""
+    from engine.model import PagedLMMixin
+
+    f = PagedLMMixin.prefill_bucket_of
+    assert [f(n) for n in (1, 64, 65, 128, 129, 556, 1024, 1025, 4096, 4097, 9000)] == \
+        [64, 64, 128, 128, 256, 640, 1024, 1280, 4096, 8192, 16384]
+    assert all(f(n) >= n and f(f(n)) == f(n) for n in range(1, 5000, 7))

@@ -131,3 +131,44 @@ def test_spec_sample_logits_matches_oracle_softmax_path():
                               [props[b].tolist() for b in range(B)], osamp.UniformStream(us))
     nn, tk = n.tolist(), toks.tolist()
     assert [tk[b][: nn[b]] for b in range(B)] == want
+
+
+def _set_mode(mode):
+    from engine import _lib
+
+    _lib.check(_lib.load().sdl_set_spec_sampler_mode(mode), "sdl_set_spec_sampler_mode")
+
+
+@pytest.mark.parametrize("B,gamma,V,spread", [(32, 5, 151936, 2.0), (1, 1, 7, 0.3), (7, 4, 8193, 0.5),
+                                              (100, 4, 151936, 1.0), (300, 4, 20000, 0.4), (700, 3, 5000, 0.4),
+                                              (16, 32, 3000, 0.2)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_one_launch_sampler_equals_the_chain(B, gamma, V, spread, dtype):
+    """sdl_spec_sample_logits' one-launch kernel (a cluster per sequence,
+    the accept walk's uniform offsets found by waiting on lower sequences)
+    against the five-launch chain: the same tokens, accept lengths and
+    stream counter, on three consecutive rounds (the launch epoch moves on),
+    with u_skip and a stream that does not start at 0.  Batches too large
+    for one resident grid take the chain in both modes."""
+    pl, ql = _block(B, gamma, V, seed=B + gamma, spread=spread, dtype=dtype)
+    T = 0.9
+    q = probs_rows(ql.reshape(B * gamma, V), T, False).reshape(B, gamma, V)
+    us0 = np.random.default_rng(B + 5).random(B * gamma, dtype=np.float32)
+    props = sample_rows(q.reshape(B * gamma, V), _stream(us0)).reshape(B, gamma).to(torch.int32).contiguous()
+    us = np.random.default_rng(B + 6).random(3 * B * (gamma + 1) + 64, dtype=np.float32)
+    results = []
+    try:
+        for mode in (0, 1):  # the chain, then the one-launch kernel
+            _set_mode(mode)
+            s = _stream(us, 3)
+            rounds = []
+            for _ in range(3):
+                t, n = spec_sample_logits(pl, ql, T, props, s, u_skip=2)
+                rounds.append((t.tolist(), n.tolist(), s.consumed()))
+            results.append(rounds)
+    finally:
+        _set_mode(0)
+    chain, fused = results
+    for (t1, n1, c1), (t2, n2, c2) in zip(chain, fused):
+        assert n1 == n2 and c1 == c2
+        assert [t1[i][: n1[i]] for i in range(B)] == [t2[i][: n2[i]] for i in range(B)]

@@ -43,9 +43,9 @@ def _case(seed: int, lens, chunk: int):
     return kv, q, AttnBatch.from_lists(DEV, list(range(len(lens))), lens, chunk)
 
 
-def _noalloc(q, kv, batch):
-    out = torch.zeros(q.shape, dtype=q.dtype, device=DEV)
-    args = _paged_args(q, kv, 0, batch, out)
+def _noalloc(q, kv, batch, out_dtype=None, **kw):
+    out = torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=DEV)
+    args = _paged_args(q, kv, 0, batch, out, **kw)
     lib = _lib.load()
     assert lib.sdl_attention_workspace_bytes(args) > 0, "case must exercise the split-K scratch"
     rc = lib.sdl_paged_attention_noalloc(ctypes.byref(args), _lib.stream_handle(DEV))
@@ -65,14 +65,50 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
         kv.check_errors()
 
 
+def test_noalloc_shrinks_its_split_to_fit_the_array():
+    """64 rows of a 7-row verify over 32k keys with 16 q heads: the
+    automatic mma.sync plan's partials would exceed the array, so the
+    allocation-free call takes larger splits until they fit; the result
+    agrees with the workspace entry point within the attention tolerance."""
+    lib = _lib.load()
+    B, chunk, Hq, Hkv, d, bs, L = 64, 7, 16, 2, 128, 16, 32760
+    cap = B * (-(-(L + chunk) // bs))
+    kv = PagedKVCache(1, Hkv, d, cap, bs, DEV, torch.bfloat16, max_blocks_per_seq=-(-(L + chunk) // bs), max_seqs=B)
+    sids = list(range(B))
+    for sid in sids:
+        kv.add_sequence(sid)
+    kv.reserve(sids, [0] * B, [L + chunk] * B)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(3)
+    kv._k.normal_(generator=g)
+    kv._v.normal_(generator=g)
+    q = torch.randn((B, chunk, Hq, d), generator=g, device=DEV).to(torch.bfloat16)
+    # no key count: the automatic split fills the GPU as if every row were
+    # long, which needs more partials than the array holds
+    full = AttnBatch.from_lists(DEV, sids, [L] * B, chunk)
+    batch = AttnBatch(full.rows, full.starts, full.max_limit)
+    args = _paged_args(q, kv, 0, batch, q, use_umma=-1)
+    assert lib.sdl_attention_workspace_bytes(args) > lib.sdl_noalloc_scratch_bytes()
+    for _ in range(2):
+        got = _noalloc(q, kv, batch, out_dtype=torch.float32, use_umma=-1)
+        want = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, use_umma=-1)
+        torch.cuda.synchronize()
+        scale = want.abs().max().item()
+        assert (got - want).abs().max().item() <= 2e-3 * scale
+    kv.check_errors()
+
+
 def test_noalloc_refuses_scratch_beyond_its_array():
+    """A plan that cannot shrink (an explicit split size) and needs more
+    scratch than the array is refused on the host, before any launch."""
     lib = _lib.load()
     kv = PagedKVCache(1, 2, 128, 8, 16, DEV, torch.bfloat16, max_blocks_per_seq=2100)
     q = torch.zeros((64, 7, 16, 128), device=DEV, dtype=torch.bfloat16)
     rows = torch.arange(64, dtype=torch.int32, device=DEV)
     starts = torch.zeros(64, dtype=torch.int32, device=DEV)
     batch = AttnBatch(rows, starts, 32768)
-    args = _paged_args(q, kv, 0, batch, q, use_umma=-1)  # the mma.sync plan: 64 rows x 32k keys of partials
+    # the mma.sync plan with 256-key splits: 64 rows x 128 splits of partials
+    args = _paged_args(q, kv, 0, batch, q, use_umma=-1, pages_per_split=16)
     assert lib.sdl_attention_workspace_bytes(args) > lib.sdl_noalloc_scratch_bytes()
     rc = lib.sdl_paged_attention_noalloc(ctypes.byref(args), _lib.stream_handle(DEV))
     assert rc == 4  # SDL_ERR_WORKSPACE, refused on the host before any launch
