@@ -889,10 +889,12 @@ def main(argv=None) -> int:
     ap.add_argument("--append", choices=["fused", "separate"], default="fused",
                     help="store each layer's new K/V rows inside the attention launch (default) or with a "
                          "separate append launch before it")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c4",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "c4attn"], default="c4",
                     help="c4: continuous-batching spec scheduler end to end (default, the spec-decode "
                          "tokens/s headline); c2: decode attention + KV append; c3: verify step at gamma=5; "
-                         "c5: the attention of one long-context round at gamma=6 (draft decodes + target verify)")
+                         "c5: the attention of one long-context round at gamma=6 (draft decodes + target verify); "
+                         "c4attn: C4's two attention ops alone at --batch sequences of C4 contexts (a profiling "
+                         "target, one JSON line per op)")
     ap.add_argument("--requests", type=int, default=2048,
                     help="c4: requests in the whole job's arrival stream (the config's 2048)")
     ap.add_argument("--eager", action="store_true", help="c4: run the model forwards eagerly instead of CUDA graphs")
@@ -904,9 +906,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.steps is None:
-        args.steps = 20 if args.workload == "c4" else 400
+        args.steps = 20 if args.workload in ("c4", "c4attn") else 400
     if args.warmup is None:
-        args.warmup = 3 if args.workload == "c4" else 10
+        args.warmup = 3 if args.workload in ("c4", "c4attn") else 10
     if args.warmup < 3:
         args.warmup = 3
     if args.batch is None:
@@ -915,6 +917,8 @@ def main(argv=None) -> int:
         return main_c5(args)
     if args.workload == "c4":
         return main_c4(args)
+    if args.workload == "c4attn":
+        return main_c4attn(args)
     if args.layers is None:
         args.layers = 28
     if args.workload == "c3":
@@ -1402,7 +1406,7 @@ def main_c5(args) -> int:
     return 0
 
 
-def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps):
+def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw):
     """One attention op as a model forward launches it -- the K/V rows of
     ``chunk`` new positions stored inside the paged attention launch -- over
     contexts ``ctx`` (a random-permutation pool of exactly those pages), timed
@@ -1439,7 +1443,7 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps):
 
     def run():
         for layer in range(layers):
-            paged_attention(q[layer], kv, layer, batch, out=out[layer], k_new=kn[layer], v_new=vn[layer])
+            paged_attention(q[layer], kv, layer, batch, out=out[layer], k_new=kn[layer], v_new=vn[layer], **akw)
 
     run()
     torch.cuda.synchronize(device)
@@ -1459,11 +1463,43 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps):
     ms = e0.elapsed_time(e1) / (reps * layers)
     nbytes = (sum((x + chunk) * 2 * Hkv * d * 2 for x in ctx) + 2 * B * chunk * Hq * d * 2
               + sum(-(-(x + chunk) // bs) * 4 for x in ctx) + 2 * (B * chunk * 2 * Hkv * d * 2))
-    kern = attention_kernel(q[0], kv, batch)
-    launches = attention_launches(q[0], kv, batch, k_new=kn[0], v_new=vn[0])
+    kern = attention_kernel(q[0], kv, batch, **akw)
+    launches = attention_launches(q[0], kv, batch, k_new=kn[0], v_new=vn[0], **akw)
     del graph
     return {"kernel": kern, "ms": ms, "bytes": nbytes, "launches_per_op": launches, "batch": B,
             "mean_ctx": round(sum(ctx) / max(1, B), 1)}
+
+
+def main_c4attn(args) -> int:
+    """C4's attention ops alone (one GPU): the 0.5B-shaped draft decode
+    (14 q / 2 kv heads, head_dim 64) and the 1.5B-shaped 5-row verify (12 q
+    heads, head_dim 128), each with its K/V append fused, over ``--batch``
+    sequences whose contexts follow C4's prompt distribution plus up to 300
+    generated tokens; ``--layers`` layers per graph (default 8), ``--steps``
+    graph replays.  Prints one JSON line per op (not a bench line: a
+    profiling target for the batch sizes a C4 run reaches)."""
+    import torch
+
+    from engine import workloads
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the B200 path has no CPU fallback)")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    c = workloads.C4
+    rng = np.random.default_rng(args.seed)
+    ctx = [int(min(c["prompt_cap"], max(16, np.floor(rng.lognormal(c["prompt_mu"], c["prompt_sigma"])))))
+           + int(rng.integers(0, 300)) for _ in range(args.batch)]
+    akw = dict(use_umma=UMMA_FLAG[args.attn_kernel], mma_layout=LAYOUT_FLAG[args.mma_layout])
+    hbm, _ = _peaks()
+    layers = args.layers or 8
+    for name, chunk, Hq, d in (("draft decode (0.5B shape)", 1, 14, 64), ("5-row verify (1.5B shape)", 5, 12, 128)):
+        r = _time_attention_op(device, ctx, chunk, Hq, 2, d, layers, args.seed + 7, max(1, args.steps), **akw)
+        gbs = r["bytes"] / (r["ms"] * 1e-3) / 1e9
+        print(json.dumps({"op": name, "batch": args.batch, "mean_ctx": r["mean_ctx"], "kernel": ATTN_KERNELS[r["kernel"]],
+                          "us_per_launch": round(r["ms"] * 1e3, 2), "algorithmic_mb": round(r["bytes"] / 1e6, 1),
+                          "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 4)}), flush=True)
+    return 0
 
 
 def main_c4(args) -> int:
@@ -1502,7 +1538,8 @@ def main_c4(args) -> int:
            "outputs": "U[64, 512] new tokens",
            "arrivals": "Poisson, 64 requests/s per GPU ({:g}/s for the whole job), wall clock: a request is "
                        "admitted at the first round boundary after its arrival".format(rate),
-           "kv_pool": "80% of free HBM after weights, block_size 16, target and draft pools",
+           "kv_pool": "80% of free HBM after weights, block_size 16, target and draft pools; recompute "
+                      "preemption when a round would not fit (per_rank.preempted counts it)",
            "forwards": "eager" if args.eager else "CUDA-graph replays (batch x key-span buckets, all captured "
                                                   "before the warm-up)",
            "warmup": "{} requests of a different stream (seed {})".format(max(1, (total * W) // K), args.seed + 1000003),
@@ -1578,6 +1615,7 @@ def main_c4(args) -> int:
         draft.enable_cuda_graphs()
     sched = SpeculativePagedScheduler(target, kv, draft, dkv, ecfg, SpecSampling(temperature=c["temperature"]),
                                       c["gamma"])
+    sched.preemption = "recompute"  # a full pool parks and later re-prefills sequences instead of raising
     t_cap = time.perf_counter()
     n_graphs = sched.capture_graphs()
     cap_s = time.perf_counter() - t_cap
@@ -1630,6 +1668,7 @@ def main_c4(args) -> int:
     e1.record(stream)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
+    preempted = sched.preemptions
     sched.round_hook = None
     calls = _lib.calls() - calls0
     clk = clocks.stop() if clocks else None
@@ -1669,7 +1708,8 @@ def main_c4(args) -> int:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = CpuC4(seed=args.seed).measure(args.cpu_seconds)
     payload = {"tokens": tokens, "ms": ms, "e2e_tokens": e2e_tokens, "e2e_ms": e2e_ms, "rounds": n_rounds,
-               "rows": n_rows, "calls": calls, "draft_ms": draft_op["ms"], "verify_ms": verify_op["ms"]}
+               "rows": n_rows, "calls": calls, "draft_ms": draft_op["ms"], "verify_ms": verify_op["ms"],
+               "preempted": preempted}
     allp = gather_results(payload)
     if dist:
         dist.barrier()
@@ -1705,7 +1745,8 @@ def main_c4(args) -> int:
         "generated_tokens": tok_sum,
         "makespan_ms": round(ms_max, 2),
         "per_rank": [{"tokens": p["tokens"], "ms": round(p["ms"], 1), "rounds": p["rounds"],
-                      "mean_batch": round(p["rows"] / max(1, p["rounds"]), 2)} for p in allp],
+                      "mean_batch": round(p["rows"] / max(1, p["rounds"]), 2), "preempted": p["preempted"]}
+                     for p in allp],
         "graphs_captured": n_graphs,
         "graph_capture_s": round(cap_s, 2),
         "roofline": {"bound": "hbm", "achieved": round(d_gbs, 1), "peak": hbm, "unit": "GB/s",

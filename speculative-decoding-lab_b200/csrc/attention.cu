@@ -63,6 +63,7 @@ struct TcParams {
     int g_cta, wpg, ncoltiles;
     int stage_bytes;
     int ring_bytes;  // shared bytes before the mbarriers: the TMA ring, reused for cluster partials
+    int stages;      // ring depth of the rows-on-M kernel
     int cluster;     // 1: the splits of a row form one cluster and merge their partials on chip
     float scale_log2;
     float* o_part;
@@ -1053,8 +1054,9 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     constexpr int STAGE_BYTES = rows_stage_bytes<HD>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRowStages * STAGE_BYTES);
-    uint64_t* empty = full + kRowStages;
+    const int NS = p.stages;  // ring depth (the plan's; kRowStages)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * STAGE_BYTES);
+    uint64_t* empty = full + NS;
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
@@ -1095,7 +1097,7 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
 
     if (threadIdx.x == 0) {
         *s_abort = 0;
-        for (int s = 0; s < kRowStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], ncons);
         }
@@ -1143,16 +1145,16 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             const int cnt = min(32, np - i0);
             for (int k = 0; k < cnt; k += kTilePages) {
                 const int i = (i0 + k) / kTilePages;
-                const int st = i % kRowStages;
+                const int st = i % NS;
                 const int t0 = __shfl_sync(0xffffffffu, tok, k);
                 // a lone last page is loaded twice: its second copy's keys lie
                 // past every row's limit and are masked
                 const int t1 = __shfl_sync(0xffffffffu, tok, min(k + 1, cnt - 1));
                 const int pg0 = pbeg + i0 + k;
                 if (app_page >= pg0 && app_page < pg0 + kTilePages) append_rows();  // app_page < pend
-                if (i >= kRowStages) {
+                if (i >= NS) {
                     int ok = 1;
-                    if (lane == 0) ok = mbar_wait_bounded(&empty[st], ((i / kRowStages) - 1) & 1, kWaitLimit) ? 1 : 0;
+                    if (lane == 0) ok = mbar_wait_bounded(&empty[st], ((i / NS) - 1) & 1, kWaitLimit) ? 1 : 0;
                     ok = __shfl_sync(0xffffffffu, ok, 0);
                     if (!ok || *s_abort) {
                         if (lane == 0 && !ok) { sdl_raise(p.err, SDL_DEVERR_TIMEOUT); *s_abort = 1; }
@@ -1180,8 +1182,8 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         __syncthreads();
         // Drain: never leave the CTA with bulk copies still landing in smem.
         if (lane == 0 && *s_abort) {
-            for (int i = max(0, issued - kRowStages); i < issued; ++i)
-                (void)mbar_wait_bounded(&full[i % kRowStages], (i / kRowStages) & 1, kWaitLimit);
+            for (int i = max(0, issued - NS); i < issued; ++i)
+                (void)mbar_wait_bounded(&full[i % NS], (i / NS) & 1, kWaitLimit);
         }
         pdl_launch_dependents();
         return;
@@ -1234,8 +1236,8 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     bool aborted = false;
 
     for (int i = 0; i < ntile; ++i) {
-        const int st = i % kRowStages;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (i / kRowStages) & 1, kWaitLimit));
+        const int st = i % NS;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (i / NS) & 1, kWaitLimit));
         if (!ok) {
             if (lane == 0) { sdl_raise(p.err, SDL_DEVERR_TIMEOUT); *s_abort = 1; }
             aborted = true;
@@ -2210,6 +2212,7 @@ struct Plan {
     bool rows = false;     // rows-on-M mma.sync kernel (ncoltiles = row tiles, wpg = consumer warps)
     bool umma = false;     // tcgen05 verify kernel
     bool direct = false;   // register-direct decode kernel (one CTA per split, kv head and sequence)
+    int stages = 0;        // rows-on-M kernel: ring depth
     size_t smem = 0;
     size_t ws_bytes = 0;
 };
@@ -2502,8 +2505,9 @@ Plan make_rows_plan(const sdl_attn_args* a) {
     pl.g_cta = 1;
     pl.kvgroups = a->Hkv;
     pl.stage_bytes = a->head_dim == 128 ? rows_stage_bytes<128>() : rows_stage_bytes<64>();
-    pl.ring_bytes = kRowStages * pl.stage_bytes;
-    pl.smem = (size_t)pl.ring_bytes + 1024 + 2 * kRowStages * sizeof(uint64_t);
+    pl.stages = kRowStages;
+    pl.ring_bytes = pl.stages * pl.stage_bytes;
+    pl.smem = (size_t)pl.ring_bytes + 1024 + 2 * pl.stages * sizeof(uint64_t);
     const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
     const long base_ctas = (long)a->B * pl.ncoltiles * pl.kvgroups;
     const int occ = a->key_count > 0 ? rows_occupancy(a->head_dim, a->dtype, pl.smem, (pl.wpg + 1) * 32) : 0;
@@ -2541,14 +2545,24 @@ int direct_occupancy(int hd, int dtype) {
 // (18.5 against 21.1 us), and at head_dim 128 the TMA ring keeps more bytes
 // in flight per SM than the registers can (C2 decode 30.1 against 33.4 us).
 constexpr int kDirAutoMaxKeys = 1280;
+// ... except for mid-sized batches of such rows: 0.5B-shaped draft decode
+// over C4 contexts (mean ~720 keys) measured 29.7 against 35.5 us at 256
+// sequences and 48.7 against 77.4 us at 512 for the TMA kernel, while the
+// register-direct kernel stays ahead at 64 (12.3 against 14.3 us) and at
+// 1024 sequences (111 against 131 us).  Between these key counts the TMA
+// kernel runs.
+constexpr int64_t kDirMidKeysLo = 160 * 1024;
+constexpr int64_t kDirMidKeysHi = 560 * 1024;
 bool direct_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->mma_layout == 2 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->chunk * (a->Hq / a->Hkv) > kDirCols) return false;
     const void* k = a->k_pool ? a->k_pool : a->k_dense;
     const void* v = a->k_pool ? a->v_pool : a->v_dense;
     if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) return false;
-    return a->mma_layout == 3 || (a->chunk == 1 && a->head_dim == 64 && a->key_count > 0 &&
-                                  a->key_count <= (int64_t)kDirAutoMaxKeys * a->B);
+    if (a->mma_layout == 3) return true;
+    const bool mid = a->key_count > kDirMidKeysLo && a->key_count <= kDirMidKeysHi;
+    return a->chunk == 1 && a->head_dim == 64 && a->key_count > 0 &&
+           a->key_count <= (int64_t)kDirAutoMaxKeys * a->B && !mid;
 }
 
 Plan make_direct_plan(const sdl_attn_args* a) {
@@ -2847,6 +2861,7 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.g_cta = pl.g_cta; tp.wpg = pl.wpg; tp.ncoltiles = pl.ncoltiles;
         tp.stage_bytes = pl.stage_bytes;
         tp.ring_bytes = pl.ring_bytes;
+        tp.stages = pl.stages;
         tp.cluster = pl.cluster ? 1 : 0;
         tp.scale_log2 = a->scale * 1.4426950408889634f;
         tp.o_part = a->workspace;

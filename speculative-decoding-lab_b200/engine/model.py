@@ -310,7 +310,8 @@ class PagedLMMixin:
     logits agree with the eager path to rounding, not bit for bit.
     """
 
-    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256)
+    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512,
+                     640, 768, 896, 1024, 1280, 1536)
 
     def enable_cuda_graphs(self, enabled: bool = True) -> None:
         self._graphs_enabled = bool(enabled)

@@ -108,6 +108,12 @@ class SpeculativePagedScheduler(PagedScheduler):
         # optional observer of every round: called with (sequence ids, target
         # start positions, draft lengths) before the round's first launch
         self.round_hook: Optional[Callable[[List[int], List[int], List[int]], None]] = None
+        # What a full KV pool does: "raise" (the reference: BlockExhaustedError,
+        # engine/kv.py:61-66) or "recompute" -- admit only what fits, and
+        # before a round that would not fit, park the most recently admitted
+        # sequences (their blocks freed) and re-prefill them later.
+        self.preemption = "raise"
+        self.preemptions = 0  # sequences parked by the last run
 
     # ------------------------------------------------------------ admission
     def _flush_arrivals(self, arrivals: List[WorkloadRequest], when: int, result: SchedulerResult,
@@ -145,6 +151,94 @@ class SpeculativePagedScheduler(PagedScheduler):
             seq.generated.append(int(tok[0].item()))
         seq.prefilled = True
         return watch.elapsed_ms
+
+    # ------------------------------------------------------------ preemption
+    def _blocks(self, kv: PagedKVCache, tokens: int) -> int:
+        return -(-int(tokens) // kv.block_size)
+
+    def _round_need(self, seqs: Seq[Sequence]) -> tuple:
+        """Blocks a round of ``seqs`` can take from each pool at most: gamma+1
+        target positions, gamma draft positions and the draft catch-up
+        (from the caches' host shadows: no device access)."""
+        g1 = self.gamma + 1
+        bt, bd = self.kv.block_size, self.draft_kv.block_size
+        lt, nbt = self.kv._h_len, self.kv._h_nb
+        ld, nbd = self.draft_kv._h_len, self.draft_kv._h_nb
+        nt = nd = 0
+        for s in seqs:
+            i = s.sid
+            nt += max(0, -(-(lt[i] + g1) // bt) - nbt[i])
+            nd += max(0, -(-(ld[i] + g1) // bd) - nbd[i])
+        return nt, nd
+
+    def _fits(self, need_t: int, need_d: int) -> bool:
+        return need_t <= self.kv.allocator._h_free and need_d <= self.draft_kv.allocator._h_free
+
+    def _context_need(self, tokens: int) -> tuple:
+        """Blocks a sequence of ``tokens`` cached positions needs to join a round."""
+        n = tokens + self.gamma + 1
+        return self._blocks(self.kv, n), self._blocks(self.draft_kv, n)
+
+    def _park(self, seq: Sequence) -> None:
+        """Preempt ``seq``: free its blocks in both pools; it keeps its tokens."""
+        self.kv.clear(seq.sid)
+        self.draft_kv.clear(seq.sid)
+        self.preemptions += 1
+
+    def _recompute(self, seq: Sequence) -> None:
+        """Re-prefill a parked sequence's prompt and generated tokens but the
+        last (whose K/V a round writes), restoring the cache invariant
+        ``seq_len == len(prompt) + len(generated) - 1``; nothing is sampled."""
+        dev = self.model.device
+        tail = _lib.to_device([list(seq.generated[:-1])], torch.long, dev)
+        if isinstance(seq.prompt_ids, torch.Tensor):
+            head = seq.prompt_ids.to(dev, torch.long).reshape(1, -1)
+        else:
+            head = _lib.to_device([list(seq.prompt_ids)], torch.long, dev)
+        ids = torch.cat((head, tail), dim=1)
+        n = ids.shape[1]
+        self.model.prefill(ids, self.kv, [seq.sid], [n])
+        self.draft_model.prefill(ids, self.draft_kv, [seq.sid], [n])
+
+    def _admit_fitting(self, queue: List[WorkloadRequest], parked: List[Sequence], running: List[Sequence],
+                       when: int, result: SchedulerResult, stream: Optional[UniformStream]) -> None:
+        """Recompute policy: re-admit parked sequences, then queued arrivals,
+        in order, while each fits beside the running round's needs."""
+        # the pools' free counts drop by what a sequence holds once it is
+        # in; its round need on top of that is what it has not reserved yet
+        need_t, need_d = self._round_need(running)
+        while parked:
+            t, d = self._context_need(len(parked[0].prompt_ids) + len(parked[0].generated) - 1)
+            if not self._fits(need_t + t, need_d + d):
+                return
+            seq = parked.pop(0)
+            self._recompute(seq)
+            rt, rd = self._round_need([seq])
+            need_t, need_d = need_t + rt, need_d + rd
+            running.append(seq)
+        while queue:
+            t, d = self._context_need(len(queue[0].prompt))
+            if not self._fits(need_t + t, need_d + d):
+                return
+            seq = self._flush_arrivals([queue.pop(0)], when, result, stream)[0]
+            rt, rd = self._round_need([seq])
+            need_t, need_d = need_t + rt, need_d + rd
+            running.append(seq)
+
+    def _make_room(self, running: List[Sequence], parked: List[Sequence]) -> List[Sequence]:
+        """Recompute policy: park the most recently admitted sequences until
+        the round fits both pools; returns the sequences that run."""
+        running = list(running)
+        need_t, need_d = self._round_need(running)
+        while running and not self._fits(need_t, need_d):
+            victim = max(running, key=lambda s: s.sid)
+            vt, vd = self._round_need([victim])
+            running.remove(victim)
+            self._park(victim)  # frees what it held: the free counts grow
+            need_t, need_d = need_t - vt, need_d - vd
+            parked.append(victim)
+            parked.sort(key=lambda s: s.sid)
+        return running
 
     # ------------------------------------------------------------ start-up
     def capture_graphs(self) -> int:
@@ -192,25 +286,48 @@ class SpeculativePagedScheduler(PagedScheduler):
             def clock():
                 return (time.perf_counter() - t0) if wall else step
 
+            recompute = self.preemption == "recompute"
+            if self.preemption not in ("raise", "recompute"):
+                raise ValueError("preemption must be 'raise' or 'recompute'")
+            self.preemptions = 0
+            queue: List[WorkloadRequest] = []  # arrived, not admitted (recompute policy)
+            parked: List[Sequence] = []        # preempted, waiting to be recomputed
+
+            def live() -> List[Sequence]:
+                held = {s.sid for s in parked}
+                return [s for s in result.sequences if not s.finished and s.sid not in held]
+
+            def admit(due_now: List[WorkloadRequest]) -> None:
+                if not recompute:
+                    if due_now:
+                        self._flush_arrivals(due_now, step, result, stream)
+                    return
+                queue.extend(due_now)
+                self._admit_fitting(queue, parked, live(), step, result, stream)
+
             now = clock()
             due = [r for r in arrivals if r.arrive_time <= now]
             pending = [r for r in arrivals if r.arrive_time > now]
-            self._flush_arrivals(due, step, result, stream)
-            running = [s for s in result.sequences if not s.finished]
-            while running or pending:
-                running = [s for s in result.sequences if not s.finished]
+            admit(due)
+            running = live()
+            while running or pending or queue or parked:
+                running = live()
+                if recompute and running:
+                    running = self._make_room(running, parked)
                 if running:
                     self._spec_step(running, result, stream)
                     result.total_forwards += 1
+                elif queue or parked:
+                    # nothing runs and the oldest waiting request still does not fit
+                    raise _exhausted(self.kv.capacity)
                 elif wall and pending:
                     time.sleep(max(0.0, pending[0].arrive_time - clock()))
                 step += 1
                 now = clock()
                 due = [r for r in pending if r.arrive_time <= now]
                 pending = [r for r in pending if r.arrive_time > now]
-                if due:
-                    self._flush_arrivals(due, step, result, stream)
-                running = [s for s in result.sequences if not s.finished]
+                admit(due)
+                running = live()
                 result.batch_hist.append(len(running))
                 result.block_util_hist.append(self.kv.block_utilization)
                 if self.kv.num_allocated_blocks > result.kv_peak_blocks:

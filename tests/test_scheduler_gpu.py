@@ -160,3 +160,39 @@ def test_static_greedy_matches_continuous_and_metrics():
     assert payload["generated_tokens"] > 0 and payload["steps"] >= 1
     assert payload["throughput_tokens_per_s"] is not None
     assert 0.0 < payload["slot_utilization"] <= 1.0
+
+
+def test_recompute_preemption_serves_c1_in_a_small_pool():
+    """A pool too small for the C1 batch: the reference's policy raises
+    BlockExhaustedError; the recompute policy admits what fits, parks the
+    most recently admitted sequences before a round that would not fit,
+    re-prefills them later, and finishes every request with the greedy
+    tokens of the roomy run (recomputed K/V hold the same values)."""
+    from engine.kv import BlockExhaustedError
+
+    g = load_json("c1_spec.json")
+    run = g["runs"]["greedy"]
+    C1 = workloads.C1
+    target = _c1_model("c1-target", C1["target_seed"])
+    draft = _c1_model("c1-draft", C1["draft_seed"])
+    reqs = [WorkloadRequest(prompt=ids, max_new_tokens=n, arrive_time=a) for ids, n, a in workloads.c1_requests(0)]
+
+    def make(policy, blocks):
+        cfg = EngineConfig(block_size=C1["block_size"], max_num_blocks=blocks)
+        sched = SpeculativePagedScheduler(target, build_kv(target, cfg, DEV), draft, build_kv(draft, cfg, DEV), cfg,
+                                          SpecSampling(temperature=0.0), C1["gamma"])
+        sched.preemption = policy
+        return sched
+
+    with pytest.raises(BlockExhaustedError):
+        make("raise", 20).run_spec_continuous(reqs, seed=0, measure=False)
+    sched = make("recompute", 20)
+    res = sched.run_spec_continuous(reqs, seed=0, measure=False)
+    assert sched.preemptions > 0
+    assert [s.generated for s in res.sequences] == run["generated"]
+    assert sched.kv.num_allocated_blocks == 0 and sched.draft_kv.num_allocated_blocks == 0
+    sched.kv.check_errors()
+    sched.draft_kv.check_errors()
+    # a single request larger than the whole pool cannot be served either way
+    with pytest.raises(BlockExhaustedError):
+        make("recompute", 3).run_spec_continuous(reqs[:1], seed=0, measure=False)
