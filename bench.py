@@ -898,6 +898,8 @@ def main(argv=None) -> int:
     ap.add_argument("--requests", type=int, default=2048,
                     help="c4: requests in the whole job's arrival stream (the config's 2048)")
     ap.add_argument("--eager", action="store_true", help="c4: run the model forwards eagerly instead of CUDA graphs")
+    ap.add_argument("--no-batch-prefill", action="store_true",
+                    help="c4: prefill same-round arrivals one by one (graph replays) instead of one chunked batch")
     ap.add_argument("--layers", type=int, default=None,
                     help="fewer layers only for profiling captures (default: the workload's model depth)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (C2: 64, C3: 32)")
@@ -1542,6 +1544,8 @@ def main_c4(args) -> int:
                       "preemption when a round would not fit (per_rank.preempted counts it)",
            "forwards": "eager" if args.eager else "CUDA-graph replays (batch x key-span buckets, all captured "
                                                   "before the warm-up)",
+           "admission": ("one prefill per arrival" if args.no_batch_prefill else
+                         "same-round arrivals prefilled together in 128-token chunks (one forward per model)"),
            "warmup": "{} requests of a different stream (seed {})".format(max(1, (total * W) // K), args.seed + 1000003),
            "l2": "no flush needed: weights (4.1 GB) and the KV pages of a round are far larger than L2",
            "parallelism": "dp{} (request-sharded, independent engines and KV pools)".format(world)}
@@ -1616,6 +1620,7 @@ def main_c4(args) -> int:
     sched = SpeculativePagedScheduler(target, kv, draft, dkv, ecfg, SpecSampling(temperature=c["temperature"]),
                                       c["gamma"])
     sched.preemption = "recompute"  # a full pool parks and later re-prefills sequences instead of raising
+    sched.batch_prefill = not args.no_batch_prefill
     t_cap = time.perf_counter()
     n_graphs = sched.capture_graphs()
     cap_s = time.perf_counter() - t_cap

@@ -99,13 +99,17 @@ class ForwardPlan:
     (-1 for padded prefill positions); ``batch`` describes the attention rows.
     """
 
-    __slots__ = ("slots", "batch", "positions", "chunk")
+    __slots__ = ("slots", "batch", "positions", "chunk", "append_first")
 
-    def __init__(self, slots: torch.Tensor, batch: AttnBatch, positions: torch.Tensor, chunk: int) -> None:
+    def __init__(self, slots: torch.Tensor, batch: AttnBatch, positions: torch.Tensor, chunk: int,
+                 append_first: bool = False) -> None:
         self.slots = slots
         self.batch = batch
         self.positions = positions
         self.chunk = chunk
+        # rows of one sequence may read each other's new K/V (chunked
+        # prefill): every layer stores all new rows before it attends
+        self.append_first = append_first
 
 
 def plan_decode(kv: PagedKVCache, seq_ids: Sequence[int], ctx_lengths: Sequence[int],
@@ -150,6 +154,10 @@ def paged_attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv: PagedKVC
     first) -- one fused call; the positions were reserved by the plan."""
     B = q.shape[0]
     q4 = q.reshape(B, plan.chunk, q.shape[-2], q.shape[-1])
+    if plan.append_first:
+        kv.append(layer, plan.slots, k.reshape(B * plan.chunk, k.shape[-2], k.shape[-1]),
+                  v.reshape(B * plan.chunk, v.shape[-2], v.shape[-1]))
+        return paged_attention(q4, kv, layer, plan.batch)
     return paged_attention(q4, kv, layer, plan.batch, k_new=k.reshape(B * plan.chunk, -1),
                            v_new=v.reshape(B * plan.chunk, -1))
 
@@ -585,6 +593,63 @@ class PagedLMMixin:
         hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
         last = _lib.to_device([int(x) - 1 for x in seq_lengths], torch.long, self.device)
         h_last = hidden[torch.arange(B, device=self.device), last]
+        return self._logits(h_last)
+
+    PREFILL_CHUNK = 128
+
+    def prefill_batch(self, prompts: Sequence, kv: PagedKVCache, seq_ids: Sequence[int]) -> torch.Tensor:
+        """Prefill several prompts (lists of ids or 1-D id tensors) of
+        registered, empty sequences in one forward; returns first-token
+        logits ``(B, V)``.
+
+        Every prompt is cut into PREFILL_CHUNK-token chunks and each chunk is
+        one row of an extend-attention batch: row j of chunk c attends
+        positions ``0 .. c*CHUNK + j`` of its own sequence, the earlier
+        chunks' K/V coming from the pool -- so each layer stores all the new
+        K/V rows (one append launch) before it attends.  The GEMMs run over
+        the chunks, padded only in each prompt's last chunk.  Positions are
+        reserved in the reference's order (sequence by sequence)."""
+        self.forward_calls += 1
+        C = self.PREFILL_CHUNK
+        dev = self.device
+        lens = [int(len(p)) for p in prompts]
+        B = len(lens)
+        slots = kv.reserve(seq_ids, [0] * B, lens)
+        rows, starts, valid, src, idx = [], [], [], [], []
+        off = 0
+        last_row = []
+        for i, L in enumerate(lens):
+            for c0 in range(0, L, C):
+                n = min(C, L - c0)
+                rows.append(int(seq_ids[i]))
+                starts.append(c0)
+                valid.append(n)
+                idx.append((off + c0, n))
+            last_row.append((len(rows) - 1, valid[-1] - 1))
+            off += L
+        R = len(rows)
+        # token ids and the slot of every (row, position), -1 past a chunk's end
+        pieces = [p.to(dev, torch.long).reshape(-1) if isinstance(p, torch.Tensor)
+                  else _lib.to_device(list(p), torch.long, dev) for p in prompts]
+        flat_ids = torch.cat(pieces) if B > 1 else pieces[0]
+        gather = torch.full((R, C), -1, dtype=torch.long)
+        for r, (o, n) in enumerate(idx):
+            gather[r, :n] = torch.arange(o, o + n)
+        gather = gather.to(dev, non_blocking=True)
+        mask = gather >= 0
+        safe = gather.clamp(min=0)
+        ids = torch.where(mask, flat_ids[safe], torch.zeros_like(safe))
+        grid = torch.where(mask, slots[safe].to(torch.int32), torch.full_like(safe, -1, dtype=torch.int32))
+        packed = _lib.i32(rows + starts + valid, dev)
+        batch = AttnBatch(packed[:R], packed[R:2 * R], max(lens), packed[2 * R:],
+                          key_count=sum(s_ + C for s_ in starts))
+        positions = packed[R:2 * R].long().unsqueeze(1) + torch.arange(C, device=dev).unsqueeze(0)
+        plan = ForwardPlan(grid.reshape(-1), batch, positions, C, append_first=True)
+        hidden = self.embed_tokens(ids)
+        cos, sin = self._rope(positions)
+        hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+        sel = _lib.to_device([r * C + j for r, j in last_row], torch.long, dev)
+        h_last = hidden.reshape(R * C, -1).index_select(0, sel)
         return self._logits(h_last)
 
     def decode(self, input_ids: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],

@@ -114,26 +114,86 @@ class SpeculativePagedScheduler(PagedScheduler):
         # sequences (their blocks freed) and re-prefill them later.
         self.preemption = "raise"
         self.preemptions = 0  # sequences parked by the last run
+        # prefill same-round arrivals together (16-bit models; see _flush_batched)
+        self.batch_prefill = True
 
     # ------------------------------------------------------------ admission
+    PREFILL_BATCH_TOKENS = 16384  # prompt tokens one batched prefill takes at most
+
+    def _batch_prefill_ok(self) -> bool:
+        """Same-round arrivals are prefilled together (``prefill_batch``) for
+        16-bit models; fp32 models keep the reference's one-by-one prefill,
+        whose reductions the parity runs pin."""
+        if not self.batch_prefill:
+            return False
+        for m in (self.model, self.draft_model):
+            emb = getattr(m, "embed_tokens", None)
+            if not hasattr(m, "prefill_batch") or emb is None or emb.weight.dtype not in (torch.bfloat16,
+                                                                                          torch.float16):
+                return False
+        return True
+
     def _flush_arrivals(self, arrivals: List[WorkloadRequest], when: int, result: SchedulerResult,
                         stream: Optional[UniformStream]) -> List[Sequence]:
+        if len(arrivals) > 1 and self._batch_prefill_ok():
+            return self._flush_batched(arrivals, when, result, stream)
         admitted: List[Sequence] = []
         for request in arrivals:
-            seq = Sequence(
-                sid=self._next_sid,
-                # a CUDA tensor of ids is taken as is (prompts staged in HBM)
-                prompt_ids=(request.prompt if isinstance(request.prompt, torch.Tensor)
-                            else self.model.encode(request.prompt)),
-                max_new_tokens=request.max_new_tokens,
-                arrive_time=request.arrive_time,
-                admit_step=when,
-            )
-            self._next_sid += 1
-            self.kv.add_sequence(seq.sid)
-            self.draft_kv.add_sequence(seq.sid)
+            seq = self._new_sequence(request, when)  # a CUDA tensor of ids is taken as is (prompts staged in HBM)
             seq.ttft_ms = self._prefill_spec_one(seq, result, stream)
             admitted.append(seq)
+        result.sequences.extend(admitted)
+        return admitted
+
+    def _new_sequence(self, request: WorkloadRequest, when: int) -> Sequence:
+        seq = Sequence(
+            sid=self._next_sid,
+            prompt_ids=(request.prompt if isinstance(request.prompt, torch.Tensor)
+                        else self.model.encode(request.prompt)),
+            max_new_tokens=request.max_new_tokens,
+            arrive_time=request.arrive_time,
+            admit_step=when,
+        )
+        self._next_sid += 1
+        self.kv.add_sequence(seq.sid)
+        self.draft_kv.add_sequence(seq.sid)
+        return seq
+
+    def _flush_batched(self, arrivals: List[WorkloadRequest], when: int, result: SchedulerResult,
+                       stream: Optional[UniformStream]) -> List[Sequence]:
+        """Admit several arrivals with one chunked prefill per model (groups of
+        at most PREFILL_BATCH_TOKENS prompt tokens): the same positions,
+        allocation order and first-token draws (one uniform per sequence, in
+        arrival order) as admitting them one by one."""
+        admitted: List[Sequence] = []
+        group: List[Sequence] = []
+        tokens = 0
+
+        def flush() -> None:
+            watch = Stopwatch()
+            with watch:
+                prompts = [s.prompt_ids for s in group]
+                sids = [s.sid for s in group]
+                logits = self.model.prefill_batch(prompts, self.kv, sids)
+                toks = self._next_tokens(logits, stream)
+                self.draft_model.prefill_batch(prompts, self.draft_kv, sids)
+                first = toks.tolist()
+            for s, t in zip(group, first):
+                s.generated.append(int(t))
+                s.prefilled = True
+                s.ttft_ms = watch.elapsed_ms
+
+        for request in arrivals:
+            seq = self._new_sequence(request, when)
+            n = len(seq.prompt_ids)
+            if group and tokens + n > self.PREFILL_BATCH_TOKENS:
+                flush()
+                group, tokens = [], 0
+            group.append(seq)
+            tokens += n
+            admitted.append(seq)
+        if group:
+            flush()
         result.sequences.extend(admitted)
         return admitted
 
@@ -216,14 +276,15 @@ class SpeculativePagedScheduler(PagedScheduler):
             rt, rd = self._round_need([seq])
             need_t, need_d = need_t + rt, need_d + rd
             running.append(seq)
+        take: List[WorkloadRequest] = []
         while queue:
             t, d = self._context_need(len(queue[0].prompt))
             if not self._fits(need_t + t, need_d + d):
-                return
-            seq = self._flush_arrivals([queue.pop(0)], when, result, stream)[0]
-            rt, rd = self._round_need([seq])
-            need_t, need_d = need_t + rt, need_d + rd
-            running.append(seq)
+                break
+            take.append(queue.pop(0))
+            need_t, need_d = need_t + t, need_d + d  # its reservation plus its round need
+        if take:
+            running.extend(self._flush_arrivals(take, when, result, stream))
 
     def _make_room(self, running: List[Sequence], parked: List[Sequence]) -> List[Sequence]:
         """Recompute policy: park the most recently admitted sequences until

@@ -189,3 +189,38 @@ def test_wall_clock_admission_waits_for_arrivals():
     assert [s.arrive_time for s in res.sequences] == [0.0, 0.3, 0.6]
     with pytest.raises(ValueError):
         sched.run_spec_continuous(reqs, seed=0, arrival_clock="tick")
+
+
+def test_batched_chunked_prefill_matches_one_by_one():
+    """``prefill_batch`` (prompts cut into 128-token chunks, one
+    extend-attention row per chunk, each layer's K/V stored before it
+    attends) gives the first-token logits and the stored K/V of one-by-one
+    prefills to bf16 rounding, with the same block tables (reference
+    allocation order)."""
+    m = _model("c1-target", 3, torch.bfloat16)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (5, 128, 129, 300)]
+    cfg = EngineConfig(block_size=16, max_num_blocks=256)
+    kv1 = build_kv(m, cfg, DEV, max_seqs=4)
+    kv2 = build_kv(m, cfg, DEV, max_seqs=4)
+    one = []
+    for sid, p in enumerate(prompts):
+        kv1.add_sequence(sid)
+        one.append(m.prefill(torch.tensor([p], device=DEV), kv1, [sid], [len(p)]).float())
+    for sid in range(len(prompts)):
+        kv2.add_sequence(sid)
+    both = m.prefill_batch([prompts[0], torch.tensor(prompts[1], device=DEV)] + prompts[2:], kv2,
+                           list(range(len(prompts)))).float()
+    assert both.shape == (4, 1024)
+    for sid in range(len(prompts)):
+        a, b = one[sid][0], both[sid]
+        assert (a - b).abs().max().item() <= 5e-2 * a.abs().max().item(), sid
+        for layer in range(m.num_layers):
+            ke = gather_ctx(kv1, layer, sid, len(prompts[sid]))
+            kb = gather_ctx(kv2, layer, sid, len(prompts[sid]))
+            for x, y in zip(ke, kb):
+                assert (x.float() - y.float()).abs().max().item() <= 5e-2 * x.float().abs().max().item()
+    assert kv1.block_tables == kv2.block_tables
+    assert kv1.seq_lengths == kv2.seq_lengths
+    kv1.check_errors()
+    kv2.check_errors()
