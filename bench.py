@@ -898,6 +898,9 @@ def main(argv=None) -> int:
     ap.add_argument("--requests", type=int, default=2048,
                     help="c4: requests in the whole job's arrival stream (the config's 2048)")
     ap.add_argument("--eager", action="store_true", help="c4: run the model forwards eagerly instead of CUDA graphs")
+    ap.add_argument("--kernel-table", type=str, default=None, metavar="A:B",
+                    help="c4: record rounds A..B of the warm-up run with torch.profiler (CUPTI) and print each "
+                         "kernel's time per round and share of the GPU time to stderr")
     ap.add_argument("--no-batch-prefill", action="store_true",
                     help="c4: prefill same-round arrivals one by one (graph replays) instead of one chunked batch")
     ap.add_argument("--layers", type=int, default=None,
@@ -1472,6 +1475,38 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw
             "mean_ctx": round(sum(ctx) / max(1, B), 1)}
 
 
+def _print_kernel_table(p, rounds, wall_s, b0, b1) -> None:
+    """Kernel time per round and share of the GPU time (CUPTI activity of a
+    torch.profiler window), with the GPU-busy fraction of the window."""
+    import collections
+
+    import torch
+
+    evs = [e for e in p.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    spans = sorted((e.time_range.start, e.time_range.end) for e in evs)
+    busy, cur = 0.0, None
+    for a, b in spans:
+        if cur is None or a > cur[1]:
+            if cur:
+                busy += cur[1] - cur[0]
+            cur = [a, b]
+        else:
+            cur[1] = max(cur[1], b)
+    if cur:
+        busy += cur[1] - cur[0]
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in evs:
+        k = e.name.replace("(anonymous namespace)::", "").split("(")[0][:80]
+        agg[k][0] += 1
+        agg[k][1] += e.time_range.end - e.time_range.start
+    tot = sum(v[1] for v in agg.values()) or 1.0
+    out = sys.stderr
+    print("kernel table: {} rounds (batch {} -> {}), wall {:.2f} ms/round, GPU busy {:.2f} ms/round ({:.0%})".format(
+        rounds, b0, b1, 1e3 * wall_s / rounds, busy / 1e3 / rounds, busy / 1e3 / (1e3 * wall_s)), file=out)
+    for k, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:30]:
+        print("  {:8.3f} ms/round {:5.1f}%  {:6d} launches  {}".format(t / 1e3 / rounds, 100 * t / tot, n, k), file=out)
+
+
 def main_c4attn(args) -> int:
     """C4's attention ops alone (one GPU): the 0.5B-shaped draft decode
     (14 q / 2 kv heads, head_dim 64) and the 1.5B-shaped 5-row verify (12 q
@@ -1648,10 +1683,32 @@ def main_c4(args) -> int:
         sched._next_sid = first_sid
         return sched.run_spec_continuous(reqs, seed=seed, measure=False, arrival_clock="wall").generated_tokens
 
+    prof = {}
+    if args.kernel_table:
+        lo, hi = (int(x) for x in args.kernel_table.split(":"))
+
+        def prof_hook(sids, starts, d0):
+            prof["n"] = prof.get("n", 0) + 1
+            if prof["n"] == lo:
+                torch.cuda.synchronize(device)
+                prof["p"] = torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA])
+                prof["p"].__enter__()
+                prof["t0"] = time.perf_counter()
+                prof["b0"] = len(sids)
+            elif prof["n"] == hi:
+                torch.cuda.synchronize(device)
+                prof["wall"] = time.perf_counter() - prof["t0"]
+                prof["p"].__exit__(None, None, None)
+                prof["b1"] = len(sids)
+
+        sched.round_hook = prof_hook
     serve(requests_of(warm, False), 7000)
+    sched.round_hook = None
     torch.cuda.synchronize(device)
     kv.check_errors()
     dkv.check_errors()
+    if "wall" in prof:
+        _print_kernel_table(prof["p"], hi - lo, prof["wall"], prof["b0"], prof["b1"])
 
     # timed: prompts staged in HBM before the region (the "inputs resident" figure)
     staged = requests_of(timed, True)

@@ -354,24 +354,38 @@ class SpeculativePagedScheduler(PagedScheduler):
             queue: List[WorkloadRequest] = []  # arrived, not admitted (recompute policy)
             parked: List[Sequence] = []        # preempted, waiting to be recomputed
 
+            active: List[Sequence] = []  # admitted and not finished (parked ones included)
+            nxt = 0                       # arrivals[:nxt] have arrived
+
+            def take_due(now_: float) -> List[WorkloadRequest]:
+                nonlocal nxt
+                k = nxt
+                while k < len(arrivals) and arrivals[k].arrive_time <= now_:
+                    k += 1
+                due_ = arrivals[nxt:k]
+                nxt = k
+                return due_
+
             def live() -> List[Sequence]:
+                active[:] = [s for s in active if not s.finished]
+                if not parked:
+                    return list(active)
                 held = {s.sid for s in parked}
-                return [s for s in result.sequences if not s.finished and s.sid not in held]
+                return [s for s in active if s.sid not in held]
 
             def admit(due_now: List[WorkloadRequest]) -> None:
+                n0 = len(result.sequences)
                 if not recompute:
                     if due_now:
                         self._flush_arrivals(due_now, step, result, stream)
-                    return
-                queue.extend(due_now)
-                self._admit_fitting(queue, parked, live(), step, result, stream)
+                else:
+                    queue.extend(due_now)
+                    self._admit_fitting(queue, parked, live(), step, result, stream)
+                active.extend(result.sequences[n0:])
 
-            now = clock()
-            due = [r for r in arrivals if r.arrive_time <= now]
-            pending = [r for r in arrivals if r.arrive_time > now]
-            admit(due)
+            admit(take_due(clock()))
             running = live()
-            while running or pending or queue or parked:
+            while running or nxt < len(arrivals) or queue or parked:
                 running = live()
                 if recompute and running:
                     running = self._make_room(running, parked)
@@ -381,13 +395,10 @@ class SpeculativePagedScheduler(PagedScheduler):
                 elif queue or parked:
                     # nothing runs and the oldest waiting request still does not fit
                     raise _exhausted(self.kv.capacity)
-                elif wall and pending:
-                    time.sleep(max(0.0, pending[0].arrive_time - clock()))
+                elif wall and nxt < len(arrivals):
+                    time.sleep(max(0.0, arrivals[nxt].arrive_time - clock()))
                 step += 1
-                now = clock()
-                due = [r for r in pending if r.arrive_time <= now]
-                pending = [r for r in pending if r.arrive_time > now]
-                admit(due)
+                admit(take_due(clock()))
                 running = live()
                 result.batch_hist.append(len(running))
                 result.block_util_hist.append(self.kv.block_utilization)
