@@ -901,6 +901,8 @@ def main(argv=None) -> int:
     ap.add_argument("--kernel-table", type=str, default=None, metavar="A:B",
                     help="c4: record rounds A..B of the warm-up run with torch.profiler (CUPTI) and print each "
                          "kernel's time per round and share of the GPU time to stderr")
+    ap.add_argument("--exact-plan", action="store_true",
+                    help="c4attn: plan with the exact key count instead of the captured forwards' ragged plan")
     ap.add_argument("--no-batch-prefill", action="store_true",
                     help="c4: prefill same-round arrivals one by one (graph replays) instead of one chunked batch")
     ap.add_argument("--layers", type=int, default=None,
@@ -1411,12 +1413,17 @@ def main_c5(args) -> int:
     return 0
 
 
-def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw):
+def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, span_cap=None, **akw):
     """One attention op as a model forward launches it -- the K/V rows of
     ``chunk`` new positions stored inside the paged attention launch -- over
     contexts ``ctx`` (a random-permutation pool of exactly those pages), timed
     with CUDA events over ``reps`` replays of a graph of ``layers`` launches.
-    Returns the kernel name, ms per launch and algorithmic bytes per launch."""
+    With ``span_cap`` (the block-table width in tokens of the serving pools)
+    the call carries what a captured model forward passes: the key-span
+    bucket as max_limit and no key count (ragged rows, key_count < 0), so the
+    plan is the one the C4 run's graphs replay; without it, the exact key
+    count.  Returns the kernel name, ms per launch and algorithmic bytes per
+    launch."""
     import torch
 
     from engine.attention import AttnBatch, attention_kernel, attention_launches, paged_attention
@@ -1426,6 +1433,13 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw
     B = len(ctx)
     cap = sum(-(-(x + chunk) // bs) for x in ctx) + B
     width = max(-(-(x + chunk) // bs) for x in ctx) + 1
+    span = None
+    if span_cap is not None:
+        span = 1024
+        while span < max(ctx) + chunk:
+            span *= 2
+        span = min(span, int(span_cap))
+        width = max(width, -(-span // bs))
     kv = PagedKVCache(layers, Hkv, d, cap, bs, device, torch.bfloat16, max_blocks_per_seq=width, max_seqs=B)
     g = torch.Generator(device="cpu")
     g.manual_seed(seed)
@@ -1444,6 +1458,8 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw
     vn = torch.randn((layers, B * chunk, Hkv, d), generator=gd, device=device).to(bf)
     out = torch.empty_like(q)
     batch = AttnBatch.from_lists(device, sids, ctx, chunk)
+    if span is not None:
+        batch = AttnBatch(batch.rows, batch.starts, span, key_count=-1)
     kv.reserve(sids, ctx, [chunk] * B)
 
     def run():
@@ -1472,7 +1488,8 @@ def _time_attention_op(device, ctx, chunk, Hq, Hkv, d, layers, seed, reps, **akw
     launches = attention_launches(q[0], kv, batch, k_new=kn[0], v_new=vn[0], **akw)
     del graph
     return {"kernel": kern, "ms": ms, "bytes": nbytes, "launches_per_op": launches, "batch": B,
-            "mean_ctx": round(sum(ctx) / max(1, B), 1)}
+            "mean_ctx": round(sum(ctx) / max(1, B), 1), "plan": "exact key count" if span is None else
+            "ragged rows, span {} (the captured forwards' plan)".format(span)}
 
 
 def _print_kernel_table(p, rounds, wall_s, b0, b1) -> None:
@@ -1530,10 +1547,14 @@ def main_c4attn(args) -> int:
     akw = dict(use_umma=UMMA_FLAG[args.attn_kernel], mma_layout=LAYOUT_FLAG[args.mma_layout])
     hbm, _ = _peaks()
     layers = args.layers or 8
+    # the C4 pools' block-table width in tokens (prompt cap + output cap), as the run's graphs see it
+    span_cap = None if args.exact_plan else ((c["prompt_cap"] + c["out_hi"] + 16) // 16 + 2) * 16
     for name, chunk, Hq, d in (("draft decode (0.5B shape)", 1, 14, 64), ("5-row verify (1.5B shape)", 5, 12, 128)):
-        r = _time_attention_op(device, ctx, chunk, Hq, 2, d, layers, args.seed + 7, max(1, args.steps), **akw)
+        r = _time_attention_op(device, ctx, chunk, Hq, 2, d, layers, args.seed + 7, max(1, args.steps),
+                               span_cap=span_cap, **akw)
         gbs = r["bytes"] / (r["ms"] * 1e-3) / 1e9
-        print(json.dumps({"op": name, "batch": args.batch, "mean_ctx": r["mean_ctx"], "kernel": ATTN_KERNELS[r["kernel"]],
+        print(json.dumps({"op": name, "batch": args.batch, "mean_ctx": r["mean_ctx"], "plan": r["plan"],
+                          "kernel": ATTN_KERNELS[r["kernel"]],
                           "us_per_launch": round(r["ms"] * 1e3, 2), "algorithmic_mb": round(r["bytes"] / 1e6, 1),
                           "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 4)}), flush=True)
     return 0
@@ -1762,10 +1783,11 @@ def main_c4(args) -> int:
     torch.cuda.synchronize(device)
     torch.cuda.empty_cache()
     reps = 5
+    span_cap = width * 16  # the pools' block-table width in tokens caps the graphs' key-span buckets
     draft_op = _time_attention_op(device, d0_max, 1, dcfg.num_attention_heads, dcfg.num_key_value_heads,
-                                  dcfg.head_dim, dcfg.num_hidden_layers, args.seed + 5, reps)
+                                  dcfg.head_dim, dcfg.num_hidden_layers, args.seed + 5, reps, span_cap=span_cap)
     verify_op = _time_attention_op(device, starts_max, chunk, tcfg.num_attention_heads, tcfg.num_key_value_heads,
-                                   tcfg.head_dim, tcfg.num_hidden_layers, args.seed + 6, reps)
+                                   tcfg.head_dim, tcfg.num_hidden_layers, args.seed + 6, reps, span_cap=span_cap)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = CpuC4(seed=args.seed).measure(args.cpu_seconds)
@@ -1815,7 +1837,7 @@ def main_c4(args) -> int:
                      "frac": round(d_gbs / hbm, 4), "traffic": None,
                      "kernel": names[draft_op["kernel"]] + ": draft decode attention (0.5B shape, 24 layers), "
                                "K/V append fused, on the heaviest round's draft contexts",
-                     "batch": draft_op["batch"], "mean_ctx": draft_op["mean_ctx"],
+                     "batch": draft_op["batch"], "mean_ctx": draft_op["mean_ctx"], "plan": draft_op["plan"],
                      "algorithmic_bytes_per_launch": draft_op["bytes"], "ms_per_launch": round(d_ms, 5),
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
         "verify_roofline": {"bound": "hbm", "achieved": round(v_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -1823,6 +1845,7 @@ def main_c4(args) -> int:
                             "kernel": names[verify_op["kernel"]] + ": 5-row verify attention (1.5B shape, 28 "
                                       "layers), K/V append fused, on the heaviest round's target contexts",
                             "batch": verify_op["batch"], "mean_ctx": verify_op["mean_ctx"],
+                            "plan": verify_op["plan"],
                             "algorithmic_bytes_per_launch": verify_op["bytes"], "ms_per_launch": round(v_ms, 5)},
         "e2e": {"value": round(e2e_sum / (e2e_max * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": round(h2d / K), "d2h_bytes_per_step": round(d2h / K),

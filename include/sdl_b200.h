@@ -207,9 +207,17 @@ typedef struct sdl_attn_args {
     int64_t key_count;        /* 0, or the host's count of keys the call
                                  attends, sum over b of starts[b] + chunk:
                                  the mma.sync plan then sizes its split-K
-                                 grid to one wave of resident CTAs.  Only
-                                 the launch shape depends on it, never the
-                                 result (the grid still covers max_limit) */
+                                 grid to one wave of resident CTAs; or < 0:
+                                 ragged rows of unknown lengths (a plan a
+                                 CUDA graph captures and replays over other
+                                 batches), split into CTAs of at most
+                                 n/16 pages (4..64; n = unsplit CTAs, one
+                                 per sequence and kv-head group), with
+                                 rows on M for head_dim-128 blocks of
+                                 24+ rows and no automatic tcgen05 or
+                                 register-direct kernel.  Only the launch
+                                 shape depends on it, never the result (the
+                                 grid still covers max_limit)              */
     int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
                                  on the MMA M dimension for blocks of at
                                  least 48 query rows per kv head, 16 at

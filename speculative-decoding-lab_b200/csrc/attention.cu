@@ -2251,6 +2251,7 @@ bool umma_applicable(const sdl_attn_args* a) {
     const int rows = a->chunk * (a->Hq / a->Hkv);
     if (rows > kURows || (long)a->B * a->Hkv > kSkMaxPairs) return false;
     if (a->use_umma > 0) return true;
+    if (a->key_count < 0) return false;  // ragged rows of unknown lengths: the mma.sync plans
     // Automatic choice: the mma.sync kernels spend many issue slots per
     // page, so large blocks over long contexts are instruction bound there;
     // the tcgen05 kernel issues the products from one thread.  Measured on
@@ -2458,8 +2459,32 @@ int rows_occupancy(int hd, int dtype, size_t smem, int threads) {
 // SM).  Each work item holds about key_count / B keys and leaves on average
 // half a split of remainder; a second wave for a few CTAs costs more than
 // the per-SM balance smaller splits buy.
+//
+// key_count < 0 declares ragged rows of unknown lengths: a plan captured in
+// a CUDA graph and replayed over other batches, of which only the grid's
+// bounds (B, max_limit) are known.  A one-wave plan sized for max_limit
+// leaves the longest rows of a skewed batch in one CTA each, and those
+// CTAs set the launch's duration; instead no split exceeds about
+// base_ctas / kRaggedSplitDiv pages (4..kRaggedMaxSplitPages), which
+// balances list-scheduled CTAs against per-CTA and merge overhead, and no
+// row takes more than kRaggedMaxSplits splits.  Measured on B200 over
+// C4-shaped batches (contexts floor(lognormal(6, 0.8)) + U[0, 512) tokens,
+// grid sized for an 8192-key span): 5-row verify (12 q / 2 kv heads,
+// head_dim 128, rows on M) 83 / 110 / 136 / 239 us at 256 / 358 / 512 /
+// 1024 sequences against 111 / 145 / 155 / 240 for the exact-count plan and
+// 220 / 214 / 215 / 298 for a one-wave plan at 55 % of the span; draft
+// decode (14 q / 2 kv heads, head_dim 64) 31 / 38-41 / 52 / 84-89 us against
+// 30 / 37 / 48 / 114 and 72 / 103 / 159 / 159.
+constexpr int kRaggedSplitDiv = 16;
+constexpr int kRaggedMaxSplitPages = 64;
+constexpr int kRaggedMaxSplits = 64;
 int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) {
     if (a->pages_per_split > 0) return a->pages_per_split;
+    if (a->key_count < 0) {
+        long pps = std::min<long>(kRaggedMaxSplitPages, std::max<long>(kMinSplitPages, base_ctas / kRaggedSplitDiv));
+        pps = std::max<long>(pps, (max_pages + kRaggedMaxSplits - 1) / kRaggedMaxSplits);
+        return (int)std::min<long>(pps, max_pages);
+    }
     const long target = (long)sm_count() * 4;
     const int nsplit_target = (int)std::max(1L, (target + base_ctas - 1) / base_ctas);
     int pps = std::max(kMinSplitPages, (max_pages + nsplit_target - 1) / nsplit_target);
@@ -2491,8 +2516,11 @@ bool rows_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 2) return true;
     const int rows = a->chunk * (a->Hq / a->Hkv);
     if (rows >= (a->head_dim == 64 ? kRowsMinRows64 : kRowsMinRows128)) return true;
-    return a->head_dim == 128 && rows >= kRowsMinRows128Short && a->key_count > 0 &&
-           a->key_count < (int64_t)kRowsShortKeys * a->B;
+    // ragged rows of unknown lengths (key_count < 0) split at most
+    // kRaggedMaxSplitPages pages per CTA, where rows on M measured ahead
+    // (C4 verify, 30 rows: 110 against 131 us at 358 sequences)
+    return a->head_dim == 128 && rows >= kRowsMinRows128Short &&
+           (a->key_count < 0 || (a->key_count > 0 && a->key_count < (int64_t)kRowsShortKeys * a->B));
 }
 
 Plan make_rows_plan(const sdl_attn_args* a) {

@@ -357,10 +357,18 @@ class PagedLMMixin:
         return None
 
     def _graph_forward(self, input_ids_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
-                       starts: Sequence[int], bucket: int) -> torch.Tensor:
+                       starts: Sequence[int], bucket: int, logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Logits ``(B, chunk, V)`` of positions ``starts[b] + j`` (already
-        reserved) through the captured forward for ``bucket`` rows."""
+        reserved) through the captured forward for ``bucket`` rows.
+
+        With ``graph_head`` False the graphs end at the final norm and the LM
+        head runs after the replay, on all ``bucket`` rows (the shape the
+        captured head would have), writing into ``logits_out`` (at least
+        ``bucket`` rows of ``(chunk, V)``) when given: a caller that keeps
+        several forwards' logits gets them without a copy.  With the head in
+        the graph, ``logits_out`` receives a copy of the logits."""
         B, chunk = input_ids_2d.shape
+        head = bool(getattr(self, "graph_head", True))
         graphs = self.__dict__.setdefault("_graphs", {})
         # key span bucket: the attention plan (split size, kernel choice) is
         # fixed at capture, so graphs are kept per power-of-two bound of the
@@ -371,7 +379,7 @@ class PagedLMMixin:
         while span < need:
             span *= 2
         span = min(span, span_cap)
-        key = (id(kv), chunk, bucket, span)
+        key = (id(kv), chunk, bucket, span) if head else (id(kv), chunk, bucket, span, "headless")
         g = graphs.get(key)
         if g is not None and g.table_ptr != kv._table.data_ptr():
             # the cache grew its block table (more sequence rows): recapture
@@ -394,12 +402,13 @@ class PagedLMMixin:
             s_rows = torch.zeros(bucket, dtype=torch.int32, device=self.device)
             s_starts = torch.zeros(bucket, dtype=torch.int32, device=self.device)
             fill(s_ids, s_rows, s_starts)
-            # the launch shapes follow this capture's lengths (padded rows repeat row 0)
-            keys = sum(int(x) for x in starts) + (bucket - B) * int(starts[0]) + bucket * chunk
-            batch = AttnBatch(s_rows, s_starts, span, key_count=keys)
+            # replays run other lengths than this capture's: the attention
+            # plans are the ones for ragged rows of unknown lengths
+            # (key_count < 0), bounded by the bucket and the span
+            batch = AttnBatch(s_rows, s_starts, span, key_count=-1)
             steps = torch.arange(chunk, device=self.device)
 
-            logits_out = self._graph_logits_buffer(chunk, bucket)
+            shared_logits = self._graph_logits_buffer(chunk, bucket) if head else None
 
             def run() -> torch.Tensor:
                 positions = s_starts.long().unsqueeze(1) + steps.unsqueeze(0)
@@ -407,8 +416,10 @@ class PagedLMMixin:
                 hidden = self.embed_tokens(s_ids)
                 cos, sin = self._rope(positions)
                 hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+                if not head:
+                    return self.norm(hidden)  # the head runs after the replay
                 # the head writes into the logits buffer every graph of this chunk shares
-                return torch.matmul(self.norm(hidden), self.lm_head.weight.t(), out=logits_out)
+                return torch.matmul(self.norm(hidden), self.lm_head.weight.t(), out=shared_logits)
 
             # one eager pass sizes every workspace and stores this call's K/V;
             # the replay below stores the same bytes again
@@ -425,7 +436,17 @@ class PagedLMMixin:
             fill(g.ids, g.rows, g.starts)
         g.graph.replay()
         _lib.count_calls(g.calls)
-        return g.logits[:B]
+        if head:
+            if logits_out is None:
+                return g.logits[:B]
+            dst = logits_out[:B].view(B, chunk, -1)
+            dst.copy_(g.logits[:B])
+            return dst
+        V = self.lm_head.weight.shape[0]
+        dst = logits_out if logits_out is not None else self._graph_logits_buffer(chunk, bucket)
+        dst = dst[:bucket].view(bucket, chunk, V)
+        torch.matmul(g.logits, self.lm_head.weight.t(), out=dst)
+        return dst[:B]
 
     @staticmethod
     def graph_spans(kv: PagedKVCache) -> List[int]:
@@ -653,23 +674,34 @@ class PagedLMMixin:
         return self._logits(h_last)
 
     def decode(self, input_ids: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
-               ctx_lengths: Sequence[int], slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+               ctx_lengths: Sequence[int], slots: Optional[torch.Tensor] = None,
+               logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One token per row at position ``ctx_lengths[b]``; returns ``(B, V)``.
 
         ``slots`` (optional) are positions already reserved by a commit kernel.
+        ``logits_out`` (optional, contiguous ``(R, V)`` with R at least B and at
+        least the graph bucket of B) receives the logits, which are then
+        returned as its first B rows.
         """
         self.forward_calls += 1
-        bucket = self._graph_bucket(len(seq_ids))
+        B = len(seq_ids)
+        bucket = self._graph_bucket(B)
+        if logits_out is not None and (logits_out.shape[0] < max(B, bucket or 0) or not logits_out.is_contiguous()):
+            raise ValueError("logits_out needs max(B, graph bucket) contiguous rows")
         if bucket is not None:
             ctx = [int(c) for c in ctx_lengths]
             if slots is None:
                 kv.reserve(seq_ids, ctx, [1] * len(ctx))
-            return self._graph_forward(input_ids.reshape(-1, 1), kv, seq_ids, ctx, bucket)[:, 0]
+            return self._graph_forward(input_ids.reshape(-1, 1), kv, seq_ids, ctx, bucket, logits_out)[:, 0]
         plan = plan_decode(kv, seq_ids, ctx_lengths, slots)
         hidden = self.embed_tokens(input_ids.to(self.device).reshape(-1))
         cos, sin = self._rope(plan.positions[:, 0])
         hidden = self._run_layers(hidden, kv, plan, cos.unsqueeze(1), sin.unsqueeze(1))
-        return self._logits(hidden)
+        logits = self._logits(hidden)
+        if logits_out is None:
+            return logits
+        logits_out[:B].copy_(logits)
+        return logits_out[:B]
 
     def decode_block(self, input_ids_2d: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
                      start_positions: Sequence[int]) -> torch.Tensor:

@@ -105,6 +105,12 @@ class SpeculativePagedScheduler(PagedScheduler):
         if not 1 <= self.gamma <= 32:
             raise ValueError("gamma must be within [1, 32]")
         self._q_buf: Optional[torch.Tensor] = None
+        # the draft's captured decodes end at the final norm and its LM head
+        # writes each step's logits straight into the round's (gamma, rows, V)
+        # buffer the rejection sampler reads, instead of a shared buffer
+        # copied out after every step
+        if hasattr(draft_model, "_graph_forward"):
+            draft_model.graph_head = False
         # optional observer of every round: called with (sequence ids, target
         # start positions, draft lengths) before the round's first launch
         self.round_hook: Optional[Callable[[List[int], List[int], List[int]], None]] = None
@@ -302,6 +308,22 @@ class SpeculativePagedScheduler(PagedScheduler):
         return running
 
     # ------------------------------------------------------------ start-up
+    def _round_buffer(self, B: int, gamma: int, V: int, dtype: torch.dtype, device: torch.device,
+                      t_slot: Optional[int] = None) -> torch.Tensor:
+        """The round's draft rows, laid out ``(gamma, R, V)`` with R at least
+        B and the draft's graph bucket of B: returns the ``(B, gamma, V)``
+        view the samplers read, or with ``t_slot`` the contiguous ``(R, V)``
+        slice of draft step ``t_slot`` (the draft's LM head output)."""
+        bucket = getattr(self.draft_model, "_graph_bucket", lambda n: None)(B) or B
+        rows = max(B, bucket)
+        buf = self._q_buf
+        if buf is None or buf.shape[0] < gamma or buf.shape[1] < rows or buf.shape[2] != V or buf.dtype != dtype:
+            rows = max(rows, buf.shape[1] if buf is not None and buf.shape[2] == V else 0)
+            self._q_buf = buf = torch.empty((gamma, rows, V), dtype=dtype, device=device)
+        if t_slot is not None:
+            return buf[t_slot]
+        return buf[:gamma, :B].permute(1, 0, 2)
+
     def capture_graphs(self) -> int:
         """Capture every CUDA graph the models can replay in a run (draft
         decode, target verify of gamma+1 rows, both models' prefill, at every
@@ -458,8 +480,17 @@ class SpeculativePagedScheduler(PagedScheduler):
             stream.reserve(gamma * B)
         cur = _lib.to_device([s.generated[-1] for s in running], torch.long, device)
         fused = False
+        V_d = getattr(getattr(draft, "lm_head", None), "weight", None)
+        # plain temperature: each draft step's logits land in step t's slice of
+        # the round buffer, which the fused rejection sampler reads in place
+        direct = (not greedy and V_d is not None and hasattr(draft, "_graph_forward")
+                  and self._plain_temperature(V_d.shape[0]))
         for t in range(gamma):
-            q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0])
+            if direct:
+                qb = self._round_buffer(B, gamma, V_d.shape[0], V_d.dtype, device, t_slot=t)
+                q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0], logits_out=qb)
+            else:
+                q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0])
             result.draft_forward_calls += 1
             if greedy:
                 prop_t = argmax_rows(q_logits)
@@ -469,13 +500,10 @@ class SpeculativePagedScheduler(PagedScheduler):
                 # plain temperature keeps the draft logits (the fused sampler reads
                 # them); filtering keeps the filtered probability rows instead
                 dt = q_logits.dtype if fused else torch.float32
-                if (self._q_buf is None or self._q_buf.shape[0] < B or self._q_buf.shape[2] != V
-                        or self._q_buf.dtype != dt):
-                    rows_cap = max(B, self._q_buf.shape[0] if self._q_buf is not None else 0)
-                    self._q_buf = torch.empty((rows_cap, gamma, V), dtype=dt, device=device)
-                q_probs = self._q_buf[:B]
+                q_probs = self._round_buffer(B, gamma, V, dt, device)
                 if fused:
-                    q_probs[:, t, :].copy_(q_logits.reshape(B, V))
+                    if not direct:
+                        q_probs[:, t, :].copy_(q_logits.reshape(B, V))
                     prop_t = sample_logits_rows(q_probs[:, t, :], self.sampling.temperature, stream, offset=t * B,
                                                 err=self.draft_kv.err_word, eps=1e-12)
                 else:

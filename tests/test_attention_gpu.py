@@ -183,6 +183,28 @@ def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
     kv.check_errors()
 
 
+@pytest.mark.parametrize("layout", [0, 1, 2])
+@pytest.mark.parametrize("chunk,Hq,d", [(5, 12, 128), (1, 14, 64)])
+def test_ragged_plan_matches_oracle(chunk, Hq, d, layout):
+    """The plan a captured model forward replays (key_count < 0: ragged rows
+    of unknown lengths, grid sized by an 8192-key span bucket) on a skewed
+    batch -- most rows short, a few near 4600 keys, split into up to 36
+    CTAs each -- gives the oracle's result for C4's verify and draft decode
+    shapes."""
+    rng = np.random.default_rng(77)
+    starts = [int(x) for x in np.minimum(np.floor(rng.lognormal(6, 0.8, 37)), 4096)] + [4600, 3100, 0]
+    kv, ref = _build([s + chunk for s in starts], 2, d, 16, torch.bfloat16, seed=78)
+    B = len(starts)
+    q = torch.from_numpy(rng.standard_normal((B, chunk, Hq, d)).astype(np.float32)).to(DEV, torch.bfloat16)
+    exact_batch = AttnBatch.from_lists(DEV, list(range(B)), starts, chunk)
+    batch = AttnBatch(exact_batch.rows, exact_batch.starts, 8192, key_count=-1)
+    out = paged_attention(q, kv, 0, batch, mma_layout=layout)
+    out32 = paged_attention(q, kv, 0, batch, out_dtype=torch.float32, mma_layout=layout)
+    exact = oatt.paged_attention_extend(q.float().cpu().numpy(), ref, 0, range(B), starts)
+    _check_bf16(out.float().cpu().numpy(), out32.cpu().numpy(), exact)
+    kv.check_errors()
+
+
 @pytest.mark.parametrize("pps,chunk,cluster,layout", [(4, 1, False, 0), (0, 1, False, 0), (0, 6, True, 0),
                                                       (16, 6, True, 0), (0, 6, False, 0), (4, 6, False, 0),
                                                       (0, 6, False, 2), (4, 6, False, 2), (0, 1, False, 2),

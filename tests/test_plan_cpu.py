@@ -66,6 +66,12 @@ def _kernel(a):
     ((1, 512, 12, 2, 128, 512), {}, "mma_rows"),                  # prefill chunk
     ((8, 1, 4, 2, 16, 100), {"dtype": _lib.SDL_F32}, "generic"),  # fp32 pool
     ((32, 6, 12, 2, 128, 2048), {"force_generic": 1}, "generic"),
+    # ragged rows of unknown lengths (a captured graph): no register-direct or tcgen05 auto choice
+    ((358, 5, 12, 2, 128, 4656), {"key_count": -1}, "mma_rows"),   # C4 verify, 30 rows
+    ((358, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),         # C4 draft decode
+    ((64, 1, 14, 2, 64, 1500), {"key_count": -1}, "mma"),
+    ((16, 7, 16, 2, 128, 32768), {"key_count": -1}, "mma_rows"),   # 56 rows: rows on M, not tcgen05
+    ((16, 7, 16, 2, 128, 32768), {"key_count": -1, "use_umma": 1}, "tcgen05"),
 ])
 def test_kernel_choice(shape, flags, want):
     assert _kernel(_args(*shape, **flags)) == want
@@ -102,3 +108,31 @@ def test_invalid_arguments_are_refused():
     assert lib.sdl_attention_kernel(ctypes.byref(a)) == -1
     assert lib.sdl_attention_launches(ctypes.byref(a)) == -1
     assert lib.sdl_attention_workspace_bytes(ctypes.byref(a)) == 0
+
+
+
+def _split_of(a):
+    """(splits per row, pages per split) of a plan, from its workspace bytes."""
+    lib = _lib.load()
+    ws = lib.sdl_attention_workspace_bytes(ctypes.byref(a))
+    return ws // (a.B * a.chunk * a.Hq * (a.head_dim + 2) * 4)
+
+
+@pytest.mark.parametrize("B,chunk,Hq,d,span,base", [
+    (358, 5, 12, 128, 4656, 716),    # verify rows on M: one CTA per (sequence, kv head)
+    (1024, 5, 12, 128, 4656, 2048),
+    (64, 5, 12, 128, 4656, 128),
+    (358, 1, 14, 64, 4656, 358),     # decode keys on M: both kv heads in one CTA
+    (16, 1, 14, 64, 32768, 16),
+])
+def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
+    """key_count < 0: no split exceeds base/16 pages (4..64), rows take at
+    most 64 splits, and the grid still covers the span."""
+    a = _args(B, chunk, Hq, 2, d, span, key_count=-1)
+    max_pages = -(-span // 16)
+    pps = min(64, max(4, base // 16))
+    pps = min(max(pps, -(-max_pages // 64)), max_pages)
+    if chunk > 1:
+        pps += pps % 2  # the rows-on-M kernel splits at whole 32-key tiles
+    assert _split_of(a) == -(-max_pages // pps)
+    assert _lib.load().sdl_attention_launches(ctypes.byref(a)) == 2
