@@ -246,6 +246,18 @@ typedef struct sdl_attn_args {
     const void* v_new;
     int64_t new_row_stride;
     int32_t* err;
+    /* RoPE inside the launch (engine/model.py:50-56 apply_rotary, called on
+     * q and k at engine/qwen.py:157-164 before the cache write): when
+     * rope_cos != NULL the call attends x' = T(T(x*c) + T(rotate_half(x)*s))
+     * of q and stores that of k_new, c / s being row b*chunk + j of rope_cos
+     * / rope_sin (q's dtype, rope_stride elements apart, head_dim wide) --
+     * the framework chain's roundings, so the result equals rotating q and k
+     * first.  q and k_new are only read.  Only plans whose kernel stores the
+     * new rows itself take it (sdl_attention_fuses_rope); others refuse it
+     * with SDL_ERR_UNSUPPORTED. */
+    const void* rope_cos;
+    const void* rope_sin;
+    int64_t rope_stride;
 } sdl_attn_args;
 
 /* Bytes of workspace sdl_paged_attention needs for `args` (0 when one
@@ -258,6 +270,12 @@ size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
  * a path that does not write inside the attention kernel.  -1 when `args`
  * is invalid.  No counterpart in the reference. */
 int sdl_attention_launches(const sdl_attn_args* args);
+
+/* 1 when sdl_paged_attention applies RoPE (rope_cos / rope_sin) inside the
+ * launch for `args` -- the mma.sync kernels with keys or query rows on M,
+ * writing the new K/V rows themselves -- else 0; -1 when `args` is invalid.
+ * No counterpart in the reference. */
+int sdl_attention_fuses_rope(const sdl_attn_args* args);
 
 /* Kernel sdl_paged_attention runs for `args`: 0 = CUDA-core (generic),
  * 1 = mma.sync split-K with keys on M, 2 = tcgen05 persistent, 3 = mma.sync

@@ -79,25 +79,95 @@ struct TcParams {
     const char* k_src;   // K and V rows attended (the pool, or the dense tensors): register-direct kernel
     const char* v_src;
     int32_t* err;
+    // RoPE inside the launch (mma.sync kernels with the fused append): cos /
+    // sin row b*chunk + j (rope_stride elements apart) rotates q as it is
+    // loaded and k_new as it is stored; NULL = q and k_new are used as given
+    const char* rope_cos;
+    const char* rope_sin;
+    int64_t rope_stride;
 };
 
 SDL_DEV uint32_t ld_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Rotate-half RoPE of one element, the framework chain's roundings
+// (x * cos + rotate_half(x) * sin with each product rounded to T; the caller
+// rounds the sum): x is this dim's value, y its partner's (dim +- d/2), and
+// rotate_half(x) here is -y in the first half of the head, y in the second.
+template <typename T>
+SDL_DEV float rope_elem(float x, float y, float c, float s, bool first_half) {
+    const float a = round_trip<T>(__fmul_rn(x, c));
+    const float b = round_trip<T>(__fmul_rn(first_half ? -y : y, s));
+    return __fadd_rn(a, b);
+}
+
+template <typename T> SDL_DEV float half_lo(uint32_t v) { return to_f32<T>(reinterpret_cast<const T*>(&v)[0]); }
+template <typename T> SDL_DEV float half_hi(uint32_t v) { return to_f32<T>(reinterpret_cast<const T*>(&v)[1]); }
+
+// Two dims of a row held as packed pairs: x1 = dims (e, e+1) of the first
+// half, x2 = dims (e+half, e+half+1); cr / sr the row's cos / sin.
+template <typename T>
+SDL_DEV void rope_u32(uint32_t& x1, uint32_t& x2, const T* cr, const T* sr, int e, int half) {
+    const uint32_t c1 = ld_u32(cr + e), s1 = ld_u32(sr + e), c2 = ld_u32(cr + e + half), s2 = ld_u32(sr + e + half);
+    const float a0 = half_lo<T>(x1), a1 = half_hi<T>(x1), b0 = half_lo<T>(x2), b1 = half_hi<T>(x2);
+    x1 = pack2<T>(rope_elem<T>(a0, b0, half_lo<T>(c1), half_lo<T>(s1), true),
+                  rope_elem<T>(a1, b1, half_hi<T>(c1), half_hi<T>(s1), true));
+    x2 = pack2<T>(rope_elem<T>(b0, a0, half_lo<T>(c2), half_lo<T>(s2), false),
+                  rope_elem<T>(b1, a1, half_hi<T>(c2), half_hi<T>(s2), false));
+}
+
+// Eight dims of a row as a 16-byte piece: own, the partner piece (dims +- d/2)
+// and the piece's cos / sin.
+template <typename T>
+SDL_DEV uint4 rope_piece(uint4 own, uint4 partner, uint4 c, uint4 sn, bool first_half) {
+    const uint32_t* o = reinterpret_cast<const uint32_t*>(&own);
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(&partner);
+    const uint32_t* cc = reinterpret_cast<const uint32_t*>(&c);
+    const uint32_t* ss = reinterpret_cast<const uint32_t*>(&sn);
+    uint4 r;
+    uint32_t* rr = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+        rr[w] = pack2<T>(rope_elem<T>(half_lo<T>(o[w]), half_lo<T>(q[w]), half_lo<T>(cc[w]), half_lo<T>(ss[w]),
+                                      first_half),
+                         rope_elem<T>(half_hi<T>(o[w]), half_hi<T>(q[w]), half_hi<T>(cc[w]), half_hi<T>(ss[w]),
+                                      first_half));
+    return r;
+}
+
 // Fused append: copies the K and V rows of one kv head for up to kAppendBatch
 // new positions (byte offsets `src` into k_new / v_new and `dst` into the
-// pools; dst < 0 skips a position).  Lanes own 16-byte pieces (K pieces, then
-// V pieces) and issue every load of the batch before any store, so a batch
-// costs one memory round trip.
+// pools; dst < 0 skips a position; `nrow` the new-row index b*chunk + j).
+// Lanes own 16-byte pieces (K pieces, then V pieces) and issue every load of
+// the batch before any store, so a batch costs one memory round trip.  With
+// RoPE a K lane also loads its rotate-half partner piece (dims +- d/2; the
+// piece count is a power of two) and its cos / sin pieces.
 constexpr int kAppendBatch = 4;
 template <int HD, typename T>
 SDL_DEV void copy_new_rows(const TcParams& p, int lane, const int64_t (&src)[kAppendBatch],
-                           const int64_t (&dst)[kAppendBatch], int n) {
+                           const int64_t (&dst)[kAppendBatch], const int (&nrow)[kAppendBatch], int n) {
     constexpr int kChunks = HD * (int)sizeof(T) / 16;
     if (lane >= 2 * kChunks) return;
     const bool isv = lane >= kChunks;
-    const int cb = (lane % kChunks) * 16;
+    const int c = lane % kChunks;
+    const int cb = c * 16;
     const char* s0 = isv ? p.v_new : p.k_new;
     char* d0 = isv ? p.v_pool : p.k_pool;
+    if (!isv && p.rope_cos != nullptr) {
+        // one row at a time: four 16-byte loads per row, few registers (the
+        // batch arrays would be live across the whole producer)
+        const int pcb = (c ^ (kChunks / 2)) * 16;
+#pragma unroll 1
+        for (int u = 0; u < n; ++u) {
+            if (dst[u] < 0) continue;
+            const int64_t ro = (int64_t)nrow[u] * p.rope_stride * (int64_t)sizeof(T) + cb;
+            const uint4 own = *reinterpret_cast<const uint4*>(s0 + src[u] + cb);
+            const uint4 par = *reinterpret_cast<const uint4*>(s0 + src[u] + pcb);
+            const uint4 cv = *reinterpret_cast<const uint4*>(p.rope_cos + ro);
+            const uint4 sv = *reinterpret_cast<const uint4*>(p.rope_sin + ro);
+            *reinterpret_cast<uint4*>(d0 + dst[u] + cb) = rope_piece<T>(own, par, cv, sv, c < kChunks / 2);
+        }
+        return;
+    }
     uint4 v[kAppendBatch];
 #pragma unroll
     for (int u = 0; u < kAppendBatch; ++u)
@@ -221,12 +291,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 for (int gi = 0; gi < p.g_cta; ++gi) {
                     const int hoff = (kvgrp * p.g_cta + gi) * HD * (int)sizeof(T);
                     int64_t src[kAppendBatch], dst[kAppendBatch];
+                    int nrow[kAppendBatch];
 #pragma unroll
                     for (int u = 0; u < kAppendBatch; ++u) {
-                        src[u] = ((int64_t)b * p.chunk + j0 + u) * p.new_stride + hoff;
+                        nrow[u] = b * p.chunk + j0 + u;
+                        src[u] = (int64_t)nrow[u] * p.new_stride + hoff;
                         dst[u] = tr[u] >= 0 ? tr[u] * row_bytes + hoff : -1;
                     }
-                    copy_new_rows<HD, T>(p, lane, src, dst, min(kAppendBatch, nvalid - j0));
+                    copy_new_rows<HD, T>(p, lane, src, dst, nrow, min(kAppendBatch, nvalid - j0));
                 }
             }
             asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -290,15 +362,23 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     for (int nt = 0; nt < NTG; ++nt) {
         const int col = cbase + nt * 8 + grp;
         const bool ok = col < ncol && col / p.ratio < nvalid;
+        const int j = ok ? col / p.ratio : 0;
         const T* qp = nullptr;
-        if (ok) {
-            const int j = col / p.ratio, h = g * p.ratio + col % p.ratio;
-            qp = reinterpret_cast<const T*>(p.q) + b * p.q_sb + j * p.q_sj + h * p.q_sh;
-        }
+        if (ok) qp = reinterpret_cast<const T*>(p.q) + b * p.q_sb + j * p.q_sj + (g * p.ratio + col % p.ratio) * p.q_sh;
 #pragma unroll
         for (int ks = 0; ks < KSTEPS; ++ks) {
             qf[ks][nt][0] = ok ? ld_u32(qp + ks * 16 + 2 * tq) : 0u;
             qf[ks][nt][1] = ok ? ld_u32(qp + ks * 16 + 8 + 2 * tq) : 0u;
+        }
+        if (ok && p.rope_cos != nullptr) {  // dims e and e + d/2 sit in k-steps ks and ks + KSTEPS/2
+            const int64_t ro = (int64_t)(b * p.chunk + j) * p.rope_stride;
+            const T* cr = reinterpret_cast<const T*>(p.rope_cos) + ro;
+            const T* sr = reinterpret_cast<const T*>(p.rope_sin) + ro;
+#pragma unroll
+            for (int ks = 0; ks < KSTEPS / 2; ++ks) {
+                rope_u32<T>(qf[ks][nt][0], qf[ks + KSTEPS / 2][nt][0], cr, sr, ks * 16 + 2 * tq, HD / 2);
+                rope_u32<T>(qf[ks][nt][1], qf[ks + KSTEPS / 2][nt][1], cr, sr, ks * 16 + 8 + 2 * tq, HD / 2);
+            }
         }
     }
     int lim[NTG][2];
@@ -1127,13 +1207,15 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                     }
                 }
                 int64_t src[kAppendBatch], dst[kAppendBatch];
+                int nrow[kAppendBatch];
 #pragma unroll
                 for (int u = 0; u < kAppendBatch; ++u) {
                     const int64_t tr = __shfl_sync(0xffffffffu, trow, u);
-                    src[u] = ((int64_t)b * p.chunk + j0 + u) * p.new_stride + hoff;
+                    nrow[u] = b * p.chunk + j0 + u;
+                    src[u] = (int64_t)nrow[u] * p.new_stride + hoff;
                     dst[u] = tr >= 0 ? tr * row_bytes + hoff : -1;
                 }
-                copy_new_rows<HD, T>(p, lane, src, dst, min(kAppendBatch, nvalid - j0));
+                copy_new_rows<HD, T>(p, lane, src, dst, nrow, min(kAppendBatch, nvalid - j0));
             }
             asm volatile("fence.proxy.async.global;" ::: "memory");
             __syncwarp();
@@ -1211,6 +1293,20 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             qa[ks][1] = vb ? ld_u32(qpb + ks * 16 + 2 * t4) : 0u;
             qa[ks][2] = va ? ld_u32(qpa + ks * 16 + 8 + 2 * t4) : 0u;
             qa[ks][3] = vb ? ld_u32(qpb + ks * 16 + 8 + 2 * t4) : 0u;
+        }
+        if (p.rope_cos != nullptr) {  // dims e and e + d/2 sit in k-steps ks and ks + KS/2
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                if (!(hr ? vb : va)) continue;
+                const int64_t ro = (int64_t)(b * p.chunk + (hr ? jb : ja)) * p.rope_stride;
+                const T* cr = reinterpret_cast<const T*>(p.rope_cos) + ro;
+                const T* sr = reinterpret_cast<const T*>(p.rope_sin) + ro;
+#pragma unroll
+                for (int ks = 0; ks < KS / 2; ++ks) {
+                    rope_u32<T>(qa[ks][hr], qa[ks + KS / 2][hr], cr, sr, ks * 16 + 2 * t4, HD / 2);
+                    rope_u32<T>(qa[ks][2 + hr], qa[ks + KS / 2][2 + hr], cr, sr, ks * 16 + 8 + 2 * t4, HD / 2);
+                }
+            }
         }
     }
     float o[ON][4];
@@ -2775,6 +2871,10 @@ int validate(const sdl_attn_args* a) {
             return sdl::fail(SDL_ERR_INVALID, "sdl_paged_attention: bad fused-append arguments (k_new/v_new need a "
                                               "paged pool, rows of at least Hkv*head_dim and 4-byte alignment)");
     }
+    if ((a->rope_cos != nullptr) != (a->rope_sin != nullptr) ||
+        (a->rope_cos && (!a->k_new || a->rope_stride < a->head_dim || a->head_dim % 2)))
+        return sdl::fail(SDL_ERR_INVALID, "sdl_paged_attention: bad RoPE arguments (rope_cos and rope_sin together, "
+                                          "with k_new and rows of at least head_dim)");
     return SDL_OK;
 }
 
@@ -2783,6 +2883,16 @@ bool append_fusable(const sdl_attn_args* a) {
     const int64_t sb = a->new_row_stride * sdl::dtype_bytes(a->dtype);
     auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     return a->k_new && al16(a->k_new) && al16(a->v_new) && al16(a->k_pool) && al16(a->v_pool) && sb % 16 == 0;
+}
+
+// Whether plan `pl` applies RoPE inside the launch: the mma.sync kernels with
+// keys or query rows on M that store the new rows themselves, over 16-byte
+// aligned cos / sin rows (K pieces are rotated as 16-byte pieces).
+bool rope_fusable(const sdl_attn_args* a, const Plan& pl) {
+    auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    const int64_t rb = a->rope_stride * sdl::dtype_bytes(a->dtype);
+    return a->rope_cos && pl.tc && !pl.umma && !pl.direct && append_fusable(a) && al16(a->rope_cos) &&
+           al16(a->rope_sin) && rb % 16 == 0;
 }
 
 // Separate positional append (paths that do not write inside the kernel).
@@ -2833,6 +2943,14 @@ extern "C" int sdl_attention_kernel(const sdl_attn_args* args) {
     return !pl.tc ? 0 : pl.umma ? 2 : pl.rows ? 3 : pl.direct ? 4 : 1;
 }
 
+extern "C" int sdl_attention_fuses_rope(const sdl_attn_args* args) {
+    if (validate(args) != SDL_OK) return -1;
+    sdl_attn_args tmp = *args;
+    tmp.workspace = nullptr;
+    tmp.workspace_bytes = 0;
+    return rope_fusable(&tmp, make_plan(&tmp)) ? 1 : 0;
+}
+
 extern "C" int sdl_attention_launches(const sdl_attn_args* args) {
     if (validate(args) != SDL_OK) return -1;
     if (args->B == 0) return 0;
@@ -2857,6 +2975,8 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
     // tcgen05 kernel does not: a store + proxy fence inside its producer
     // stalls a deep TMA pipeline longer than a separate append launch costs.
     const bool fused_append = a->k_new && pl.tc && !pl.umma && append_fusable(a);
+    if (a->rope_cos && !rope_fusable(a, pl))
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_paged_attention: this plan cannot apply RoPE inside the launch");
     if (a->k_new && !fused_append && (rc = launch_append_pos(a, st)) != SDL_OK) return rc;
     if (pl.tc) {
         if (pl.ws_bytes > 0 && (!a->workspace || a->workspace_bytes < pl.ws_bytes))
@@ -2900,6 +3020,9 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.new_stride = 0;
         tp.k_src = static_cast<const char*>(a->k_pool ? a->k_pool : a->k_dense);
         tp.v_src = static_cast<const char*>(a->k_pool ? a->v_pool : a->v_dense);
+        tp.rope_cos = static_cast<const char*>(a->rope_cos);
+        tp.rope_sin = static_cast<const char*>(a->rope_sin);
+        tp.rope_stride = a->rope_stride;
         if (fused_append) {
             tp.k_pool = static_cast<char*>(const_cast<void*>(a->k_pool));
             tp.v_pool = static_cast<char*>(const_cast<void*>(a->v_pool));

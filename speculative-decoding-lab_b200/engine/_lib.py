@@ -53,6 +53,7 @@ EXPORTED_SYMBOLS = (
     "sdl_attention_workspace_bytes",
     "sdl_attention_launches",
     "sdl_attention_kernel",
+    "sdl_attention_fuses_rope",
     "sdl_paged_attention",
     "sdl_paged_attention_noalloc",
     "sdl_noalloc_scratch_bytes",
@@ -127,6 +128,9 @@ class SdlAttnArgs(ctypes.Structure):
         ("v_new", c_void),
         ("new_row_stride", c_i64),
         ("err", c_void),
+        ("rope_cos", c_void),
+        ("rope_sin", c_void),
+        ("rope_stride", c_i64),
     ]
 
 
@@ -148,6 +152,7 @@ _SIGS = {
     "sdl_attention_workspace_bytes": (c_size, [_P(SdlAttnArgs)]),
     "sdl_attention_launches": (c_int, [_P(SdlAttnArgs)]),
     "sdl_attention_kernel": (c_int, [_P(SdlAttnArgs)]),
+    "sdl_attention_fuses_rope": (c_int, [_P(SdlAttnArgs)]),
     "sdl_paged_attention": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_paged_attention_noalloc": (c_int, [_P(SdlAttnArgs), c_void]),
     "sdl_noalloc_scratch_bytes": (c_size, []),

@@ -23,7 +23,7 @@ import ctypes
 import math
 import threading
 import weakref
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 
@@ -169,12 +169,13 @@ class _ArgsEntry:
     change from call to call (q, out, the new rows, the workspace) and the
     layer."""
 
-    __slots__ = ("args", "need", "kv")
+    __slots__ = ("args", "need", "kv", "rope_fused")
 
-    def __init__(self, args: _lib.SdlAttnArgs, need: int, kv: PagedKVCache) -> None:
+    def __init__(self, args: _lib.SdlAttnArgs, need: int, kv: PagedKVCache, rope_fused: bool = False) -> None:
         self.args = args
         self.need = need
         self.kv = weakref.ref(kv)  # the struct points at the cache's tensor maps
+        self.rope_fused = rope_fused  # the launch rotates q and k_new itself
 
 
 _ARGS_CACHE = {}
@@ -213,6 +214,7 @@ def paged_attention(
     v_new: Optional[torch.Tensor] = None,
     cluster_merge: bool = False,
     mma_layout: int = 0,
+    rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
 ) -> torch.Tensor:
     """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
 
@@ -220,6 +222,13 @@ def paged_attention(
     call first stores them at positions ``starts[b] + j`` of layer ``layer``
     (the positions must already be reserved) -- the write-then-attend of a
     decoder layer in one launch on the tensor-core path.
+
+    ``rope = (cos, sin)`` (one head_dim row per (b, j), e.g. ``(B, chunk, 1,
+    d)``) applies the reference's rotate-half RoPE (engine/model.py:50-56) to
+    ``q`` and ``k_new`` as part of the call, with the framework chain's
+    roundings: the mma.sync kernels rotate q as they load it and k_new as
+    they store it (no separate launch, q and k_new only read); other plans
+    rotate ``q`` and ``k_new`` in place first.
 
     ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` /
     ``cluster_merge`` / ``mma_layout`` override the launch plan (pages per
@@ -246,6 +255,15 @@ def paged_attention(
     kn = vn = None
     if k_new is not None:
         kn, vn = _new_rows_2d(q, kv, k_new, v_new)
+    rc = rs = None
+    if rope is not None:
+        if kn is None:
+            raise ValueError("rope needs k_new (the rows it rotates before storing)")
+        rc, rs = (t.reshape(-1, q.shape[3]) for t in rope)
+        if rc.shape[0] != q.shape[0] * q.shape[1] or rs.shape[0] != rc.shape[0]:
+            raise ValueError("rope: cos / sin need one row per (b, j) of q")
+        rc = rc if (rc.dtype == q.dtype and rc.stride(-1) == 1) else rc.to(q.dtype).contiguous()
+        rs = rs if (rs.dtype == q.dtype and rs.stride(-1) == 1) else rs.to(q.dtype).contiguous()
     vr = batch.valid_rows
     # Everything the launch plan and the struct's fixed fields depend on,
     # including the pointer alignments the plan tests.
@@ -253,22 +271,37 @@ def paged_attention(
            vr.data_ptr() if vr is not None else 0, batch.max_limit, batch.key_count, tuple(q.shape), q.stride(),
            q.dtype, q.data_ptr() % 16, out.stride(), out.dtype, force_generic, pages_per_split, kv_heads_per_cta,
            use_umma, cluster_merge, mma_layout,
-           -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16), threading.get_ident())
+           -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16),
+           -1 if rc is None else (rc.stride(0), rc.data_ptr() % 16, rs.data_ptr() % 16), threading.get_ident())
     ent = _ARGS_CACHE.get(key)
     if ent is None or ent.kv() is not kv:
         a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma,
                         cluster_merge, mma_layout)
         if kn is not None:
             a.k_new, a.v_new, a.new_row_stride = kn.data_ptr(), vn.data_ptr(), kn.stride(0)
+        fused = False
+        if rc is not None:
+            a.rope_cos, a.rope_sin, a.rope_stride = rc.data_ptr(), rs.data_ptr(), rc.stride(0)
+            fused = _lib.load().sdl_attention_fuses_rope(a) == 1
+            if not fused:
+                a.rope_cos = a.rope_sin = None
+                a.rope_stride = 0
         need = int(_lib.load().sdl_attention_workspace_bytes(a))
         if len(_ARGS_CACHE) >= _ARGS_CACHE_MAX:
             _ARGS_CACHE.clear()
-        ent = _ArgsEntry(a, need, kv)
+        ent = _ArgsEntry(a, need, kv, fused)
         _ARGS_CACHE[key] = ent
     a = ent.args
     a.q = q.data_ptr()
     a.out = out.data_ptr()
     a.layer = layer
+    if rc is not None:
+        if ent.rope_fused:
+            a.rope_cos, a.rope_sin = rc.data_ptr(), rs.data_ptr()
+        else:  # this plan's kernel cannot rotate inside the launch: rotate in place first
+            from . import layer_ops
+            layer_ops.rope_(q, rs.reshape(q.shape[0], q.shape[1], 1, -1), rc.reshape(q.shape[0], q.shape[1], 1, -1))
+            layer_ops.rope_(kn.view(kn.shape[0], kv.num_kv_heads, kv.head_dim), rs, rc)
     if kn is not None:
         a.k_new, a.v_new = kn.data_ptr(), vn.data_ptr()
     dev = q.device

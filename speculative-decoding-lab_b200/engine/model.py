@@ -149,17 +149,22 @@ def plan_prefill(kv: PagedKVCache, seq_ids: Sequence[int], seq_lengths: Sequence
 
 
 def paged_attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv: PagedKVCache, layer: int,
-                 plan: ForwardPlan) -> torch.Tensor:
+                 plan: ForwardPlan, rope=None) -> torch.Tensor:
     """Store this layer's K/V at the plan's positions, then attend (write
-    first) -- one fused call; the positions were reserved by the plan."""
+    first) -- one fused call; the positions were reserved by the plan.
+    ``rope = (cos, sin)``: q and k arrive unrotated and the call applies
+    RoPE (inside the attention launch where its kernel can; not with
+    ``append_first``, whose rows are stored before the call)."""
     B = q.shape[0]
     q4 = q.reshape(B, plan.chunk, q.shape[-2], q.shape[-1])
     if plan.append_first:
+        if rope is not None:
+            raise ValueError("paged_attend: rope with append_first (rotate q and k before the call)")
         kv.append(layer, plan.slots, k.reshape(B * plan.chunk, k.shape[-2], k.shape[-1]),
                   v.reshape(B * plan.chunk, v.shape[-2], v.shape[-1]))
         return paged_attention(q4, kv, layer, plan.batch)
     return paged_attention(q4, kv, layer, plan.batch, k_new=k.reshape(B * plan.chunk, -1),
-                           v_new=v.reshape(B * plan.chunk, -1))
+                           v_new=v.reshape(B * plan.chunk, -1), rope=rope)
 
 
 # ------------------------------------------------------------- decoder layer

@@ -104,18 +104,25 @@ class QwenDecoderLayer(nn.Module):
             x = self.input_layernorm(hidden)
         lead = tuple(hidden.shape[:-1])
         d, hq, hkv = attn.head_dim, attn.num_heads, attn.num_kv_heads
+        rope = None
         if layer_ops.fusable(x):
-            # 16-bit models: one projection GEMM, and one RoPE launch over the
-            # q and k heads, which sit side by side in each row of its output
+            # 16-bit models: one projection GEMM; RoPE rides the attention
+            # launch (q rotated as it is loaded, k as it is stored), or -- when
+            # the rows are stored before attending -- one launch over the q
+            # and k heads, which sit side by side in each row of its output
             qkv = attn.qkv_fused(x)
-            qk = layer_ops.rope_(qkv[..., :(hq + hkv) * d].view(*lead, hq + hkv, d), sin, cos)
+            qk = qkv[..., :(hq + hkv) * d].view(*lead, hq + hkv, d)
+            if plan.append_first:
+                layer_ops.rope_(qk, sin, cos)
+            else:
+                rope = (cos, sin)
             q, k = qk[..., :hq, :], qk[..., hq:, :]
             v = qkv[..., (hq + hkv) * d:].view(*lead, hkv, d)
         else:
             q = apply_rotary_(attn.q_proj(x).view(*lead, hq, d), sin, cos)
             k = apply_rotary_(attn.k_proj(x).view(*lead, hkv, d), sin, cos)
             v = attn.v_proj(x).view(*lead, hkv, d)
-        out = paged_attend(q, k, v, kv, layer_index, plan)
+        out = paged_attend(q, k, v, kv, layer_index, plan, rope=rope)
         o = attn.o_proj(out.reshape(*lead, -1))
         if layer_ops.fusable(hidden):  # residual add + post-attention norm in one launch
             norm = self.post_attention_layernorm

@@ -398,6 +398,89 @@ def test_fused_append_equals_append_then_attend(case):
         kvc.check_errors()
 
 
+ROPE_CASES = [c for c in range(len(FUSED_CASES)) if FUSED_CASES[c][6] != torch.float32]
+
+
+@pytest.mark.parametrize("case", ROPE_CASES)
+def test_rope_in_launch_equals_rope_then_attend(case):
+    """``paged_attention(..., rope=(cos, sin))`` on unrotated q / k_new gives
+    the bits of RoPE first (the fused rope kernel, bit-exact to the
+    reference's apply_rotary) and attention after: the same output and the
+    same pool.  Plans whose kernel rotates inside the launch leave q and
+    k_new untouched; the others rotate them in place first."""
+    from engine import _lib as lib
+    from engine import layer_ops
+    from engine.model import make_rotary_cache
+
+    Hq, Hkv, d, chunk, starts, valid, dtype, kw = FUSED_CASES[case]
+    kw = dict(kw)
+    key_count = kw.pop("key_count", 0)
+    B = len(starts)
+    valid = valid or [chunk] * B
+    pair = [_build(starts, Hkv, d, 16, dtype, seed=400 + case, extra_blocks=4 + chunk, layers=2)[0]
+            for _ in range(2)]
+    for kvc in pair:
+        kvc.reserve(list(range(B)), starts, valid)
+    g = torch.Generator().manual_seed(1000 + case)
+    q = torch.randn(B, chunk, Hq, d, generator=g).to(DEV, dtype)
+    k_new = torch.randn(B * chunk, Hkv * d, generator=g).to(DEV, dtype)
+    v_new = torch.randn(B * chunk, Hkv * d, generator=g).to(DEV, dtype)
+    table = make_rotary_cache(d, 1e6, 8192, DEV).to(dtype)
+    pos = torch.tensor([[s + j for j in range(chunk)] for s in starts], device=DEV)
+    cos, sin = table[pos][:, :, 0, :], table[pos][:, :, 1, :]  # (B, chunk, d), rows 2d apart
+    packed = _lib_i32(list(range(B)) + starts + valid)
+    batch = AttnBatch(packed[:B], packed[B:2 * B], max(s + chunk for s in starts), packed[2 * B:], key_count)
+    q_r = layer_ops.rope_(q.clone(), sin.unsqueeze(2), cos.unsqueeze(2))
+    k_r = layer_ops.rope_(k_new.clone().view(B * chunk, Hkv, d), sin.reshape(-1, d), cos.reshape(-1, d))
+    ref = paged_attention(q_r, pair[0], 1, batch, k_new=k_r.view(B * chunk, -1), v_new=v_new, **kw)
+    q0, k0 = q.clone(), k_new.clone()
+    got = paged_attention(q, pair[1], 1, batch, k_new=k_new, v_new=v_new, rope=(cos.unsqueeze(2), sin.unsqueeze(2)),
+                          **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(ref, got)
+    assert torch.equal(pair[0]._k, pair[1]._k)
+    assert torch.equal(pair[0]._v, pair[1]._v)
+    if torch.equal(q, q0):  # rotated inside the launch: inputs only read
+        assert torch.equal(k_new, k0)
+    else:  # rotated in place first
+        assert torch.equal(q, q_r) and torch.equal(k_new.view(B * chunk, Hkv, d), k_r)
+    for kvc in pair:
+        kvc.check_errors()
+
+
+def test_rope_fusion_query():
+    """sdl_attention_fuses_rope: the mma.sync kernels that store the new rows
+    themselves rotate inside the launch; tcgen05, register-direct and
+    CUDA-core plans do not (the Python call rotates in place first), and a
+    call that asks a non-fusing plan for RoPE is refused."""
+    import ctypes
+
+    from engine import _lib as lib
+    from engine.attention import _paged_args
+
+    kv, _ = _build([100, 200], 2, 128, 16, torch.bfloat16, seed=9, layers=1)
+    kn = torch.randn(10, 256, device=DEV, dtype=torch.bfloat16)
+    cs = torch.randn(10, 128, device=DEV, dtype=torch.bfloat16)
+
+    def args(chunk, **kw):
+        q = torch.randn(2, chunk, 12, 128, device=DEV, dtype=torch.bfloat16)
+        batch = AttnBatch.from_lists(DEV, [0, 1], [100, 200], chunk)
+        a = _paged_args(q, kv, 0, batch, q, **kw)
+        a.k_new, a.v_new, a.new_row_stride = kn.data_ptr(), kn.data_ptr(), 256
+        a.rope_cos, a.rope_sin, a.rope_stride = cs.data_ptr(), cs.data_ptr(), 128
+        return a, (q, batch)
+
+    fuses = lambda a: lib.load().sdl_attention_fuses_rope(ctypes.byref(a))  # noqa: E731
+    for layout in (0, 1, 2):  # verify block: rows or keys on M
+        assert fuses(args(5, mma_layout=layout, use_umma=-1)[0]) == 1, layout
+    assert fuses(args(1, mma_layout=1)[0]) == 1   # decode, keys on M
+    assert fuses(args(1, mma_layout=3)[0]) == 0   # register-direct decode
+    assert fuses(args(5, force_generic=True)[0]) == 0
+    a, keep = args(5, use_umma=1)                  # tcgen05
+    assert fuses(a) == 0
+    assert lib.load().sdl_paged_attention(ctypes.byref(a), None) == 2  # SDL_ERR_UNSUPPORTED, nothing launched
+
+
 def test_fused_append_unaligned_rows_fall_back_to_separate_append():
     """k_new rows that are 4- but not 16-byte aligned take the separate
     positional append and still match."""
