@@ -100,18 +100,80 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_regs_kernel(const T* __r
     }
 }
 
+// rmsnorm_kernel over rows held as 16-byte pieces: one CTA per row, one
+// 8-element piece per thread (dim % 8 == 0, dim <= 8 * 1024, 16-byte aligned
+// rows), so a row costs one 16-byte load per input per thread.  The sum of
+// squares is per-thread in element order, then a warp tree, then the warps'
+// sums in order: another fixed order than rmsnorm_kernel's.
+template <typename T>
+__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const T* __restrict__ x, int64_t xs,
+                                                           const T* __restrict__ delta, int64_t ds,
+                                                           T* __restrict__ x_out, int64_t xos,
+                                                           const T* __restrict__ w, T* __restrict__ out,
+                                                           int64_t os, int dim, float eps) {
+    __shared__ float s_warp[32];
+    __shared__ float s_total;
+    const int64_t row = blockIdx.x;
+    const int c = threadIdx.x * 8;
+    const bool on = c < dim;
+    float v[8];
+    uint4 wv = make_uint4(0, 0, 0, 0);
+    float ss = 0.f;
+    if (on) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(x + row * xs + c);
+        wv = *reinterpret_cast<const uint4*>(w + c);
+        const T* xe = reinterpret_cast<const T*>(&xv);
+        if (delta != nullptr) {
+            const uint4 dv = *reinterpret_cast<const uint4*>(delta + row * ds + c);
+            const T* de = reinterpret_cast<const T*>(&dv);
+            uint4 hv;
+            T* he = reinterpret_cast<T*>(&hv);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                he[k] = from_f32<T>(__fadd_rn(to_f32<T>(xe[k]), to_f32<T>(de[k])));
+                v[k] = to_f32<T>(he[k]);
+            }
+            *reinterpret_cast<uint4*>(x_out + row * xos + c) = hv;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = to_f32<T>(xe[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss = __fmaf_rn(v[k], v[k], ss);
+    }
+    ss = warp_sum(ss);
+    const int warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    if ((threadIdx.x & 31) == 0) s_warp[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < nw; ++i) t = __fadd_rn(t, s_warp[i]);
+        s_total = t;
+    }
+    __syncthreads();
+    if (!on) return;
+    const float r = __fsqrt_rn(__fadd_rn(__fmul_rn(s_total, __frcp_rn((float)dim)), eps));
+    const T* we = reinterpret_cast<const T*>(&wv);
+    uint4 ov;
+    T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oe[k] = from_f32<T>(__fmul_rn(__fdiv_rn(v[k], r), to_f32<T>(we[k])));
+    *reinterpret_cast<uint4*>(out + row * os + c) = ov;
+}
+
 // One thread per (row, head, i < d/2) pair of rotated elements.
 template <typename T>
 __global__ void rope_kernel(T* __restrict__ x, int64_t xs, int heads, int d, const T* __restrict__ cs,
                             int64_t cs_stride, const T* __restrict__ sn, int64_t sn_stride, int rows) {
     const int half = d / 2;
-    const int64_t n = (int64_t)rows * heads * half;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
-        const int i = (int)(t % half);
-        const int64_t rh = t / half;
-        const int h = (int)(rh % heads);
-        const int64_t r = rh / heads;
-        T* p = x + r * xs + (int64_t)h * d;
+    const int per_row = heads * half;  // the host keeps rows * per_row below 2^31: 32-bit index math
+    const int n = rows * per_row;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
+        const int r = t / per_row;
+        const int rem = t - r * per_row;
+        const int h = rem / half;
+        const int i = rem - h * half;
+        T* p = x + (int64_t)r * xs + (int64_t)h * d;
         const float x1 = to_f32<T>(p[i]), x2 = to_f32<T>(p[i + half]);
         const T* c = cs + r * cs_stride;
         const T* s = sn + r * sn_stride;
@@ -172,6 +234,29 @@ __global__ void swiglu_pair_kernel(const T* __restrict__ x, int64_t xs, T* __res
     *reinterpret_cast<T2*>(out + (int64_t)blockIdx.y * os + i) = y;
 }
 
+// The same on 8 columns per thread (16-byte accesses: inter and the row
+// strides multiples of 8, 16-byte aligned rows); one row per blockIdx.y.
+template <typename T>
+__global__ void __launch_bounds__(128) swiglu_vec_kernel(const T* __restrict__ x, int64_t xs, T* __restrict__ out,
+                                                         int64_t os, int inter) {
+    const int i = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= inter) return;
+    const T* xr = x + (int64_t)blockIdx.y * xs;
+    const uint4 gv = *reinterpret_cast<const uint4*>(xr + i);
+    const uint4 uv = *reinterpret_cast<const uint4*>(xr + inter + i);
+    const T* ge = reinterpret_cast<const T*>(&gv);
+    const T* ue = reinterpret_cast<const T*>(&uv);
+    uint4 yv;
+    T* ye = reinterpret_cast<T*>(&yv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float g = to_f32<T>(ge[k]);
+        const float sv = round_trip<T>(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
+        ye[k] = from_f32<T>(__fmul_rn(sv, to_f32<T>(ue[k])));
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)blockIdx.y * os + i) = yv;
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t b = (n + threads - 1) / threads;
     return (int)std::min<int64_t>(std::max<int64_t>(b, 1), 148 * 16);
@@ -186,7 +271,12 @@ void launch_rmsnorm(const void* x, int64_t xs, const void* delta, int64_t ds, vo
     T* xo = static_cast<T*>(x_out);
     const T* wp = static_cast<const T*>(weight);
     T* op = static_cast<T*>(out);
-    if (dim <= 4 * kNormThreads)
+    auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    if (dim % 8 == 0 && dim <= 8 * 1024 && xs % 8 == 0 && os % 8 == 0 && al16(x) && al16(weight) && al16(out) &&
+        (delta == nullptr || (ds % 8 == 0 && xos % 8 == 0 && al16(delta) && al16(x_out)))) {
+        const int threads = (dim / 8 + 31) / 32 * 32;
+        rmsnorm_vec_kernel<T><<<rows, threads, 0, st>>>(xp, xs, dp, ds, xo, xos, wp, op, os, dim, eps);
+    } else if (dim <= 4 * kNormThreads)
         rmsnorm_regs_kernel<T, 4><<<rows, kNormThreads, 0, st>>>(xp, xs, dp, ds, xo, xos, wp, op, os, dim, eps);
     else if (dim <= 8 * kNormThreads)
         rmsnorm_regs_kernel<T, 8><<<rows, kNormThreads, 0, st>>>(xp, xs, dp, ds, xo, xos, wp, op, os, dim, eps);
@@ -218,6 +308,8 @@ extern "C" int sdl_rope(void* x, int64_t x_row_stride, int32_t rows, int32_t hea
                         int32_t dtype, void* stream) {
     if (!x || !cos || !sin || rows < 0 || heads < 1 || head_dim < 2 || head_dim % 2)
         return sdl::fail(SDL_ERR_INVALID, "sdl_rope: bad arguments");
+    if ((int64_t)rows * heads * (head_dim / 2) >= (int64_t(1) << 31))
+        return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_rope: more than 2^31 rotated pairs in one call");
     if (rows == 0) return SDL_OK;
     cudaStream_t st = sdl::as_stream(stream);
     const int64_t n = (int64_t)rows * heads * (head_dim / 2);
@@ -260,6 +352,19 @@ extern "C" int sdl_swiglu(const void* x, int64_t x_row_stride, void* out, int64_
     if (rows == 0) return SDL_OK;
     cudaStream_t st = sdl::as_stream(stream);
     auto al4 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 4 == 0; };
+    auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    if (inter % 8 == 0 && x_row_stride % 8 == 0 && out_row_stride % 8 == 0 && al16(x) && al16(out) && rows <= 65535 &&
+        (dtype == SDL_BF16 || dtype == SDL_F16)) {
+        const dim3 grid((inter / 8 + 127) / 128, rows);
+        if (dtype == SDL_BF16) {
+            using T = __nv_bfloat16;
+            swiglu_vec_kernel<T><<<grid, 128, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, inter);
+        } else {
+            using T = __half;
+            swiglu_vec_kernel<T><<<grid, 128, 0, st>>>((const T*)x, x_row_stride, (T*)out, out_row_stride, inter);
+        }
+        return sdl::check_launch("swiglu_vec_kernel");
+    }
     if (inter % 2 == 0 && x_row_stride % 2 == 0 && out_row_stride % 2 == 0 && al4(x) && al4(out) && rows <= 65535 &&
         (dtype == SDL_BF16 || dtype == SDL_F16)) {
         const dim3 grid((inter / 2 + 255) / 256, rows);
