@@ -7,7 +7,9 @@ mirror ``include/sdl_b200.h``.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import gc
 import os
 from typing import Optional
 
@@ -275,6 +277,20 @@ def i32(values, device: torch.device) -> torch.Tensor:
     if isinstance(values, torch.Tensor):
         return values.to(device=device, dtype=torch.int32).contiguous()
     return torch.tensor(list(values), dtype=torch.int32).to(device, non_blocking=True)
+
+
+@contextlib.contextmanager
+def no_gc():
+    """Keep Python's cyclic garbage collector from running inside a CUDA
+    graph capture: collecting an unreachable object that holds a captured
+    graph would destroy that graph mid-capture and invalidate the capture."""
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
 
 
 class Workspace:

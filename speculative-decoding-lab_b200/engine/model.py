@@ -378,12 +378,7 @@ class PagedLMMixin:
         # key span bucket: the attention plan (split size, kernel choice) is
         # fixed at capture, so graphs are kept per power-of-two bound of the
         # rows' key span rather than per the whole table width
-        span_cap = kv.width * kv.block_size
-        need = max(int(x) for x in starts) + chunk
-        span = 1024
-        while span < need:
-            span *= 2
-        span = min(span, span_cap)
+        span = self.span_bucket(kv, max(int(x) for x in starts) + chunk)
         key = (id(kv), chunk, bucket, span) if head else (id(kv), chunk, bucket, span, "headless")
         g = graphs.get(key)
         if g is not None and g.table_ptr != kv._table.data_ptr():
@@ -417,14 +412,11 @@ class PagedLMMixin:
 
             def run() -> torch.Tensor:
                 positions = s_starts.long().unsqueeze(1) + steps.unsqueeze(0)
-                plan = ForwardPlan(None, batch, positions, chunk)
-                hidden = self.embed_tokens(s_ids)
-                cos, sin = self._rope(positions)
-                hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+                normed = self._body(s_ids, kv, batch, positions)
                 if not head:
-                    return self.norm(hidden)  # the head runs after the replay
+                    return normed  # the head runs after the replay
                 # the head writes into the logits buffer every graph of this chunk shares
-                return torch.matmul(self.norm(hidden), self.lm_head.weight.t(), out=shared_logits)
+                return torch.matmul(normed, self.lm_head.weight.t(), out=shared_logits)
 
             # one eager pass sizes every workspace and stores this call's K/V;
             # the replay below stores the same bytes again
@@ -432,7 +424,7 @@ class PagedLMMixin:
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
             c0 = _lib.calls()
-            with torch.cuda.graph(graph, pool=self._graph_pool()):
+            with _lib.no_gc(), torch.cuda.graph(graph, pool=self._graph_pool()):
                 logits = run()
             g = _GraphedForward(graph, s_ids, s_rows, s_starts, logits, (steps, batch, kv), kv._table.data_ptr(),
                                 _lib.calls() - c0)
@@ -453,12 +445,46 @@ class PagedLMMixin:
         torch.matmul(g.logits, self.lm_head.weight.t(), out=dst)
         return dst[:B]
 
-    @staticmethod
-    def graph_spans(kv: PagedKVCache) -> List[int]:
+    def _body(self, ids_2d: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, positions: torch.Tensor) -> torch.Tensor:
+        """Embedding, decoder layers and final norm of one forward over rows
+        ``ids_2d`` (B, chunk) at ``positions`` (already reserved), from
+        device tensors only, so a CUDA graph can capture it."""
+        chunk = ids_2d.shape[1]
+        plan = ForwardPlan(None, batch, positions, chunk)
+        hidden = self.embed_tokens(ids_2d)
+        cos, sin = self._rope(positions)
+        hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+        return self.norm(hidden)
+
+    def max_positions(self) -> int:
+        """Positions the rotary table covers (a forward may not reach past)."""
+        return int(self._rope_table().shape[0])
+
+    def _check_reach(self, need: int) -> None:
+        """Raise on the host before a forward reaches position ``need - 1``
+        past the rotary table (on the device that is an out-of-range gather)."""
+        if need > self.max_positions():
+            raise ValueError("position {} is past the rotary table ({} positions)".format(need - 1,
+                                                                                         self.max_positions()))
+
+    def _span_cap(self, kv: PagedKVCache) -> int:
+        return min(kv.width * kv.block_size, self.max_positions())
+
+    def span_bucket(self, kv: PagedKVCache, need: int) -> int:
+        """The key-span bucket of a forward whose rows reach position
+        ``need - 1``: a power of two from 1024, capped at the table width and
+        the rotary table's length (a larger ``need`` raises)."""
+        self._check_reach(need)
+        span = 1024
+        while span < need:
+            span *= 2
+        return min(span, self._span_cap(kv))
+
+    def graph_spans(self, kv: PagedKVCache) -> List[int]:
         """The key-span buckets ``_graph_forward`` keys its graphs by for
         ``kv``: powers of two from 1024, the last one capped at the table's
-        width in tokens."""
-        cap = kv.width * kv.block_size
+        width in tokens and the rotary table's length."""
+        cap = self._span_cap(kv)
         spans, s = [], 1024
         while True:
             spans.append(min(s, cap))
@@ -590,7 +616,7 @@ class PagedLMMixin:
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
             c0 = _lib.calls()
-            with torch.cuda.graph(graph, pool=self._graph_pool()):
+            with _lib.no_gc(), torch.cuda.graph(graph, pool=self._graph_pool()):
                 logits = run()
             g = _GraphedPrefill(graph, s_ids, s_meta, logits, (s_starts, positions, batch, kv), kv._table.data_ptr(),
                                 _lib.calls() - c0)
@@ -609,6 +635,7 @@ class PagedLMMixin:
         replays a captured prefill padded to a length bucket (``prefill_bucket_of``)."""
         self.forward_calls += 1
         B, chunk = prompt_2d.shape
+        self._check_reach(chunk)
         cb = self._prefill_bucket(kv, B, chunk, int(seq_lengths[0]) if B == 1 else -1)
         if cb is not None:
             kv.reserve(seq_ids, [0], [chunk])
@@ -640,6 +667,7 @@ class PagedLMMixin:
         dev = self.device
         lens = [int(len(p)) for p in prompts]
         B = len(lens)
+        self._check_reach(max(lens))
         slots = kv.reserve(seq_ids, [0] * B, lens)
         rows, starts, valid, src, idx = [], [], [], [], []
         off = 0
@@ -670,6 +698,8 @@ class PagedLMMixin:
         batch = AttnBatch(packed[:R], packed[R:2 * R], max(lens), packed[2 * R:],
                           key_count=sum(s_ + C for s_ in starts))
         positions = packed[R:2 * R].long().unsqueeze(1) + torch.arange(C, device=dev).unsqueeze(0)
+        # a last chunk's padding positions may pass the rotary table: they are never stored or read
+        positions = positions.clamp(max=self.max_positions() - 1)
         plan = ForwardPlan(grid.reshape(-1), batch, positions, C, append_first=True)
         hidden = self.embed_tokens(ids)
         cos, sin = self._rope(positions)
@@ -690,6 +720,8 @@ class PagedLMMixin:
         """
         self.forward_calls += 1
         B = len(seq_ids)
+        if B:
+            self._check_reach(max(int(c) for c in ctx_lengths) + 1)
         bucket = self._graph_bucket(B)
         if logits_out is not None and (logits_out.shape[0] < max(B, bucket or 0) or not logits_out.is_contiguous()):
             raise ValueError("logits_out needs max(B, graph bucket) contiguous rows")
@@ -713,6 +745,8 @@ class PagedLMMixin:
         """``chunk`` consecutive tokens per row; returns ``(B, chunk, V)``."""
         self.forward_calls += 1
         B, chunk = input_ids_2d.shape
+        if B:
+            self._check_reach(max(int(x) for x in start_positions) + chunk)
         bucket = self._graph_bucket(B)
         if bucket is not None:
             starts = [int(x) for x in start_positions]

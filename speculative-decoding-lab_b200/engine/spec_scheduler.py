@@ -34,6 +34,7 @@ import torch
 
 from . import _lib
 from .config import EngineConfig, SamplingConfig, WorkloadRequest
+from .attention import AttnBatch
 from .kv import PagedKVCache, _exhausted
 from .scheduler import PagedScheduler, SchedulerResult, Sequence
 from .utils import Stopwatch, setup_logger, sync_device
@@ -50,6 +51,107 @@ from specdec.sampler import (
 )
 
 logger = setup_logger(__name__)
+
+
+class _DraftLoop:
+    """The gamma draft steps of a round as one CUDA graph, for one (batch
+    bucket, draft key-span bucket): per step the reserve of one position per
+    row (``sdl_kv_reserve`` on device rows / starts / counts), the draft
+    forward, its LM head into step t's slice of the round buffer, the draw
+    (``sdl_sample_logits_rows``, then the uniform counter advances by the
+    batch size on the device) or the argmax, and the next step's input ids
+    -- no host work between the steps.  (The reference captures one draft
+    step, specdec/graph_draft.py:70-110.)
+
+    Rows past the batch repeat row 0 with a count of 0 (nothing reserved);
+    their ids are reset to row 0's after every step, so the K/V rows they
+    store are row 0's own bytes.  Their draws read uniforms past the batch's,
+    inside the stream storage's capacity, and are discarded."""
+
+    def __init__(self, sched: "SpeculativePagedScheduler", bucket: int, span: int, greedy: bool) -> None:
+        draft, kv = sched.draft_model, sched.draft_kv
+        dev = draft.device
+        g = sched.gamma
+        W = draft.lm_head.weight
+        V = W.shape[0]
+        self.bucket, self.span, self.greedy, self.gamma = bucket, span, greedy, g
+        b = bucket
+        self.meta_h = torch.zeros(4 * b + 1, dtype=torch.int32).pin_memory()
+        self.meta = torch.zeros(4 * b + 1, dtype=torch.int32, device=dev)
+        self.props = torch.zeros((g, b), dtype=torch.int32, device=dev)
+        self.q = sched._loop_q_buffer(V, W.dtype, dev)  # (gamma, rows, V): the round buffer
+        self.slots = torch.zeros(b, dtype=torch.int32, device=dev)
+        self.draft, self.kv, self.W, self.V = draft, kv, W, V
+        self.ws = None
+        self.temp = float(sched.sampling.temperature)
+        if not greedy:
+            need = int(_lib.load().sdl_sampler_workspace_bytes(b, V))
+            self.ws = _lib.Workspace.get(dev, need, tag="sampler")
+            self.ubuf, self.ucnt = sched._u_storage
+        self.graph = None
+        self.calls = 0
+
+    def _run(self) -> None:
+        """The loop body (a method, not a closure: the loop holds its graph,
+        and a reference cycle through it would let the garbage collector
+        destroy a graph while another capture is open)."""
+        lib, b, g, V, kv = _lib.load(), self.bucket, self.gamma, self.V, self.kv
+        meta = self.meta
+        rows, d0, counts = meta[:b], meta[b:2 * b], meta[2 * b:3 * b]
+        keep = counts > 0
+        n64 = meta[4 * b:4 * b + 1].to(torch.int64)
+        cur = meta[3 * b:4 * b].to(torch.int64)
+        for t in range(g):
+            starts = d0 + t
+            _lib.check(lib.sdl_kv_reserve(ctypes.byref(kv._meta), b, rows.data_ptr(), starts.data_ptr(),
+                                          counts.data_ptr(), self.slots.data_ptr(), kv._stream()), "sdl_kv_reserve")
+            batch = AttnBatch(rows, starts, self.span, key_count=-1)
+            normed = self.draft._body(cur.view(b, 1), kv, batch, starts.to(torch.int64).unsqueeze(1))
+            logits = self.q[t, :b]
+            torch.matmul(normed, self.W.t(), out=logits.view(b, 1, V))
+            if self.greedy:
+                self.props[t].copy_(argmax_rows(logits))
+            else:
+                _lib.check(lib.sdl_sample_logits_rows(
+                    logits.data_ptr(), _lib.dtype_code(logits.dtype), logits.stride(0), b, V, self.temp, 1e-12,
+                    self.ubuf.data_ptr(), self.ubuf.numel(), self.ucnt.data_ptr(), 0, self.props[t].data_ptr(),
+                    self.ws.data_ptr(), self.ws.numel() * 4, kv.err_word.data_ptr(), _lib.stream_handle(meta.device)),
+                    "sdl_sample_logits_rows")
+                self.ucnt.add_(n64)
+            nxt = self.props[t].to(torch.int64)
+            cur = torch.where(keep, nxt, nxt[:1])
+
+    def capture(self, sids: List[int], d0: List[int], last: List[int]) -> None:
+        """One eager pass over the staged scratch rows (it reserves their
+        positions and, sampling, advances the uniform counter: the caller
+        undoes both), then the capture."""
+        self.stage(sids, d0, last)
+        self._run()
+        torch.cuda.synchronize(self.meta.device)
+        self.graph = torch.cuda.CUDAGraph()
+        c0 = _lib.calls()
+        with _lib.no_gc(), torch.cuda.graph(self.graph, pool=self.draft._graph_pool()):
+            self._run()
+        self.calls = _lib.calls() - c0
+
+    def stage(self, sids: List[int], d0: List[int], last: List[int]) -> None:
+        """Fill the static inputs (one pinned host-to-device copy)."""
+        b, B = self.bucket, len(sids)
+        m = self.meta_h.numpy()
+        m[0:B] = sids
+        m[B:b] = sids[0]
+        m[b:b + B] = d0
+        m[b + B:2 * b] = d0[0]
+        m[2 * b:2 * b + B] = 1
+        m[2 * b + B:3 * b] = 0
+        m[3 * b:3 * b + B] = last
+        m[3 * b + B:4 * b] = last[0]
+        m[4 * b] = B
+        self.meta.copy_(self.meta_h, non_blocking=True)
+
+    def replay(self) -> None:
+        self.graph.replay()
+        _lib.count_calls(self.calls)
 
 
 def _draw_uniform(generator: torch.Generator) -> float:
@@ -111,6 +213,14 @@ class SpeculativePagedScheduler(PagedScheduler):
         # copied out after every step
         if hasattr(draft_model, "_graph_forward"):
             draft_model.graph_head = False
+        # captured gamma-step draft loops (capture_graphs), keyed by (batch
+        # bucket, key-span bucket); the round buffer and the uniform storage
+        # they write and read live as long as the scheduler
+        self.draft_loops = True
+        self._loops: Dict[Any, _DraftLoop] = {}
+        self._loop_q: Optional[torch.Tensor] = None
+        self._u_storage = None
+        self.loop_replays = 0  # rounds whose draft phase was one loop replay
         # optional observer of every round: called with (sequence ids, target
         # start positions, draft lengths) before the round's first launch
         self.round_hook: Optional[Callable[[List[int], List[int], List[int]], None]] = None
@@ -316,6 +426,10 @@ class SpeculativePagedScheduler(PagedScheduler):
         slice of draft step ``t_slot`` (the draft's LM head output)."""
         bucket = getattr(self.draft_model, "_graph_bucket", lambda n: None)(B) or B
         rows = max(B, bucket)
+        lq = self._loop_q
+        if lq is not None and lq.shape[0] >= gamma and lq.shape[1] >= rows and lq.shape[2] == V and lq.dtype == dtype:
+            buf = lq  # the captured loops' buffer serves the step-wise path too
+            return buf[t_slot] if t_slot is not None else buf[:gamma, :B].permute(1, 0, 2)
         buf = self._q_buf
         if buf is None or buf.shape[0] < gamma or buf.shape[1] < rows or buf.shape[2] != V or buf.dtype != dtype:
             rows = max(rows, buf.shape[1] if buf is not None and buf.shape[2] == V else 0)
@@ -324,12 +438,76 @@ class SpeculativePagedScheduler(PagedScheduler):
             return buf[t_slot]
         return buf[:gamma, :B].permute(1, 0, 2)
 
+    # uniform storage of the captured loops: 2^20 valid uniforms plus room
+    # for the draws of padding rows past them
+    U_CAPACITY = 1 << 20
+    U_MARGIN = 4096
+
+    def _loop_q_buffer(self, V: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+        """The round buffer the captured loops write: (gamma, largest graph
+        bucket, V), allocated once (the graphs hold its address)."""
+        rows = max(self.draft_model.GRAPH_BUCKETS)
+        lq = self._loop_q
+        if lq is None:
+            self._loop_q = lq = torch.empty((self.gamma, rows, V), dtype=dtype, device=device)
+        if lq.shape != (self.gamma, rows, V) or lq.dtype != dtype:
+            raise RuntimeError("draft loop buffer shape changed")
+        return lq
+
+    def _make_stream(self, seed: int) -> Optional[UniformStream]:
+        """As PagedScheduler's, placed in the captured loops' storage when
+        there is one (and the stream fits it)."""
+        if self.sampling.is_greedy or self._u_storage is None:
+            return super()._make_stream(seed)
+        buf, cnt = self._u_storage
+        view = (buf[:self.U_CAPACITY], cnt)
+        if self._uniforms is not None:
+            if self._uniforms.numel() > self.U_CAPACITY:
+                return super()._make_stream(seed)
+            return UniformStream(self.model.device, uniforms=self._uniforms, storage=view)
+        return UniformStream(self.model.device, seed=seed, storage=view)
+
+    def _capture_draft_loops(self, sid: int) -> int:
+        """Capture the draft loop for every batch bucket and key-span bucket
+        of the draft's graphs (plain temperature or greedy sampling), on the
+        scratch sequence ``sid``."""
+        draft, kv = self.draft_model, self.draft_kv
+        greedy = self.sampling.is_greedy
+        W = getattr(getattr(draft, "lm_head", None), "weight", None)
+        if (not self.draft_loops or not getattr(draft, "_graphs_enabled", False) or W is None
+                or not hasattr(draft, "_body") or not (greedy or self._plain_temperature(W.shape[0]))):
+            return 0
+        dev = draft.device
+        if self._u_storage is None:
+            self._u_storage = (torch.zeros(self.U_CAPACITY + self.U_MARGIN, dtype=torch.float32, device=dev),
+                               torch.zeros(1, dtype=torch.int64, device=dev))
+        n, prev, g = 0, 0, self.gamma
+        for span in draft.graph_spans(kv):
+            need = max(prev + 1, int(0.55 * span), g + 1)
+            prev = span
+            kv.reserve([sid], [0], [need - g])
+            for b in draft.GRAPH_BUCKETS:
+                loop = _DraftLoop(self, b, span, greedy)
+                kv._plan_reserve([sid], [need - g], [g])  # the scratch pass's reserves, on the host shadows
+                saved = self._u_storage[1].clone()
+                loop.capture([sid], [need - g], [0])
+                self._u_storage[1].copy_(saved)
+                kv.truncate(sid, need - g)
+                self._loops[(b, span, greedy, float(self.sampling.temperature))] = loop
+                n += 1
+            kv.clear(sid)
+        kv.check_errors()
+        return n
+
     def capture_graphs(self) -> int:
         """Capture every CUDA graph the models can replay in a run (draft
         decode, target verify of gamma+1 rows, both models' prefill, at every
         batch and key-span bucket) before serving, on a scratch sequence id.
         A no-op unless the models have CUDA graphs enabled.  Returns the
         number of graphs captured."""
+        import gc
+
+        gc.collect()  # dead objects that hold graphs go now, not inside a capture
         sid = self._next_sid
         self._next_sid += 1
         n = 0
@@ -338,6 +516,8 @@ class SpeculativePagedScheduler(PagedScheduler):
                 continue
             kv.add_sequence(sid)
             n += model.capture_graphs(kv, sid, chunk)
+        if hasattr(self.draft_model, "capture_graphs"):
+            n += self._capture_draft_loops(sid)
         return n
 
     # ------------------------------------------------------------ spec loop
@@ -442,6 +622,22 @@ class SpeculativePagedScheduler(PagedScheduler):
         return result
 
     # ------------------------------------------------------------ one round
+    def _draft_loop_for(self, B: int, d0: List[int], stream: Optional[UniformStream]) -> Optional[_DraftLoop]:
+        """The captured draft loop for this round's batch and draft contexts,
+        or None (not captured, a batch beyond the largest bucket, or a
+        stream outside the loops' storage)."""
+        if not self._loops:
+            return None
+        draft = self.draft_model
+        if stream is not None and (self._u_storage is None or
+                                   stream.storage[0].data_ptr() != self._u_storage[0].data_ptr()):
+            return None
+        bucket = draft._graph_bucket(B)
+        if bucket is None:
+            return None
+        span = draft.span_bucket(self.draft_kv, max(d0) + self.gamma)
+        return self._loops.get((bucket, span, self.sampling.is_greedy, float(self.sampling.temperature)))
+
     def _plain_temperature(self, vocab: int) -> bool:
         """True when sampling is softmax(logits / T) with no top-k / top-p."""
         s = self.sampling
@@ -474,18 +670,36 @@ class SpeculativePagedScheduler(PagedScheduler):
             self.round_hook(sids, starts, d0)
 
         # ---- 1. draft proposes gamma tokens per sequence
-        proposals = torch.empty((B, gamma), dtype=torch.int32, device=device)
         q_probs = None
         if not greedy:
             stream.reserve(gamma * B)
-        cur = _lib.to_device([s.generated[-1] for s in running], torch.long, device)
+        last = [s.generated[-1] for s in running]
         fused = False
+        u_skip = gamma * B  # uniforms the draft draws read ahead of the accept walk
         V_d = getattr(getattr(draft, "lm_head", None), "weight", None)
+        loop = self._draft_loop_for(B, d0, stream)
+        if loop is not None:
+            # the whole draft phase is one graph replay: reserves, forwards,
+            # heads into the round buffer, draws (advancing the counter)
+            self.draft_kv._plan_reserve(sids, d0, [gamma] * B)
+            loop.stage(sids, d0, last)
+            loop.replay()
+            self.loop_replays += 1
+            result.draft_forward_calls += gamma
+            draft.forward_calls = getattr(draft, "forward_calls", 0) + gamma
+            proposals = loop.props[:, :B].t().contiguous()
+            if not greedy:
+                fused = True
+                q_probs = loop.q[:, :B].permute(1, 0, 2)
+                u_skip = 0
+        else:
+            proposals = torch.empty((B, gamma), dtype=torch.int32, device=device)
+        cur = _lib.to_device(last, torch.long, device)
         # plain temperature: each draft step's logits land in step t's slice of
         # the round buffer, which the fused rejection sampler reads in place
         direct = (not greedy and V_d is not None and hasattr(draft, "_graph_forward")
                   and self._plain_temperature(V_d.shape[0]))
-        for t in range(gamma):
+        for t in range(gamma if loop is None else 0):
             if direct:
                 qb = self._round_buffer(B, gamma, V_d.shape[0], V_d.dtype, device, t_slot=t)
                 q_logits = draft.decode(cur, self.draft_kv, sids, [d + t for d in d0], logits_out=qb)
@@ -527,10 +741,10 @@ class SpeculativePagedScheduler(PagedScheduler):
             if pl.dtype != ql.dtype:  # upcasts are exact, so the probabilities do not change
                 pl, ql = pl.float(), ql.float()
             tokens, n_out = spec_sample_logits(pl, ql, self.sampling.temperature, proposals, stream,
-                                               u_skip=gamma * B, err=self.kv.err_word, eps=1e-12)
+                                               u_skip=u_skip, err=self.kv.err_word, eps=1e-12)
         else:
             p_probs = self._probs_spec(p_logits).reshape(B, chunk, -1)
-            tokens, n_out = spec_sample(p_probs, q_probs, proposals, stream, greedy=False, u_skip=gamma * B,
+            tokens, n_out = spec_sample(p_probs, q_probs, proposals, stream, greedy=False, u_skip=u_skip,
                                         err=self.kv.err_word)
 
         # ---- 4. device commit: clip, EOS cut, rewind, draft alignment, clears

@@ -37,48 +37,92 @@ _EPS = 1e-12
 class UniformStream:
     """fp32 uniforms in HBM with a device-side read counter.
 
-    ``seed`` draws them on the device in chunks (deterministic: the values
-    consumed are the generator's output sequence whatever the refill points);
-    ``uniforms`` pins a pre-drawn stream (parity harnesses).
+    ``seed`` draws them on the device in chunks (deterministic for a given
+    seed and consumption); ``uniforms`` pins a pre-drawn stream (parity
+    harnesses).  ``storage = (buffer, counter)`` places the stream in
+    caller-owned device tensors (fp32 of some capacity, int64 of one entry)
+    that outlive it: a CUDA graph captured over those addresses reads every
+    later stream built on the same storage.  Refills then happen in place,
+    and ``capacity`` may exceed the valid length (``len``), so a captured
+    launch whose padding rows read past the valid uniforms stays in bounds.
     """
 
     def __init__(self, device: torch.device, seed: Optional[int] = None,
-                 uniforms: Optional[torch.Tensor] = None, chunk: int = 1 << 20) -> None:
+                 uniforms: Optional[torch.Tensor] = None, chunk: int = 1 << 20,
+                 storage: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> None:
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError("UniformStream lives in HBM: device must be CUDA")
         self.device = device
         self._chunk = int(chunk)
+        self._gen = None
         if uniforms is not None:
-            self._gen = None
-            self._buf = uniforms.detach().to(device=device, dtype=torch.float32).reshape(-1).contiguous()
+            u = uniforms.detach().to(device=device, dtype=torch.float32).reshape(-1)
         else:
             self._gen = torch.Generator(device=device)
             self._gen.manual_seed(int(0 if seed is None else seed))
-            self._buf = torch.rand(self._chunk, generator=self._gen, device=device, dtype=torch.float32)
-        self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+        if storage is not None:
+            buf, counter = storage
+            if buf.dtype != torch.float32 or counter.dtype != torch.int64 or buf.device != device:
+                raise ValueError("storage must be (fp32 buffer, int64 counter) on the stream's device")
+            n = u.numel() if uniforms is not None else min(self._chunk, buf.numel())
+            if n > buf.numel():
+                raise ValueError("uniform storage holds {} values, the stream needs {}".format(buf.numel(), n))
+            if uniforms is not None:
+                buf[:n].copy_(u)
+            else:
+                buf[:n].copy_(torch.rand(n, generator=self._gen, device=device, dtype=torch.float32))
+            buf[n:].zero_()
+            counter.zero_()
+            self._buf, self.counter, self._len, self._fixed = buf, counter, n, True
+        else:
+            if uniforms is not None:
+                self._buf = u.contiguous()
+            else:
+                self._buf = torch.rand(self._chunk, generator=self._gen, device=device, dtype=torch.float32)
+            self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+            self._len, self._fixed = self._buf.numel(), False
         self._hi = 0  # host upper bound of the counter
 
     @property
     def buffer(self) -> torch.Tensor:
-        return self._buf
+        """The valid uniforms (a view starting at the storage's address)."""
+        return self._buf[:self._len]
+
+    @property
+    def storage(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The whole buffer (its capacity) and the counter."""
+        return self._buf, self.counter
 
     def __len__(self) -> int:
-        return self._buf.numel()
+        return self._len
 
     def reserve(self, n: int) -> None:
         """Make sure ``n`` more uniforms can be read; refills when needed."""
-        if self._hi + n <= self._buf.numel():
+        if self._hi + n <= self._len:
             self._hi += n
             return
         c = int(self.counter.item())
         self._hi = c
-        if c + n > self._buf.numel():
+        if c + n > self._len:
             if self._gen is None:
                 raise RuntimeError("uniform stream exhausted ({} consumed, {} more needed)".format(c, n))
-            tail = self._buf[c:]
-            fresh = torch.rand(max(self._chunk, n), generator=self._gen, device=self.device, dtype=torch.float32)
-            self._buf = torch.cat((tail, fresh))
+            tail = self._buf[c:self._len].clone()
+            k = tail.numel()
+            if self._fixed:
+                # in place: captured graphs hold the storage's address
+                fill = self._buf.numel() - k
+                if fill < n:
+                    raise RuntimeError("uniform storage of {} values cannot hold {} more".format(self._buf.numel(), n))
+                fill = min(fill, max(self._chunk, n))
+                self._buf[:k].copy_(tail)
+                self._buf[k:k + fill].copy_(torch.rand(fill, generator=self._gen, device=self.device,
+                                                       dtype=torch.float32))
+                self._len = k + fill
+            else:
+                fresh = torch.rand(max(self._chunk, n), generator=self._gen, device=self.device, dtype=torch.float32)
+                self._buf = torch.cat((tail, fresh))
+                self._len = self._buf.numel()
             self.counter.zero_()
             self._hi = 0
         self._hi += n

@@ -153,16 +153,20 @@ def test_precaptured_graphs_and_wall_clock_admission_reproduce_c1(label):
                                       C1["gamma"], uniforms=torch.from_numpy(workloads.c1_uniforms(0)))
     n = sched.capture_graphs()
     spans = len(target.graph_spans(kv))
-    assert n == spans * len(target.GRAPH_BUCKETS) * 2  # draft decode + target verify; fp32: no prefill graphs
+    # draft decode + target verify + the captured draft loops; fp32: no prefill graphs
+    assert n == spans * len(target.GRAPH_BUCKETS) * 3
     assert kv.num_allocated_blocks == 0 and dkv.num_allocated_blocks == 0
     before = (len(target._graphs), len(draft._graphs))
     sched._next_sid = 0  # the scratch row is empty again: the run's sequence ids start at 0 as in the reference
     reqs = [WorkloadRequest(prompt=ids, max_new_tokens=n_, arrive_time=0.0)
             for ids, n_, _ in workloads.c1_requests(0)]
+    rounds = []
+    sched.round_hook = lambda sids, starts, d0: rounds.append(len(sids))
     res = sched.run_spec_continuous(reqs, seed=0, measure=False, arrival_clock="wall")
     assert [s.generated for s in res.sequences] == run["generated"]
     assert res.tokens_per_round == run["tokens_per_round"]
     assert (len(target._graphs), len(draft._graphs)) == before
+    assert sched.loop_replays == len(rounds) > 0  # every round's draft phase was one replay
     kv.check_errors()
     dkv.check_errors()
 
@@ -224,3 +228,37 @@ def test_batched_chunked_prefill_matches_one_by_one():
     assert kv1.seq_lengths == kv2.seq_lengths
     kv1.check_errors()
     kv2.check_errors()
+
+
+@pytest.mark.parametrize("temperature", [0.0, 1.0])
+def test_captured_draft_loop_matches_step_by_step(temperature):
+    """The draft phase as one captured loop (reserve, forward, head and draw
+    for all gamma steps in one graph) gives the tokens, round structure and
+    uniform consumption of the step-by-step path on 16-bit models."""
+    runs = []
+    for loops in (False, True):
+        target = _model("c1-target", 5, torch.bfloat16)
+        draft = _model("c1-draft", 6, torch.bfloat16)
+        target.enable_cuda_graphs()
+        draft.enable_cuda_graphs()
+        cfg = EngineConfig(block_size=16, max_num_blocks=512)
+        kv = build_kv(target, cfg, DEV, max_seqs=16)
+        dkv = build_kv(draft, cfg, DEV, max_seqs=16)
+        sched = SpeculativePagedScheduler(target, kv, draft, dkv, cfg, SpecSampling(temperature=temperature), 4)
+        sched.draft_loops = loops
+        sched.capture_graphs()
+        assert bool(sched._loops) == loops
+        sched._next_sid = 0
+        g = torch.Generator().manual_seed(21)
+        reqs = [WorkloadRequest(prompt=torch.randint(0, 1024, (int(n),), generator=g).tolist(), max_new_tokens=24,
+                                arrive_time=float(i // 3))
+                for i, n in enumerate((5, 40, 130, 17, 300, 64, 9))]
+        rounds = []
+        sched.round_hook = lambda sids, starts, d0: rounds.append(len(sids))
+        res = sched.run_spec_continuous(reqs, seed=3, measure=False)
+        runs.append(([s.generated for s in res.sequences], res.tokens_per_round, res.draft_forward_calls,
+                     rounds, sched.loop_replays))
+        kv.check_errors()
+        dkv.check_errors()
+    assert runs[0][:4] == runs[1][:4]
+    assert runs[0][4] == 0 and runs[1][4] == len(runs[1][3]) > 0
