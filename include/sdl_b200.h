@@ -258,6 +258,15 @@ typedef struct sdl_attn_args {
     const void* rope_cos;
     const void* rope_sin;
     int64_t rope_stride;
+    /* 1: the caller launches attention over distinct layers back to back on
+     * the stream (a decode step of an attention stack), so no kernel still
+     * running when this one starts writes this layer's older pool pages.
+     * The mma.sync kernels then let the next launch become resident at once
+     * and, with the fused append, stream their first pages of older keys
+     * before waiting on the preceding kernel, so a layer's ramp overlaps
+     * the previous layer's tail and split merge.  0 (default): dependents
+     * start after the main loop and every pool read follows the wait. */
+    int32_t overlap_layers;
 } sdl_attn_args;
 
 /* Bytes of workspace sdl_paged_attention needs for `args` (0 when one

@@ -85,6 +85,7 @@ struct TcParams {
     const char* rope_cos;
     const char* rope_sin;
     int64_t rope_stride;
+    int overlap;  // distinct layers back to back: dependents start early, older pages stream before the wait
 };
 
 SDL_DEV uint32_t ld_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
@@ -192,6 +193,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
+    if (p.overlap) pdl_launch_dependents();  // the next layer's launch may become resident now
     const int b = blockIdx.z;
     const int split = blockIdx.x;
     const int coltile = blockIdx.y % p.ncoltiles;
@@ -260,7 +262,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
         fence_mbar_init();
     }
-    pdl_wait();
     __syncthreads();
 
     if (warp == ncons) {
@@ -272,6 +273,31 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         // first page that holds one is issued -- the earlier pages' copies are
         // in flight meanwhile.
         const int app_page = p.k_new != nullptr ? max(pbeg, start / kPage) : pend;
+        // Layers back to back (p.overlap) with the fused append: the pages
+        // before the first new row hold keys of earlier, completed launches
+        // (the caller's contract), so the first ring stages of them are
+        // issued before griddepcontrol.wait and stream while the preceding
+        // kernel drains.  Without k_new a separate append may just have
+        // written any page.
+        const int npre = p.overlap && p.k_new != nullptr ? min(kStages, min(np, app_page - pbeg)) : 0;
+        for (int i = 0; i < npre; ++i) {
+            const int t0 = __shfl_sync(0xffffffffu, tok_first, i);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[i], p.stage_bytes);
+                uint8_t* sbuf = smem + i * p.stage_bytes;
+                for (int gi = 0; gi < p.g_cta; ++gi) {
+                    const int g = kvgrp * p.g_cta + gi;
+                    uint8_t* kb = sbuf + gi * (2 * DO * kBoxBytes);
+#pragma unroll
+                    for (int dd = 0; dd < DO; ++dd) {
+                        tma_load_4d(kb + dd * kBoxBytes, &tmk, &full[i], 0, dd, g, t0);
+                        tma_load_4d(kb + (DO + dd) * kBoxBytes, &tmv, &full[i], 0, dd, g, t0);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        pdl_wait();
         auto append_rows = [&]() {
             const int row_bytes = p.Hkv * HD * (int)sizeof(T);
             for (int j0 = 0; j0 < nvalid; j0 += kAppendBatch) {
@@ -313,6 +339,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const int t0 = __shfl_sync(0xffffffffu, tok0, k);
                 const int i = i0 + k;
                 const int st = i % kStages;
+                if (i < npre) { issued = i + 1; continue; }  // issued before the wait
                 if (pbeg + i == app_page) append_rows();
                 if (i >= kStages) {
                     int ok = 1;
@@ -352,6 +379,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     }
 
     // ----------------------------------------------------------- consumers
+    pdl_wait();  // Q comes from the preceding kernels
     const int gi = warp / p.wpg, wc = warp % p.wpg;
     const int g = kvgrp * p.g_cta + gi;
     const int cbase = col0 + wc * NTG * 8;
@@ -990,6 +1018,7 @@ attn_direct_kernel(const TcParams p) {
 // dependent rounds, the splits' (m, l) pairs (lane s holds split s, reduced
 // by an online max/sum across lanes), then 16 partial rows at a time.
 __global__ void __launch_bounds__(128) attn_combine_kernel(TcParams p, int hd) {
+    if (p.overlap) pdl_launch_dependents();  // layers back to back: the next attention may become resident
     pdl_wait();  // partials come from the attention launch just before
     pdl_launch_dependents();  // the next launch may become resident; it waits for this grid to finish
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1140,6 +1169,7 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     __shared__ int s_abort_flag;
     volatile int* s_abort = &s_abort_flag;
 
+    if (p.overlap) pdl_launch_dependents();  // the next layer's launch may become resident now
     const int b = blockIdx.z, split = blockIdx.x;
     const int g = blockIdx.y % p.Hkv, rt = blockIdx.y / p.Hkv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1183,7 +1213,6 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         }
         fence_mbar_init();
     }
-    pdl_wait();
     __syncthreads();
 
     if (warp == ncons) {
@@ -1191,6 +1220,33 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         if (lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmv); }
         // first page of this split that holds a new row (-1: no append)
         const int app_page = p.k_new != nullptr && max(pbeg, start / kPage) < pend ? max(pbeg, start / kPage) : -1;
+        // Layers back to back (p.overlap) with the fused append: tiles wholly
+        // before the first new row's page hold keys of earlier, completed
+        // launches, and the first ring stages of them are issued before
+        // griddepcontrol.wait (as in attn_tc_kernel).
+        const int npre = p.overlap && p.k_new != nullptr
+                             ? min(NS, min(ntile, max(0, (start / kPage - pbeg) / kTilePages))) : 0;
+        for (int i = 0; i < npre; ++i) {
+            const int k = i * kTilePages;
+            const int cnt0 = min(32, np);
+            const int t0 = __shfl_sync(0xffffffffu, tok_first, k);
+            const int t1 = __shfl_sync(0xffffffffu, tok_first, min(k + 1, cnt0 - 1));
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
+                uint8_t* sbuf = smem + i * STAGE_BYTES;
+#pragma unroll
+                for (int q = 0; q < kTilePages; ++q) {
+                    const int tq = q == 0 ? t0 : t1;
+#pragma unroll
+                    for (int dd = 0; dd < DO; ++dd) {
+                        tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[i], 0, dd, g, tq);
+                        tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[i], 0, dd, g, tq);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        pdl_wait();
         // Fused append of kv head g's slice of every new row whose page lies
         // in [pbeg, pend), before the tile holding the first of them is issued.
         auto append_rows = [&]() {
@@ -1233,6 +1289,7 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                 // past every row's limit and are masked
                 const int t1 = __shfl_sync(0xffffffffu, tok, min(k + 1, cnt - 1));
                 const int pg0 = pbeg + i0 + k;
+                if (i < npre) { issued = i + 1; continue; }  // issued before the wait
                 if (app_page >= pg0 && app_page < pg0 + kTilePages) append_rows();  // app_page < pend
                 if (i >= NS) {
                     int ok = 1;
@@ -1272,6 +1329,7 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     }
 
     // ----------------------------------------------------------- consumers
+    pdl_wait();  // Q comes from the preceding kernels
     const int t4 = lane & 3, gq = lane >> 2;
     const int r0 = r_lo + warp * 16;
     const int ra = r0 + gq, rb = ra + 8;
@@ -3020,6 +3078,7 @@ extern "C" int sdl_paged_attention(const sdl_attn_args* a, void* stream) {
         tp.new_stride = 0;
         tp.k_src = static_cast<const char*>(a->k_pool ? a->k_pool : a->k_dense);
         tp.v_src = static_cast<const char*>(a->k_pool ? a->v_pool : a->v_dense);
+        tp.overlap = a->overlap_layers ? 1 : 0;
         tp.rope_cos = static_cast<const char*>(a->rope_cos);
         tp.rope_sin = static_cast<const char*>(a->rope_sin);
         tp.rope_stride = a->rope_stride;

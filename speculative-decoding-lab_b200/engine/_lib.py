@@ -133,6 +133,7 @@ class SdlAttnArgs(ctypes.Structure):
         ("rope_cos", c_void),
         ("rope_sin", c_void),
         ("rope_stride", c_i64),
+        ("overlap_layers", c_int),
     ]
 
 

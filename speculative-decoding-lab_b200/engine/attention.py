@@ -111,7 +111,7 @@ def _paged_args(q, kv, layer, batch, out, force_generic=False, pages_per_split=0
 
 def attention_launches(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
                        k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None,
-                       mma_layout: int = 0) -> int:
+                       mma_layout: int = 0, overlap_layers: bool = False) -> int:
     """Kernel launches one ``paged_attention`` call with these arguments
     makes: the attention launch, the split-K merge when the plan splits a
     row's pages across CTAs, and a positional append when ``k_new`` is given
@@ -129,7 +129,7 @@ KERNEL_NAMES = ("generic", "mma", "tcgen05", "mma_rows", "mma_direct")
 
 
 def attention_kernel(q: torch.Tensor, kv: PagedKVCache, batch: AttnBatch, use_umma: int = 0,
-                     mma_layout: int = 0) -> str:
+                     mma_layout: int = 0, overlap_layers: bool = False) -> str:
     """Which kernel ``paged_attention`` runs for these arguments: "generic"
     (CUDA cores), "mma" (mma.sync split-K, keys on the MMA M dimension),
     "mma_rows" (mma.sync split-K, query rows on M), "mma_direct" (keys on M,
@@ -215,6 +215,7 @@ def paged_attention(
     cluster_merge: bool = False,
     mma_layout: int = 0,
     rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+    overlap_layers: bool = False,
 ) -> torch.Tensor:
     """Attention of ``q`` (B, chunk, Hq, d) against the pages of ``kv``.
 
@@ -229,6 +230,13 @@ def paged_attention(
     roundings: the mma.sync kernels rotate q as they load it and k_new as
     they store it (no separate launch, q and k_new only read); other plans
     rotate ``q`` and ``k_new`` in place first.
+
+    ``overlap_layers``: the caller launches attention over distinct layers
+    back to back on the stream (an attention stack's decode step), so no
+    kernel still running when this one starts writes this layer's older
+    pages; the launch then overlaps its ramp with the previous layer's tail
+    (sdl_attn_args.overlap_layers).  Leave it off when the previous kernel
+    may have appended to this layer.
 
     ``pages_per_split`` / ``kv_heads_per_cta`` / ``use_umma`` /
     ``cluster_merge`` / ``mma_layout`` override the launch plan (pages per
@@ -272,13 +280,15 @@ def paged_attention(
            q.dtype, q.data_ptr() % 16, out.stride(), out.dtype, force_generic, pages_per_split, kv_heads_per_cta,
            use_umma, cluster_merge, mma_layout,
            -1 if kn is None else (kn.stride(0), kn.data_ptr() % 16, vn.data_ptr() % 16),
-           -1 if rc is None else (rc.stride(0), rc.data_ptr() % 16, rs.data_ptr() % 16), threading.get_ident())
+           -1 if rc is None else (rc.stride(0), rc.data_ptr() % 16, rs.data_ptr() % 16), bool(overlap_layers),
+           threading.get_ident())
     ent = _ARGS_CACHE.get(key)
     if ent is None or ent.kv() is not kv:
         a = _paged_args(q, kv, layer, batch, out, force_generic, pages_per_split, kv_heads_per_cta, use_umma,
                         cluster_merge, mma_layout)
         if kn is not None:
             a.k_new, a.v_new, a.new_row_stride = kn.data_ptr(), vn.data_ptr(), kn.stride(0)
+        a.overlap_layers = 1 if overlap_layers else 0
         fused = False
         if rc is not None:
             a.rope_cos, a.rope_sin, a.rope_stride = rc.data_ptr(), rs.data_ptr(), rc.stride(0)

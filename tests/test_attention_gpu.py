@@ -448,6 +448,38 @@ def test_rope_in_launch_equals_rope_then_attend(case):
         kvc.check_errors()
 
 
+@pytest.mark.parametrize("chunk,Hq,d", [(1, 12, 128), (6, 12, 128), (1, 14, 64), (5, 12, 128)])
+def test_overlap_layers_gives_the_same_bits(chunk, Hq, d):
+    """Distinct layers launched back to back with overlap_layers (each launch
+    lets the next become resident early and streams its older pages before
+    waiting) store and return exactly what the plain launches do, for the
+    keys-on-M and rows-on-M kernels with split merges."""
+    starts = [5, 700, 1500, 2047, 31]
+    layers = 4
+    pair = [_build([s_ + chunk for s_ in starts], 2, d, 16, torch.bfloat16, seed=600 + chunk, layers=layers)[0]
+            for _ in range(2)]
+    g = torch.Generator().manual_seed(chunk * d)
+    B = len(starts)
+    q = torch.randn(layers, B, chunk, Hq, d, generator=g).to(DEV, torch.bfloat16)
+    kn = torch.randn(layers, B * chunk, 2 * d, generator=g).to(DEV, torch.bfloat16)
+    vn = torch.randn(layers, B * chunk, 2 * d, generator=g).to(DEV, torch.bfloat16)
+    outs = []
+    for kvc, ov in zip(pair, (False, True)):
+        kvc.reserve(list(range(B)), starts, [chunk] * B)
+        batch = AttnBatch.from_lists(DEV, list(range(B)), starts, chunk)
+        o = torch.empty_like(q)
+        for _ in range(2):  # the second pass stores the same rows again and reads them
+            for layer in range(layers):
+                paged_attention(q[layer], kvc, layer, batch, out=o[layer], k_new=kn[layer], v_new=vn[layer],
+                                pages_per_split=8, overlap_layers=ov)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(pair[0]._k, pair[1]._k) and torch.equal(pair[0]._v, pair[1]._v)
+    for kvc in pair:
+        kvc.check_errors()
+
+
 def test_rope_fusion_query():
     """sdl_attention_fuses_rope: the mma.sync kernels that store the new rows
     themselves rotate inside the launch; tcgen05, register-direct and
