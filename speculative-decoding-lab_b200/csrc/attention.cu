@@ -1229,18 +1229,19 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         for (int i = 0; i < npre; ++i) {
             const int k = i * kTilePages;
             const int cnt0 = min(32, np);
-            const int t0 = __shfl_sync(0xffffffffu, tok_first, k);
-            const int t1 = __shfl_sync(0xffffffffu, tok_first, min(k + 1, cnt0 - 1));
+            int tq[kTilePages];
+#pragma unroll
+            for (int q = 0; q < kTilePages; ++q) tq[q] = __shfl_sync(0xffffffffu, tok_first, min(k + q, cnt0 - 1));
             if (lane == 0) {
                 mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
                 uint8_t* sbuf = smem + i * STAGE_BYTES;
 #pragma unroll
                 for (int q = 0; q < kTilePages; ++q) {
-                    const int tq = q == 0 ? t0 : t1;
 #pragma unroll
                     for (int dd = 0; dd < DO; ++dd) {
-                        tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[i], 0, dd, g, tq);
-                        tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[i], 0, dd, g, tq);
+                        tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[i], 0, dd, g, tq[q]);
+                        tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[i], 0, dd, g,
+                                    tq[q]);
                     }
                 }
             }
@@ -1284,10 +1285,12 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             for (int k = 0; k < cnt; k += kTilePages) {
                 const int i = (i0 + k) / kTilePages;
                 const int st = i % NS;
-                const int t0 = __shfl_sync(0xffffffffu, tok, k);
-                // a lone last page is loaded twice: its second copy's keys lie
-                // past every row's limit and are masked
-                const int t1 = __shfl_sync(0xffffffffu, tok, min(k + 1, cnt - 1));
+                // a ragged last tile (the split's last pages) repeats its last
+                // page: the repeats' keys lie past every row's limit and are
+                // masked (non-final splits hold whole tiles: pps is aligned)
+                int tq[kTilePages];
+#pragma unroll
+                for (int q = 0; q < kTilePages; ++q) tq[q] = __shfl_sync(0xffffffffu, tok, min(k + q, cnt - 1));
                 const int pg0 = pbeg + i0 + k;
                 if (i < npre) { issued = i + 1; continue; }  // issued before the wait
                 if (app_page >= pg0 && app_page < pg0 + kTilePages) append_rows();  // app_page < pend
@@ -1306,11 +1309,11 @@ attn_rows_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                     uint8_t* sbuf = smem + st * STAGE_BYTES;
 #pragma unroll
                     for (int q = 0; q < kTilePages; ++q) {
-                        const int tq = q == 0 ? t0 : t1;
 #pragma unroll
                         for (int dd = 0; dd < DO; ++dd) {
-                            tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[st], 0, dd, g, tq);
-                            tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[st], 0, dd, g, tq);
+                            tma_load_4d(sbuf + q * PAGE_BYTES + dd * kBoxBytes, &tmk, &full[st], 0, dd, g, tq[q]);
+                            tma_load_4d(sbuf + q * PAGE_BYTES + (DO + dd) * kBoxBytes, &tmv, &full[st], 0, dd, g,
+                                        tq[q]);
                         }
                     }
                 }
