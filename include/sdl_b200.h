@@ -210,9 +210,11 @@ typedef struct sdl_attn_args {
                                  grid to one wave of resident CTAs; or < 0:
                                  ragged rows of unknown lengths (a plan a
                                  CUDA graph captures and replays over other
-                                 batches), split into CTAs of at most
-                                 n/16 pages (4..64; n = unsplit CTAs, one
-                                 per sequence and kv-head group), with
+                                 batches), split into CTAs of
+                                 max(n/16, max_limit/256) pages for decode
+                                 and max(n/16, max_limit/512) for blocks,
+                                 8..64 (n = unsplit CTAs, one per sequence
+                                 and kv-head group), with
                                  rows on M for head_dim-128 blocks of
                                  24+ rows and no automatic tcgen05 or
                                  register-direct kernel.  Only the launch

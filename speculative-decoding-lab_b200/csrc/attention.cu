@@ -2621,25 +2621,31 @@ int rows_occupancy(int hd, int dtype, size_t smem, int threads) {
 // a CUDA graph and replayed over other batches, of which only the grid's
 // bounds (B, max_limit) are known.  A one-wave plan sized for max_limit
 // leaves the longest rows of a skewed batch in one CTA each, and those
-// CTAs set the launch's duration; instead no split exceeds about
-// base_ctas / kRaggedSplitDiv pages (4..kRaggedMaxSplitPages), which
-// balances list-scheduled CTAs against per-CTA and merge overhead, and no
-// row takes more than kRaggedMaxSplits splits.  Measured on B200 over
-// C4-shaped batches (contexts floor(lognormal(6, 0.8)) + U[0, 512) tokens,
-// grid sized for an 8192-key span): 5-row verify (12 q / 2 kv heads,
-// head_dim 128, rows on M) 83 / 110 / 136 / 239 us at 256 / 358 / 512 /
-// 1024 sequences against 111 / 145 / 155 / 240 for the exact-count plan and
-// 220 / 214 / 215 / 298 for a one-wave plan at 55 % of the span; draft
-// decode (14 q / 2 kv heads, head_dim 64) 31 / 38-41 / 52 / 84-89 us against
-// 30 / 37 / 48 / 114 and 72 / 103 / 159 / 159.
+// CTAs set the launch's duration; tiny splits instead fill the grid with
+// CTAs past short rows' ends and multiply the merge's partials.  So a
+// split holds max(n/16, max_pages/16) pages for decode and max(n/16,
+// max_pages/32) for blocks (n = the unsplit CTAs), within 8..64.  Measured
+// on B200 over C4-shaped batches (contexts floor(lognormal(6, 0.8)) +
+// U[0, 512) tokens) at the C4 pools' 4656-key span, fixed pages per split:
+//   decode (14 q / 2 kv heads, d 64), pages 4 / 8 / 12 / 20 / 40:
+//     16 seqs 9.7 / 8.0 / 8.5 / 9.4 / 12.6 us; 64 seqs 26.5 / 19.3 / 17.0 /
+//     13.8 / 18.4; 256 seqs 48.7 / 34.6 / 31.2 / 28.9 / 35.0
+//   5-row verify (12 q / 2 kv heads, d 128, rows on M):
+//     16 seqs 15.5 / 13.9 / 15.7 / 20.6 / 30.6; 64 seqs 51.2 / 36.6 /
+//     33.4 / 29.7 / 40.0; 256 seqs 175 / 114 / 94 / 82 / 79
+// and, with the grid for an 8192-key span, verify at 358 / 512 / 1024
+// sequences 110 / 144 / 266 us at 32 pages and 108 / 135 / 239 at 64,
+// against 145 / 155 / 240 for the exact-count plan and 214 / 215 / 298 for
+// a one-wave plan at 55 % of the span.
 constexpr int kRaggedSplitDiv = 16;
+constexpr int kRaggedMinSplitPages = 8;
 constexpr int kRaggedMaxSplitPages = 64;
-constexpr int kRaggedMaxSplits = 64;
 int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) {
     if (a->pages_per_split > 0) return a->pages_per_split;
     if (a->key_count < 0) {
-        long pps = std::min<long>(kRaggedMaxSplitPages, std::max<long>(kMinSplitPages, base_ctas / kRaggedSplitDiv));
-        pps = std::max<long>(pps, (max_pages + kRaggedMaxSplits - 1) / kRaggedMaxSplits);
+        const long span_div = a->chunk > 1 ? 32 : 16;
+        long pps = std::max<long>(base_ctas / kRaggedSplitDiv, (max_pages + span_div - 1) / span_div);
+        pps = std::min<long>(kRaggedMaxSplitPages, std::max<long>(kRaggedMinSplitPages, pps));
         return (int)std::min<long>(pps, max_pages);
     }
     const long target = (long)sm_count() * 4;

@@ -122,16 +122,21 @@ def _split_of(a):
     (358, 5, 12, 128, 4656, 716),    # verify rows on M: one CTA per (sequence, kv head)
     (1024, 5, 12, 128, 4656, 2048),
     (64, 5, 12, 128, 4656, 128),
+    (16, 5, 12, 128, 4656, 32),
     (358, 1, 14, 64, 4656, 358),     # decode keys on M: both kv heads in one CTA
+    (64, 1, 14, 64, 4656, 64),
     (16, 1, 14, 64, 32768, 16),
+    (16, 1, 14, 64, 1024, 16),
 ])
 def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
-    """key_count < 0: no split exceeds base/16 pages (4..64), rows take at
-    most 64 splits, and the grid still covers the span."""
+    """key_count < 0: splits of max(base/16, span pages/16) pages for decode
+    and max(base/16, span pages/32) for blocks, within 8..64; the grid still
+    covers the span."""
     a = _args(B, chunk, Hq, 2, d, span, key_count=-1)
     max_pages = -(-span // 16)
-    pps = min(64, max(4, base // 16))
-    pps = min(max(pps, -(-max_pages // 64)), max_pages)
+    div = 32 if chunk > 1 else 16
+    pps = min(64, max(8, max(base // 16, -(-max_pages // div))))
+    pps = min(pps, max_pages)
     if chunk > 1:
         pps += pps % 2  # the rows-on-M kernel splits at whole 32-key tiles
     assert _split_of(a) == -(-max_pages // pps)
