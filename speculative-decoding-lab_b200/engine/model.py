@@ -293,6 +293,27 @@ class _GraphedForward:
         self.table_ptr = table_ptr  # the block table the graph reads; a grown (moved) table needs a new capture
 
 
+class _GraphedPrefillRows:
+    """One captured batched prefill of ``bucket`` 128-token chunk rows (the
+    decoder layers and the final norm; the head runs on the selected last
+    positions after the replay).  Static inputs: the chunk rows' token ids,
+    the slot of every (row, position) (-1 past a chunk's end), and per row
+    the sequence, start position and valid count; rows past the call's repeat
+    row 0 with nothing valid, so they store nothing and attend nothing."""
+
+    __slots__ = ("graph", "ids", "grid", "meta", "normed", "keep", "table_ptr", "calls")
+
+    def __init__(self, graph, ids, grid, meta, normed, keep, table_ptr, calls=0) -> None:
+        self.graph = graph
+        self.ids = ids
+        self.grid = grid
+        self.meta = meta
+        self.normed = normed
+        self.keep = keep
+        self.table_ptr = table_ptr
+        self.calls = calls
+
+
 class _GraphedPrefill:
     """One captured prefill of a single prompt, padded to a length bucket
     (``prefill_bucket_of``).  Static inputs (token ids, block-table row, prompt length,
@@ -526,6 +547,16 @@ class PagedLMMixin:
                 self.prefill(torch.zeros((1, cb), dtype=torch.long, device=self.device), kv, [sid], [cb])
                 kv.clear(sid)
                 cb = self.prefill_bucket_of(cb + 1)
+            if self._prefill_rows_bucket(kv, 1) is not None:
+                # batched prefills: every row one full chunk of the scratch
+                # sequence at position 0 (the rows store the same bytes)
+                C = self.PREFILL_CHUNK
+                slots = kv.reserve([sid], [0], [C])
+                ids0 = torch.zeros((1, C), dtype=torch.long, device=self.device)
+                for rb in self.PREFILL_ROW_BUCKETS:
+                    self._graph_prefill_rows(kv, ids0.expand(rb, C), slots.repeat(rb), [sid] * rb, [0] * rb,
+                                             [C] * rb, rb)
+                kv.clear(sid)
         torch.cuda.synchronize(self.device)
         return len(graphs) - n0
 
@@ -682,6 +713,7 @@ class PagedLMMixin:
             last_row.append((len(rows) - 1, valid[-1] - 1))
             off += L
         R = len(rows)
+        rb = self._prefill_rows_bucket(kv, R)
         # token ids and the slot of every (row, position), -1 past a chunk's end
         pieces = [p.to(dev, torch.long).reshape(-1) if isinstance(p, torch.Tensor)
                   else _lib.to_device(list(p), torch.long, dev) for p in prompts]
@@ -694,6 +726,11 @@ class PagedLMMixin:
         safe = gather.clamp(min=0)
         ids = torch.where(mask, flat_ids[safe], torch.zeros_like(safe))
         grid = torch.where(mask, slots[safe].to(torch.int32), torch.full_like(safe, -1, dtype=torch.int32))
+        if rb is not None:
+            normed = self._graph_prefill_rows(kv, ids, grid.reshape(-1), rows, starts, valid, rb)
+            sel = _lib.to_device([r * C + j for r, j in last_row], torch.long, dev)
+            h_last = normed.reshape(rb * C, -1).index_select(0, sel)
+            return torch.matmul(h_last, self.lm_head.weight.t())
         packed = _lib.i32(rows + starts + valid, dev)
         batch = AttnBatch(packed[:R], packed[R:2 * R], max(lens), packed[2 * R:],
                           key_count=sum(s_ + C for s_ in starts))
@@ -707,6 +744,84 @@ class PagedLMMixin:
         sel = _lib.to_device([r * C + j for r, j in last_row], torch.long, dev)
         h_last = hidden.reshape(R * C, -1).index_select(0, sel)
         return self._logits(h_last)
+
+    PREFILL_ROW_BUCKETS = (1, 2, 3, 4, 6, 8, 12, 16, 24, 32, 48, 64, 96, 128)
+
+    def _prefill_rows_bucket(self, kv: PagedKVCache, R: int) -> Optional[int]:
+        """Row bucket of a graphed batched prefill of ``R`` chunk rows, or
+        None for the eager path (graphs off, an fp32 model -- whose
+        reductions the parity runs pin -- or more rows than the largest
+        bucket)."""
+        if not getattr(self, "_graphs_enabled", False):
+            return None
+        if self.embed_tokens.weight.dtype not in (torch.bfloat16, torch.float16):
+            return None
+        for b in self.PREFILL_ROW_BUCKETS:
+            if b >= R:
+                return b
+        return None
+
+    def _graph_prefill_rows(self, kv: PagedKVCache, ids: torch.Tensor, grid: torch.Tensor, rows: List[int],
+                            starts: List[int], valid: List[int], rb: int) -> torch.Tensor:
+        """Normed hidden states ``(rb, C, H)`` of ``prefill_batch``'s chunk
+        rows (positions already reserved) through the captured layers for
+        ``rb`` rows; rows past ``len(rows)`` repeat row 0 with nothing valid.
+        The attention plans are the ragged-rows ones over the table's whole
+        reach, so one capture serves every prompt mix."""
+        C = self.PREFILL_CHUNK
+        R = len(rows)
+        graphs = self.__dict__.setdefault("_graphs", {})
+        key = (id(kv), "prefill_rows", rb)
+        g = graphs.get(key)
+        if g is not None and g.table_ptr != kv._table.data_ptr():
+            del graphs[key]  # the block table grew (moved): recapture
+            g = None
+        pad = rb - R
+        meta = _lib.i32(rows + [rows[0]] * pad + starts + [starts[0]] * pad + valid + [0] * pad, self.device)
+
+        def fill(dst_ids, dst_grid, dst_meta):
+            dst_ids[:R].copy_(ids)
+            dst_grid[:R * C].copy_(grid)
+            if pad:
+                dst_ids[R:].zero_()
+                dst_grid[R * C:].fill_(-1)
+            dst_meta.copy_(meta.view(3, rb))
+
+        if g is None:
+            s_ids = torch.zeros((rb, C), dtype=torch.long, device=self.device)
+            s_grid = torch.full((rb * C,), -1, dtype=torch.int32, device=self.device)
+            s_meta = torch.zeros((3, rb), dtype=torch.int32, device=self.device)
+            fill(s_ids, s_grid, s_meta)
+            batch = AttnBatch(s_meta[0], s_meta[1], self._span_cap(kv), s_meta[2], key_count=-1)
+            steps = torch.arange(C, device=self.device)
+            top = self.max_positions() - 1
+
+            def run() -> torch.Tensor:
+                # a last chunk's padding positions may pass the rotary table:
+                # they are never stored or read
+                positions = (s_meta[1].long().unsqueeze(1) + steps.unsqueeze(0)).clamp(max=top)
+                plan = ForwardPlan(s_grid, batch, positions, C, append_first=True)
+                hidden = self.embed_tokens(s_ids)
+                cos, sin = self._rope(positions)
+                hidden = self._run_layers(hidden, kv, plan, cos[:, :, None, :], sin[:, :, None, :])
+                return self.norm(hidden)
+
+            # one eager pass sizes every workspace and stores this call's K/V;
+            # the replay below stores the same bytes again
+            run()
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            c0 = _lib.calls()
+            with _lib.no_gc(), torch.cuda.graph(graph, pool=self._graph_pool()):
+                normed = run()
+            g = _GraphedPrefillRows(graph, s_ids, s_grid, s_meta, normed, (steps, batch, kv),
+                                    kv._table.data_ptr(), _lib.calls() - c0)
+            graphs[key] = g
+        else:
+            fill(g.ids, g.grid, g.meta)
+        g.graph.replay()
+        _lib.count_calls(g.calls)
+        return g.normed
 
     def decode(self, input_ids: torch.Tensor, kv: PagedKVCache, seq_ids: Sequence[int],
                ctx_lengths: Sequence[int], slots: Optional[torch.Tensor] = None,
