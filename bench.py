@@ -1625,8 +1625,10 @@ def main_c4(args) -> int:
                        "admitted at the first round boundary after its arrival".format(rate),
            "kv_pool": "80% of free HBM after weights, block_size 16, target and draft pools; recompute "
                       "preemption when a round would not fit (per_rank.preempted counts it)",
-           "forwards": "eager" if args.eager else "CUDA-graph replays (batch x key-span buckets, all captured "
-                                                  "before the warm-up)",
+           "forwards": "eager" if args.eager else "CUDA-graph replays, all captured before the warm-up: a round's "
+                                                  "gamma draft steps as one graph, the verify forward, and the "
+                                                  "prefill chunk-row buckets (batch x key-span buckets; attention "
+                                                  "plans for ragged rows)",
            "admission": ("one prefill per arrival" if args.no_batch_prefill else
                          "same-round arrivals prefilled together in 128-token chunks (one forward per model)"),
            "warmup": "{} requests of a different stream (seed {})".format(max(1, (total * W) // K), args.seed + 1000003),
