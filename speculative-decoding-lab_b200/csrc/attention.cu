@@ -2639,6 +2639,7 @@ int rows_occupancy(int hd, int dtype, size_t smem, int threads) {
 // a one-wave plan at 55 % of the span.
 constexpr int kRaggedSplitDiv = 16;
 constexpr int kRaggedMinSplitPages = 8;
+constexpr int kRaggedBlockChunk = 32;  // positions per row from which a block is prefill-sized
 constexpr int kRaggedMaxSplitPages = 64;
 int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) {
     if (a->pages_per_split > 0) return a->pages_per_split;
@@ -2646,6 +2647,13 @@ int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) 
         const long span_div = a->chunk > 1 ? 32 : 16;
         long pps = std::max<long>(base_ctas / kRaggedSplitDiv, (max_pages + span_div - 1) / span_div);
         pps = std::min<long>(kRaggedMaxSplitPages, std::max<long>(kRaggedMinSplitPages, pps));
+        if (a->chunk >= kRaggedBlockChunk) {
+            // prefill-sized blocks: a split's fp32 partials (chunk x Hq rows)
+            // outweigh the pages it saves, so rows split only as far as it
+            // takes to give every SM a CTA
+            const long want = (sm_count() + base_ctas - 1) / base_ctas;
+            pps = std::max<long>(pps, (max_pages + want - 1) / want);
+        }
         return (int)std::min<long>(pps, max_pages);
     }
     const long target = (long)sm_count() * 4;

@@ -745,7 +745,10 @@ class PagedLMMixin:
         h_last = hidden.reshape(R * C, -1).index_select(0, sel)
         return self._logits(h_last)
 
-    PREFILL_ROW_BUCKETS = (1, 2, 3, 4, 6, 8, 12, 16, 24, 32, 48, 64, 96, 128)
+    # chunk-row buckets of graphed batched prefills: padding rows cost full
+    # GEMM rows, so the steps stay within ~1/7 of the bucket
+    PREFILL_ROW_BUCKETS = (1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 14, 16, 18, 20, 23, 26, 30, 34, 39, 44, 50, 57,
+                           64, 73, 83, 95, 108, 128)
 
     def _prefill_rows_bucket(self, kv: PagedKVCache, R: int) -> Optional[int]:
         """Row bucket of a graphed batched prefill of ``R`` chunk rows, or

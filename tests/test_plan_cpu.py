@@ -141,3 +141,17 @@ def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
         pps += pps % 2  # the rows-on-M kernel splits at whole 32-key tiles
     assert _split_of(a) == -(-max_pages // pps)
     assert _lib.load().sdl_attention_launches(ctypes.byref(a)) == 2
+
+
+@pytest.mark.parametrize("R,want_splits", [(8, 1), (1, 7)])
+def test_ragged_prefill_rows_split_only_to_fill_the_sms(R, want_splits):
+    """Ragged prefill chunk rows (128 positions, 12 q / 2 kv heads: 12 row
+    tiles per kv head) split only until every SM has a CTA: their partials
+    outweigh the pages a split saves."""
+    a = _args(R, 128, 12, 2, 128, 4656, key_count=-1)
+    lib = _lib.load()
+    ws = lib.sdl_attention_workspace_bytes(ctypes.byref(a))
+    if want_splits == 1:
+        assert ws == 0 and lib.sdl_attention_launches(ctypes.byref(a)) == 1
+    else:
+        assert _split_of(a) == want_splits
