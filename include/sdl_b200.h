@@ -144,6 +144,17 @@ int sdl_spec_commit(const sdl_kv_meta* target, const sdl_kv_meta* draft,
                     const int32_t* starts, int32_t* k_out, int32_t* flags_out,
                     int32_t* catchup_slot, void* stream);
 
+/* sdl_spec_commit for a batch padded to n rows (a captured round): only
+ * the first *n_valid rows (device int32, read when the kernel runs) are
+ * committed; the rest are left alone.  No counterpart in the reference. */
+int sdl_spec_commit_n(const sdl_kv_meta* target, const sdl_kv_meta* draft,
+                      int32_t n, const int32_t* rows, const int32_t* n_out,
+                      const int32_t* tokens, int32_t tok_stride,
+                      const int32_t* remaining, int32_t eos,
+                      const int32_t* starts, int32_t* k_out, int32_t* flags_out,
+                      int32_t* catchup_slot, const int32_t* n_valid,
+                      void* stream);
+
 /* ------------------------------------------------------------- attention */
 
 /* Encode the TMA descriptor (128-byte CUtensorMap) the tensor-core attention
@@ -422,6 +433,21 @@ int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj,
                            int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
                            int32_t* tokens, int32_t* n_out, void* workspace,
                            size_t workspace_bytes, int32_t* err, void* stream);
+
+/* sdl_spec_sample_logits for a batch padded to B sequences (a captured
+ * round): the accept walk consumes uniforms for the first *n_valid
+ * sequences only (device int32) and the counter advances by theirs; the
+ * padding sequences' outputs are bonus draws to be ignored.  Always the
+ * five-launch chain.  No counterpart in the reference. */
+int sdl_spec_sample_logits_n(const void* p_logits, int64_t p_sb, int64_t p_sj,
+                             const void* q_logits, int64_t q_sb, int64_t q_sj,
+                             int32_t dtype, float temperature, float eps,
+                             const int32_t* proposals, int32_t B, int32_t gamma,
+                             int32_t vocab, const float* uniforms,
+                             int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
+                             int32_t* tokens, int32_t* n_out, void* workspace,
+                             size_t workspace_bytes, int32_t* err,
+                             const int32_t* n_valid, void* stream);
 
 /* 0 (default): sdl_spec_sample_logits runs its five-launch chain; 1: its
  * one-launch kernel wherever that applies.  Process-wide.  No counterpart in

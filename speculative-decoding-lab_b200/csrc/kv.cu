@@ -293,12 +293,14 @@ __global__ void spec_commit_kernel(sdl_kv_meta tgt, sdl_kv_meta drf, int32_t has
                                    const int32_t* rows, const int32_t* n_out, const int32_t* tokens,
                                    int32_t tok_stride, const int32_t* remaining, int32_t eos,
                                    const int32_t* starts, int32_t* k_out, int32_t* flags_out,
-                                   int32_t* catchup_slot) {
+                                   int32_t* catchup_slot, const int32_t* n_valid) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane != 0 || warp > 1) return;
     const bool is_target = (warp == 0);
     if (!is_target && !has_draft) return;
     const sdl_kv_meta& m = is_target ? tgt : drf;
+    // rows past *n_valid pad a captured batch: they are not committed
+    if (n_valid != nullptr) n = min(n, max(0, *n_valid));
     int32_t top = *m.free_top;
     for (int32_t b = 0; b < n; ++b) {
         int32_t row = rows[b];
@@ -442,10 +444,11 @@ extern "C" int sdl_kv_truncate(const sdl_kv_meta* meta, int32_t n, const int32_t
     return sdl_kv_release(meta, n, rows, new_lens, nullptr, stream);
 }
 
-extern "C" int sdl_spec_commit(const sdl_kv_meta* target, const sdl_kv_meta* draft, int32_t n, const int32_t* rows,
-                               const int32_t* n_out, const int32_t* tokens, int32_t tok_stride,
-                               const int32_t* remaining, int32_t eos, const int32_t* starts, int32_t* k_out,
-                               int32_t* flags_out, int32_t* catchup_slot, void* stream) {
+namespace {
+int spec_commit_impl(const sdl_kv_meta* target, const sdl_kv_meta* draft, int32_t n, const int32_t* rows,
+                     const int32_t* n_out, const int32_t* tokens, int32_t tok_stride, const int32_t* remaining,
+                     int32_t eos, const int32_t* starts, int32_t* k_out, int32_t* flags_out, int32_t* catchup_slot,
+                     const int32_t* n_valid, void* stream) {
     if (!meta_ok(target) || (draft && !meta_ok(draft)) || n < 0 ||
         (n > 0 && (!rows || !n_out || !tokens || !remaining || !starts || !k_out || !flags_out ||
                    (draft && !catchup_slot))))
@@ -454,8 +457,27 @@ extern "C" int sdl_spec_commit(const sdl_kv_meta* target, const sdl_kv_meta* dra
     sdl_kv_meta d = draft ? *draft : *target;
     spec_commit_kernel<<<1, 64, 0, sdl::as_stream(stream)>>>(*target, d, draft ? 1 : 0, n, rows, n_out, tokens,
                                                             tok_stride, remaining, eos, starts, k_out, flags_out,
-                                                            catchup_slot);
+                                                            catchup_slot, n_valid);
     return sdl::check_launch("spec_commit_kernel");
+}
+}  // namespace
+
+extern "C" int sdl_spec_commit(const sdl_kv_meta* target, const sdl_kv_meta* draft, int32_t n, const int32_t* rows,
+                               const int32_t* n_out, const int32_t* tokens, int32_t tok_stride,
+                               const int32_t* remaining, int32_t eos, const int32_t* starts, int32_t* k_out,
+                               int32_t* flags_out, int32_t* catchup_slot, void* stream) {
+    return spec_commit_impl(target, draft, n, rows, n_out, tokens, tok_stride, remaining, eos, starts, k_out,
+                            flags_out, catchup_slot, nullptr, stream);
+}
+
+extern "C" int sdl_spec_commit_n(const sdl_kv_meta* target, const sdl_kv_meta* draft, int32_t n,
+                                 const int32_t* rows, const int32_t* n_out, const int32_t* tokens,
+                                 int32_t tok_stride, const int32_t* remaining, int32_t eos, const int32_t* starts,
+                                 int32_t* k_out, int32_t* flags_out, int32_t* catchup_slot,
+                                 const int32_t* n_valid, void* stream) {
+    if (!n_valid) return sdl::fail(SDL_ERR_INVALID, "sdl_spec_commit_n: n_valid is NULL");
+    return spec_commit_impl(target, draft, n, rows, n_out, tokens, tok_stride, remaining, eos, starts, k_out,
+                            flags_out, catchup_slot, n_valid, stream);
 }
 
 extern "C" int sdl_get_error(int32_t* err_word, int32_t* out_host, int32_t clear, void* stream) {

@@ -482,12 +482,14 @@ __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> 
                                                              const int* __restrict__ prop, int B, int gamma,
                                                              const float* __restrict__ uniforms, int64_t nu,
                                                              int64_t* u_base, int64_t u_skip, int* n_acc,
-                                                             int* u_bits, int* err) {
+                                                             int* u_bits, int* err, const int* n_valid) {
     extern __shared__ double s_dyn[];
     double* a = s_dyn;                                                // [B*gamma]
     float* uc = reinterpret_cast<float*>(s_dyn + (size_t)B * gamma);  // [B*(gamma+1)]
     pdl_wait();
     const int64_t base = (u_base ? *u_base : 0) + u_skip;
+    // sequences past *n_valid pad a captured batch: no uniforms, a harmless bonus draw
+    const int Bn = n_valid != nullptr ? min(B, max(0, *n_valid)) : B;
     for (int idx = threadIdx.x; idx < B * gamma; idx += blockDim.x) {
         const int b = idx / gamma, j = idx % gamma;
         const int x = prop[idx];
@@ -515,7 +517,11 @@ __global__ void __launch_bounds__(1024) accept_logits_kernel(Rows<T> A, Rows<T> 
     const int lane = threadIdx.x;
     int off = 0;
     bool bad_u = false;
-    for (int b = 0; b < B; ++b) {
+    for (int b = Bn + lane; b < B; b += 32) {
+        n_acc[b] = gamma;
+        u_bits[b] = __float_as_int(0.5f);
+    }
+    for (int b = 0; b < Bn; ++b) {
         bool reject = false;
         if (lane < gamma) {
             const float u = uc[off + lane];
@@ -1035,9 +1041,12 @@ template <typename T>
 int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t q_sb, int64_t q_sj, float temp,
                   const int* prop, int B, int gamma, int V, const float* uniforms, int64_t nu, int64_t* u_base,
                   int64_t u_skip, int* tokens, int* n_out, void* ws_base, size_t ws_bytes, int* err,
-                  cudaStream_t st) {
-    const int fused = spec_fused_try<T>(pl, p_sb, p_sj, ql, q_sb, q_sj, temp, prop, B, gamma, V, uniforms, nu, u_base,
-                                        u_skip, tokens, n_out, ws_base, ws_bytes, err, st);
+                  const int* n_valid, cudaStream_t st) {
+    // a device sequence count (padded captured batches) takes the chain
+    const int fused = n_valid != nullptr ? 0
+                                         : spec_fused_try<T>(pl, p_sb, p_sj, ql, q_sb, q_sj, temp, prop, B, gamma, V,
+                                                             uniforms, nu, u_base, u_skip, tokens, n_out, ws_base,
+                                                             ws_bytes, err, st);
     if (fused != 0) return fused > 0 ? SDL_OK : -fused;
     const int nchunks = (V + kChunk - 1) / kChunk;
     const int ndc = (V + kDrawChunk - 1) / kDrawChunk;
@@ -1061,7 +1070,7 @@ int spec_logits_t(const T* pl, int64_t p_sb, int64_t p_sj, const T* ql, int64_t 
     if (e == cudaSuccess)
         e = sdl::launch_pdl(accept_logits_kernel<T>, dim3(1), dim3(1024), smem, st, A, Q, V, temp,
                             (const float2*)w.rowstat, prop, B, gamma, uniforms, nu, u_base, u_skip, w.n_acc, w.u_bits,
-                            err);
+                            err, n_valid);
     if (e == cudaSuccess)
         e = sdl::launch_pdl(wsum_kernel<T>, dim3(ndc, B), dim3(kGroup), 0, st, A, Q, V, temp,
                             (const float2*)w.rowstat, ndc, 1, gamma, (const int*)w.n_acc, w.wsum);
@@ -1131,12 +1140,12 @@ extern "C" int sdl_sample_logits_rows(const void* logits, int32_t dtype, int64_t
     return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_sample_logits_rows: dtype");
 }
 
-extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj, const void* q_logits,
-                                      int64_t q_sb, int64_t q_sj, int32_t dtype, float temperature, float eps,
-                                      const int32_t* proposals, int32_t B, int32_t gamma, int32_t vocab,
-                                      const float* uniforms, int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
-                                      int32_t* tokens, int32_t* n_out, void* workspace, size_t workspace_bytes,
-                                      int32_t* err, void* stream) {
+namespace {
+int spec_sample_logits_impl(const void* p_logits, int64_t p_sb, int64_t p_sj, const void* q_logits, int64_t q_sb,
+                            int64_t q_sj, int32_t dtype, float temperature, float eps, const int32_t* proposals,
+                            int32_t B, int32_t gamma, int32_t vocab, const float* uniforms, int64_t num_uniforms,
+                            int64_t* u_base, int64_t u_skip, int32_t* tokens, int32_t* n_out, void* workspace,
+                            size_t workspace_bytes, int32_t* err, const int32_t* n_valid, void* stream) {
     if (!p_logits || !q_logits || !proposals || !uniforms || !tokens || !n_out || B < 0 || gamma < 1 || gamma > 32 ||
         vocab < 1)
         return sdl::fail(SDL_ERR_INVALID, "sdl_spec_sample_logits: bad args (gamma must be 1..32)");
@@ -1156,17 +1165,41 @@ extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_
     if (dtype == SDL_F32)
         return spec_logits_t<float>((const float*)p_logits, p_sb, p_sj, (const float*)q_logits, q_sb, q_sj, t,
                                     proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens, n_out,
-                                    workspace, workspace_bytes, err, st);
+                                    workspace, workspace_bytes, err, n_valid, st);
     if (dtype == SDL_BF16)
         return spec_logits_t<__nv_bfloat16>((const __nv_bfloat16*)p_logits, p_sb, p_sj,
                                             (const __nv_bfloat16*)q_logits, q_sb, q_sj, t, proposals, B, gamma, vocab,
                                             uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace,
-                                            workspace_bytes, err, st);
+                                            workspace_bytes, err, n_valid, st);
     if (dtype == SDL_F16)
         return spec_logits_t<__half>((const __half*)p_logits, p_sb, p_sj, (const __half*)q_logits, q_sb, q_sj, t,
                                      proposals, B, gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens,
-                                     n_out, workspace, workspace_bytes, err, st);
+                                     n_out, workspace, workspace_bytes, err, n_valid, st);
     return sdl::fail(SDL_ERR_UNSUPPORTED, "sdl_spec_sample_logits: dtype");
+}
+}  // namespace
+
+extern "C" int sdl_spec_sample_logits(const void* p_logits, int64_t p_sb, int64_t p_sj, const void* q_logits,
+                                      int64_t q_sb, int64_t q_sj, int32_t dtype, float temperature, float eps,
+                                      const int32_t* proposals, int32_t B, int32_t gamma, int32_t vocab,
+                                      const float* uniforms, int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
+                                      int32_t* tokens, int32_t* n_out, void* workspace, size_t workspace_bytes,
+                                      int32_t* err, void* stream) {
+    return spec_sample_logits_impl(p_logits, p_sb, p_sj, q_logits, q_sb, q_sj, dtype, temperature, eps, proposals, B,
+                                   gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace,
+                                   workspace_bytes, err, nullptr, stream);
+}
+
+extern "C" int sdl_spec_sample_logits_n(const void* p_logits, int64_t p_sb, int64_t p_sj, const void* q_logits,
+                                        int64_t q_sb, int64_t q_sj, int32_t dtype, float temperature, float eps,
+                                        const int32_t* proposals, int32_t B, int32_t gamma, int32_t vocab,
+                                        const float* uniforms, int64_t num_uniforms, int64_t* u_base, int64_t u_skip,
+                                        int32_t* tokens, int32_t* n_out, void* workspace, size_t workspace_bytes,
+                                        int32_t* err, const int32_t* n_valid, void* stream) {
+    if (!n_valid) return sdl::fail(SDL_ERR_INVALID, "sdl_spec_sample_logits_n: n_valid is NULL");
+    return spec_sample_logits_impl(p_logits, p_sb, p_sj, q_logits, q_sb, q_sj, dtype, temperature, eps, proposals, B,
+                                   gamma, vocab, uniforms, num_uniforms, u_base, u_skip, tokens, n_out, workspace,
+                                   workspace_bytes, err, n_valid, stream);
 }
 
 extern "C" int sdl_set_spec_sampler_mode(int32_t mode) {

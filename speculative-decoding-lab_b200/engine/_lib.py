@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "sdl_kv_release",
     "sdl_kv_truncate",
     "sdl_spec_commit",
+    "sdl_spec_commit_n",
     "sdl_make_kv_tensor_map",
     "sdl_attention_workspace_bytes",
     "sdl_attention_launches",
@@ -71,6 +72,7 @@ EXPORTED_SYMBOLS = (
     "sdl_sampler_workspace_bytes",
     "sdl_sample_logits_rows",
     "sdl_spec_sample_logits",
+    "sdl_spec_sample_logits_n",
     "sdl_set_spec_sampler_mode",
     "sdl_get_error",
     "sdl_rmsnorm",
@@ -151,6 +153,8 @@ _SIGS = {
     "sdl_kv_truncate": (c_int, [_P(SdlKvMeta), c_int, c_void, c_void, c_void]),
     "sdl_spec_commit": (c_int, [_P(SdlKvMeta), _P(SdlKvMeta), c_int, c_void, c_void, c_void, c_int, c_void,
                                 c_int, c_void, c_void, c_void, c_void, c_void]),
+    "sdl_spec_commit_n": (c_int, [_P(SdlKvMeta), _P(SdlKvMeta), c_int, c_void, c_void, c_void, c_int, c_void,
+                                  c_int, c_void, c_void, c_void, c_void, c_void, c_void]),
     "sdl_make_kv_tensor_map": (c_int, [c_void, c_void, c_int, c_i64, c_int, c_int]),
     "sdl_attention_workspace_bytes": (c_size, [_P(SdlAttnArgs)]),
     "sdl_attention_launches": (c_int, [_P(SdlAttnArgs)]),
@@ -178,6 +182,9 @@ _SIGS = {
     "sdl_spec_sample_logits": (c_int, [c_void, c_i64, c_i64, c_void, c_i64, c_i64, c_int, c_float, c_float, c_void,
                                        c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void, c_void,
                                        c_size, c_void, c_void]),
+    "sdl_spec_sample_logits_n": (c_int, [c_void, c_i64, c_i64, c_void, c_i64, c_i64, c_int, c_float, c_float,
+                                         c_void, c_int, c_int, c_int, c_void, c_i64, c_void, c_i64, c_void, c_void,
+                                         c_void, c_size, c_void, c_void, c_void]),
     "sdl_set_spec_sampler_mode": (c_int, [c_int]),
     "sdl_get_error": (c_int, [c_void, c_void, c_int, c_void]),
     "sdl_rmsnorm": (c_int, [c_void, c_i64, c_void, c_i64, c_void, c_i64, c_void, c_void, c_i64, c_int, c_int, c_float,

@@ -68,6 +68,8 @@ class _DraftLoop:
     store are row 0's own bytes.  Their draws read uniforms past the batch's,
     inside the stream storage's capacity, and are discarded."""
 
+    EXTRA_FIELDS = 0  # per-row int32 fields staged between the ids and the batch size
+
     def __init__(self, sched: "SpeculativePagedScheduler", bucket: int, span: int, greedy: bool) -> None:
         draft, kv = sched.draft_model, sched.draft_kv
         dev = draft.device
@@ -76,8 +78,9 @@ class _DraftLoop:
         V = W.shape[0]
         self.bucket, self.span, self.greedy, self.gamma = bucket, span, greedy, g
         b = bucket
-        self.meta_h = torch.zeros(4 * b + 1, dtype=torch.int32).pin_memory()
-        self.meta = torch.zeros(4 * b + 1, dtype=torch.int32, device=dev)
+        self.n_off = (4 + self.EXTRA_FIELDS) * b  # meta: rows | d0 | counts | ids | extra fields | batch size
+        self.meta_h = torch.zeros(self.n_off + 1, dtype=torch.int32).pin_memory()
+        self.meta = torch.zeros(self.n_off + 1, dtype=torch.int32, device=dev)
         self.props = torch.zeros((g, b), dtype=torch.int32, device=dev)
         self.q = sched._loop_q_buffer(V, W.dtype, dev)  # (gamma, rows, V): the round buffer
         self.slots = torch.zeros(b, dtype=torch.int32, device=dev)
@@ -99,7 +102,7 @@ class _DraftLoop:
         meta = self.meta
         rows, d0, counts = meta[:b], meta[b:2 * b], meta[2 * b:3 * b]
         keep = counts > 0
-        n64 = meta[4 * b:4 * b + 1].to(torch.int64)
+        n64 = meta[self.n_off:self.n_off + 1].to(torch.int64)
         cur = meta[3 * b:4 * b].to(torch.int64)
         for t in range(g):
             starts = d0 + t
@@ -146,12 +149,101 @@ class _DraftLoop:
         m[2 * b + B:3 * b] = 0
         m[3 * b:3 * b + B] = last
         m[3 * b + B:4 * b] = last[0]
-        m[4 * b] = B
+        m[self.n_off] = B
+        self._stage_extra(m, B)
         self.meta.copy_(self.meta_h, non_blocking=True)
+
+    def _stage_extra(self, m, B: int) -> None:
+        """Fill the subclass's extra per-row fields of the pinned staging row."""
 
     def replay(self) -> None:
         self.graph.replay()
         _lib.count_calls(self.calls)
+
+
+class _RoundGraph(_DraftLoop):
+    """A whole speculative round as one CUDA graph, for one (batch bucket,
+    key-span bucket of both caches): the captured draft loop, then the
+    target's reserve of gamma+1 positions per row, its verify forward over
+    [last token | proposals] with the head into the verify logits buffer,
+    the rejection sampling (``sdl_spec_sample_logits_n``, or the argmax
+    chain when greedy) and the device commit (``sdl_spec_commit_n``) -- both
+    stop at the staged batch size, so padding rows consume no uniforms and
+    commit nothing, and padding rows verify row 0's proposals, so what they
+    store at row 0's positions is row 0's own K/V.  The host stages one
+    pinned row, replays, and reads the packed results once, as the
+    step-by-step round does."""
+
+    EXTRA_FIELDS = 3  # target start, target count, remaining budget
+
+    def __init__(self, sched: "SpeculativePagedScheduler", bucket: int, span: int, greedy: bool) -> None:
+        super().__init__(sched, bucket, span, greedy)
+        dev = self.meta.device
+        b, g = bucket, sched.gamma
+        self.target, self.tkv = sched.model, sched.kv
+        self.Wt = sched.model.lm_head.weight
+        self.eos = -1 if sched._eos is None else int(sched._eos)
+        self.tslots = torch.zeros(b * (g + 1), dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros((b, g + 1), dtype=torch.int32, device=dev)
+        self.n_out = torch.zeros(b, dtype=torch.int32, device=dev)
+        self.outs = torch.zeros((3, b), dtype=torch.int32, device=dev)
+        self.steps = torch.arange(g + 1, device=dev)
+        if not greedy:
+            V = self.Wt.shape[0]
+            need = int(_lib.load().sdl_sampler_workspace_bytes(b * (2 * g + 1), V))
+            self.sws = _lib.Workspace.get(dev, need, tag="sampler")
+
+    def _stage_extra(self, m, B: int) -> None:
+        b = self.bucket
+        m[4 * b:4 * b + B] = self._tstart
+        m[4 * b + B:5 * b] = self._tstart[0]
+        m[5 * b:5 * b + B] = self.gamma + 1
+        m[5 * b + B:6 * b] = 0
+        m[6 * b:6 * b + B] = self._remaining
+        m[6 * b + B:7 * b] = 0
+
+    def stage_round(self, sids: List[int], d0: List[int], last: List[int], tstart: List[int],
+                    remaining: List[int]) -> None:
+        self._tstart, self._remaining = tstart, remaining
+        self.stage(sids, d0, last)
+
+    def _run(self) -> None:
+        super()._run()  # the draft loop: proposals in self.props, draft logits in self.q
+        lib, b, g, V = _lib.load(), self.bucket, self.gamma, self.Wt.shape[0]
+        C = g + 1
+        meta, dev = self.meta, self.meta.device
+        rows, tstart, tcounts = meta[:b], meta[4 * b:5 * b], meta[5 * b:6 * b]
+        remaining, nvalid = meta[6 * b:7 * b], meta[self.n_off:self.n_off + 1]
+        # padding rows verify row 0's proposals (their own draws differ), so
+        # the K/V rows they store at row 0's positions are row 0's bytes
+        keep = meta[2 * b:3 * b] > 0
+        props = torch.where(keep.unsqueeze(0), self.props, self.props[:, :1]).t().contiguous()  # (b, gamma)
+        ids = torch.cat((meta[3 * b:4 * b].to(torch.int64).unsqueeze(1), props.to(torch.int64)), dim=1)
+        tkv = self.tkv
+        _lib.check(lib.sdl_kv_reserve(ctypes.byref(tkv._meta), b, rows.data_ptr(), tstart.data_ptr(),
+                                      tcounts.data_ptr(), self.tslots.data_ptr(), tkv._stream()), "sdl_kv_reserve")
+        batch = AttnBatch(rows, tstart, self.span, key_count=-1)
+        positions = tstart.to(torch.int64).unsqueeze(1) + self.steps.unsqueeze(0)
+        normed = self.target._body(ids, tkv, batch, positions)
+        plog = self.target._graph_logits_buffer(C, b)
+        torch.matmul(normed, self.Wt.t(), out=plog)
+        st = _lib.stream_handle(dev)
+        if self.greedy:
+            p_arg = argmax_rows(plog.reshape(b * C, V)).reshape(b, C)
+            tok, n_out = spec_sample(None, None, props, None, greedy=True, p_arg=p_arg)
+            self.tokens.copy_(tok)
+            self.n_out.copy_(n_out)
+        else:
+            R = self.q.shape[1]
+            _lib.check(lib.sdl_spec_sample_logits_n(
+                plog.data_ptr(), C * V, V, self.q.data_ptr(), V, R * V, _lib.dtype_code(plog.dtype), self.temp,
+                1e-12, props.data_ptr(), b, g, V, self.ubuf.data_ptr(), self.ubuf.numel(), self.ucnt.data_ptr(), 0,
+                self.tokens.data_ptr(), self.n_out.data_ptr(), self.sws.data_ptr(), self.sws.numel() * 4,
+                tkv.err_word.data_ptr(), nvalid.data_ptr(), st), "sdl_spec_sample_logits_n")
+        _lib.check(lib.sdl_spec_commit_n(
+            ctypes.byref(tkv.meta), ctypes.byref(self.kv.meta), b, rows.data_ptr(), self.n_out.data_ptr(),
+            self.tokens.data_ptr(), C, remaining.data_ptr(), self.eos, tstart.data_ptr(), self.outs[0].data_ptr(),
+            self.outs[1].data_ptr(), self.outs[2].data_ptr(), nvalid.data_ptr(), st), "sdl_spec_commit_n")
 
 
 def _draw_uniform(generator: torch.Generator) -> float:
@@ -217,10 +309,14 @@ class SpeculativePagedScheduler(PagedScheduler):
         # bucket, key-span bucket); the round buffer and the uniform storage
         # they write and read live as long as the scheduler
         self.draft_loops = True
+        # with draft_loops: capture whole rounds (draft loop, verify, sampling,
+        # commit) rather than the draft phase alone
+        self.round_graphs = True
         self._loops: Dict[Any, _DraftLoop] = {}
         self._loop_q: Optional[torch.Tensor] = None
         self._u_storage = None
         self.loop_replays = 0  # rounds whose draft phase was one loop replay
+        self.round_replays = 0  # rounds that were one whole-round replay
         # optional observer of every round: called with (sequence ids, target
         # start positions, draft lengths) before the round's first launch
         self.round_hook: Optional[Callable[[List[int], List[int], List[int]], None]] = None
@@ -482,21 +578,35 @@ class SpeculativePagedScheduler(PagedScheduler):
             self._u_storage = (torch.zeros(self.U_CAPACITY + self.U_MARGIN, dtype=torch.float32, device=dev),
                                torch.zeros(1, dtype=torch.int64, device=dev))
         n, prev, g = 0, 0, self.gamma
+        whole = self.round_graphs and hasattr(self.model, "_body") and \
+            getattr(self.model, "_graphs_enabled", False) and \
+            self.model.graph_spans(self.kv) == draft.graph_spans(kv)
+        tkv = self.kv
         for span in draft.graph_spans(kv):
-            need = max(prev + 1, int(0.55 * span), g + 1)
+            need = max(prev + 1, int(0.55 * span), g + 2)
             prev = span
-            kv.reserve([sid], [0], [need - g])
             for b in draft.GRAPH_BUCKETS:
-                loop = _DraftLoop(self, b, span, greedy)
-                kv._plan_reserve([sid], [need - g], [g])  # the scratch pass's reserves, on the host shadows
+                # the scratch pass reserves the draft's gamma positions and the
+                # target's gamma + 1 (on the host shadows too) and, whole, commits
+                kv.reserve([sid], [0], [need - g])
+                kv._plan_reserve([sid], [need - g], [g])
                 saved = self._u_storage[1].clone()
+                if whole:
+                    tkv.reserve([sid], [0], [need - g - 1])
+                    tkv._plan_reserve([sid], [need - g - 1], [g + 1])
+                    loop = _RoundGraph(self, b, span, greedy)
+                    loop._tstart, loop._remaining = [need - g - 1], [1 << 20]
+                else:
+                    loop = _DraftLoop(self, b, span, greedy)
                 loop.capture([sid], [need - g], [0])
                 self._u_storage[1].copy_(saved)
-                kv.truncate(sid, need - g)
+                kv.clear(sid)
+                if whole:
+                    tkv.clear(sid)
                 self._loops[(b, span, greedy, float(self.sampling.temperature))] = loop
                 n += 1
-            kv.clear(sid)
         kv.check_errors()
+        tkv.check_errors()
         return n
 
     def capture_graphs(self) -> int:
@@ -622,10 +732,11 @@ class SpeculativePagedScheduler(PagedScheduler):
         return result
 
     # ------------------------------------------------------------ one round
-    def _draft_loop_for(self, B: int, d0: List[int], stream: Optional[UniformStream]) -> Optional[_DraftLoop]:
-        """The captured draft loop for this round's batch and draft contexts,
-        or None (not captured, a batch beyond the largest bucket, or a
-        stream outside the loops' storage)."""
+    def _draft_loop_for(self, B: int, d0: List[int], stream: Optional[UniformStream],
+                        starts: List[int]) -> Optional[_DraftLoop]:
+        """The captured round (or draft loop) for this round's batch and
+        contexts, or None (not captured, a batch beyond the largest bucket,
+        or a stream outside the captures' uniform storage)."""
         if not self._loops:
             return None
         draft = self.draft_model
@@ -635,7 +746,8 @@ class SpeculativePagedScheduler(PagedScheduler):
         bucket = draft._graph_bucket(B)
         if bucket is None:
             return None
-        span = draft.span_bucket(self.draft_kv, max(d0) + self.gamma)
+        need = max(max(d0) + self.gamma, max(starts) + self.gamma + 1)
+        span = draft.span_bucket(self.draft_kv, need)
         return self._loops.get((bucket, span, self.sampling.is_greedy, float(self.sampling.temperature)))
 
     def _plain_temperature(self, vocab: int) -> bool:
@@ -669,15 +781,43 @@ class SpeculativePagedScheduler(PagedScheduler):
         if self.round_hook is not None:
             self.round_hook(sids, starts, d0)
 
+        last = [s.generated[-1] for s in running]
+        remaining = [s.max_new_tokens - len(s.generated) for s in running]
+        loop = self._draft_loop_for(B, d0, stream, starts)
+        if isinstance(loop, _RoundGraph):
+            # the whole round is one graph replay; the host reads its packed results below
+            self.draft_kv._plan_reserve(sids, d0, [gamma] * B)
+            self.kv._plan_reserve(sids, starts, [chunk] * B)
+            if not greedy:
+                stream.reserve(gamma * B + B * chunk)
+            loop.stage_round(sids, d0, last, starts, remaining)
+            loop.replay()
+            self.round_replays += 1
+            result.draft_forward_calls += gamma
+            draft.forward_calls = getattr(draft, "forward_calls", 0) + gamma
+            model.forward_calls = getattr(model, "forward_calls", 0) + 1
+            tokens, outs = loop.tokens[:B], loop.outs[:, :B]
+        else:
+            tokens, outs = self._round_steps(running, result, stream, loop, sids, starts, d0, last, remaining)
+        self._finish_round(running, result, tokens, outs)
+
+    def _round_steps(self, running, result, stream, loop, sids, starts, d0, last, remaining):
+        """The round launch by launch (or with the captured draft loop):
+        returns the sampled tokens and the commit's (k, flags, catch-up slot)."""
+        model, draft = self.model, self.draft_model
+        device = model.device
+        gamma = self.gamma
+        chunk = gamma + 1
+        greedy = self.sampling.is_greedy
+        B = len(running)
+
         # ---- 1. draft proposes gamma tokens per sequence
         q_probs = None
         if not greedy:
             stream.reserve(gamma * B)
-        last = [s.generated[-1] for s in running]
         fused = False
         u_skip = gamma * B  # uniforms the draft draws read ahead of the accept walk
         V_d = getattr(getattr(draft, "lm_head", None), "weight", None)
-        loop = self._draft_loop_for(B, d0, stream)
         if loop is not None:
             # the whole draft phase is one graph replay: reserves, forwards,
             # heads into the round buffer, draws (advancing the counter)
@@ -748,7 +888,6 @@ class SpeculativePagedScheduler(PagedScheduler):
                                         err=self.kv.err_word)
 
         # ---- 4. device commit: clip, EOS cut, rewind, draft alignment, clears
-        remaining = [s.max_new_tokens - len(s.generated) for s in running]
         packed = _lib.i32(sids + remaining + starts, device)
         outs = torch.empty((3, B), dtype=torch.int32, device=device)
         eos = -1 if self._eos is None else int(self._eos)
@@ -761,6 +900,15 @@ class SpeculativePagedScheduler(PagedScheduler):
             ),
             "sdl_spec_commit",
         )
+        return tokens, outs
+
+    def _finish_round(self, running, result, tokens, outs) -> None:
+        """Read a round's packed results once and mirror them on the host
+        (sequences, shadows), then run the draft catch-up."""
+        draft = self.draft_model
+        device = self.model.device
+        chunk = self.gamma + 1
+        B = len(running)
         host = torch.cat((tokens.reshape(-1), outs.reshape(-1), self.kv.err_word, self.draft_kv.err_word)).tolist()
         tok_h = host[: B * chunk]
         k_h = host[B * chunk: B * chunk + B]

@@ -166,7 +166,7 @@ def test_precaptured_graphs_and_wall_clock_admission_reproduce_c1(label):
     assert [s.generated for s in res.sequences] == run["generated"]
     assert res.tokens_per_round == run["tokens_per_round"]
     assert (len(target._graphs), len(draft._graphs)) == before
-    assert sched.loop_replays == len(rounds) > 0  # every round's draft phase was one replay
+    assert sched.round_replays == len(rounds) > 0  # every round was one whole-round replay
     kv.check_errors()
     dkv.check_errors()
 
@@ -271,10 +271,13 @@ def test_graphed_batched_prefill_matches_eager():
 @pytest.mark.parametrize("temperature", [0.0, 1.0])
 def test_captured_draft_loop_matches_step_by_step(temperature):
     """The draft phase as one captured loop (reserve, forward, head and draw
-    for all gamma steps in one graph) gives the tokens, round structure and
-    uniform consumption of the step-by-step path on 16-bit models."""
+    for all gamma steps in one graph), and the whole round as one graph
+    (that loop, the target's reserve and verify forward, the rejection
+    sampling and the commit, padding rows inert), give the tokens, round
+    structure, block tables and uniform consumption of the step-by-step
+    path on 16-bit models."""
     runs = []
-    for loops in (False, True):
+    for loops, whole in ((False, False), (True, False), (True, True)):
         target = _model("c1-target", 5, torch.bfloat16)
         draft = _model("c1-draft", 6, torch.bfloat16)
         target.enable_cuda_graphs()
@@ -284,6 +287,7 @@ def test_captured_draft_loop_matches_step_by_step(temperature):
         dkv = build_kv(draft, cfg, DEV, max_seqs=16)
         sched = SpeculativePagedScheduler(target, kv, draft, dkv, cfg, SpecSampling(temperature=temperature), 4)
         sched.draft_loops = loops
+        sched.round_graphs = whole
         sched.capture_graphs()
         assert bool(sched._loops) == loops
         sched._next_sid = 0
@@ -292,11 +296,17 @@ def test_captured_draft_loop_matches_step_by_step(temperature):
                                 arrive_time=float(i // 3))
                 for i, n in enumerate((5, 40, 130, 17, 300, 64, 9))]
         rounds = []
-        sched.round_hook = lambda sids, starts, d0: rounds.append(len(sids))
+        tables = []
+        # (the captures' scratch reservations order each run's free lists
+        # differently, so the tables are compared by their lengths)
+        sched.round_hook = lambda sids, starts, d0: (rounds.append(len(sids)), tables.append(
+            ([len(t) for t in kv.block_tables], [len(t) for t in dkv.block_tables], list(kv.seq_lengths),
+             list(dkv.seq_lengths))))
         res = sched.run_spec_continuous(reqs, seed=3, measure=False)
         runs.append(([s.generated for s in res.sequences], res.tokens_per_round, res.draft_forward_calls,
-                     rounds, sched.loop_replays))
+                     rounds, tables, (sched.loop_replays, sched.round_replays)))
         kv.check_errors()
         dkv.check_errors()
-    assert runs[0][:4] == runs[1][:4]
-    assert runs[0][4] == 0 and runs[1][4] == len(runs[1][3]) > 0
+    assert runs[0][:5] == runs[1][:5] == runs[2][:5]
+    n = len(runs[0][3])
+    assert n > 0 and runs[0][5] == (0, 0) and runs[1][5] == (n, 0) and runs[2][5] == (0, n)
