@@ -143,12 +143,12 @@ def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
     assert _lib.load().sdl_attention_launches(ctypes.byref(a)) == 2
 
 
-@pytest.mark.parametrize("R,want_splits", [(8, 1), (1, 7)])
-def test_ragged_prefill_rows_split_only_to_fill_the_sms(R, want_splits):
+@pytest.mark.parametrize("R,span,want_splits", [(8, 4656, 1), (8, 1024, 1), (1, 4656, 7)])
+def test_ragged_prefill_rows_split_only_to_fill_the_sms(R, span, want_splits):
     """Ragged prefill chunk rows (128 positions, 12 q / 2 kv heads: 12 row
     tiles per kv head) split only until every SM has a CTA: their partials
     outweigh the pages a split saves."""
-    a = _args(R, 128, 12, 2, 128, 4656, key_count=-1)
+    a = _args(R, 128, 12, 2, 128, span, key_count=-1)
     lib = _lib.load()
     ws = lib.sdl_attention_workspace_bytes(ctypes.byref(a))
     if want_splits == 1:
