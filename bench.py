@@ -67,6 +67,12 @@ C2 = dict(layers=28, q_heads=12, kv_heads=2, head_dim=128, block_size=16, batch=
 # DRAM bytes (read + write) of one C2 attention launch of attn_tc_kernel, from the
 # ncu --set full capture summarised under profiles/ (refreshed when re-profiled).
 C2_ATTN_TRAFFIC = 154_167_040 + 3_741_184
+# DRAM bytes per algorithmic byte of C4's two attention main kernels under the
+# ragged plan, from ncu --set full captures at 358 sequences (summaries under
+# profiles/): the bench's rooflines run at the run's heaviest round, whose size
+# varies, so traffic is scaled by the algorithmic bytes the launch moves
+C4_DECODE_TRAFFIC_RATIO = (135_227_136 + 4_350_464) / 134_700_000
+C4_VERIFY_TRAFFIC_RATIO = (276_881_152 + 14_143_232) / 282_200_000
 
 # kernel names of the attention op per attention_kernel() answer
 ATTN_KERNELS = {
@@ -1863,7 +1869,11 @@ def main_c4(args) -> int:
         "graphs_captured": n_graphs,
         "graph_capture_s": round(cap_s, 2),
         "roofline": {"bound": "hbm", "achieved": round(d_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(d_gbs / hbm, 4), "traffic": None,
+                     "frac": round(d_gbs / hbm, 4),
+                     "traffic": round(draft_op["bytes"] * C4_DECODE_TRAFFIC_RATIO),
+                     "traffic_source": "ncu dram read+write of attn_tc_kernel at 358 C4 sequences "
+                                       "(profiles/attn_tc_kernel_c4_draft_decode_ragged.md), scaled by the "
+                                       "algorithmic bytes of this launch",
                      "kernel": names[draft_op["kernel"]] + ": draft decode attention (0.5B shape, 24 layers), "
                                "K/V append fused, on the heaviest round's draft contexts",
                      "batch": draft_op["batch"], "mean_ctx": draft_op["mean_ctx"], "plan": draft_op["plan"],
@@ -1871,6 +1881,10 @@ def main_c4(args) -> int:
                      "peak_source": "{} (MEASURED_PEAKS.json hbm_gbs)".format(peak_kind)},
         "verify_roofline": {"bound": "hbm", "achieved": round(v_gbs, 1), "peak": hbm, "unit": "GB/s",
                             "frac": round(v_gbs / hbm, 4),
+                            "traffic": round(verify_op["bytes"] * C4_VERIFY_TRAFFIC_RATIO),
+                            "traffic_source": "ncu dram read+write of attn_rows_kernel at 358 C4 sequences "
+                                              "(profiles/attn_rows_kernel_c4_verify_ragged.md), scaled by the "
+                                              "algorithmic bytes of this launch",
                             "kernel": names[verify_op["kernel"]] + ": 5-row verify attention (1.5B shape, 28 "
                                       "layers), K/V append fused, on the heaviest round's target contexts",
                             "batch": verify_op["batch"], "mean_ctx": verify_op["mean_ctx"],
