@@ -2756,6 +2756,15 @@ constexpr int kDirAutoMaxKeys = 1280;
 // kernel runs.
 constexpr int64_t kDirMidKeysLo = 160 * 1024;
 constexpr int64_t kDirMidKeysHi = 560 * 1024;
+// Ragged rows of unknown lengths (key_count < 0, a captured forward): the
+// register-direct kernel for head_dim-64 decode of up to kDirRaggedMaxRows
+// sequences, where it skips the TMA ring's ramp.  0.5B-shaped draft decode
+// over C4-shaped batches (contexts floor(lognormal(6, 0.8)) + U[0, 512)
+// tokens, span buckets up to 4656 keys), graphs of 8 layers, measured on
+// B200 against the keys-on-M TMA kernel, both with the ragged split rule:
+// 1 / 8 / 16 / 32 / 64 / 96 / 128 sequences 6.2 / 8.7 / 9.0 / 9.2 / 13.3 /
+// 16.2 / 20.9 us against 8.5 / 14.6 / 14.1 / 11.8 / 18.3 / 19.7 / 20.5.
+constexpr int kDirRaggedMaxRows = 96;
 bool direct_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->mma_layout == 2 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->chunk * (a->Hq / a->Hkv) > kDirCols) return false;
@@ -2763,9 +2772,10 @@ bool direct_applicable(const sdl_attn_args* a) {
     const void* v = a->k_pool ? a->v_pool : a->v_dense;
     if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) return false;
     if (a->mma_layout == 3) return true;
+    if (a->chunk != 1 || a->head_dim != 64) return false;
+    if (a->key_count < 0) return a->B <= kDirRaggedMaxRows;
     const bool mid = a->key_count > kDirMidKeysLo && a->key_count <= kDirMidKeysHi;
-    return a->chunk == 1 && a->head_dim == 64 && a->key_count > 0 &&
-           a->key_count <= (int64_t)kDirAutoMaxKeys * a->B && !mid;
+    return a->key_count > 0 && a->key_count <= (int64_t)kDirAutoMaxKeys * a->B && !mid;
 }
 
 Plan make_direct_plan(const sdl_attn_args* a) {

@@ -183,7 +183,7 @@ def test_split_plans_agree(pps, heads_per_cta, umma, cluster, layout):
     kv.check_errors()
 
 
-@pytest.mark.parametrize("layout", [0, 1, 2])
+@pytest.mark.parametrize("layout", [0, 1, 2, 3])
 @pytest.mark.parametrize("chunk,Hq,d", [(5, 12, 128), (1, 14, 64)])
 def test_ragged_plan_matches_oracle(chunk, Hq, d, layout):
     """The plan a captured model forward replays (key_count < 0: ragged rows

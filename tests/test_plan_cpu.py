@@ -66,10 +66,17 @@ def _kernel(a):
     ((1, 512, 12, 2, 128, 512), {}, "mma_rows"),                  # prefill chunk
     ((8, 1, 4, 2, 16, 100), {"dtype": _lib.SDL_F32}, "generic"),  # fp32 pool
     ((32, 6, 12, 2, 128, 2048), {"force_generic": 1}, "generic"),
-    # ragged rows of unknown lengths (a captured graph): no register-direct or tcgen05 auto choice
+    # ragged rows of unknown lengths (a captured graph): register-direct only for
+    # head_dim-64 decode of up to 96 sequences, no tcgen05 auto choice
     ((358, 5, 12, 2, 128, 4656), {"key_count": -1}, "mma_rows"),   # C4 verify, 30 rows
     ((358, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),         # C4 draft decode
-    ((64, 1, 14, 2, 64, 1500), {"key_count": -1}, "mma"),
+    ((112, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),
+    ((96, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma_direct"),   # the drain's smaller batches
+    ((64, 1, 14, 2, 64, 1500), {"key_count": -1}, "mma_direct"),
+    ((1, 1, 14, 2, 64, 1024), {"key_count": -1}, "mma_direct"),
+    ((64, 1, 14, 2, 64, 1500), {"key_count": -1, "mma_layout": 1}, "mma"),
+    ((64, 1, 12, 2, 128, 4096), {"key_count": -1}, "mma"),         # head_dim 128: the TMA kernel
+    ((64, 5, 14, 2, 64, 4656), {"key_count": -1}, "mma_rows"),     # 35-row draft blocks
     ((16, 7, 16, 2, 128, 32768), {"key_count": -1}, "mma_rows"),   # 56 rows: rows on M, not tcgen05
     ((16, 7, 16, 2, 128, 32768), {"key_count": -1, "use_umma": 1}, "tcgen05"),
 ])
@@ -124,9 +131,10 @@ def _split_of(a):
     (64, 5, 12, 128, 4656, 128),
     (16, 5, 12, 128, 4656, 32),
     (358, 1, 14, 64, 4656, 358),     # decode keys on M: both kv heads in one CTA
-    (64, 1, 14, 64, 4656, 64),
-    (16, 1, 14, 64, 32768, 16),
-    (16, 1, 14, 64, 1024, 16),
+    (64, 1, 14, 64, 4656, 128),      # register-direct decode: one CTA per (sequence, kv head)
+    (16, 1, 14, 64, 32768, 32),
+    (16, 1, 14, 64, 1024, 32),
+    (96, 1, 14, 64, 32768, 192),
 ])
 def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
     """key_count < 0: splits of max(base/16, span pages/16) pages for decode
