@@ -294,8 +294,9 @@ size_t sdl_attention_workspace_bytes(const sdl_attn_args* args);
 int sdl_attention_launches(const sdl_attn_args* args);
 
 /* 1 when sdl_paged_attention applies RoPE (rope_cos / rope_sin) inside the
- * launch for `args` -- the mma.sync kernels with keys or query rows on M,
- * writing the new K/V rows themselves -- else 0; -1 when `args` is invalid.
+ * launch for `args` -- the mma.sync kernels with keys or query rows on M
+ * (TMA-fed or register-direct), writing the new K/V rows themselves -- else
+ * 0; -1 when `args` is invalid.
  * No counterpart in the reference. */
 int sdl_attention_fuses_rope(const sdl_attn_args* args);
 

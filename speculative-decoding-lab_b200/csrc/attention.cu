@@ -782,6 +782,19 @@ attn_direct_kernel(const TcParams p) {
                 qf[2 * j + h][0] = ok ? ld_u32(qp + 32 * j + 8 * tq + 4 * h) : 0u;
                 qf[2 * j + h][1] = ok ? ld_u32(qp + 32 * j + 8 * tq + 4 * h + 2) : 0u;
             }
+        if (ok && p.rope_cos != nullptr) {  // dims e and e + d/2 sit in pieces j and j + KC/2
+            const int64_t ro = (int64_t)(b * p.chunk + col / p.ratio) * p.rope_stride;
+            const T* cr = reinterpret_cast<const T*>(p.rope_cos) + ro;
+            const T* sr = reinterpret_cast<const T*>(p.rope_sin) + ro;
+#pragma unroll
+            for (int j = 0; j < KC / 2; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int r = 0; r < 2; ++r)
+                        rope_u32<T>(qf[2 * j + h][r], qf[2 * (j + KC / 2) + h][r], cr, sr,
+                                    32 * j + 8 * tq + 4 * h + 2 * r, HD / 2);
+        }
     }
     int lim[2];
     float m_run[2], l_run[2];
@@ -803,16 +816,28 @@ attn_direct_kernel(const TcParams p) {
     // Fused append: the warp that attends page pg first stores this kv
     // head's new rows that fall in it (lanes own 16-byte pieces, K then V);
     // __syncwarp orders those stores before the warp's own loads of the page.
+    // With RoPE a K lane rotates its piece with the partner piece (dims +-
+    // d/2; the piece count is a power of two) and the row's cos / sin.
     auto append_page = [&](int pg, int t0) {
         constexpr int PC = RB / 16;
         const int lo = max(start, pg * kPage), hi = min(start + nvalid, (pg + 1) * kPage);
         for (int pos = lo; pos < hi; ++pos) {
-            const int64_t src = ((int64_t)b * p.chunk + (pos - start)) * p.new_stride + g * RB;
+            const int64_t nrow = (int64_t)b * p.chunk + (pos - start);
+            const int64_t src = nrow * p.new_stride + g * RB;
             const int64_t dst = (int64_t)(t0 + pos - pg * kPage) * rs + g * RB;
             if (lane < 2 * PC) {
                 const bool isv = lane >= PC;
-                const int cb = (lane % PC) * 16;
-                const uint4 v = *reinterpret_cast<const uint4*>((isv ? p.v_new : p.k_new) + src + cb);
+                const int c = lane % PC;
+                const int cb = c * 16;
+                const char* s0 = (isv ? p.v_new : p.k_new) + src;
+                uint4 v = *reinterpret_cast<const uint4*>(s0 + cb);
+                if (!isv && p.rope_cos != nullptr) {
+                    const uint4 par = *reinterpret_cast<const uint4*>(s0 + (c ^ (PC / 2)) * 16);
+                    const int64_t ro = nrow * p.rope_stride * (int64_t)sizeof(T) + cb;
+                    const uint4 cv = *reinterpret_cast<const uint4*>(p.rope_cos + ro);
+                    const uint4 sv = *reinterpret_cast<const uint4*>(p.rope_sin + ro);
+                    v = rope_piece<T>(v, par, cv, sv, c < PC / 2);
+                }
                 *reinterpret_cast<uint4*>((isv ? p.v_pool : p.k_pool) + dst + cb) = v;
             }
         }
@@ -2974,13 +2999,14 @@ bool append_fusable(const sdl_attn_args* a) {
     return a->k_new && al16(a->k_new) && al16(a->v_new) && al16(a->k_pool) && al16(a->v_pool) && sb % 16 == 0;
 }
 
-// Whether plan `pl` applies RoPE inside the launch: the mma.sync kernels with
-// keys or query rows on M that store the new rows themselves, over 16-byte
-// aligned cos / sin rows (K pieces are rotated as 16-byte pieces).
+// Whether plan `pl` applies RoPE inside the launch: the mma.sync kernels
+// (keys or query rows on M, TMA-fed or register-direct) that store the new
+// rows themselves, over 16-byte aligned cos / sin rows (K pieces are rotated
+// as 16-byte pieces).
 bool rope_fusable(const sdl_attn_args* a, const Plan& pl) {
     auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     const int64_t rb = a->rope_stride * sdl::dtype_bytes(a->dtype);
-    return a->rope_cos && pl.tc && !pl.umma && !pl.direct && append_fusable(a) && al16(a->rope_cos) &&
+    return a->rope_cos && pl.tc && !pl.umma && append_fusable(a) && al16(a->rope_cos) &&
            al16(a->rope_sin) && rb % 16 == 0;
 }
 

@@ -482,9 +482,9 @@ def test_overlap_layers_gives_the_same_bits(chunk, Hq, d):
 
 def test_rope_fusion_query():
     """sdl_attention_fuses_rope: the mma.sync kernels that store the new rows
-    themselves rotate inside the launch; tcgen05, register-direct and
-    CUDA-core plans do not (the Python call rotates in place first), and a
-    call that asks a non-fusing plan for RoPE is refused."""
+    themselves (TMA-fed or register-direct) rotate inside the launch;
+    tcgen05 and CUDA-core plans do not (the Python call rotates in place
+    first), and a call that asks a non-fusing plan for RoPE is refused."""
     import ctypes
 
     from engine import _lib as lib
@@ -506,7 +506,7 @@ def test_rope_fusion_query():
     for layout in (0, 1, 2):  # verify block: rows or keys on M
         assert fuses(args(5, mma_layout=layout, use_umma=-1)[0]) == 1, layout
     assert fuses(args(1, mma_layout=1)[0]) == 1   # decode, keys on M
-    assert fuses(args(1, mma_layout=3)[0]) == 0   # register-direct decode
+    assert fuses(args(1, mma_layout=3)[0]) == 1   # register-direct decode
     assert fuses(args(5, force_generic=True)[0]) == 0
     a, keep = args(5, use_umma=1)                  # tcgen05
     assert fuses(a) == 0
