@@ -2663,14 +2663,21 @@ int rows_occupancy(int hd, int dtype, size_t smem, int threads) {
 // against 145 / 155 / 240 for the exact-count plan and 214 / 215 / 298 for
 // a one-wave plan at 55 % of the span.
 constexpr int kRaggedSplitDiv = 16;
+// The register-direct kernel's splits grow with the grid at twice that rate
+// (max(n/8, max_pages/16) pages; n = sequences x kv heads): measured on B200
+// over the same C4-shaped draft batches, span bucket 2048 / 4656 keys, pages
+// per split 8 / 12 / 16 / 24: 64 seqs 15.0 / 11.8 / 12.1 / 14.1 and 19.0 /
+// 16.1 / 14.3 / 14.6 us; 96 seqs 19.1 / 17.8 / 17.2 / 15.1 and 25.3 / 21.5 /
+// 21.7 / 17.2; at 8-48 seqs 8-12 pages (span 2048) and 12-19 (span 4656).
+constexpr int kRaggedSplitDivDirect = 8;
 constexpr int kRaggedMinSplitPages = 8;
 constexpr int kRaggedBlockChunk = 32;  // positions per row from which a block is prefill-sized
 constexpr int kRaggedMaxSplitPages = 64;
-int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ) {
+int split_pages(const sdl_attn_args* a, long base_ctas, int max_pages, int occ, int ragged_div = kRaggedSplitDiv) {
     if (a->pages_per_split > 0) return a->pages_per_split;
     if (a->key_count < 0) {
         const long span_div = a->chunk > 1 ? 32 : 16;
-        long pps = std::max<long>(base_ctas / kRaggedSplitDiv, (max_pages + span_div - 1) / span_div);
+        long pps = std::max<long>(base_ctas / ragged_div, (max_pages + span_div - 1) / span_div);
         pps = std::min<long>(kRaggedMaxSplitPages, std::max<long>(kRaggedMinSplitPages, pps));
         if (a->chunk >= kRaggedBlockChunk) {
             // prefill-sized blocks: a split's fp32 partials (chunk x Hq rows)
@@ -2822,7 +2829,7 @@ Plan make_direct_plan(const sdl_attn_args* a) {
     const int max_pages = std::max(1, (a->max_limit + kPage - 1) / kPage);
     const long base_ctas = (long)a->B * pl.kvgroups;
     const int occ = a->key_count > 0 ? direct_occupancy(a->head_dim, a->dtype) : 0;
-    finish_split_plan(a, pl, split_pages(a, base_ctas, max_pages, occ), max_pages, 1);
+    finish_split_plan(a, pl, split_pages(a, base_ctas, max_pages, occ, kRaggedSplitDivDirect), max_pages, 1);
     return pl;
 }
 

@@ -125,25 +125,28 @@ def _split_of(a):
     return ws // (a.B * a.chunk * a.Hq * (a.head_dim + 2) * 4)
 
 
-@pytest.mark.parametrize("B,chunk,Hq,d,span,base", [
-    (358, 5, 12, 128, 4656, 716),    # verify rows on M: one CTA per (sequence, kv head)
-    (1024, 5, 12, 128, 4656, 2048),
-    (64, 5, 12, 128, 4656, 128),
-    (16, 5, 12, 128, 4656, 32),
-    (358, 1, 14, 64, 4656, 358),     # decode keys on M: both kv heads in one CTA
-    (64, 1, 14, 64, 4656, 128),      # register-direct decode: one CTA per (sequence, kv head)
-    (16, 1, 14, 64, 32768, 32),
-    (16, 1, 14, 64, 1024, 32),
-    (96, 1, 14, 64, 32768, 192),
+@pytest.mark.parametrize("B,chunk,Hq,d,span,base,bdiv", [
+    (358, 5, 12, 128, 4656, 716, 16),    # verify rows on M: one CTA per (sequence, kv head)
+    (1024, 5, 12, 128, 4656, 2048, 16),
+    (64, 5, 12, 128, 4656, 128, 16),
+    (16, 5, 12, 128, 4656, 32, 16),
+    (358, 1, 14, 64, 4656, 358, 16),     # decode keys on M: both kv heads in one CTA
+    (112, 1, 14, 64, 2048, 112, 16),
+    (64, 1, 14, 64, 4656, 128, 8),       # register-direct decode: one CTA per (sequence, kv head)
+    (64, 1, 14, 64, 2048, 128, 8),
+    (96, 1, 14, 64, 2048, 192, 8),
+    (96, 1, 14, 64, 4656, 192, 8),
+    (16, 1, 14, 64, 32768, 32, 8),
+    (16, 1, 14, 64, 1024, 32, 8),
 ])
-def test_ragged_split_bounds(B, chunk, Hq, d, span, base):
+def test_ragged_split_bounds(B, chunk, Hq, d, span, base, bdiv):
     """key_count < 0: splits of max(base/16, span pages/16) pages for decode
-    and max(base/16, span pages/32) for blocks, within 8..64; the grid still
-    covers the span."""
+    (base/8 for the register-direct kernel) and max(base/16, span pages/32)
+    for blocks, within 8..64; the grid still covers the span."""
     a = _args(B, chunk, Hq, 2, d, span, key_count=-1)
     max_pages = -(-span // 16)
     div = 32 if chunk > 1 else 16
-    pps = min(64, max(8, max(base // 16, -(-max_pages // div))))
+    pps = min(64, max(8, max(base // bdiv, -(-max_pages // div))))
     pps = min(pps, max_pages)
     if chunk > 1:
         pps += pps % 2  # the rows-on-M kernel splits at whole 32-key tiles
