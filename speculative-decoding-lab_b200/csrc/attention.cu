@@ -2793,10 +2793,12 @@ constexpr int64_t kDirMidKeysHi = 560 * 1024;
 // sequences, where it skips the TMA ring's ramp.  0.5B-shaped draft decode
 // over C4-shaped batches (contexts floor(lognormal(6, 0.8)) + U[0, 512)
 // tokens, span buckets up to 4656 keys), graphs of 8 layers, measured on
-// B200 against the keys-on-M TMA kernel, both with the ragged split rule:
-// 1 / 8 / 16 / 32 / 64 / 96 / 128 sequences 6.2 / 8.7 / 9.0 / 9.2 / 13.3 /
-// 16.2 / 20.9 us against 8.5 / 14.6 / 14.1 / 11.8 / 18.3 / 19.7 / 20.5.
-constexpr int kDirRaggedMaxRows = 96;
+// B200 against the keys-on-M TMA kernel, both with their ragged split rules
+// (span bucket 4656 keys): 8 / 16 / 32 / 64 / 96 / 112 / 128 sequences
+// 9.5 / 10.0 / 12.8 / 13.7 / 17.1 / 17.7 / 19.6 us against 16.4 / 15.9 /
+// 18.5 / 18.4 / 19.8 / 20.1 / 20.3; at 160 they tie (22.1 / 21.8), and
+// from 192 the TMA kernel is ahead (23.2 against 26.4; 358: 40.6 / 43.4).
+constexpr int kDirRaggedMaxRows = 128;
 bool direct_applicable(const sdl_attn_args* a) {
     if (a->mma_layout == 1 || a->mma_layout == 2 || a->cluster_merge || !tc_applicable(a)) return false;
     if (a->chunk * (a->Hq / a->Hkv) > kDirCols) return false;

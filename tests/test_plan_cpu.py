@@ -67,11 +67,12 @@ def _kernel(a):
     ((8, 1, 4, 2, 16, 100), {"dtype": _lib.SDL_F32}, "generic"),  # fp32 pool
     ((32, 6, 12, 2, 128, 2048), {"force_generic": 1}, "generic"),
     # ragged rows of unknown lengths (a captured graph): register-direct only for
-    # head_dim-64 decode of up to 96 sequences, no tcgen05 auto choice
+    # head_dim-64 decode of up to 128 sequences, no tcgen05 auto choice
     ((358, 5, 12, 2, 128, 4656), {"key_count": -1}, "mma_rows"),   # C4 verify, 30 rows
     ((358, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),         # C4 draft decode
-    ((112, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),
-    ((96, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma_direct"),   # the drain's smaller batches
+    ((160, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma"),
+    ((128, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma_direct"),  # the drain's smaller batches
+    ((96, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma_direct"),
     ((64, 1, 14, 2, 64, 1500), {"key_count": -1}, "mma_direct"),
     ((1, 1, 14, 2, 64, 1024), {"key_count": -1}, "mma_direct"),
     ((64, 1, 14, 2, 64, 1500), {"key_count": -1, "mma_layout": 1}, "mma"),
@@ -131,7 +132,8 @@ def _split_of(a):
     (64, 5, 12, 128, 4656, 128, 16),
     (16, 5, 12, 128, 4656, 32, 16),
     (358, 1, 14, 64, 4656, 358, 16),     # decode keys on M: both kv heads in one CTA
-    (112, 1, 14, 64, 2048, 112, 16),
+    (160, 1, 14, 64, 2048, 160, 16),
+    (112, 1, 14, 64, 2048, 224, 8),
     (64, 1, 14, 64, 4656, 128, 8),       # register-direct decode: one CTA per (sequence, kv head)
     (64, 1, 14, 64, 2048, 128, 8),
     (96, 1, 14, 64, 2048, 192, 8),
