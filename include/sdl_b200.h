@@ -227,9 +227,12 @@ typedef struct sdl_attn_args {
                                  8..64 (n = unsplit CTAs, one per sequence
                                  and kv-head group), with
                                  rows on M for head_dim-128 blocks of
-                                 24+ rows and no automatic tcgen05 or
-                                 register-direct kernel.  Only the launch
-                                 shape depends on it, never the result (the
+                                 24+ rows, register-direct loads for
+                                 head_dim-64 decode of at most 128
+                                 sequences (splits of max(n/8,
+                                 max_limit/256) pages) and no automatic
+                                 tcgen05 kernel.  Only the launch shape
+                                 depends on it, never the result (the
                                  grid still covers max_limit)              */
     int32_t mma_layout;       /* mma.sync kernels: 0 = automatic (query rows
                                  on the MMA M dimension for blocks of at
