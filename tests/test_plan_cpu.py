@@ -118,6 +118,25 @@ def test_invalid_arguments_are_refused():
     assert lib.sdl_attention_workspace_bytes(ctypes.byref(a)) == 0
 
 
+@pytest.mark.parametrize("shape,flags,want_kernel,fuses", [
+    ((64, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma_direct", 1),   # captured draft decode, small bucket
+    ((358, 1, 14, 2, 64, 4656), {"key_count": -1}, "mma", 1),         # captured draft decode, large bucket
+    ((358, 5, 12, 2, 128, 4656), {"key_count": -1}, "mma_rows", 1),   # captured verify
+    ((16, 7, 16, 2, 128, 32768), {}, "tcgen05", 0),                   # tcgen05: q and k rotated first
+    ((32, 6, 12, 2, 128, 2048), {"force_generic": 1}, "generic", 0),
+])
+def test_rope_fusion_follows_the_plan(shape, flags, want_kernel, fuses):
+    """sdl_attention_fuses_rope (plan logic only, nothing launched): every
+    mma.sync plan that stores the new rows itself, the register-direct one
+    included, rotates q and k inside the launch; tcgen05 and CUDA-core plans
+    do not."""
+    lib = _lib.load()
+    cs = dict(rope_cos=0xA00000, rope_sin=0xB00000, rope_stride=2 * shape[4])
+    a = _args(*shape, k_new=0x800000, v_new=0x900000, new_row_stride=2 * shape[4], **cs, **flags)
+    assert _kernel(a) == want_kernel
+    assert lib.sdl_attention_fuses_rope(ctypes.byref(a)) == fuses
+
+
 
 def _split_of(a):
     """(splits per row, pages per split) of a plan, from its workspace bytes."""
